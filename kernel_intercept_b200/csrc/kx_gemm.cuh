@@ -1,0 +1,451 @@
+// kx_gemm.cuh — persistent, SM-quota-aware tcgen05 GEMM for sm_100a.
+//
+// Computes the cuBLAS column-major contract
+//     D[b] = epi(alpha * op(A[b]) * op(B[b]) + beta * C[b] + bias)
+// for the ops the kernel_intercept shim captures (cublasSgemm_v2,
+// cublasSgemmStridedBatched, cublasGemmEx, cublasGemmStridedBatchedEx,
+// cublasLtMatmul; see src/cublas_intercept.cpp:455-491 and 1453-1500 of the
+// reference for the calls this replaces).
+//
+// Mapping onto the tensor core.  GEMM rows i (M) become UMMA M (TMEM lanes),
+// GEMM columns j (N) become UMMA N (TMEM columns).  Because C is column-major,
+// the TMEM lane -> row mapping makes every epilogue store a coalesced
+// 32-row column segment.  op(A) is K-major in memory when transa = T and
+// M-major when transa = N; op(B) is K-major when transb = N and N-major when
+// transb = T.  Both majors are native UMMA operand layouts, so no transpose
+// pass is ever needed.
+//
+// Warp roles (256 threads, one CTA per SM):
+//   warp 0      TMA producer: takes tiles from the global tile queue,
+//               publishes them to the other roles, streams A/B k-blocks.
+//   warp 1      allocates TMEM; lane 0 issues tcgen05.mma.
+//   warps 2-3   fp32 path only: split each fp32 k-block into tf32 hi (in
+//               place) and lo (separate buffer) for 3xTF32.
+//   warps 4-7   epilogue: TMEM -> registers -> alpha/beta/bias/act -> HBM.
+// The accumulator is double-buffered in TMEM so the epilogue of tile t
+// overlaps the MMAs of tile t+1.
+//
+// Scheduling controls (replacing the reference's green-context SM split,
+// src/scheduler.cpp:244-446): the grid is bounded by the caller's SM quota;
+// tiles come from an atomic queue in a per-stream work slot, so a launch
+// that yields (host-mapped flag raised, or per-launch tile budget used up)
+// can be continued by relaunching the same call.
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "kx_ptx.cuh"
+
+namespace kx {
+
+enum class Arith : int { F32x3 = 0, TF32 = 1, BF16 = 2, F16 = 3 };
+
+// Per-stream bookkeeping for persistent launches (device memory).
+struct WorkSlot {
+  unsigned int next_tile;  // head of the tile queue
+  unsigned int exited;     // CTAs of the running launch that have retired
+  int status;              // last launch: 1 = op complete, 0 = yielded
+  int err;                 // first device-side error (KX_ERR_TIMEOUT)
+};
+
+enum : int { DT_F32 = 0, DT_F16 = 2, DT_BF16 = 14 };
+
+struct GemmParams {
+  int m, n, k;
+  int num_mb, num_nb, num_kb;
+  int tiles_per_batch, num_tiles;
+  int a_bcast, b_bcast;  // batch stride 0: use batch coordinate 0
+  float alpha, beta;
+  const float* alpha_dev;  // device pointer mode (nullable)
+  const float* beta_dev;
+  void* D;
+  long long ldd, strideD;
+  int d_type;
+  const void* C;
+  long long ldc, strideC;
+  int c_type;
+  int relu, gelu;
+  const void* bias;
+  int bias_type;
+  WorkSlot* work;
+  const volatile int* yield_flag;
+  volatile int* done_flag;
+  int max_tiles;
+  unsigned long long timeout_ns;
+  int* err_word;
+};
+
+template <int BN_, Arith AR_, bool A_MN_, bool B_MN_>
+struct GemmCfg {
+  static constexpr int BM = 128;
+  static constexpr int BN = BN_;
+  static constexpr Arith AR = AR_;
+  static constexpr bool A_MN = A_MN_;
+  static constexpr bool B_MN = B_MN_;
+  static constexpr int ESIZE = (AR == Arith::BF16 || AR == Arith::F16) ? 2 : 4;
+  static constexpr int BK = 128 / ESIZE;       // elements of K per 128-byte row
+  static constexpr int UMMA_K = 32 / ESIZE;    // K per tcgen05.mma (8 tf32 / 16 x 16-bit)
+  static constexpr int CHUNK = 128 / ESIZE;    // M/N elements per 128-byte chunk (MN-major)
+  static constexpr bool SPLIT = (AR == Arith::F32x3);
+  static constexpr int A_BYTES = BM * 128;
+  static constexpr int B_BYTES = BN * 128;
+  static constexpr int LOAD_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGE_BYTES = LOAD_BYTES * (SPLIT ? 2 : 1);
+  static constexpr int STAGES_RAW = (200 * 1024) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
+  static constexpr int RING = 4;  // depth of the tile-id broadcast ring
+  static constexpr int TMEM_COLS = (2 * BN) <= 32 ? 32 : (2 * BN) <= 64 ? 64 : (2 * BN) <= 128 ? 128 : (2 * BN) <= 256 ? 256 : 512;
+  static constexpr int THREADS = 256;
+  static constexpr int NUM_CONS = 1 + (SPLIT ? 2 : 0) + 4;  // ring consumers (arrivals)
+  static constexpr uint32_t A_LBO = A_MN ? BK * 128 : 16;
+  static constexpr uint32_t B_LBO = B_MN ? BK * 128 : 16;
+  static constexpr uint32_t FMT = (AR == Arith::BF16) ? 1u : (AR == Arith::F16) ? 0u : 2u;
+  static constexpr uint32_t IDESC = make_idesc(FMT, A_MN, B_MN, BM, BN);
+  // barrier block follows the stages
+  static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
+  static constexpr int SMEM_BYTES = 1024 /*align slack*/ + BAR_OFF + 1024 /*barriers*/;
+  static_assert(STAGES >= 2, "not enough shared memory for two stages");
+  static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "bad BN");
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+};
+
+struct SmemBars {
+  uint64_t full[8], conv[8], empty[8];
+  uint64_t tfull[2], tempty[2];
+  uint64_t ring_full[4], ring_empty[4];
+  uint64_t final_mma;
+  int ring[4];
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+KX_DEV float load_scalar(const void* p, int type, size_t idx) {
+  if (type == DT_F32) return static_cast<const float*>(p)[idx];
+  unsigned short h = static_cast<const unsigned short*>(p)[idx];
+  if (type == DT_BF16) return __uint_as_float(static_cast<uint32_t>(h) << 16);
+  return __half2float(__ushort_as_half(h));
+}
+
+KX_DEV void store_scalar(void* p, int type, size_t idx, float v) {
+  if (type == DT_F32) {
+    static_cast<float*>(p)[idx] = v;
+  } else if (type == DT_BF16) {
+    static_cast<__nv_bfloat16*>(p)[idx] = __float2bfloat16_rn(v);
+  } else {
+    static_cast<__half*>(p)[idx] = __float2half_rn(v);
+  }
+}
+
+KX_DEV float gelu_tanh(float x) {
+  const float k0 = 0.7978845608028654f;
+  return 0.5f * x * (1.0f + tanhf(k0 * (x + 0.044715f * x * x * x)));
+}
+
+KX_DEV void decode_tile(int tile, const GemmParams& p, int& b, int& mb, int& nb) {
+  b = tile / p.tiles_per_batch;
+  int t = tile - b * p.tiles_per_batch;
+  // grouped raster: 8 M-blocks share each sweep over N for L2 reuse of B
+  constexpr int G = 8;
+  int group_span = G * p.num_nb;
+  int g = t / group_span;
+  int first_mb = g * G;
+  int gsize = p.num_mb - first_mb < G ? p.num_mb - first_mb : G;
+  int r = t - g * group_span;
+  mb = first_mb + r % gsize;
+  nb = r / gsize;
+}
+
+template <class Cfg>
+__global__ void __launch_bounds__(256, 1)
+    kx_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
+                      const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
+  constexpr int S = Cfg::STAGES;
+  constexpr int R = Cfg::RING;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  SmemBars* sb = reinterpret_cast<SmemBars*>(smem + Cfg::BAR_OFF);
+
+  const int warp = threadIdx.x >> 5;
+  const uint32_t lane = threadIdx.x & 31;
+
+  auto stageA = [&](uint32_t s) { return smem + s * Cfg::STAGE_BYTES; };
+  auto stageB = [&](uint32_t s) { return smem + s * Cfg::STAGE_BYTES + Cfg::A_BYTES; };
+  auto stageAlo = [&](uint32_t s) { return smem + s * Cfg::STAGE_BYTES + Cfg::LOAD_BYTES; };
+  auto stageBlo = [&](uint32_t s) {
+    return smem + s * Cfg::STAGE_BYTES + Cfg::LOAD_BYTES + Cfg::A_BYTES;
+  };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(smem_addr(&sb->full[s]), 1);
+      mbar_init(smem_addr(&sb->conv[s]), 64);
+      mbar_init(smem_addr(&sb->empty[s]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_addr(&sb->tfull[a]), 1);
+      mbar_init(smem_addr(&sb->tempty[a]), 4);
+    }
+    for (int r = 0; r < R; ++r) {
+      mbar_init(smem_addr(&sb->ring_full[r]), 1);
+      mbar_init(smem_addr(&sb->ring_empty[r]), Cfg::NUM_CONS);
+    }
+    mbar_init(smem_addr(&sb->final_mma), 1);
+    sb->abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_addr(&sb->tmem_base), Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sb->tmem_base;
+
+  WaitCtl wc{&sb->abort_flag, p.err_word, p.timeout_ns};
+
+  if (warp == 0) {
+    // ------------------------------------------------------ TMA producer --
+    if (lane == 0) {
+      uint32_t it = 0;
+      int taken = 0;
+      for (uint32_t slot = 0;; ++slot) {
+        int tile;
+        if (p.max_tiles > 0 && taken >= p.max_tiles) {
+          tile = -2;
+        } else if (p.yield_flag != nullptr && *p.yield_flag != 0) {
+          tile = -2;
+        } else {
+          tile = static_cast<int>(atomicAdd(&p.work->next_tile, 1u));
+          if (tile >= p.num_tiles) tile = -1;
+        }
+        const uint32_t r = slot % R;
+        if (!mbar_wait(smem_addr(&sb->ring_empty[r]), ((slot / R) & 1) ^ 1, wc)) break;
+        sb->ring[r] = tile;
+        mbar_arrive(smem_addr(&sb->ring_full[r]));
+        if (tile < 0) break;
+        ++taken;
+        int b, mb, nb;
+        decode_tile(tile, p, b, mb, nb);
+        const int ba = p.a_bcast ? 0 : b;
+        const int bb = p.b_bcast ? 0 : b;
+        bool ok = true;
+        for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+          const uint32_t s = it % S;
+          if (!mbar_wait(smem_addr(&sb->empty[s]), ((it / S) & 1) ^ 1, wc)) { ok = false; break; }
+          const uint32_t fb = smem_addr(&sb->full[s]);
+          mbar_arrive_expect_tx(fb, Cfg::LOAD_BYTES);
+          const uint32_t sa = smem_addr(stageA(s));
+          const uint32_t sbb = smem_addr(stageB(s));
+          if (!Cfg::A_MN) {
+            tma_load_3d(sa, &tmA, fb, kb * Cfg::BK, mb * Cfg::BM, ba);
+          } else {
+#pragma unroll
+            for (int c = 0; c < Cfg::BM / Cfg::CHUNK; ++c)
+              tma_load_3d(sa + c * Cfg::BK * 128, &tmA, fb, mb * Cfg::BM + c * Cfg::CHUNK,
+                          kb * Cfg::BK, ba);
+          }
+          if (!Cfg::B_MN) {
+            tma_load_3d(sbb, &tmB, fb, kb * Cfg::BK, nb * Cfg::BN, bb);
+          } else {
+#pragma unroll
+            for (int c = 0; c < Cfg::BN / Cfg::CHUNK; ++c)
+              tma_load_3d(sbb + c * Cfg::BK * 128, &tmB, fb, nb * Cfg::BN + c * Cfg::CHUNK,
+                          kb * Cfg::BK, bb);
+          }
+        }
+        if (!ok) break;
+      }
+      // Drain: every issued TMA load must land before the CTA can retire.
+      WaitCtl drain{&sb->abort_flag, nullptr, p.timeout_ns};
+      int dummy_abort = 0;
+      drain.abort_flag = &dummy_abort;
+      const uint32_t first = it > static_cast<uint32_t>(S) ? it - S : 0;
+      for (uint32_t j = first; j < it; ++j)
+        mbar_wait(smem_addr(&sb->full[j % S]), (j / S) & 1, drain);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------- MMA issuer ---
+    if (lane == 0) {
+      uint32_t it = 0, tc = 0;
+      for (uint32_t slot = 0;; ++slot) {
+        const uint32_t r = slot % R;
+        if (!mbar_wait(smem_addr(&sb->ring_full[r]), (slot / R) & 1, wc)) break;
+        const int tile = sb->ring[r];
+        mbar_arrive(smem_addr(&sb->ring_empty[r]));
+        if (tile < 0) break;
+        const uint32_t a = tc & 1;
+        if (!mbar_wait(smem_addr(&sb->tempty[a]), ((tc >> 1) & 1) ^ 1, wc)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + a * Cfg::BN;
+        bool ok = true;
+        for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+          const uint32_t s = it % S;
+          const uint32_t wb = Cfg::SPLIT ? smem_addr(&sb->conv[s]) : smem_addr(&sb->full[s]);
+          if (!mbar_wait(wb, (it / S) & 1, wc)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_hi = smem_addr(stageA(s));
+          const uint32_t b_hi = smem_addr(stageB(s));
+          const uint32_t a_lo = smem_addr(stageAlo(s));
+          const uint32_t b_lo = smem_addr(stageBlo(s));
+#pragma unroll
+          for (int kk = 0; kk < Cfg::BK / Cfg::UMMA_K; ++kk) {
+            const uint32_t aoff = Cfg::A_MN ? kk * Cfg::UMMA_K * 128 : kk * 32;
+            const uint32_t boff = Cfg::B_MN ? kk * Cfg::UMMA_K * 128 : kk * 32;
+            const uint64_t ad = sdesc_sw128(a_hi + aoff, Cfg::A_LBO, 1024);
+            const uint64_t bd = sdesc_sw128(b_hi + boff, Cfg::B_LBO, 1024);
+            const uint32_t acc = (kb > 0 || kk > 0) ? 1u : 0u;
+            if constexpr (Cfg::AR == Arith::F32x3) {
+              const uint64_t adl = sdesc_sw128(a_lo + aoff, Cfg::A_LBO, 1024);
+              const uint64_t bdl = sdesc_sw128(b_lo + boff, Cfg::B_LBO, 1024);
+              umma_tf32(d_tmem, adl, bd, Cfg::IDESC, acc);
+              umma_tf32(d_tmem, ad, bdl, Cfg::IDESC, 1u);
+              umma_tf32(d_tmem, ad, bd, Cfg::IDESC, 1u);
+            } else if constexpr (Cfg::AR == Arith::TF32) {
+              umma_tf32(d_tmem, ad, bd, Cfg::IDESC, acc);
+            } else {
+              umma_f16(d_tmem, ad, bd, Cfg::IDESC, acc);
+            }
+          }
+          tc_commit(smem_addr(&sb->empty[s]));
+        }
+        if (!ok) break;
+        tc_commit(smem_addr(&sb->tfull[a]));
+        ++tc;
+      }
+      // Wait (bounded) for every MMA this thread issued before TMEM is freed.
+      tc_commit(smem_addr(&sb->final_mma));
+      int dummy_abort = 0;
+      WaitCtl drain{&dummy_abort, nullptr, p.timeout_ns};
+      mbar_wait(smem_addr(&sb->final_mma), 0, drain);
+    }
+  } else if (warp < 4) {
+    // ------------------------------------------- 3xTF32 split (fp32 only) --
+    if constexpr (Cfg::SPLIT) {
+      const int ct = threadIdx.x - 64;  // 0..63
+      uint32_t it = 0;
+      for (uint32_t slot = 0;; ++slot) {
+        const uint32_t r = slot % R;
+        bool ok = mbar_wait(smem_addr(&sb->ring_full[r]), (slot / R) & 1, wc);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        const int tile = sb->ring[r];
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_addr(&sb->ring_empty[r]));
+        if (tile < 0) break;
+        for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+          const uint32_t s = it % S;
+          ok = mbar_wait(smem_addr(&sb->full[s]), (it / S) & 1, wc);
+          ok = __all_sync(0xffffffffu, ok);
+          if (!ok) break;
+          // A and B (and their lo buffers) are contiguous: [A | B] and [Alo | Blo].
+          float4* hi = reinterpret_cast<float4*>(stageA(s));
+          float4* lo = reinterpret_cast<float4*>(stageAlo(s));
+          constexpr int NV = Cfg::LOAD_BYTES / 16;
+#pragma unroll 4
+          for (int v = ct; v < NV; v += 64) {
+            float4 x = hi[v];
+            float4 h, l;
+            h.x = tf32_rna(x.x); h.y = tf32_rna(x.y); h.z = tf32_rna(x.z); h.w = tf32_rna(x.w);
+            l.x = isfinite(h.x) ? x.x - h.x : 0.f;
+            l.y = isfinite(h.y) ? x.y - h.y : 0.f;
+            l.z = isfinite(h.z) ? x.z - h.z : 0.f;
+            l.w = isfinite(h.w) ? x.w - h.w : 0.f;
+            hi[v] = h;
+            lo[v] = l;
+          }
+          fence_proxy_async_smem();
+          mbar_arrive(smem_addr(&sb->conv[s]));
+        }
+        if (!ok) break;
+      }
+    }
+  } else {
+    // ------------------------------------------------------- epilogue -----
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    const float alpha = p.alpha_dev ? *p.alpha_dev : p.alpha;
+    const float beta = p.beta_dev ? *p.beta_dev : p.beta;
+    uint32_t tc = 0;
+    for (uint32_t slot = 0;; ++slot) {
+      const uint32_t r = slot % R;
+      bool ok = mbar_wait(smem_addr(&sb->ring_full[r]), (slot / R) & 1, wc);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      const int tile = sb->ring[r];
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_addr(&sb->ring_empty[r]));
+      if (tile < 0) break;
+      const uint32_t a = tc & 1;
+      ok = mbar_wait(smem_addr(&sb->tfull[a]), (tc >> 1) & 1, wc);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      int b, mb, nb;
+      decode_tile(tile, p, b, mb, nb);
+      const int row = mb * Cfg::BM + q * 32 + static_cast<int>(lane);
+      const bool row_ok = row < p.m;
+      const float bias_v = (p.bias != nullptr && row_ok) ? load_scalar(p.bias, p.bias_type, row) : 0.f;
+      const size_t d_base = static_cast<size_t>(b) * p.strideD + row;
+      const size_t c_base = static_cast<size_t>(b) * p.strideC + row;
+#pragma unroll 1
+      for (int c0 = 0; c0 < Cfg::BN; c0 += 32) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tmem + a * Cfg::BN + c0 + ((q * 32u) << 16), v);
+        tmem_ld_wait();
+        const int col0 = nb * Cfg::BN + c0;
+        if (row_ok) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int col = col0 + j;
+            if (col < p.n) {
+              float o = alpha * __uint_as_float(v[j]);
+              if (beta != 0.f)
+                o += beta * load_scalar(p.C, p.c_type, c_base + static_cast<size_t>(col) * p.ldc);
+              o += bias_v;
+              if (p.relu) o = fmaxf(o, 0.f);
+              if (p.gelu) o = gelu_tanh(o);
+              store_scalar(p.D, p.d_type, d_base + static_cast<size_t>(col) * p.ldd, o);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_addr(&sb->tempty[a]));
+      ++tc;
+    }
+  }
+
+  // --------------------------------------------------------- teardown ----
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, Cfg::TMEM_COLS);
+  }
+  if (threadIdx.x == 0) {
+    const bool aborted = sb->abort_flag != 0;
+    __threadfence();
+    const unsigned prev = atomicAdd(&p.work->exited, 1u);
+    if (prev == gridDim.x - 1) {
+      __threadfence();
+      const unsigned nt = atomicAdd(&p.work->next_tile, 0u);
+      const bool complete = nt >= static_cast<unsigned>(p.num_tiles);
+      if (complete || aborted) atomicExch(&p.work->next_tile, 0u);
+      atomicExch(&p.work->exited, 0u);
+      p.work->status = complete ? 1 : 0;
+      if (p.done_flag != nullptr) {
+        *p.done_flag = complete ? 1 : 0;
+        __threadfence_system();
+      }
+    }
+    if (aborted) atomicCAS(&p.work->err, 0, 3);
+  }
+}
+
+}  // namespace kx

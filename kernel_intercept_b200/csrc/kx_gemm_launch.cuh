@@ -1,0 +1,109 @@
+// kx_gemm_launch.cuh — host launcher for one tcgen05 GEMM configuration.
+// Each kx_gemm_tc_<arith>.cu includes this and instantiates the launchers
+// for its arithmetic, so the 48 kernel variants compile in parallel.
+#pragma once
+#include <cstdio>
+
+#include "kx_gemm.cuh"
+#include "kx_runtime.cuh"
+
+namespace kx {
+
+struct TcProblem {
+  int m, n, k, batch;
+  const void* A;
+  long long lda, strideA;
+  const void* B;
+  long long ldb, strideB;
+};
+
+template <Arith AR>
+constexpr CUtensorMapDataType map_dtype() {
+  return AR == Arith::BF16  ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+         : AR == Arith::F16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                            : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+}
+
+template <Arith AR>
+constexpr const char* arith_name() {
+  return AR == Arith::F32x3 ? "f32x3" : AR == Arith::TF32 ? "tf32" : AR == Arith::BF16 ? "bf16" : "f16";
+}
+
+template <int BN, Arith AR, bool AMN, bool BMN>
+int launch_gemm_tc(const Exec& e, const TcProblem& pr, GemmParams p) {
+  using Cfg = GemmCfg<BN, AR, AMN, BMN>;
+  constexpr CUtensorMapDataType dt = map_dtype<AR>();
+  CUtensorMap ma, mb;
+  bool ok;
+  if (AMN)
+    ok = encode_map_3d(&ma, dt, Cfg::ESIZE, pr.A, pr.m, pr.k, pr.batch, pr.lda, pr.strideA,
+                       Cfg::CHUNK, Cfg::BK);
+  else
+    ok = encode_map_3d(&ma, dt, Cfg::ESIZE, pr.A, pr.k, pr.m, pr.batch, pr.lda, pr.strideA,
+                       Cfg::BK, Cfg::BM);
+  if (!ok) return KX_ERR_UNSUPPORTED;
+  if (BMN)
+    ok = encode_map_3d(&mb, dt, Cfg::ESIZE, pr.B, pr.n, pr.k, pr.batch, pr.ldb, pr.strideB,
+                       Cfg::CHUNK, Cfg::BK);
+  else
+    ok = encode_map_3d(&mb, dt, Cfg::ESIZE, pr.B, pr.k, pr.n, pr.batch, pr.ldb, pr.strideB,
+                       Cfg::BK, BN);
+  if (!ok) return KX_ERR_UNSUPPORTED;
+
+  p.num_mb = (pr.m + Cfg::BM - 1) / Cfg::BM;
+  p.num_nb = (pr.n + BN - 1) / BN;
+  p.num_kb = (pr.k + Cfg::BK - 1) / Cfg::BK;
+  p.tiles_per_batch = p.num_mb * p.num_nb;
+  const long long tiles = static_cast<long long>(p.tiles_per_batch) * pr.batch;
+  if (tiles <= 0 || tiles > 0x7fffffffLL) return KX_ERR_UNSUPPORTED;
+  p.num_tiles = static_cast<int>(tiles);
+  p.a_bcast = (pr.batch > 1 && pr.strideA == 0) ? 1 : 0;
+  p.b_bcast = (pr.batch > 1 && pr.strideB == 0) ? 1 : 0;
+
+  auto kern = kx_gemm_tc_kernel<Cfg>;
+  static bool attr_set[64] = {false};
+  const DeviceInfo& di = device_info();
+  if (!attr_set[di.device & 63]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             Cfg::SMEM_BYTES) != cudaSuccess)
+      return KX_ERR_DEVICE;
+    attr_set[di.device & 63] = true;
+  }
+  const int grid = persistent_grid(e, p.num_tiles);
+  kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, e.stream>>>(ma, mb, p);
+  static char name[96];
+  if (name[0] == 0)
+    snprintf(name, sizeof(name), "kx_gemm_tc<bn%d,%s,A%s,B%s>", BN, arith_name<AR>(),
+             AMN ? "mn" : "k", BMN ? "mn" : "k");
+  set_last_kernel_name(name);
+  return launch_status();
+}
+
+// Per-arithmetic dispatch over (BN, A major, B major).
+template <Arith AR>
+int dispatch_gemm_tc(int bn, bool amn, bool bmn, const Exec& e, const TcProblem& pr,
+                     const GemmParams& p) {
+#define KX_CASE(BNV)                                                           \
+  if (bn == BNV) {                                                              \
+    if (!amn && !bmn) return launch_gemm_tc<BNV, AR, false, false>(e, pr, p);   \
+    if (!amn && bmn) return launch_gemm_tc<BNV, AR, false, true>(e, pr, p);     \
+    if (amn && !bmn) return launch_gemm_tc<BNV, AR, true, false>(e, pr, p);     \
+    return launch_gemm_tc<BNV, AR, true, true>(e, pr, p);                       \
+  }
+  KX_CASE(256)
+  KX_CASE(128)
+  KX_CASE(64)
+#undef KX_CASE
+  return KX_ERR_UNSUPPORTED;
+}
+
+int dispatch_gemm_tc_f32x3(int bn, bool amn, bool bmn, const Exec& e, const TcProblem& pr,
+                           const GemmParams& p);
+int dispatch_gemm_tc_tf32(int bn, bool amn, bool bmn, const Exec& e, const TcProblem& pr,
+                          const GemmParams& p);
+int dispatch_gemm_tc_bf16(int bn, bool amn, bool bmn, const Exec& e, const TcProblem& pr,
+                          const GemmParams& p);
+int dispatch_gemm_tc_f16(int bn, bool amn, bool bmn, const Exec& e, const TcProblem& pr,
+                         const GemmParams& p);
+
+}  // namespace kx

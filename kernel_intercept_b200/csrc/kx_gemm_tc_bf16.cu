@@ -1,0 +1,9 @@
+// Instantiates the tcgen05 GEMM launchers for Arith::BF16.
+#include "kx_gemm_launch.cuh"
+
+namespace kx {
+int dispatch_gemm_tc_bf16(int bn, bool amn, bool bmn, const Exec& e, const TcProblem& pr,
+                        const GemmParams& p) {
+  return dispatch_gemm_tc<Arith::BF16>(bn, amn, bmn, e, pr, p);
+}
+}  // namespace kx

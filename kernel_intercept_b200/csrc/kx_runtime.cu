@@ -1,0 +1,209 @@
+// kx_runtime.cu — device info, work-slot pool, tensor-map encoding.
+#include "kx_runtime.cuh"
+
+#include <cstdio>
+#include <cstring>
+#include <vector>
+
+namespace kx {
+
+namespace {
+
+std::mutex g_mu;
+DeviceInfo g_dev[64];
+
+struct SlotPool {
+  WorkSlot* base = nullptr;
+  int capacity = 0;
+  int used = 0;
+  std::unordered_map<cudaStream_t, int> by_stream;
+};
+SlotPool g_pools[64];
+
+constexpr int kSlotsPerDevice = 4096;
+
+thread_local const char* tl_kernel_name = "none";
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeTiledFn g_encode = nullptr;
+bool g_encode_looked_up = false;
+
+EncodeTiledFn encode_fn() {
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_encode_looked_up) {
+    g_encode_looked_up = true;
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      g_encode = reinterpret_cast<EncodeTiledFn>(fn);
+    }
+  }
+  return g_encode;
+}
+
+}  // namespace
+
+const DeviceInfo& device_info() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  std::lock_guard<std::mutex> lk(g_mu);
+  DeviceInfo& d = g_dev[dev];
+  if (d.device < 0) {
+    cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaDeviceGetAttribute(&d.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    d.device = dev;
+  }
+  return d;
+}
+
+WorkSlot* work_slot_for(cudaStream_t stream) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  std::lock_guard<std::mutex> lk(g_mu);
+  SlotPool& pool = g_pools[dev];
+  if (pool.base == nullptr) {
+    void* p = nullptr;
+    if (cudaMalloc(&p, sizeof(WorkSlot) * kSlotsPerDevice) != cudaSuccess) return nullptr;
+    if (cudaMemset(p, 0, sizeof(WorkSlot) * kSlotsPerDevice) != cudaSuccess) return nullptr;
+    if (cudaDeviceSynchronize() != cudaSuccess) return nullptr;
+    pool.base = static_cast<WorkSlot*>(p);
+    pool.capacity = kSlotsPerDevice;
+  }
+  auto it = pool.by_stream.find(stream);
+  if (it != pool.by_stream.end()) return pool.base + it->second;
+  if (pool.used >= pool.capacity) return nullptr;
+  int idx = pool.used++;
+  pool.by_stream.emplace(stream, idx);
+  return pool.base + idx;
+}
+
+Exec resolve_exec(const kx_exec* ex) {
+  Exec e;
+  if (ex != nullptr) {
+    e.stream = static_cast<cudaStream_t>(ex->stream);
+    e.sm_quota = ex->sm_quota;
+    e.yield_flag = ex->yield_flag;
+    e.done_flag = ex->done_flag;
+    e.max_tiles = ex->max_tiles;
+    if (ex->timeout_ns != 0) e.timeout_ns = ex->timeout_ns;
+    e.fp32_mode = ex->fp32_mode;
+    e.err_word = ex->err_word;
+  }
+  return e;
+}
+
+int persistent_grid(const Exec& e, int tiles) {
+  int sms = device_info().num_sms;
+  int cap = (e.sm_quota > 0 && e.sm_quota < sms) ? e.sm_quota : sms;
+  if (tiles < cap) cap = tiles;
+  return cap < 1 ? 1 : cap;
+}
+
+bool encode_map(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* base,
+                const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box) {
+  EncodeTiledFn fn = encode_fn();
+  if (fn == nullptr) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0) return false;
+  cuuint64_t d[5];
+  cuuint64_t s[4];
+  cuuint32_t b[5];
+  cuuint32_t es[5] = {1, 1, 1, 1, 1};
+  for (int i = 0; i < rank; ++i) {
+    if (dims[i] == 0 || dims[i] > (1ull << 32)) return false;
+    d[i] = dims[i];
+    b[i] = box[i];
+  }
+  for (int i = 0; i + 1 < rank; ++i) {
+    if ((strides_bytes[i] & 15u) != 0 || strides_bytes[i] >= (1ull << 40)) return false;
+    s[i] = strides_bytes[i];
+  }
+  std::memset(map, 0, sizeof(CUtensorMap));
+  CUresult r = fn(map, dt, static_cast<cuuint32_t>(rank), const_cast<void*>(base), d, s, b, es,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+bool encode_map_3d(CUtensorMap* map, CUtensorMapDataType dt, int esize, const void* base,
+                   uint64_t inner, uint64_t outer, uint64_t batch, uint64_t ld_elems,
+                   uint64_t batch_stride_elems, uint32_t box_inner, uint32_t box_outer) {
+  uint64_t dims[3] = {inner, outer, batch};
+  uint32_t box[3] = {box_inner, box_outer, 1};
+  if (batch <= 1 || batch_stride_elems == 0) {
+    uint64_t strides[1] = {ld_elems * static_cast<uint64_t>(esize)};
+    dims[2] = 1;
+    // rank-2 map; the kernel's third coordinate is then always 0
+    uint64_t d3[3] = {inner, outer, 1};
+    uint64_t s3[2] = {strides[0], strides[0] * outer};
+    // keep the rank at 3 so kernels issue one instruction form
+    if ((s3[1] & 15u) != 0) s3[1] = (s3[1] + 15u) & ~static_cast<uint64_t>(15u);
+    return encode_map(map, dt, 3, base, d3, s3, box);
+  }
+  uint64_t strides[2] = {ld_elems * static_cast<uint64_t>(esize),
+                         batch_stride_elems * static_cast<uint64_t>(esize)};
+  return encode_map(map, dt, 3, base, dims, strides, box);
+}
+
+void set_last_kernel_name(const char* name) { tl_kernel_name = name; }
+
+}  // namespace kx
+
+extern "C" int kx_num_sms(void) { return kx::device_info().num_sms; }
+
+extern "C" const char* kx_last_kernel_name(void) { return kx::tl_kernel_name; }
+
+extern "C" const char* kx_version(void) { return "kx 0.1 sm_100a"; }
+
+extern "C" int kx_host_flags_alloc(int count, int** host, int** dev) {
+  if (count <= 0 || host == nullptr || dev == nullptr) return KX_ERR_INVALID;
+  void* h = nullptr;
+  if (cudaHostAlloc(&h, sizeof(int) * count, cudaHostAllocMapped | cudaHostAllocPortable) !=
+      cudaSuccess)
+    return KX_ERR_NOMEM;
+  std::memset(h, 0, sizeof(int) * count);
+  void* d = nullptr;
+  if (cudaHostGetDevicePointer(&d, h, 0) != cudaSuccess) {
+    cudaFreeHost(h);
+    return KX_ERR_DEVICE;
+  }
+  *host = static_cast<int*>(h);
+  *dev = static_cast<int*>(d);
+  return KX_OK;
+}
+
+extern "C" int kx_host_flags_free(int* host) {
+  if (host == nullptr) return KX_OK;
+  return cudaFreeHost(host) == cudaSuccess ? KX_OK : KX_ERR_DEVICE;
+}
+
+namespace kx {
+// One thread polls the flag with the same give-up rule as the persistent
+// kernels' bounded waits: re-check a deadline every 256 polls.
+__global__ void kx_wait_flag_kernel(const volatile int* flag, unsigned long long timeout_ns,
+                                    int* status) {
+  uint64_t t0 = globaltimer();
+  uint32_t polls = 0;
+  while (*flag == 0) {
+    if ((++polls & 255u) == 0 && globaltimer() - t0 > timeout_ns) {
+      *status = KX_ERR_TIMEOUT;
+      return;
+    }
+  }
+  *status = KX_OK;
+}
+}  // namespace kx
+
+extern "C" int kx_wait_flag(void* stream, const volatile int* flag,
+                            unsigned long long timeout_ns, int* status) {
+  if (flag == nullptr || status == nullptr) return KX_ERR_INVALID;
+  kx::kx_wait_flag_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(flag, timeout_ns,
+                                                                         status);
+  return kx::launch_status();
+}

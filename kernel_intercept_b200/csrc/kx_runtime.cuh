@@ -1,0 +1,70 @@
+// kx_runtime.cuh — host-side runtime shared by the kx entry points:
+// device properties, the per-stream work-slot pool used by persistent
+// launches, tensor-map encoding through the driver entry point, and the
+// execution-control defaults.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <mutex>
+#include <unordered_map>
+
+#include "kx.h"
+#include "kx_gemm.cuh"
+
+namespace kx {
+
+struct DeviceInfo {
+  int device = -1;
+  int num_sms = 0;
+  int max_smem_optin = 0;
+};
+
+// Properties of the current device (cached per device).
+const DeviceInfo& device_info();
+
+// A WorkSlot reserved for `stream` on the current device.  Slots live in one
+// device allocation per device (made on first use, zero-initialised) and are
+// reused by every op enqueued on the same stream: a persistent launch resets
+// its slot when it completes, and stream order serialises ops on one stream.
+WorkSlot* work_slot_for(cudaStream_t stream);
+
+// Resolved execution controls.
+struct Exec {
+  cudaStream_t stream = nullptr;
+  int sm_quota = 0;
+  const volatile int* yield_flag = nullptr;
+  volatile int* done_flag = nullptr;
+  int max_tiles = 0;
+  unsigned long long timeout_ns = 2000000000ull;
+  int fp32_mode = KX_FP32_3XTF32;
+  int* err_word = nullptr;
+};
+
+Exec resolve_exec(const kx_exec* ex);
+
+// Grid size for a persistent launch with `tiles` work items.
+int persistent_grid(const Exec& e, int tiles);
+
+// cuTensorMapEncodeTiled through cudaGetDriverEntryPoint (no libcuda link).
+// 3-D map {inner, outer, batch} with 128-byte swizzle.  Returns false when the
+// driver rejects the geometry (caller falls back to the SIMT kernel).
+bool encode_map_3d(CUtensorMap* map, CUtensorMapDataType dt, int esize, const void* base,
+                   uint64_t inner, uint64_t outer, uint64_t batch, uint64_t ld_elems,
+                   uint64_t batch_stride_elems, uint32_t box_inner, uint32_t box_outer);
+
+// Generic tiled map of rank 2..5 (dims/strides in elements / bytes as the
+// driver expects), 128-byte swizzle, zero OOB fill.
+bool encode_map(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* base,
+                const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box);
+
+void set_last_kernel_name(const char* name);
+
+// Status mapping helper.
+inline int launch_status() {
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? KX_OK : KX_ERR_DEVICE;
+}
+
+}  // namespace kx
