@@ -89,10 +89,12 @@ enum {
  *               the GPU (it replaces the green-context SM split of
  *               src/scheduler.cpp:244-446).
  *  yield_flag   host-mapped int (pinned memory).  When non-NULL, persistent
- *               CTAs read it before taking each new tile and stop while it is
- *               non-zero.  The op's progress stays in its work slot, so calling
- *               the same entry point again with identical arguments continues
- *               where it stopped.  Ops with a yield flag should pass done_flag.
+ *               CTAs read it before taking each new tile: 0 = keep going;
+ *               f > 0 = only CTAs with index < f keep taking tiles (the op
+ *               still completes, on fewer SMs); f < 0 = every CTA stops.  A
+ *               stopped op keeps its progress in its work slot, so calling the
+ *               same entry point again with identical arguments continues where
+ *               it stopped.  Ops that may stop should pass done_flag.
  *  done_flag    host-mapped int.  When non-NULL the last CTA of the launch
  *               writes 1 (all tiles finished) or 0 (yielded) to it.
  *  max_tiles    >0: each CTA takes at most this many tiles per launch (a

@@ -205,16 +205,18 @@ bool tma_ok(const void* ptr, long long ld, long long stride, int batch, int es) 
   return true;
 }
 
-int choose_bn(int m, int n, int batch, int sms) {
+// Widest N tile that still gives every SM a tile; 3xTF32 tiles stop at 128
+// (the epilogue keeps a BN-wide fp32 accumulator per thread).
+int choose_bn(int m, int n, int batch, int sms, int max_bn) {
   if (const char* f = std::getenv("KX_GEMM_BN")) {
     int v = std::atoi(f);
-    if (v == 64 || v == 128 || v == 256) return v;
+    if ((v == 64 || v == 128 || v == 256) && v <= max_bn) return v;
   }
   const long long mb = (m + 127) / 128;
   auto tiles = [&](int bn) { return mb * ((n + bn - 1) / bn) * batch; };
-  if (tiles(256) >= sms) return 256;
+  if (max_bn >= 256 && tiles(256) >= sms) return 256;
   if (tiles(128) >= sms) return 128;
-  return n > 64 ? 64 : 64;
+  return 64;
 }
 
 int run_gemm(const kx_exec* ex, const GemmCall& g) {
@@ -294,7 +296,7 @@ int run_gemm(const kx_exec* ex, const GemmCall& g) {
 
   TcProblem pr{g.m, g.n, g.k, g.batch, g.A, g.lda, g.strideA, g.B, g.ldb, g.strideB};
   const int sms = persistent_grid(e, 1 << 30);
-  const int bn = choose_bn(g.m, g.n, g.batch, sms);
+  const int bn = choose_bn(g.m, g.n, g.batch, sms, ar == Arith::F32x3 ? 128 : 256);
   const bool amn = ta == 0, bmn = tb == 1;
   int rc;
   switch (ar) {

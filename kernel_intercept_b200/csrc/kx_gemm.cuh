@@ -97,8 +97,25 @@ struct GemmCfg {
   static constexpr int TMEM_COLS = (2 * BN) <= 32 ? 32 : (2 * BN) <= 64 ? 64 : (2 * BN) <= 128 ? 128 : (2 * BN) <= 256 ? 256 : 512;
   static constexpr int THREADS = 256;
   static constexpr int NUM_CONS = 1 + (SPLIT ? 2 : 0) + 4;  // ring consumers (arrivals)
+  // 3xTF32: the tensor core's fp32 accumulation does not round to nearest, so
+  // the error of one TMEM accumulator grows linearly with its K length.  The
+  // K loop is therefore cut into segments of SEG k-blocks (256 of K); each
+  // segment accumulates in its own TMEM buffer and the epilogue warps fold it
+  // into round-to-nearest fp32 registers.
+  static constexpr bool PROMOTE = (AR == Arith::F32x3);
+  static constexpr int SEG = PROMOTE ? 8 : (1 << 30);
+  // Descriptor geometry.  K-major: 128-byte swizzle (layout 2), SBO 1024.
+  // M/N-major 16-bit: layout 2, 8-row atoms, SBO 1024.  M/N-major tf32:
+  // 32-byte-atom swizzle (layout 1), 4-row atoms, SBO 512.
+  static constexpr bool A_MN32 = A_MN && ESIZE == 4;
+  static constexpr bool B_MN32 = B_MN && ESIZE == 4;
   static constexpr uint32_t A_LBO = A_MN ? BK * 128 : 16;
   static constexpr uint32_t B_LBO = B_MN ? BK * 128 : 16;
+  static constexpr uint32_t A_SBO = A_MN32 ? 512 : 1024;
+  static constexpr uint32_t B_SBO = B_MN32 ? 512 : 1024;
+  static constexpr uint32_t A_LAYOUT = A_MN32 ? 1 : 2;
+  static constexpr uint32_t B_LAYOUT = B_MN32 ? 1 : 2;
+  static_assert(!PROMOTE || BN <= 128, "3xTF32 keeps a BN-wide fp32 accumulator per thread");
   static constexpr uint32_t FMT = (AR == Arith::BF16) ? 1u : (AR == Arith::F16) ? 0u : 2u;
   static constexpr uint32_t IDESC = make_idesc(FMT, A_MN, B_MN, BM, BN);
   // barrier block follows the stages
@@ -216,9 +233,12 @@ __global__ void __launch_bounds__(256, 1)
       int taken = 0;
       for (uint32_t slot = 0;; ++slot) {
         int tile;
+        // yield flag f: 0 = run; f > 0 = only CTAs below f keep taking tiles
+        // (the op still completes on them); f < 0 = every CTA stops.
+        const int f = p.yield_flag != nullptr ? *p.yield_flag : 0;
         if (p.max_tiles > 0 && taken >= p.max_tiles) {
           tile = -2;
-        } else if (p.yield_flag != nullptr && *p.yield_flag != 0) {
+        } else if (f < 0 || (f > 0 && static_cast<int>(blockIdx.x) >= f)) {
           tile = -2;
         } else {
           tile = static_cast<int>(atomicAdd(&p.work->next_tile, 1u));
@@ -272,51 +292,58 @@ __global__ void __launch_bounds__(256, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------- MMA issuer ---
     if (lane == 0) {
-      uint32_t it = 0, tc = 0;
-      for (uint32_t slot = 0;; ++slot) {
+      // `sc` counts accumulator segments across tiles; segment sc uses TMEM
+      // buffer sc & 1 (one segment per tile unless PROMOTE splits K).
+      uint32_t it = 0, sc = 0;
+      bool ok = true;
+      for (uint32_t slot = 0; ok; ++slot) {
         const uint32_t r = slot % R;
         if (!mbar_wait(smem_addr(&sb->ring_full[r]), (slot / R) & 1, wc)) break;
         const int tile = sb->ring[r];
         mbar_arrive(smem_addr(&sb->ring_empty[r]));
         if (tile < 0) break;
-        const uint32_t a = tc & 1;
-        if (!mbar_wait(smem_addr(&sb->tempty[a]), ((tc >> 1) & 1) ^ 1, wc)) break;
-        tc_fence_after();
-        const uint32_t d_tmem = tmem + a * Cfg::BN;
-        bool ok = true;
-        for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
-          const uint32_t s = it % S;
-          const uint32_t wb = Cfg::SPLIT ? smem_addr(&sb->conv[s]) : smem_addr(&sb->full[s]);
-          if (!mbar_wait(wb, (it / S) & 1, wc)) { ok = false; break; }
+        for (int kb = 0; kb < p.num_kb && ok; ++sc) {
+          const uint32_t a = sc & 1;
+          if (!mbar_wait(smem_addr(&sb->tempty[a]), ((sc >> 1) & 1) ^ 1, wc)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t a_hi = smem_addr(stageA(s));
-          const uint32_t b_hi = smem_addr(stageB(s));
-          const uint32_t a_lo = smem_addr(stageAlo(s));
-          const uint32_t b_lo = smem_addr(stageBlo(s));
+          const uint32_t d_tmem = tmem + a * Cfg::BN;
+          const int kend = (p.num_kb - kb > Cfg::SEG) ? kb + Cfg::SEG : p.num_kb;
+          const int kfirst = kb;
+          for (; kb < kend; ++kb, ++it) {
+            const uint32_t s = it % S;
+            const uint32_t wb = Cfg::SPLIT ? smem_addr(&sb->conv[s]) : smem_addr(&sb->full[s]);
+            if (!mbar_wait(wb, (it / S) & 1, wc)) { ok = false; break; }
+            tc_fence_after();
+            const uint32_t a_hi = smem_addr(stageA(s));
+            const uint32_t b_hi = smem_addr(stageB(s));
+            const uint32_t a_lo = smem_addr(stageAlo(s));
+            const uint32_t b_lo = smem_addr(stageBlo(s));
 #pragma unroll
-          for (int kk = 0; kk < Cfg::BK / Cfg::UMMA_K; ++kk) {
-            const uint32_t aoff = Cfg::A_MN ? kk * Cfg::UMMA_K * 128 : kk * 32;
-            const uint32_t boff = Cfg::B_MN ? kk * Cfg::UMMA_K * 128 : kk * 32;
-            const uint64_t ad = sdesc_sw128(a_hi + aoff, Cfg::A_LBO, 1024);
-            const uint64_t bd = sdesc_sw128(b_hi + boff, Cfg::B_LBO, 1024);
-            const uint32_t acc = (kb > 0 || kk > 0) ? 1u : 0u;
-            if constexpr (Cfg::AR == Arith::F32x3) {
-              const uint64_t adl = sdesc_sw128(a_lo + aoff, Cfg::A_LBO, 1024);
-              const uint64_t bdl = sdesc_sw128(b_lo + boff, Cfg::B_LBO, 1024);
-              umma_tf32(d_tmem, adl, bd, Cfg::IDESC, acc);
-              umma_tf32(d_tmem, ad, bdl, Cfg::IDESC, 1u);
-              umma_tf32(d_tmem, ad, bd, Cfg::IDESC, 1u);
-            } else if constexpr (Cfg::AR == Arith::TF32) {
-              umma_tf32(d_tmem, ad, bd, Cfg::IDESC, acc);
-            } else {
-              umma_f16(d_tmem, ad, bd, Cfg::IDESC, acc);
+            for (int kk = 0; kk < Cfg::BK / Cfg::UMMA_K; ++kk) {
+              const uint32_t aoff = Cfg::A_MN ? kk * Cfg::UMMA_K * 128 : kk * 32;
+              const uint32_t boff = Cfg::B_MN ? kk * Cfg::UMMA_K * 128 : kk * 32;
+              const uint64_t ad = sdesc_sw128(a_hi + aoff, Cfg::A_LBO, Cfg::A_SBO, Cfg::A_LAYOUT);
+              const uint64_t bd = sdesc_sw128(b_hi + boff, Cfg::B_LBO, Cfg::B_SBO, Cfg::B_LAYOUT);
+              const uint32_t acc = (kb > kfirst || kk > 0) ? 1u : 0u;
+              if constexpr (Cfg::AR == Arith::F32x3) {
+                const uint64_t adl =
+                    sdesc_sw128(a_lo + aoff, Cfg::A_LBO, Cfg::A_SBO, Cfg::A_LAYOUT);
+                const uint64_t bdl =
+                    sdesc_sw128(b_lo + boff, Cfg::B_LBO, Cfg::B_SBO, Cfg::B_LAYOUT);
+                umma_tf32(d_tmem, adl, bd, Cfg::IDESC, acc);
+                umma_tf32(d_tmem, ad, bdl, Cfg::IDESC, 1u);
+                umma_tf32(d_tmem, ad, bd, Cfg::IDESC, 1u);
+              } else if constexpr (Cfg::AR == Arith::TF32) {
+                umma_tf32(d_tmem, ad, bd, Cfg::IDESC, acc);
+              } else {
+                umma_f16(d_tmem, ad, bd, Cfg::IDESC, acc);
+              }
             }
+            tc_commit(smem_addr(&sb->empty[s]));
           }
-          tc_commit(smem_addr(&sb->empty[s]));
+          if (!ok) break;
+          tc_commit(smem_addr(&sb->tfull[a]));
         }
-        if (!ok) break;
-        tc_commit(smem_addr(&sb->tfull[a]));
-        ++tc;
       }
       // Wait (bounded) for every MMA this thread issued before TMEM is freed.
       tc_commit(smem_addr(&sb->final_mma));
@@ -370,7 +397,9 @@ __global__ void __launch_bounds__(256, 1)
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     const float alpha = p.alpha_dev ? *p.alpha_dev : p.alpha;
     const float beta = p.beta_dev ? *p.beta_dev : p.beta;
-    uint32_t tc = 0;
+    const int nseg = Cfg::PROMOTE ? (p.num_kb + Cfg::SEG - 1) / Cfg::SEG : 1;
+    const uint32_t lane_off = (q * 32u) << 16;
+    uint32_t sc = 0;
     for (uint32_t slot = 0;; ++slot) {
       const uint32_t r = slot % R;
       bool ok = mbar_wait(smem_addr(&sb->ring_full[r]), (slot / R) & 1, wc);
@@ -380,11 +409,6 @@ __global__ void __launch_bounds__(256, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_addr(&sb->ring_empty[r]));
       if (tile < 0) break;
-      const uint32_t a = tc & 1;
-      ok = mbar_wait(smem_addr(&sb->tfull[a]), (tc >> 1) & 1, wc);
-      ok = __all_sync(0xffffffffu, ok);
-      if (!ok) break;
-      tc_fence_after();
       int b, mb, nb;
       decode_tile(tile, p, b, mb, nb);
       const int row = mb * Cfg::BM + q * 32 + static_cast<int>(lane);
@@ -392,32 +416,73 @@ __global__ void __launch_bounds__(256, 1)
       const float bias_v = (p.bias != nullptr && row_ok) ? load_scalar(p.bias, p.bias_type, row) : 0.f;
       const size_t d_base = static_cast<size_t>(b) * p.strideD + row;
       const size_t c_base = static_cast<size_t>(b) * p.strideC + row;
-#pragma unroll 1
-      for (int c0 = 0; c0 < Cfg::BN; c0 += 32) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(tmem + a * Cfg::BN + c0 + ((q * 32u) << 16), v);
-        tmem_ld_wait();
+      // alpha/beta/bias/activation for 32 consecutive columns of this row
+      auto emit = [&](int c0, const float* acc) {
         const int col0 = nb * Cfg::BN + c0;
-        if (row_ok) {
+        if (!row_ok) return;
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int col = col0 + j;
-            if (col < p.n) {
-              float o = alpha * __uint_as_float(v[j]);
-              if (beta != 0.f)
-                o += beta * load_scalar(p.C, p.c_type, c_base + static_cast<size_t>(col) * p.ldc);
-              o += bias_v;
-              if (p.relu) o = fmaxf(o, 0.f);
-              if (p.gelu) o = gelu_tanh(o);
-              store_scalar(p.D, p.d_type, d_base + static_cast<size_t>(col) * p.ldd, o);
-            }
+        for (int j = 0; j < 32; ++j) {
+          const int col = col0 + j;
+          if (col < p.n) {
+            float o = alpha * acc[j];
+            if (beta != 0.f)
+              o += beta * load_scalar(p.C, p.c_type, c_base + static_cast<size_t>(col) * p.ldc);
+            o += bias_v;
+            if (p.relu) o = fmaxf(o, 0.f);
+            if (p.gelu) o = gelu_tanh(o);
+            store_scalar(p.D, p.d_type, d_base + static_cast<size_t>(col) * p.ldd, o);
           }
         }
+      };
+      if constexpr (Cfg::PROMOTE) {
+        // fold every segment's TMEM partial into round-to-nearest registers
+        float acc[Cfg::BN / 32][32];
+#pragma unroll
+        for (int c = 0; c < Cfg::BN / 32; ++c)
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc[c][j] = 0.f;
+        for (int sg = 0; sg < nseg; ++sg, ++sc) {
+          const uint32_t a = sc & 1;
+          ok = mbar_wait(smem_addr(&sb->tfull[a]), (sc >> 1) & 1, wc);
+          ok = __all_sync(0xffffffffu, ok);
+          if (!ok) break;
+          tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < Cfg::BN / 32; ++c) {
+            uint32_t v[32];
+            tmem_ld_32x32b_x32(tmem + a * Cfg::BN + c * 32 + lane_off, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) acc[c][j] += __uint_as_float(v[j]);
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(smem_addr(&sb->tempty[a]));
+        }
+        if (!ok) break;
+#pragma unroll
+        for (int c = 0; c < Cfg::BN / 32; ++c) emit(c * 32, acc[c]);
+      } else {
+        const uint32_t a = sc & 1;
+        ok = mbar_wait(smem_addr(&sb->tfull[a]), (sc >> 1) & 1, wc);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll 1
+        for (int c0 = 0; c0 < Cfg::BN; c0 += 32) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(tmem + a * Cfg::BN + c0 + lane_off, v);
+          tmem_ld_wait();
+          float f[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]);
+          emit(c0, f);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_addr(&sb->tempty[a]));
+        ++sc;
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_addr(&sb->tempty[a]));
-      ++tc;
     }
   }
 

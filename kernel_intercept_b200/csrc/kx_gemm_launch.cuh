@@ -35,16 +35,21 @@ int launch_gemm_tc(const Exec& e, const TcProblem& pr, GemmParams p) {
   constexpr CUtensorMapDataType dt = map_dtype<AR>();
   CUtensorMap ma, mb;
   bool ok;
+  // M/N-major tf32 operands need the 32-byte-atom variant of the 128-byte swizzle
+  constexpr CUtensorMapSwizzle swzA =
+      Cfg::A_MN32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B;
+  constexpr CUtensorMapSwizzle swzB =
+      Cfg::B_MN32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B;
   if (AMN)
     ok = encode_map_3d(&ma, dt, Cfg::ESIZE, pr.A, pr.m, pr.k, pr.batch, pr.lda, pr.strideA,
-                       Cfg::CHUNK, Cfg::BK);
+                       Cfg::CHUNK, Cfg::BK, swzA);
   else
     ok = encode_map_3d(&ma, dt, Cfg::ESIZE, pr.A, pr.k, pr.m, pr.batch, pr.lda, pr.strideA,
                        Cfg::BK, Cfg::BM);
   if (!ok) return KX_ERR_UNSUPPORTED;
   if (BMN)
     ok = encode_map_3d(&mb, dt, Cfg::ESIZE, pr.B, pr.n, pr.k, pr.batch, pr.ldb, pr.strideB,
-                       Cfg::CHUNK, Cfg::BK);
+                       Cfg::CHUNK, Cfg::BK, swzB);
   else
     ok = encode_map_3d(&mb, dt, Cfg::ESIZE, pr.B, pr.k, pr.n, pr.batch, pr.ldb, pr.strideB,
                        Cfg::BK, BN);
@@ -90,7 +95,9 @@ int dispatch_gemm_tc(int bn, bool amn, bool bmn, const Exec& e, const TcProblem&
     if (amn && !bmn) return launch_gemm_tc<BNV, AR, true, false>(e, pr, p);     \
     return launch_gemm_tc<BNV, AR, true, true>(e, pr, p);                       \
   }
-  KX_CASE(256)
+  if constexpr (AR != Arith::F32x3) {
+    KX_CASE(256)
+  }
   KX_CASE(128)
   KX_CASE(64)
 #undef KX_CASE

@@ -204,15 +204,20 @@ KX_DEV void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "
 // MN-major, 128B swizzle: 128-byte chunks along M/N, one row per K index,
 //   8 K-rows per 1024 B atom; LBO = byte distance between 128-byte M/N chunks,
 //   SBO = 1024 (next 8 K rows).
-KX_DEV uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+KX_DEV uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes,
+                            uint32_t layout = 2) {
   uint64_t d = 0;
   d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
   d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
   d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
   d |= static_cast<uint64_t>(1) << 46;
-  d |= static_cast<uint64_t>(2) << 61;
+  d |= static_cast<uint64_t>(layout & 7u) << 61;
   return d;
 }
+// Layout 1 (128-byte swizzle of 32-byte atoms) is the only M/N-major layout
+// the tensor core accepts for 32-bit (tf32) operands: rows of 128 bytes, one
+// per K index, 4-row (512 B) swizzle atoms, so SBO = 512.  TMA writes it with
+// CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B.
 
 // Instruction descriptor for kind::tf32 / kind::f16 with an fp32 accumulator.
 // fmt: 0 = f16, 1 = bf16, 2 = tf32.  *_mn: operand is M/N-major in smem.

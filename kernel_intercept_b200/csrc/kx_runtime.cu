@@ -84,6 +84,38 @@ WorkSlot* work_slot_for(cudaStream_t stream) {
   return pool.base + idx;
 }
 
+namespace {
+struct Scratch {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+};
+std::unordered_map<cudaStream_t, Scratch> g_scratch[64];
+}  // namespace
+
+void* scratch_for(cudaStream_t stream, size_t bytes) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (bytes == 0) bytes = 256;
+  std::lock_guard<std::mutex> lk(g_mu);
+  Scratch& s = g_scratch[dev][stream];
+  if (s.bytes >= bytes) return s.ptr;
+  if (s.ptr != nullptr) {
+    cudaFree(s.ptr);
+    s.ptr = nullptr;
+    s.bytes = 0;
+  }
+  size_t want = bytes + bytes / 8;  // headroom against repeated small growth
+  want = (want + 255) & ~static_cast<size_t>(255);
+  if (cudaMalloc(&s.ptr, want) != cudaSuccess) {
+    cudaGetLastError();
+    s.ptr = nullptr;
+    return nullptr;
+  }
+  s.bytes = want;
+  return s.ptr;
+}
+
 Exec resolve_exec(const kx_exec* ex) {
   Exec e;
   if (ex != nullptr) {
@@ -107,7 +139,8 @@ int persistent_grid(const Exec& e, int tiles) {
 }
 
 bool encode_map(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* base,
-                const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box) {
+                const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+                CUtensorMapSwizzle swz) {
   EncodeTiledFn fn = encode_fn();
   if (fn == nullptr) return false;
   if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0) return false;
@@ -126,14 +159,15 @@ bool encode_map(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* 
   }
   std::memset(map, 0, sizeof(CUtensorMap));
   CUresult r = fn(map, dt, static_cast<cuuint32_t>(rank), const_cast<void*>(base), d, s, b, es,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
 bool encode_map_3d(CUtensorMap* map, CUtensorMapDataType dt, int esize, const void* base,
                    uint64_t inner, uint64_t outer, uint64_t batch, uint64_t ld_elems,
-                   uint64_t batch_stride_elems, uint32_t box_inner, uint32_t box_outer) {
+                   uint64_t batch_stride_elems, uint32_t box_inner, uint32_t box_outer,
+                   CUtensorMapSwizzle swz) {
   uint64_t dims[3] = {inner, outer, batch};
   uint32_t box[3] = {box_inner, box_outer, 1};
   if (batch <= 1 || batch_stride_elems == 0) {
@@ -144,11 +178,11 @@ bool encode_map_3d(CUtensorMap* map, CUtensorMapDataType dt, int esize, const vo
     uint64_t s3[2] = {strides[0], strides[0] * outer};
     // keep the rank at 3 so kernels issue one instruction form
     if ((s3[1] & 15u) != 0) s3[1] = (s3[1] + 15u) & ~static_cast<uint64_t>(15u);
-    return encode_map(map, dt, 3, base, d3, s3, box);
+    return encode_map(map, dt, 3, base, d3, s3, box, swz);
   }
   uint64_t strides[2] = {ld_elems * static_cast<uint64_t>(esize),
                          batch_stride_elems * static_cast<uint64_t>(esize)};
-  return encode_map(map, dt, 3, base, dims, strides, box);
+  return encode_map(map, dt, 3, base, dims, strides, box, swz);
 }
 
 void set_last_kernel_name(const char* name) { tl_kernel_name = name; }

@@ -30,6 +30,12 @@ const DeviceInfo& device_info();
 // its slot when it completes, and stream order serialises ops on one stream.
 WorkSlot* work_slot_for(cudaStream_t stream);
 
+// Scratch device memory reserved for `stream` on the current device, at least
+// `bytes` long.  Growing it frees the previous buffer (cudaFree waits for the
+// device), so ops on one stream may reuse it back to back; ops on different
+// streams get different buffers.  Returns nullptr on allocation failure.
+void* scratch_for(cudaStream_t stream, size_t bytes);
+
 // Resolved execution controls.
 struct Exec {
   cudaStream_t stream = nullptr;
@@ -52,12 +58,14 @@ int persistent_grid(const Exec& e, int tiles);
 // driver rejects the geometry (caller falls back to the SIMT kernel).
 bool encode_map_3d(CUtensorMap* map, CUtensorMapDataType dt, int esize, const void* base,
                    uint64_t inner, uint64_t outer, uint64_t batch, uint64_t ld_elems,
-                   uint64_t batch_stride_elems, uint32_t box_inner, uint32_t box_outer);
+                   uint64_t batch_stride_elems, uint32_t box_inner, uint32_t box_outer,
+                   CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B);
 
 // Generic tiled map of rank 2..5 (dims/strides in elements / bytes as the
 // driver expects), 128-byte swizzle, zero OOB fill.
 bool encode_map(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* base,
-                const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box);
+                const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
+                CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B);
 
 void set_last_kernel_name(const char* name);
 

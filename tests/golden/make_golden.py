@@ -48,16 +48,22 @@ def _parent() -> int:
     env["LD_PRELOAD"] = REF_SHIM
     env["ORION_ASYNC_MODE"] = "0"
     env["ORION_LOG_LEVEL"] = "WARN"
-    env["KX_GOLDEN_CHILD"] = "1"
-    return subprocess.run([sys.executable, os.path.abspath(__file__)], env=env,
-                          timeout=600).returncode
+    env["KX_GOLDEN_CHILD"] = "gemm"
+    rc = subprocess.run([sys.executable, os.path.abspath(__file__)], env=env,
+                        timeout=300).returncode
+    # convolutions do not pass through the shim: run them without the preload
+    env = dict(os.environ)
+    env.pop("LD_PRELOAD", None)
+    env["KX_GOLDEN_CHILD"] = "conv"
+    rc2 = subprocess.run([sys.executable, os.path.abspath(__file__)], env=env,
+                         timeout=300).returncode
+    return rc or rc2
 
 
-def _child() -> int:
+def _child_gemm() -> int:
     import torch
 
     torch.backends.cuda.matmul.allow_tf32 = False
-    torch.backends.cudnn.allow_tf32 = False
     torch.zeros(1, device="cuda")
     g = ctypes.CDLL(None)  # global scope: the preloaded reference shim comes first
     for name in ("orion_init_scheduler", "orion_start_scheduler_thread", "orion_set_capture",
@@ -150,8 +156,19 @@ def _child() -> int:
                             A=bits(dA), B=bits(dB), C_out=bits(dC))
         written.append(path)
 
-    g.orion_stop_scheduler()
+    for p in written:
+        print(os.path.relpath(p, ROOT), os.path.getsize(p), flush=True)
+    # The reference's orion_stop_scheduler can block in its worker join; the
+    # fixtures are written, so leave without tearing the shim down.
+    sys.stdout.flush()
+    os._exit(0)
 
+
+def _child_conv() -> int:
+    import torch
+
+    torch.backends.cudnn.allow_tf32 = False
+    written = []
     # ---- cuDNN convolutions (via PyTorch, TF32 off) ---------------------------
     conv_cases = [(2, 8, 12, 12, 16, 3, 3, (1, 1), (1, 1), (1, 1)),
                   (2, 5, 13, 11, 7, 3, 3, (0, 1), (2, 1), (1, 1))]
@@ -177,4 +194,9 @@ def _child() -> int:
 
 
 if __name__ == "__main__":
-    sys.exit(_child() if os.environ.get("KX_GOLDEN_CHILD") == "1" else _parent())
+    mode = os.environ.get("KX_GOLDEN_CHILD")
+    if mode == "gemm":
+        sys.exit(_child_gemm())
+    if mode == "conv":
+        sys.exit(_child_conv())
+    sys.exit(_parent())
