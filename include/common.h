@@ -48,6 +48,8 @@ enum class OperationType : uint8_t {
     CUBLAS_GEMM_EX,                  // cublasGemmEx / cublasSgemmEx / cublasHgemm
     CUBLAS_GEMM_STRIDED_BATCHED_EX,  // cublasGemmStridedBatchedEx / cublasHgemmStridedBatched
     CUDNN_BATCHNORM_INF,             // cudnnBatchNormalizationForwardInference
+    EVENT_RECORD,                    // cudaEventRecord(WithFlags): kept in client order
+    STREAM_WAIT_EVENT,               // cudaStreamWaitEvent: kept in client order
     UNKNOWN
 };
 
@@ -84,6 +86,8 @@ inline const char* op_type_name(OperationType type) {
         case OperationType::CUBLAS_GEMM_EX: return "CUBLAS_GEMM_EX";
         case OperationType::CUBLAS_GEMM_STRIDED_BATCHED_EX: return "CUBLAS_GEMM_STRIDED_BATCHED_EX";
         case OperationType::CUDNN_BATCHNORM_INF: return "CUDNN_BATCHNORM_INF";
+        case OperationType::EVENT_RECORD: return "EVENT_RECORD";
+        case OperationType::STREAM_WAIT_EVENT: return "STREAM_WAIT_EVENT";
         default: return "UNKNOWN";
     }
 }

@@ -20,7 +20,7 @@
 #ifndef ORION_GPU_CAPTURE_H
 #define ORION_GPU_CAPTURE_H
 
-#include <cuda_runtime.h>
+#include <cuda_runtime_api.h>
 
 #include <atomic>
 #include <cstddef>
@@ -104,6 +104,7 @@ struct MemsetParams {
 struct SyncParams {
     cudaStream_t stream;
     cudaEvent_t event;
+    unsigned int flags;
 };
 
 /** Decoded convolution geometry (NCHW / KCRS, 2-D, groups = 1). */

@@ -30,10 +30,14 @@ struct KernelProfile {
     int grid_size;
     int block_size;
     size_t shared_mem_bytes;
+    // additions: client, captured op type and its algorithmic work (FLOPs or bytes)
+    int client_idx;
+    std::string op_type;
+    double work;
 
     KernelProfile()
         : duration_ms(0.0f), sm_needed(0), profile_type(ProfileType::UNKNOWN), grid_size(0),
-          block_size(0), shared_mem_bytes(0) {}
+          block_size(0), shared_mem_bytes(0), client_idx(-1), work(0.0) {}
 };
 
 class KernelProfileTable {
@@ -65,6 +69,7 @@ public:
     void end_session(const std::string& output_path);
     void record_kernel(const std::string& kernel_id, float duration_ms, int sm_needed,
                        ProfileType profile_type);
+    void record(const KernelProfile& p);
     void get_profile_table(KernelProfileTable& table) const;
     bool active() const { return session_active_; }
 

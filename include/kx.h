@@ -234,6 +234,10 @@ const char* kx_last_kernel_name(void);
 /* Version string of the library. */
 const char* kx_version(void);
 
+/* Number of kernels this library has launched in this process (all devices,
+ * all threads; the count is taken on the host just before each launch). */
+unsigned long long kx_launch_count(void);
+
 #ifdef __cplusplus
 }
 #endif

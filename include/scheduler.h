@@ -23,7 +23,7 @@
 #ifndef ORION_SCHEDULER_H
 #define ORION_SCHEDULER_H
 
-#include <cuda_runtime.h>
+#include <cuda_runtime_api.h>
 
 #include <atomic>
 #include <chrono>
@@ -123,6 +123,8 @@ public:
 
     /** Applies fixed HP/BE SM budgets (ISOLATED mode). */
     bool init_green_contexts(const GreenCtxConfig& gc_config);
+    /** Returns to DEFAULT mode (shared SMs, HP flag). */
+    void clear_budgets() { isolated_ = false; }
     /** Wave-model choice of budgets from the loaded kernel_info profiles. */
     GreenCtxConfig choose_best_green_ctx_config_from_profiles() const;
 
@@ -137,6 +139,9 @@ public:
     int* hp_flag_device() const { return hp_flag_dev_; }
 
     ClientStats& stats(int client_idx) { return stats_[client_idx < 0 ? 0 : client_idx % MAX_CLIENTS]; }
+
+    /** Resolves the CUDA events recorded around profiled ops into g_profiler. */
+    void flush_profile();
 
     std::atomic<bool> running_{false};
 
@@ -171,6 +176,13 @@ private:
     std::mutex hp_mu_;
 
     ClientStats stats_[MAX_CLIENTS];
+
+    struct PendingProfile {
+        cudaEvent_t start, end;
+        KernelProfile rec;
+    };
+    std::mutex prof_mu_;
+    std::vector<PendingProfile> pending_prof_;
 };
 
 extern Scheduler g_scheduler;

@@ -362,11 +362,13 @@ extern "C" int kx_bn_fwd_training(const kx_exec* ex, int mode, const float* alph
     const int G = c * HW;
     float2* coef = static_cast<float2*>(scratch_for(e.stream, sizeof(float2) * G));
     if (!coef) return KX_ERR_NOMEM;
+    note_launch();
     bn_stats_per_activation<<<(G + 255) / 256, 256, 0, e.stream>>>(
         x, n, G, scale, bias, exp_avg_factor, running_mean, running_var, eps, save_mean,
         save_inv_var, coef, nullptr, nullptr);
     const size_t total = static_cast<size_t>(n) * G;
     int blocks = static_cast<int>((total + 255) / 256 < 8u * device_info().num_sms ? (total + 255) / 256 : 8u * device_info().num_sms);
+    note_launch();
     bn_apply_per_activation<<<blocks, 256, 0, e.stream>>>(x, y, n, G, coef, *alpha, *beta);
     set_last_kernel_name("kx_bn_apply_per_activation");
     return launch_status();
@@ -378,12 +380,15 @@ extern "C" int kx_bn_fwd_training(const kx_exec* ex, int mode, const float* alph
   if (!base) return KX_ERR_NOMEM;
   double* part = reinterpret_cast<double*>(base);
   float2* coef = reinterpret_cast<float2*>(base + ((part_bytes + 255) & ~static_cast<size_t>(255)));
+  note_launch();
   bn_stats_spatial<<<dim3(c, S), kThreads, 0, e.stream>>>(x, n, c, HW, S, part);
+  note_launch();
   bn_finalize_spatial<<<(c + 127) / 128, 128, 0, e.stream>>>(x, n, c, HW, S, part, scale, bias,
                                                              exp_avg_factor, running_mean,
                                                              running_var, eps, save_mean,
                                                              save_inv_var, coef);
   const long long rows = static_cast<long long>(n) * c;
+  note_launch();
   bn_apply_spatial<<<apply_grid(rows, HW), kThreads, 0, e.stream>>>(x, y, c, HW, rows, coef,
                                                                    *alpha, *beta);
   set_last_kernel_name("kx_bn_apply_spatial");
@@ -403,14 +408,17 @@ extern "C" int kx_bn_fwd_inference(const kx_exec* ex, int mode, const float* alp
   const int G = mode == 0 ? c * HW : c;
   float2* coef = static_cast<float2*>(scratch_for(e.stream, sizeof(float2) * G));
   if (!coef) return KX_ERR_NOMEM;
+  note_launch();
   bn_stats_per_activation<<<(G + 255) / 256, 256, 0, e.stream>>>(
       x, n, G, scale, bias, 0.0, nullptr, nullptr, eps, nullptr, nullptr, coef, est_mean, est_var);
   if (mode == 0) {
     const size_t total = static_cast<size_t>(n) * G;
     int blocks = static_cast<int>((total + 255) / 256 < 8u * device_info().num_sms ? (total + 255) / 256 : 8u * device_info().num_sms);
+    note_launch();
     bn_apply_per_activation<<<blocks, 256, 0, e.stream>>>(x, y, n, G, coef, *alpha, *beta);
   } else {
     const long long rows = static_cast<long long>(n) * c;
+    note_launch();
     bn_apply_spatial<<<apply_grid(rows, HW), kThreads, 0, e.stream>>>(x, y, c, HW, rows, coef,
                                                                      *alpha, *beta);
   }
@@ -451,11 +459,14 @@ extern "C" int kx_bn_bwd(const kx_exec* ex, int mode, const float* alpha_data,
   if (mu == nullptr || iv == nullptr) {
     // recompute batch statistics into scratch (scale/bias only feed fcoef)
     if (mode == 0) {
+      note_launch();
       bn_stats_per_activation<<<(G + 255) / 256, 256, 0, e.stream>>>(
           x, n, G, scale, scale, 0.0, nullptr, nullptr, eps, mean_g, inv_g, fcoef, nullptr,
           nullptr);
     } else {
+      note_launch();
       bn_stats_spatial<<<dim3(c, S), kThreads, 0, e.stream>>>(x, n, c, HW, S, part);
+      note_launch();
       bn_finalize_spatial<<<(c + 127) / 128, 128, 0, e.stream>>>(
           x, n, c, HW, S, part, scale, scale, 0.0, nullptr, nullptr, eps, mean_g, inv_g, fcoef);
     }
@@ -463,15 +474,19 @@ extern "C" int kx_bn_bwd(const kx_exec* ex, int mode, const float* alpha_data,
     iv = inv_g;
   }
   if (mode == 0) {
+    note_launch();
     bn_bwd_per_activation<<<(G + 255) / 256, 256, 0, e.stream>>>(
         x, dy, dx, n, G, mu, iv, scale, dscale, dbias, *alpha_data, *beta_data, *alpha_param,
         *beta_param);
   } else {
+    note_launch();
     bn_bwd_reduce_spatial<<<dim3(c, S), kThreads, 0, e.stream>>>(x, dy, n, c, HW, S, mu, part);
+    note_launch();
     bn_bwd_finalize<<<(c + 127) / 128, 128, 0, e.stream>>>(
         c, static_cast<double>(n) * HW, S, part, mu, iv, scale, dscale, dbias, *alpha_param,
         *beta_param, coef);
     const long long rows = static_cast<long long>(n) * c;
+    note_launch();
     bn_bwd_apply_spatial<<<apply_grid(rows, HW), kThreads, 0, e.stream>>>(
         x, dy, dx, c, HW, rows, coef, *alpha_data, *beta_data);
   }

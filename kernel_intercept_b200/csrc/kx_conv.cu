@@ -166,7 +166,10 @@ __global__ void set_flag(volatile int* flag, int v) {
 }
 
 int finish_done(const Exec& e) {
-  if (e.done_flag != nullptr) set_flag<<<1, 1, 0, e.stream>>>(e.done_flag, 1);
+  if (e.done_flag != nullptr) {
+    note_launch();
+    set_flag<<<1, 1, 0, e.stream>>>(e.done_flag, 1);
+  }
   return launch_status();
 }
 
@@ -200,6 +203,7 @@ extern "C" int kx_conv_fwd(const kx_exec* ex, const kx_conv_desc* d, const float
   const float* wt = w;
   if (repack) {
     float* wf = col + col_elems;
+    note_launch();
     prepare_filter<<<grid_1d(wf_elems), 256, 0, e.stream>>>(w, wf, g.K, g.C, g.R, g.S, Kp,
                                                             g.xcorr ? 0 : 1);
     wt = wf;
@@ -209,6 +213,7 @@ extern "C" int kx_conv_fwd(const kx_exec* ex, const kx_conv_desc* d, const float
   for (int n0 = 0; n0 < g.N; n0 += nb) {
     const int cnt = g.N - n0 < nb ? g.N - n0 : nb;
     dim3 grid((g.PQ + 255) / 256 < 64 ? (g.PQ + 255) / 256 : 64, g.CRS, cnt);
+    note_launch();
     im2col_tap_major<<<grid, 256, 0, e.stream>>>(x, col, g, n0);
     // y_n (PQ x K, ld PQ) = colT_n^T * W^T
     int rc = kx_sgemm_strided_batched(&ie, KX_OP_N, KX_OP_N, g.PQ, g.K, g.CRS, &a, col, g.ldpq,
@@ -235,6 +240,7 @@ extern "C" int kx_conv_bwd_data(const kx_exec* ex, const kx_conv_desc* d, const 
   const float* wt = w;
   if (repack) {
     float* wf = col + col_elems;
+    note_launch();
     prepare_filter<<<grid_1d(wf_elems), 256, 0, e.stream>>>(w, wf, g.K, g.C, g.R, g.S, Kp,
                                                             g.xcorr ? 0 : 1);
     wt = wf;
@@ -250,6 +256,7 @@ extern "C" int kx_conv_bwd_data(const kx_exec* ex, const kx_conv_desc* d, const 
                                       col, g.ldpq, static_cast<long long>(g.CRS) * g.ldpq, cnt);
     if (rc != KX_OK) return rc;
     dim3 grid((g.H * g.W + 255) / 256 < 64 ? (g.H * g.W + 255) / 256 : 64, g.C, cnt);
+    note_launch();
     col2im_gather<<<grid, 256, 0, e.stream>>>(col, dx, g, n0, *alpha, *beta);
   }
   return finish_done(e);
@@ -274,6 +281,7 @@ extern "C" int kx_conv_bwd_filter(const kx_exec* ex, const kx_conv_desc* d, cons
   for (int n0 = 0; n0 < g.N; n0 += nb) {
     const int cnt = g.N - n0 < nb ? g.N - n0 : nb;
     dim3 grid((g.PQ + 255) / 256 < 64 ? (g.PQ + 255) / 256 : 64, g.CRS, cnt);
+    note_launch();
     im2col_tap_major<<<grid, 256, 0, e.stream>>>(x, col, g, n0);
     for (int i = 0; i < cnt; ++i) {
       // dW (CRS x K col-major, ld CRS) += colT_n (CRS x PQ) * dy_n^T (PQ x K)
@@ -286,6 +294,7 @@ extern "C" int kx_conv_bwd_filter(const kx_exec* ex, const kx_conv_desc* d, cons
     }
   }
   if (!g.xcorr) {
+    note_launch();
     flip_accumulate<<<grid_1d(acc_elems), 256, 0, e.stream>>>(dst, dw, g.K * g.C, g.R, g.S,
                                                               *alpha, *beta);
   }

@@ -193,6 +193,7 @@ int launch_simt(const Exec& e, const GemmCall& g, bool dev_scalars) {
   p.done_flag = e.done_flag;
   dim3 grid((g.m + 63) / 64, (g.n + 63) / 64, g.batch);
   if (grid.y > 65535 || grid.z > 65535) return KX_ERR_UNSUPPORTED;
+  note_launch();
   kx_gemm_simt_kernel<<<grid, 256, 0, e.stream>>>(p);
   set_last_kernel_name("kx_gemm_simt");
   return launch_status();

@@ -75,6 +75,7 @@ int launch_gemm_tc(const Exec& e, const TcProblem& pr, GemmParams p) {
     attr_set[di.device & 63] = true;
   }
   const int grid = persistent_grid(e, p.num_tiles);
+  note_launch();
   kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, e.stream>>>(ma, mb, p);
   static char name[96];
   if (name[0] == 0)

@@ -1,6 +1,7 @@
 // kx_runtime.cu — device info, work-slot pool, tensor-map encoding.
 #include "kx_runtime.cuh"
 
+#include <atomic>
 #include <cstdio>
 #include <cstring>
 #include <vector>
@@ -187,7 +188,15 @@ bool encode_map_3d(CUtensorMap* map, CUtensorMapDataType dt, int esize, const vo
 
 void set_last_kernel_name(const char* name) { tl_kernel_name = name; }
 
+static std::atomic<unsigned long long> g_launches{0};
+
+void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
 }  // namespace kx
+
+extern "C" unsigned long long kx_launch_count(void) {
+  return kx::g_launches.load(std::memory_order_relaxed);
+}
 
 extern "C" int kx_num_sms(void) { return kx::device_info().num_sms; }
 
@@ -237,6 +246,7 @@ __global__ void kx_wait_flag_kernel(const volatile int* flag, unsigned long long
 extern "C" int kx_wait_flag(void* stream, const volatile int* flag,
                             unsigned long long timeout_ns, int* status) {
   if (flag == nullptr || status == nullptr) return KX_ERR_INVALID;
+  kx::note_launch();
   kx::kx_wait_flag_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(flag, timeout_ns,
                                                                          status);
   return kx::launch_status();

@@ -69,6 +69,10 @@ bool encode_map(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* 
 
 void set_last_kernel_name(const char* name);
 
+// Counts one kernel launch of this library (process-wide, read back by
+// kx_launch_count).  Every `<<<...>>>` site calls it just before launching.
+void note_launch();
+
 // Status mapping helper.
 inline int launch_status() {
   cudaError_t e = cudaGetLastError();

@@ -2,7 +2,7 @@
 // (libkx.so, include/kx.h), runtime ops on the real CUDA runtime.
 #pragma once
 
-#include <cuda_runtime.h>
+#include <cuda_runtime_api.h>
 
 #include "gpu_capture.h"
 #include "kx.h"

@@ -318,3 +318,16 @@ int orion_resolve_client_idx(void* stream, void* handle) {
 }
 
 }  // extern "C"
+
+extern "C" {
+
+// Async mode: 0 = client waits for the worker, 1 = worker-async (default),
+// 2 = run on the calling thread.  Same C API as the reference
+// (src/cuda_intercept.cpp:1299-1311).
+void orion_set_async_mode(int mode) {
+  if (mode >= 0 && mode <= 2) orion::set_async_mode_internal(mode);
+}
+
+int orion_get_async_mode() { return orion::get_async_mode_internal(); }
+
+}  // extern "C"

@@ -8,6 +8,8 @@
 // tokenizer of its own.
 #include "kernel_profile.h"
 
+#include "scheduler.h"
+
 #include <algorithm>
 #include <cctype>
 #include <cstdlib>
@@ -218,8 +220,9 @@ void KernelProfiler::end_session(const std::string& output_path) {
     f << "    {\"kernel_id\": \"" << p.kernel_id << "\", \"duration_ms\": " << p.duration_ms
       << ", \"sm_needed\": " << p.sm_needed << ", \"profile_type\": \""
       << profile_type_str(p.profile_type) << "\", \"grid_size\": " << p.grid_size
-      << ", \"block_size\": " << p.block_size << "}" << (i + 1 < recorded_profiles_.size() ? "," : "")
-      << "\n";
+      << ", \"block_size\": " << p.block_size << ", \"client\": " << p.client_idx
+      << ", \"op_type\": \"" << p.op_type << "\", \"work\": " << p.work << "}"
+      << (i + 1 < recorded_profiles_.size() ? "," : "") << "\n";
   }
   f << "  ]\n}\n";
 }
@@ -236,6 +239,11 @@ void KernelProfiler::record_kernel(const std::string& kernel_id, float duration_
   p.grid_size = sm_needed;
   p.block_size = 256;
   recorded_profiles_.push_back(p);
+}
+
+void KernelProfiler::record(const KernelProfile& p) {
+  std::lock_guard<std::mutex> lk(mutex_);
+  if (session_active_) recorded_profiles_.push_back(p);
 }
 
 void KernelProfiler::get_profile_table(KernelProfileTable& table) const {
@@ -262,6 +270,7 @@ void orion_start_profiling(const char* model_name) {
 }
 
 void orion_end_profiling(const char* output_path) {
+  orion::g_scheduler.flush_profile();
   orion::g_profiler.end_session(output_path ? output_path : "");
 }
 

@@ -1,0 +1,633 @@
+// scheduler.cpp — Orion-style HP/BE scheduler on SM-quota-aware kx kernels.
+//
+// One worker thread per client pops that client's captured operations in
+// FIFO order and runs them on the stream the client issued them on.  Client 0
+// is high priority (HP); clients 1.. are best effort (BE).
+//
+//  * Admission (orion_should_schedule) keeps the reference's profile-table
+//    rule (src/scheduler.cpp:997-1034 of the reference): a BE kernel op runs
+//    when HP's next kernel plus this BE kernel fit in the GPU's SMs according
+//    to kernel_info.csv, or when the HP queue is empty; otherwise it waits.
+//  * Sharing (replaces the green-context split, src/scheduler.cpp:244-446):
+//    dense BE ops run as persistent kx kernels that read the HP flag (pinned,
+//    device-mapped) before every tile.  The HP worker raises the flag to
+//    be_keep_sms while HP work is queued or in flight; BE CTAs whose index is
+//    at or above it retire at their next tile boundary and the lower ones
+//    finish the op.  With be_keep_sms = 0 the flag is -1: every BE CTA stops
+//    and the BE worker relaunches the op (same arguments, continuing from its
+//    tile queue) once HP is idle.  ISOLATED mode instead gives HP and BE fixed
+//    disjoint SM budgets (hp_sm_count / be_sm_count).
+//  * kernel_info.csv rows are parsed right-to-left (Name may contain commas),
+//    as in the reference (src/scheduler.cpp:84-153).
+#include "scheduler.h"
+
+#include <time.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdlib>
+#include <cstring>
+#include <thread>
+
+#include "dispatch.h"
+#include "real_libs.h"
+
+namespace orion {
+
+Scheduler g_scheduler;
+OrionSchedulingState g_orion_state;
+
+namespace {
+
+bool is_memory_op(OperationType t) {
+  return t == OperationType::MALLOC || t == OperationType::FREE ||
+         t == OperationType::MEMCPY || t == OperationType::MEMCPY_ASYNC ||
+         t == OperationType::MEMSET || t == OperationType::MEMSET_ASYNC;
+}
+
+bool is_kernel_op(OperationType t) {
+  return t == OperationType::KERNEL_LAUNCH || t == OperationType::KERNEL_LAUNCH_EX ||
+         t == OperationType::KERNEL_LAUNCH_DRV || is_dense_op(t);
+}
+
+int64_t mono_ns() {
+  timespec ts;
+  clock_gettime(CLOCK_MONOTONIC, &ts);
+  return static_cast<int64_t>(ts.tv_sec) * 1000000000LL + ts.tv_nsec;
+}
+
+cudaStream_t op_stream(const OperationRecord& op) {
+  switch (op.type) {
+    case OperationType::KERNEL_LAUNCH:
+    case OperationType::KERNEL_LAUNCH_EX:
+    case OperationType::KERNEL_LAUNCH_DRV:
+      return std::get<KernelLaunchParams>(op.params).stream;
+    case OperationType::MEMCPY_ASYNC:
+      return std::get<MemcpyParams>(op.params).stream;
+    case OperationType::MEMSET_ASYNC:
+      return std::get<MemsetParams>(op.params).stream;
+    case OperationType::CUBLAS_SGEMM:
+    case OperationType::CUBLAS_SGEMM_BATCHED:
+    case OperationType::CUBLAS_SGEMM_STRIDED_BATCHED:
+    case OperationType::CUBLAS_GEMM_EX:
+    case OperationType::CUBLAS_GEMM_STRIDED_BATCHED_EX:
+      return std::get<CublasGemmParams>(op.params).stream;
+    case OperationType::CUBLASLT_MATMUL:
+      return std::get<CublasLtMatmulParams>(op.params).stream;
+    case OperationType::CUDNN_CONV_FWD:
+    case OperationType::CUDNN_CONV_BWD_DATA:
+    case OperationType::CUDNN_CONV_BWD_FILTER:
+      return std::get<CudnnConvParams>(op.params).stream;
+    case OperationType::CUDNN_BATCHNORM_FWD:
+    case OperationType::CUDNN_BATCHNORM_BWD:
+    case OperationType::CUDNN_BATCHNORM_INF:
+      return std::get<CudnnBatchNormParams>(op.params).stream;
+    default:
+      return nullptr;
+  }
+}
+
+// Algorithmic work of a captured dense op: FLOPs for GEMMs / convolutions,
+// HBM bytes for batch norm (the units its roofline uses).
+double op_work(const OperationRecord& op) {
+  switch (op.type) {
+    case OperationType::CUBLAS_SGEMM:
+    case OperationType::CUBLAS_GEMM_EX: {
+      const auto& p = std::get<CublasGemmParams>(op.params);
+      return 2.0 * p.m * p.n * p.k;
+    }
+    case OperationType::CUBLAS_SGEMM_BATCHED:
+    case OperationType::CUBLAS_SGEMM_STRIDED_BATCHED:
+    case OperationType::CUBLAS_GEMM_STRIDED_BATCHED_EX: {
+      const auto& p = std::get<CublasGemmParams>(op.params);
+      return 2.0 * p.m * p.n * p.k * p.batchCount;
+    }
+    case OperationType::CUBLASLT_MATMUL: {
+      const auto& d = std::get<CublasLtMatmulParams>(op.params).dec;
+      return 2.0 * d.m * d.n * d.k * (d.batch > 0 ? d.batch : 1);
+    }
+    case OperationType::CUDNN_CONV_FWD:
+    case OperationType::CUDNN_CONV_BWD_DATA:
+    case OperationType::CUDNN_CONV_BWD_FILTER: {
+      const ConvGeometry& g = std::get<CudnnConvParams>(op.params).geom;
+      const int P = (g.h + 2 * g.pad_h - ((g.r - 1) * g.dil_h + 1)) / g.stride_h + 1;
+      const int Q = (g.w + 2 * g.pad_w - ((g.s - 1) * g.dil_w + 1)) / g.stride_w + 1;
+      return 2.0 * g.n * g.k * g.c * g.r * g.s * P * Q;
+    }
+    case OperationType::CUDNN_BATCHNORM_FWD:
+    case OperationType::CUDNN_BATCHNORM_INF:
+    case OperationType::CUDNN_BATCHNORM_BWD: {
+      const auto& p = std::get<CudnnBatchNormParams>(op.params);
+      const double elems = static_cast<double>(p.n) * p.c * p.h * p.w;
+      const double passes = op.type == OperationType::CUDNN_BATCHNORM_INF ? 2.0
+                            : op.type == OperationType::CUDNN_BATCHNORM_FWD ? 3.0 : 5.0;
+      return passes * elems * 4.0;
+    }
+    default:
+      return 0.0;
+  }
+}
+
+int populate_kernel_info(int client_idx, const std::string& path) {
+  std::ifstream f(path);
+  if (!f.is_open()) {
+    LOG_ERROR("failed to open kernel_info file %s", path.c_str());
+    return -1;
+  }
+  std::vector<KernelProfileInfo> rows;
+  std::string line;
+  bool header = true;
+  while (std::getline(f, line)) {
+    if (header) {
+      header = false;
+      continue;
+    }
+    if (!line.empty() && line.back() == '\r') line.pop_back();
+    if (line.empty()) continue;
+    // last four comma-separated fields are numeric; the name is the rest
+    size_t cut[4];
+    size_t pos = line.size();
+    bool ok = true;
+    for (int i = 3; i >= 0; --i) {
+      size_t c = line.rfind(',', pos == 0 ? std::string::npos : pos - 1);
+      if (c == std::string::npos) {
+        ok = false;
+        break;
+      }
+      cut[i] = c;
+      pos = c;
+    }
+    if (!ok) continue;
+    try {
+      KernelProfileInfo info;
+      info.name = line.substr(0, cut[0]);
+      info.profile = std::stoi(line.substr(cut[0] + 1, cut[1] - cut[0] - 1));
+      info.mem = std::stoi(line.substr(cut[1] + 1, cut[2] - cut[1] - 1));
+      info.sm_used = std::stoi(line.substr(cut[2] + 1, cut[3] - cut[2] - 1));
+      info.duration = std::stof(line.substr(cut[3] + 1));
+      rows.push_back(info);
+    } catch (...) {
+      continue;
+    }
+  }
+  std::lock_guard<std::mutex> lk(g_orion_state.mutex);
+  if (client_idx < 0 || client_idx >= static_cast<int>(g_orion_state.op_info_vector.size()))
+    return -1;
+  g_orion_state.op_info_vector[client_idx] = std::move(rows);
+  return static_cast<int>(g_orion_state.op_info_vector[client_idx].size());
+}
+
+}  // namespace
+
+Scheduler::Scheduler() = default;
+
+Scheduler::~Scheduler() {
+  stop();
+  join();
+}
+
+bool Scheduler::init(int num_clients, const SchedulerConfig& config) {
+  if (initialized_.load()) return true;
+  num_clients_ = num_clients;
+  config_ = config;
+  int dev = config_.device_id;
+  ORION_REAL(cudart, cudaGetDevice)(&dev);
+  config_.device_id = dev;
+  int sms = 0;
+  if (ORION_REAL(cudart, cudaDeviceGetAttribute)(&sms, cudaDevAttrMultiProcessorCount, dev) !=
+      cudaSuccess) {
+    LOG_ERROR("cannot query the device's SM count");
+    return false;
+  }
+  config_.num_sms = sms;
+  if (config_.sm_threshold == 0) config_.sm_threshold = sms / 2;
+  if (!create_streams()) return false;
+  // HP flag shared with BE kernels (pinned, device-mapped)
+  int* h = nullptr;
+  int* d = nullptr;
+  if (kx_host_flags_alloc(2, &h, &d) != KX_OK) {
+    LOG_ERROR("cannot allocate the HP flag");
+    return false;
+  }
+  hp_flag_host_ = h;
+  hp_flag_dev_ = d;
+  int keep = sms / 4;
+  if (const char* s = std::getenv("KX_BE_KEEP_SMS")) keep = std::atoi(s);
+  be_keep_sms_.store(std::max(0, std::min(keep, sms)));
+  ORION_REAL(cudart, cudaEventCreateWithFlags)(&hp_last_event_, cudaEventDisableTiming);
+  g_orion_state.init(num_clients, sms);
+  g_orion_state.sm_threshold = config_.sm_threshold;
+  const char* hp = std::getenv("ORION_HP_SMS");
+  const char* be = std::getenv("ORION_BE_SMS");
+  if (hp && be) {
+    GreenCtxConfig gc;
+    gc.hp_sm_count = static_cast<unsigned>(std::atoi(hp));
+    gc.be_sm_count = static_cast<unsigned>(std::atoi(be));
+    gc.enabled = gc.hp_sm_count > 0 && gc.be_sm_count > 0;
+    if (gc.enabled) init_green_contexts(gc);
+  }
+  initialized_.store(true);
+  LOG_INFO("scheduler initialized: %d clients, %d SMs, BE keeps %d SMs under HP load",
+           num_clients, sms, be_keep_sms_.load());
+  return true;
+}
+
+bool Scheduler::create_streams() {
+  int lo = 0, hi = 0;
+  ORION_REAL(cudart, cudaDeviceGetStreamPriorityRange)(&lo, &hi);
+  auto create = ORION_REAL(cudart, cudaStreamCreateWithPriority);
+  if (create(&hp_stream_, cudaStreamNonBlocking, hi) != cudaSuccess) return false;
+  be_streams_.assign(std::max(0, num_clients_ - 1), nullptr);
+  for (size_t i = 0; i < be_streams_.size(); ++i)
+    if (create(&be_streams_[i], cudaStreamNonBlocking, lo) != cudaSuccess) return false;
+  return true;
+}
+
+void Scheduler::destroy_streams() {
+  auto destroy = ORION_REAL(cudart, cudaStreamDestroy);
+  if (hp_stream_) destroy(hp_stream_);
+  hp_stream_ = nullptr;
+  for (auto s : be_streams_)
+    if (s) destroy(s);
+  be_streams_.clear();
+}
+
+bool Scheduler::init_green_contexts(const GreenCtxConfig& gc) {
+  const unsigned total = static_cast<unsigned>(config_.num_sms);
+  if (!gc.enabled || gc.hp_sm_count == 0 || gc.be_sm_count == 0 ||
+      gc.hp_sm_count + gc.be_sm_count > total) {
+    LOG_ERROR("invalid SM budgets HP=%u BE=%u (GPU has %u SMs)", gc.hp_sm_count,
+              gc.be_sm_count, total);
+    return false;
+  }
+  gc_config_ = gc;
+  isolated_ = true;
+  LOG_INFO("ISOLATED mode: HP budget %u SMs, BE budget %u SMs", gc.hp_sm_count, gc.be_sm_count);
+  return true;
+}
+
+int Scheduler::hp_quota() const { return isolated_ ? static_cast<int>(gc_config_.hp_sm_count) : 0; }
+
+int Scheduler::be_quota() const { return isolated_ ? static_cast<int>(gc_config_.be_sm_count) : 0; }
+
+double Scheduler::estimate_client_time_ns(int client_idx, unsigned int allocated_sms) const {
+  // Wave model: a kernel needing S SMs run on A < S SMs takes ceil(S/A) waves.
+  auto& rows = g_orion_state.op_info_vector[client_idx];
+  double t = 0.0;
+  const unsigned a = std::max(1u, allocated_sms);
+  for (const auto& r : rows) {
+    const unsigned need = static_cast<unsigned>(std::max(1, r.sm_used));
+    const double waves = std::ceil(static_cast<double>(need) / a);
+    t += r.duration * (need > a ? waves : 1.0);
+  }
+  return t;
+}
+
+Scheduler::GreenCtxConfig Scheduler::choose_best_green_ctx_config_from_profiles() const {
+  // Minimise the slower of HP and the slowest BE client over budgets in steps
+  // of 8 SMs (the granularity the reference's green contexts used).
+  GreenCtxConfig best;
+  best.enabled = false;
+  const unsigned total = static_cast<unsigned>(config_.num_sms);
+  double best_t = 1e300;
+  for (unsigned hp = 8; hp + 8 <= total; hp += 8) {
+    const unsigned be = total - hp;
+    double t_hp = estimate_client_time_ns(0, hp);
+    double t_be = 0.0;
+    for (int c = 1; c < num_clients_; ++c) t_be = std::max(t_be, estimate_client_time_ns(c, be));
+    const double t = std::max(t_hp, t_be);
+    if (t < best_t) {
+      best_t = t;
+      best.hp_sm_count = hp;
+      best.be_sm_count = be;
+      best.enabled = true;
+    }
+  }
+  return best;
+}
+
+int Scheduler::autotune_green_ctx() {
+  GreenCtxConfig gc = choose_best_green_ctx_config_from_profiles();
+  if (!gc.enabled) return -1;
+  return init_green_contexts(gc) ? 0 : -1;
+}
+
+int Scheduler::peek_sm_requirement(int client_idx, int offset) {
+  std::lock_guard<std::mutex> lk(g_orion_state.mutex);
+  if (client_idx < 0 || client_idx >= static_cast<int>(g_orion_state.op_info_vector.size()))
+    return 0;
+  auto& rows = g_orion_state.op_info_vector[client_idx];
+  if (rows.empty()) return 0;
+  const int n = static_cast<int>(rows.size());
+  const int idx = ((g_orion_state.seen[client_idx] + offset) % n + n) % n;
+  return rows[idx].sm_used;
+}
+
+bool Scheduler::orion_should_schedule(OperationPtr op, int client_idx) {
+  if (is_memory_op(op->type) || !is_kernel_op(op->type)) return true;
+  if (isolated_) return true;  // disjoint budgets: no interference to arbitrate
+  const int hp = peek_sm_requirement(0);
+  const int be = peek_sm_requirement(client_idx);
+  if (hp + be <= config_.num_sms) return true;
+  auto& q = g_capture_state.client_queues[0];
+  return q && q->empty();
+}
+
+void Scheduler::hp_activity_begin() {
+  if (isolated_ || hp_flag_host_ == nullptr) return;
+  const int keep = be_keep_sms_.load();
+  const int v = keep > 0 ? keep : -1;
+  if (hp_flag_host_[0] != v) {
+    hp_flag_host_[0] = v;
+    std::atomic_thread_fence(std::memory_order_seq_cst);
+  }
+}
+
+void Scheduler::hp_activity_poll() {
+  // Lower the flag once the HP queue is drained and HP's last op finished.
+  if (hp_flag_host_ == nullptr || hp_flag_host_[0] == 0) return;
+  auto& q = g_capture_state.client_queues[0];
+  if (q && !q->empty()) return;
+  std::lock_guard<std::mutex> lk(hp_mu_);
+  if (hp_event_pending_.load()) {
+    if (ORION_REAL(cudart, cudaEventQuery)(hp_last_event_) != cudaSuccess) return;
+    hp_event_pending_.store(false);
+  }
+  hp_flag_host_[0] = 0;
+}
+
+cudaError_t Scheduler::execute_operation(OperationPtr op, cudaStream_t fallback) {
+  op->started.store(true);
+  const int c = op->client_idx;
+  ClientStats& st = stats(c);
+  st.ops.fetch_add(1);
+  if (!is_dense_op(op->type)) return dispatch_runtime(*op, fallback);
+
+  ExecPolicy pol;
+  pol.stream = op_stream(*op);
+  if (pol.stream == nullptr) pol.stream = nullptr;  // legacy default stream of the client
+  const bool be = c > 0;
+  pol.sm_quota = be ? be_quota() : hp_quota();
+  const bool can_stop = be && !isolated_ && be_keep_sms_.load() <= 0;
+  if (be && !isolated_) pol.yield_flag = hp_flag_dev_;
+  if (can_stop) {
+    hp_flag_host_[1] = -1;
+    pol.done_flag = hp_flag_dev_ + 1;
+  }
+  cudaEvent_t ev_start = nullptr, ev_end = nullptr;
+  const bool profiling = g_profiler.active();
+  if (profiling) {
+    ORION_REAL(cudart, cudaEventCreate)(&ev_start);
+    ORION_REAL(cudart, cudaEventCreate)(&ev_end);
+    ORION_REAL(cudart, cudaEventRecord)(ev_start, pol.stream);
+  }
+  tl_in_scheduler_execution = true;
+  int rc = dispatch_dense(*op, pol);
+  while (rc == KX_OK && can_stop) {
+    // BE op that may have stopped entirely: wait for it, then resume once HP is idle.
+    ORION_REAL(cudart, cudaStreamSynchronize)(pol.stream);
+    if (hp_flag_host_[1] == 1) break;
+    st.yields.fetch_add(1);
+    const int64_t deadline = mono_ns() + wait_timeout_ns();
+    while (hp_flag_host_[0] != 0 && running_.load() && mono_ns() < deadline)
+      std::this_thread::sleep_for(std::chrono::microseconds(20));
+    hp_flag_host_[1] = -1;
+    rc = dispatch_dense(*op, pol);
+  }
+  tl_in_scheduler_execution = false;
+  if (c == 0 && rc == KX_OK && !isolated_) {
+    std::lock_guard<std::mutex> lk(hp_mu_);
+    ORION_REAL(cudart, cudaEventRecord)(hp_last_event_, pol.stream);
+    hp_event_pending_.store(true);
+  }
+  if (profiling) {
+    // resolved without blocking the worker; see flush_profile()
+    ORION_REAL(cudart, cudaEventRecord)(ev_end, pol.stream);
+    PendingProfile pp;
+    pp.start = ev_start;
+    pp.end = ev_end;
+    pp.rec.kernel_id = kx_last_kernel_name();
+    pp.rec.sm_needed = pol.sm_quota > 0 ? pol.sm_quota : config_.num_sms;
+    pp.rec.grid_size = pp.rec.sm_needed;
+    pp.rec.block_size = 256;
+    pp.rec.profile_type = (op->type == OperationType::CUDNN_BATCHNORM_FWD ||
+                           op->type == OperationType::CUDNN_BATCHNORM_BWD ||
+                           op->type == OperationType::CUDNN_BATCHNORM_INF)
+                              ? ProfileType::MEMORY_BOUND
+                              : ProfileType::COMPUTE_BOUND;
+    pp.rec.client_idx = c;
+    pp.rec.op_type = op_type_name(op->type);
+    pp.rec.work = op_work(*op);
+    std::lock_guard<std::mutex> lk(prof_mu_);
+    pending_prof_.push_back(pp);
+  }
+  if (rc == KX_OK) {
+    st.kx_ops.fetch_add(1);
+    return cudaSuccess;
+  }
+  st.errors.fetch_add(1);
+  LOG_ERROR("client %d: %s failed in kx (status %d)", c, op_type_name(op->type), rc);
+  return kx_to_cuda(rc);
+}
+
+void Scheduler::run_worker(int client_idx) {
+  tl_is_scheduler_thread = true;
+  tl_worker_idx = client_idx;
+  ORION_REAL(cudart, cudaSetDevice)(config_.device_id);
+  cudaStream_t fallback = client_idx == 0 ? hp_stream_ : be_streams_[client_idx - 1];
+  ClientQueue* q = g_capture_state.client_queues[client_idx].get();
+  uint32_t idle = 0;
+  while (running_.load()) {
+    OperationPtr op = q->peek();
+    if (!op) {
+      if (client_idx == 0) hp_activity_poll();
+      if (++idle > 64) std::this_thread::sleep_for(std::chrono::microseconds(5));
+      else std::this_thread::yield();
+      continue;
+    }
+    idle = 0;
+    if (client_idx == 0 && is_kernel_op(op->type)) hp_activity_begin();
+    if (client_idx > 0 && !orion_should_schedule(op, client_idx)) {
+      // FIFO order is kept: the op stays at the head until admitted
+      stats(client_idx).be_blocked.fetch_add(1);
+      std::this_thread::yield();
+      continue;
+    }
+    op = q->try_pop();
+    if (!op) continue;
+    cudaError_t err = execute_operation(op, fallback);
+    if (err != cudaSuccess) set_last_error(client_idx, err);
+    if (is_kernel_op(op->type)) {
+      std::lock_guard<std::mutex> lk(g_orion_state.mutex);
+      if (client_idx < static_cast<int>(g_orion_state.seen.size())) g_orion_state.seen[client_idx]++;
+    }
+    op->mark_completed(err);
+  }
+  // drain what is left so no client waits forever
+  while (OperationPtr op = q->try_pop()) {
+    cudaError_t err = execute_operation(op, fallback);
+    op->mark_completed(err);
+  }
+  ORION_REAL(cudart, cudaStreamSynchronize)(fallback);
+}
+
+void Scheduler::start() {
+  if (!initialized_.load() || running_.load()) return;
+  running_.store(true);
+  workers_.clear();
+  for (int i = 0; i < num_clients_; ++i) workers_.emplace_back(&Scheduler::run_worker, this, i);
+}
+
+void Scheduler::stop() {
+  if (!running_.load()) return;
+  running_.store(false);
+  for (auto& q : g_capture_state.client_queues)
+    if (q) q->shutdown();
+}
+
+void Scheduler::join() {
+  for (auto& w : workers_)
+    if (w.joinable()) w.join();
+  workers_.clear();
+  if (hp_flag_host_) hp_flag_host_[0] = 0;
+}
+
+void Scheduler::reset() {
+  if (running_.load()) return;
+  destroy_streams();
+  if (hp_last_event_) {
+    ORION_REAL(cudart, cudaEventDestroy)(hp_last_event_);
+    hp_last_event_ = nullptr;
+  }
+  if (hp_flag_host_) {
+    kx_host_flags_free(const_cast<int*>(hp_flag_host_));
+    hp_flag_host_ = nullptr;
+    hp_flag_dev_ = nullptr;
+  }
+  isolated_ = false;
+  initialized_.store(false);
+  num_clients_ = 0;
+  g_orion_state.reset();
+}
+
+void Scheduler::sync_client_stream(int client_idx) {
+  // wait until the client's queue has been executed, then for its work on the GPU
+  if (client_idx >= 0 && client_idx < g_capture_state.num_clients) {
+    auto& q = g_capture_state.client_queues[client_idx];
+    const int64_t deadline = mono_ns() + wait_timeout_ns();
+    while (q && !q->empty() && running_.load() && mono_ns() < deadline) std::this_thread::yield();
+  }
+  ORION_REAL(cudart, cudaDeviceSynchronize)();
+}
+
+void Scheduler::flush_profile() {
+  std::vector<PendingProfile> pend;
+  {
+    std::lock_guard<std::mutex> lk(prof_mu_);
+    pend.swap(pending_prof_);
+  }
+  for (auto& pp : pend) {
+    ORION_REAL(cudart, cudaEventSynchronize)(pp.end);
+    float ms = 0.f;
+    ORION_REAL(cudart, cudaEventElapsedTime)(&ms, pp.start, pp.end);
+    pp.rec.duration_ms = ms;
+    g_profiler.record(pp.rec);
+    ORION_REAL(cudart, cudaEventDestroy)(pp.start);
+    ORION_REAL(cudart, cudaEventDestroy)(pp.end);
+  }
+}
+
+bool start_scheduler(int num_clients, const SchedulerConfig& config) {
+  if (init_capture_layer(num_clients) != 0) return false;
+  if (!g_scheduler.init(num_clients, config)) return false;
+  g_scheduler.start();
+  return true;
+}
+
+void stop_scheduler() {
+  g_scheduler.stop();
+  g_scheduler.join();
+  g_scheduler.reset();
+  shutdown_capture_layer();
+}
+
+}  // namespace orion
+
+extern "C" {
+
+int orion_init_scheduler(int num_clients) {
+  if (orion::init_capture_layer(num_clients) != 0) return -1;
+  return orion::g_scheduler.init(num_clients) ? 0 : -1;
+}
+
+int orion_start_scheduler_thread() {
+  orion::g_scheduler.start();
+  return 0;
+}
+
+int orion_start_scheduler(int num_clients) {
+  return orion::start_scheduler(num_clients) ? 0 : -1;
+}
+
+void orion_stop_scheduler() { orion::stop_scheduler(); }
+
+int orion_load_kernel_info(int client_idx, const char* file_path) {
+  if (file_path == nullptr) return -1;
+  return orion::populate_kernel_info(client_idx, file_path);
+}
+
+void orion_set_client_kernels(int client_idx, int num_kernels) {
+  std::lock_guard<std::mutex> lk(orion::g_orion_state.mutex);
+  if (client_idx < 0 || client_idx >= static_cast<int>(orion::g_orion_state.num_client_kernels.size()))
+    return;
+  orion::g_orion_state.num_client_kernels[client_idx] = num_kernels;
+}
+
+void orion_set_sm_threshold(int threshold) {
+  std::lock_guard<std::mutex> lk(orion::g_orion_state.mutex);
+  orion::g_orion_state.sm_threshold = threshold;
+  orion::g_scheduler.get_mutable_config().sm_threshold = threshold;
+}
+
+int orion_get_sm_threshold() {
+  std::lock_guard<std::mutex> lk(orion::g_orion_state.mutex);
+  return orion::g_orion_state.sm_threshold;
+}
+
+void orion_sync_client_stream(int client_idx) { orion::g_scheduler.sync_client_stream(client_idx); }
+
+void orion_reset_state() { orion::g_orion_state.reset(); }
+
+int orion_autotune_green_ctx() { return orion::g_scheduler.autotune_green_ctx(); }
+
+void orion_set_be_keep_sms(int sms) { orion::g_scheduler.set_be_keep_sms(sms < 0 ? 0 : sms); }
+
+int orion_get_be_keep_sms() { return orion::g_scheduler.be_keep_sms(); }
+
+int orion_set_sm_budgets(int hp_sms, int be_sms) {
+  if (hp_sms == 0 && be_sms == 0) {
+    orion::g_scheduler.clear_budgets();
+    return 0;
+  }
+  orion::Scheduler::GreenCtxConfig gc;
+  gc.hp_sm_count = static_cast<unsigned>(hp_sms);
+  gc.be_sm_count = static_cast<unsigned>(be_sms);
+  gc.enabled = true;
+  return orion::g_scheduler.init_green_contexts(gc) ? 0 : -1;
+}
+
+int orion_get_client_stats(int client_idx, unsigned long long* out6) {
+  if (out6 == nullptr || client_idx < 0 || client_idx >= orion::MAX_CLIENTS) return -1;
+  orion::ClientStats& s = orion::g_scheduler.stats(client_idx);
+  out6[0] = s.ops.load();
+  out6[1] = s.kx_ops.load();
+  out6[2] = s.passthrough_ops.load();
+  out6[3] = s.be_blocked.load();
+  out6[4] = s.yields.load();
+  out6[5] = s.errors.load();
+  return 0;
+}
+
+void block(int client_idx) { orion::g_scheduler.sync_client_stream(client_idx); }
+
+}  // extern "C"

@@ -1,0 +1,378 @@
+"""Host-side harness: the ``libgpu_scheduler.so`` C API, the benchmark
+workloads, and the HP/BE client loop.
+
+It mirrors what the reference's Python drivers do (python/test_orion_blocking.py
+``load_library`` 143-189 and ``run_test`` 192-423; python/launch_jobs.py
+``OrionScheduler`` 32-127): load the preloaded scheduler library through
+ctypes, build the models, warm them up with capture off, register one thread
+per client (client 0 = HP, 1.. = BE), start the workers, turn capture on and
+run the client loops.  Differences: HP latency is measured per iteration with
+CUDA events recorded in the client's stream order (the interposer keeps
+``cudaEventRecord`` in order), and BE throughput is measured over the same
+window.
+
+Workloads follow the configurations the reference is benchmarked on:
+* ``make_gpt``   — decoder with per-head q/k/v projections (the reference's
+  CharGPT layout, python/GPT.py:42-149): 6 layers, d_model 512, 8 heads,
+  FFN 2048 with GELU, pre-LayerNorm, learned positions, vocab 32000.
+* ``make_vgg16`` — torchvision VGG16 (13 conv3x3 + ReLU, 5 max-pools,
+  FC 25088-4096-4096-1000), Kaiming-normal init.
+* ``make_llama`` — RMSNorm / RoPE / SwiGLU decoder (python/LLaMA.py layout):
+  12 layers, d_model 2048, 16 heads, FFN 5504, vocab 32000.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+import os
+import threading
+import time
+
+from . import LIBSHIM
+
+# ---------------------------------------------------------------- library ---
+
+
+class Orion:
+    """ctypes view of the scheduler library (the reference driver's API set)."""
+
+    def __init__(self, path: str = LIBSHIM):
+        self.lib = ctypes.CDLL(path, mode=ctypes.RTLD_GLOBAL)
+        L = self.lib
+        I, P = ctypes.c_int, ctypes.c_void_p
+        sig = {
+            "orion_init_scheduler": ([I], I), "orion_start_scheduler_thread": ([], I),
+            "orion_start_scheduler": ([I], I), "orion_stop_scheduler": ([], None),
+            "orion_set_client_idx": ([I], None), "orion_get_client_idx": ([], I),
+            "orion_load_kernel_info": ([I, ctypes.c_char_p], I),
+            "orion_set_client_kernels": ([I, I], None), "orion_set_sm_threshold": ([I], None),
+            "orion_get_sm_threshold": ([], I), "orion_sync_client_stream": ([I], None),
+            "orion_reset_state": ([], None), "orion_autotune_green_ctx": ([], I),
+            "orion_set_capture": ([I], I), "orion_set_enabled": ([I], None),
+            "orion_is_enabled": ([], I), "orion_register_client_stream": ([I, P], None),
+            "orion_register_client_handle": ([I, P], None),
+            "orion_resolve_client_idx": ([P, P], I), "orion_set_async_mode": ([I], None),
+            "orion_get_async_mode": ([], I), "orion_init": ([I], I), "orion_shutdown": ([], None),
+            "orion_set_be_keep_sms": ([I], None), "orion_get_be_keep_sms": ([], I),
+            "orion_set_sm_budgets": ([I, I], I),
+            "orion_get_client_stats": ([I, ctypes.POINTER(ctypes.c_ulonglong)], I),
+            "orion_load_profile": ([ctypes.c_char_p], I),
+            "orion_start_profiling": ([ctypes.c_char_p], None),
+            "orion_end_profiling": ([ctypes.c_char_p], None),
+        }
+        for name, (args, res) in sig.items():
+            fn = getattr(L, name)
+            fn.argtypes = args
+            fn.restype = res
+
+    def __getattr__(self, name):
+        return getattr(self.lib, name)
+
+    def stats(self, client: int) -> dict:
+        out = (ctypes.c_ulonglong * 6)()
+        self.lib.orion_get_client_stats(client, out)
+        keys = ("ops", "kx_ops", "passthrough_ops", "be_blocked", "yields", "errors")
+        return dict(zip(keys, (int(v) for v in out)))
+
+
+def preloaded() -> bool:
+    """True when libgpu_scheduler.so is in LD_PRELOAD of this process."""
+    return os.path.basename(LIBSHIM) in os.environ.get("LD_PRELOAD", "")
+
+
+def preload_env(extra: dict | None = None) -> dict:
+    env = dict(os.environ)
+    pre = env.get("LD_PRELOAD", "")
+    if os.path.basename(LIBSHIM) not in pre:
+        env["LD_PRELOAD"] = (LIBSHIM + (":" + pre if pre else ""))
+    if extra:
+        env.update(extra)
+    return env
+
+
+# -------------------------------------------------------------- workloads ---
+
+def make_gpt(vocab=32000, emb=512, head_size=64, layers=6, seq=256, device="cuda",
+             dtype=None):
+    import torch
+    import torch.nn as nn
+    import torch.nn.functional as F
+
+    class Head(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.key = nn.Linear(emb, head_size, bias=False)
+            self.query = nn.Linear(emb, head_size, bias=False)
+            self.value = nn.Linear(emb, head_size, bias=False)
+            self.register_buffer("tril", torch.tril(torch.ones(seq, seq)))
+
+        def forward(self, x):
+            T = x.shape[1]
+            q, k, v = self.query(x), self.key(x), self.value(x)
+            s = q @ k.transpose(-2, -1) / math.sqrt(head_size)
+            s = s.masked_fill(self.tril[:T, :T] == 0, float("-inf"))
+            return F.softmax(s, dim=-1) @ v
+
+    class Block(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.heads = nn.ModuleList([Head() for _ in range(emb // head_size)])
+            self.proj = nn.Linear(emb, emb)
+            self.l1 = nn.Linear(emb, 4 * emb)
+            self.l2 = nn.Linear(4 * emb, emb)
+            self.ln1 = nn.LayerNorm(emb)
+            self.ln2 = nn.LayerNorm(emb)
+
+        def forward(self, x):
+            h = self.ln1(x)
+            x = x + self.proj(torch.cat([hd(h) for hd in self.heads], dim=-1))
+            return x + self.l2(F.gelu(self.l1(self.ln2(x))))
+
+    class GPT(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.tok = nn.Embedding(vocab, emb)
+            self.pos = nn.Embedding(seq, emb)
+            self.blocks = nn.Sequential(*[Block() for _ in range(layers)])
+            self.ln = nn.LayerNorm(emb)
+            self.lm = nn.Linear(emb, vocab)
+            for m in self.modules():
+                if isinstance(m, nn.Linear):
+                    nn.init.normal_(m.weight, 0.0, 0.02)
+                    if m.bias is not None:
+                        nn.init.zeros_(m.bias)
+                elif isinstance(m, nn.Embedding):
+                    nn.init.normal_(m.weight, 0.0, 0.02)
+
+        def forward(self, tokens):
+            T = tokens.shape[1]
+            x = self.tok(tokens) + self.pos(torch.arange(T, device=tokens.device))
+            return self.lm(self.ln(self.blocks(x)))
+
+    m = GPT().to(device)
+    if dtype is not None:
+        m = m.to(dtype)
+    return m
+
+
+def make_vgg16(device="cuda"):
+    from torchvision.models import vgg16
+    return vgg16(weights=None).to(device)
+
+
+def make_llama(vocab=32000, hidden=2048, heads=16, layers=12, inter=5504, eps=1e-6,
+               theta=10000.0, seq=1024, device="cuda", dtype=None):
+    import torch
+    import torch.nn as nn
+    import torch.nn.functional as F
+
+    hd = hidden // heads
+
+    class RMSNorm(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.weight = nn.Parameter(torch.ones(hidden))
+
+        def forward(self, x):
+            v = x.float().pow(2).mean(-1, keepdim=True)
+            return (x.float() * torch.rsqrt(v + eps)).to(x.dtype) * self.weight
+
+    inv = 1.0 / (theta ** (torch.arange(0, hd, 2).float() / hd))
+    ang = torch.outer(torch.arange(seq).float(), inv)
+    cos, sin = ang.cos(), ang.sin()
+
+    def rope(x):
+        T = x.shape[2]
+        c = cos[:T].to(x.device, x.dtype)
+        s = sin[:T].to(x.device, x.dtype)
+        x1, x2 = x[..., 0::2], x[..., 1::2]
+        return torch.stack((x1 * c - x2 * s, x1 * s + x2 * c), dim=-1).flatten(-2)
+
+    class Attn(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.wq = nn.Linear(hidden, hidden, bias=False)
+            self.wk = nn.Linear(hidden, hidden, bias=False)
+            self.wv = nn.Linear(hidden, hidden, bias=False)
+            self.wo = nn.Linear(hidden, hidden, bias=False)
+            self.register_buffer("mask", torch.triu(torch.full((seq, seq), float("-inf")), 1))
+
+        def forward(self, x):
+            B, T, _ = x.shape
+            q = rope(self.wq(x).view(B, T, heads, hd).transpose(1, 2))
+            k = rope(self.wk(x).view(B, T, heads, hd).transpose(1, 2))
+            v = self.wv(x).view(B, T, heads, hd).transpose(1, 2)
+            s = (q @ k.transpose(-2, -1)) / math.sqrt(hd) + self.mask[:T, :T].to(x.dtype)
+            o = F.softmax(s.float(), dim=-1).to(x.dtype) @ v
+            return self.wo(o.transpose(1, 2).reshape(B, T, hidden))
+
+    class Block(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.attn = Attn()
+            self.gate = nn.Linear(hidden, inter, bias=False)
+            self.up = nn.Linear(hidden, inter, bias=False)
+            self.down = nn.Linear(inter, hidden, bias=False)
+            self.n1 = RMSNorm()
+            self.n2 = RMSNorm()
+
+        def forward(self, x):
+            x = x + self.attn(self.n1(x))
+            h = self.n2(x)
+            return x + self.down(F.silu(self.gate(h)) * self.up(h))
+
+    class LLaMA(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.emb = nn.Embedding(vocab, hidden)
+            self.layers = nn.Sequential(*[Block() for _ in range(layers)])
+            self.norm = RMSNorm()
+            self.head = nn.Linear(hidden, vocab, bias=False)
+            for m in self.modules():
+                if isinstance(m, (nn.Linear, nn.Embedding)):
+                    nn.init.normal_(m.weight, 0.0, 0.02)
+
+        def forward(self, tokens):
+            return self.head(self.norm(self.layers(self.emb(tokens))))
+
+    m = LLaMA().to(device)
+    if dtype is not None:
+        m = m.to(dtype)
+    return m
+
+
+def gpt_flops_forward(batch, seq=256, emb=512, layers=6, vocab=32000, ffn=2048):
+    """Captured-GEMM FLOPs of one config-0 GPT forward."""
+    tok = batch * seq
+    per_layer = (2 * tok * emb * emb * 3          # q, k, v (all heads)
+                 + 2 * batch * seq * seq * emb * 2  # scores + att@v (all heads)
+                 + 2 * tok * emb * emb            # proj
+                 + 2 * tok * emb * ffn * 2)       # l1 + l2
+    return layers * per_layer + 2 * tok * emb * vocab
+
+
+def vgg16_flops_forward(batch):
+    """Conv + FC FLOPs of one VGG16 forward at 224x224."""
+    cfg = [(3, 64, 224), (64, 64, 224), (64, 128, 112), (128, 128, 112), (128, 256, 56),
+           (256, 256, 56), (256, 256, 56), (256, 512, 28), (512, 512, 28), (512, 512, 28),
+           (512, 512, 14), (512, 512, 14), (512, 512, 14)]
+    conv = sum(2 * batch * ci * co * 9 * hw * hw for ci, co, hw in cfg)
+    fc = 2 * batch * (25088 * 4096 + 4096 * 4096 + 4096 * 1000)
+    return conv + fc
+
+
+# ------------------------------------------------------------ client loop ---
+
+class ClientResult:
+    def __init__(self):
+        self.latencies_ms: list[float] = []
+        self.iters = 0
+        self.elapsed_ms = 0.0
+        self.error: BaseException | None = None
+
+
+def percentile(xs, q):
+    if not xs:
+        return float("nan")
+    s = sorted(xs)
+    k = (len(s) - 1) * q
+    f = math.floor(k)
+    c = min(f + 1, len(s) - 1)
+    return s[f] + (s[c] - s[f]) * (k - f)
+
+
+def run_clients(orion: Orion | None, hp_step, be_step, hp_steps: int, hp_warmup: int,
+                be_warmup: int = 1, with_be: bool = True, with_hp: bool = True,
+                be_seconds: float | None = None, hp_period_ms: float = 0.0):
+    """Runs the HP loop (hp_warmup + hp_steps timed iterations, CUDA events per
+    iteration in the HP client's stream order) and, concurrently, the BE loop
+    until HP finishes (or for be_seconds when HP is off).  Client identity:
+    HP = 0, BE = 1, registered on each thread as the reference drivers do."""
+    import torch
+
+    hp_res, be_res = ClientResult(), ClientResult()
+    stop = threading.Event()
+    ready = threading.Barrier(2 if (with_hp and with_be) else 1)
+
+    def hp_thread():
+        try:
+            s = torch.cuda.Stream()
+            if orion is not None:
+                orion.orion_set_client_idx(0)
+                orion.orion_register_client_stream(0, ctypes.c_void_p(s.cuda_stream))
+            with torch.cuda.stream(s):
+                for _ in range(hp_warmup):
+                    hp_step()
+                s.synchronize()
+                ready.wait()
+                evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                       for _ in range(hp_steps)]
+                first = torch.cuda.Event(enable_timing=True)
+                last = torch.cuda.Event(enable_timing=True)
+                first.record(s)
+                for a, b in evs:
+                    t_issue = time.perf_counter()
+                    a.record(s)
+                    hp_step()
+                    b.record(s)
+                    if hp_period_ms > 0:
+                        while (time.perf_counter() - t_issue) * 1e3 < hp_period_ms:
+                            time.sleep(0.0002)
+                last.record(s)
+                s.synchronize()
+                hp_res.latencies_ms = [a.elapsed_time(b) for a, b in evs]
+                hp_res.elapsed_ms = first.elapsed_time(last)
+                hp_res.iters = hp_steps
+        except BaseException as e:  # noqa: BLE001 - reported by the caller
+            hp_res.error = e
+        finally:
+            stop.set()
+            if orion is not None:
+                orion.orion_set_client_idx(-1)
+
+    def be_thread():
+        try:
+            s = torch.cuda.Stream()
+            if orion is not None:
+                orion.orion_set_client_idx(1)
+                orion.orion_register_client_stream(1, ctypes.c_void_p(s.cuda_stream))
+            with torch.cuda.stream(s):
+                for _ in range(be_warmup):
+                    be_step()
+                s.synchronize()
+                ready.wait()
+                start = torch.cuda.Event(enable_timing=True)
+                end = torch.cuda.Event(enable_timing=True)
+                start.record(s)
+                t0 = time.perf_counter()
+                n = 0
+                while True:
+                    be_step()
+                    n += 1
+                    if with_hp and stop.is_set():
+                        break
+                    if not with_hp and be_seconds is not None and time.perf_counter() - t0 >= be_seconds:
+                        break
+                end.record(s)
+                s.synchronize()
+                be_res.iters = n
+                be_res.elapsed_ms = start.elapsed_time(end)
+        except BaseException as e:  # noqa: BLE001
+            be_res.error = e
+        finally:
+            if orion is not None:
+                orion.orion_set_client_idx(-1)
+
+    threads = []
+    if with_hp:
+        threads.append(threading.Thread(target=hp_thread, name="HP-Client"))
+    if with_be:
+        threads.append(threading.Thread(target=be_thread, name="BE1-Client"))
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    for r in (hp_res, be_res):
+        if r.error is not None:
+            raise r.error
+    return hp_res, be_res

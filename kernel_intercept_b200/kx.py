@@ -107,6 +107,8 @@ def lib() -> ctypes.CDLL:
                 fn.restype = _I
             L.kx_last_kernel_name.restype = ctypes.c_char_p
             L.kx_version.restype = ctypes.c_char_p
+            L.kx_launch_count.argtypes = []
+            L.kx_launch_count.restype = ctypes.c_ulonglong
             _lib = L
     return _lib
 

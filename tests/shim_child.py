@@ -1,0 +1,285 @@
+"""Child process for the interposer GPU tests.
+
+Runs under LD_PRELOAD=libgpu_scheduler.so (the parent test sets it) and
+prints one JSON object on its last stdout line.  Each scenario computes the
+same PyTorch ops twice on the same inputs: once with capture off (the real
+cuBLAS / cuDNN behind the interposer, TF32 disabled, i.e. the reference
+shim's own path) and once captured on client 0 (queued to the worker and run
+on the kx kernels), and reports the normwise relative error of every output.
+
+Usage: python tests/shim_child.py <scenario>
+"""
+from __future__ import annotations
+
+import ctypes
+import json
+import os
+import sys
+import threading
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+
+
+def rel(got, ref):
+    import torch
+    got = got.double()
+    ref = ref.double()
+    den = ref.abs().max().item()
+    return (got - ref).abs().max().item() / (den if den > 0 else 1.0)
+
+
+def run_on_client(orion, client, fn):
+    """Runs fn() on a thread registered as `client`, on its own stream."""
+    import torch
+    out = {}
+
+    def body():
+        try:
+            s = torch.cuda.Stream()
+            orion.orion_set_client_idx(client)
+            orion.orion_register_client_stream(client, ctypes.c_void_p(s.cuda_stream))
+            with torch.cuda.stream(s):
+                out["v"] = fn()
+            s.synchronize()
+        except BaseException as e:  # noqa: BLE001 - reported to the parent
+            out["e"] = e
+        finally:
+            orion.orion_set_client_idx(-1)
+
+    t = threading.Thread(target=body)
+    t.start()
+    t.join()
+    if "e" in out:
+        raise out["e"]
+    return out["v"]
+
+
+def gemm_cases(torch):
+    """(name, fn, dtype) triples; fn(inputs) -> output tensor."""
+    g = torch.Generator(device="cuda").manual_seed(0)
+
+    def r(*shape, dtype=torch.float32):
+        return torch.randn(*shape, device="cuda", generator=g).to(dtype)
+
+    F = torch.nn.functional
+    bf = torch.bfloat16
+    cases = []
+    a, b = r(256, 512), r(512, 384)
+    cases.append(("mm_256x512x384", lambda: a @ b, "f32"))
+    at = r(512, 256)
+    cases.append(("mm_tn", lambda: at.t() @ b, "f32"))
+    bt = r(384, 512)
+    cases.append(("mm_nt", lambda: a @ bt.t(), "f32"))
+    x, w = r(2048, 512), r(64, 512)  # GPT per-head projection: m=64, n=2048, k=512
+    cases.append(("linear_head", lambda: F.linear(x, w), "f32"))
+    w2, bias = r(2048, 512), r(2048)
+    cases.append(("linear_bias_lt", lambda: F.linear(x, w2, bias), "f32"))
+    q, k = r(8, 256, 64), r(8, 256, 64)
+    cases.append(("bmm_qk", lambda: q @ k.transpose(-2, -1), "f32"))
+    p, v = r(8, 256, 256), r(8, 256, 64)
+    cases.append(("bmm_pv", lambda: p @ v, "f32"))
+    o1, o2 = r(33, 70), r(70, 45)
+    cases.append(("mm_odd", lambda: o1 @ o2, "f32"))
+    xb, wb, bb = r(1024, 2048, dtype=bf), r(2048, 2048, dtype=bf), r(2048, dtype=bf)
+    cases.append(("bf16_linear", lambda: F.linear(xb, wb), "bf16"))
+    cases.append(("bf16_linear_bias", lambda: F.linear(xb, wb, bb), "bf16"))
+    qb, kb = r(16, 512, 128, dtype=bf), r(16, 512, 128, dtype=bf)
+    cases.append(("bf16_bmm", lambda: qb @ kb.transpose(-2, -1), "bf16"))
+    return cases
+
+
+def scenario_gemm(orion):
+    import torch
+    torch.backends.cuda.matmul.allow_tf32 = False
+    cases = gemm_cases(torch)
+    assert orion.orion_init_scheduler(1) == 0
+    orion.orion_set_capture(0)
+    refs = {n: fn().float() for n, fn, _ in cases}
+    torch.cuda.synchronize()
+    orion.orion_start_scheduler_thread()
+    orion.orion_set_capture(1)
+    outs = run_on_client(orion, 0, lambda: {n: fn().float() for n, fn, _ in cases})
+    orion.orion_set_capture(0)
+    stats = orion.stats(0)
+    orion.orion_stop_scheduler()
+    errs = {n: rel(outs[n], refs[n]) for n, _, _ in cases}
+    kinds = {n: d for n, _, d in cases}
+    return {"errors": errs, "dtypes": kinds, "stats": stats}
+
+
+def conv_cases():
+    # (N, C, H, W, K, R, S, pad, stride, dil)
+    return [(4, 16, 32, 32, 32, 3, 3, 1, 1, 1),
+            (2, 3, 64, 64, 64, 3, 3, 1, 1, 1),
+            (2, 32, 28, 28, 48, 3, 3, 1, 2, 1),
+            (2, 64, 14, 14, 64, 1, 1, 0, 1, 1),
+            (1, 8, 20, 20, 16, 3, 3, 2, 1, 2)]
+
+
+def scenario_conv(orion):
+    import torch
+    F = torch.nn.functional
+    torch.backends.cudnn.allow_tf32 = False
+    torch.backends.cudnn.benchmark = False
+    g = torch.Generator(device="cuda").manual_seed(1)
+    inputs = []
+    for (n, c, h, w, k, r, s, pad, stride, dil) in conv_cases():
+        x = torch.randn(n, c, h, w, device="cuda", generator=g)
+        wt = torch.randn(k, c, r, s, device="cuda", generator=g) * (2.0 / (c * r * s)) ** 0.5
+        bias = torch.randn(k, device="cuda", generator=g)
+        inputs.append((x, wt, bias, pad, stride, dil))
+
+    def run():
+        res = []
+        for x, wt, bias, pad, stride, dil in inputs:
+            xx = x.clone().requires_grad_(True)
+            ww = wt.clone().requires_grad_(True)
+            y = F.conv2d(xx, ww, bias, stride=stride, padding=pad, dilation=dil)
+            gy = torch.ones_like(y) + 0.01 * torch.arange(y.numel(), device=y.device).view_as(y) % 7
+            y.backward(gy)
+            res.append((y.detach(), xx.grad.detach(), ww.grad.detach()))
+        return res
+
+    assert orion.orion_init_scheduler(1) == 0
+    orion.orion_set_capture(0)
+    refs = run()
+    torch.cuda.synchronize()
+    orion.orion_start_scheduler_thread()
+    orion.orion_set_capture(1)
+    outs = run_on_client(orion, 0, run)
+    orion.orion_set_capture(0)
+    stats = orion.stats(0)
+    orion.orion_stop_scheduler()
+    errs = {}
+    for i, ((y, dx, dw), (ry, rdx, rdw)) in enumerate(zip(outs, refs)):
+        errs[f"fwd_{i}"] = rel(y, ry)
+        errs[f"dgrad_{i}"] = rel(dx, rdx)
+        errs[f"wgrad_{i}"] = rel(dw, rdw)
+    return {"errors": errs, "stats": stats}
+
+
+def scenario_bn(orion):
+    import torch
+    F = torch.nn.functional
+    g = torch.Generator(device="cuda").manual_seed(2)
+    shapes = [(8, 64, 28, 28), (4, 128, 14, 14), (16, 32, 7, 7)]
+    inputs = [(torch.randn(*s, device="cuda", generator=g) * 2 + 0.5,
+               torch.rand(s[1], device="cuda", generator=g) + 0.5,
+               torch.randn(s[1], device="cuda", generator=g)) for s in shapes]
+
+    def run():
+        res = []
+        for x, wgt, b in inputs:
+            xx = x.clone().requires_grad_(True)
+            ww = wgt.clone().requires_grad_(True)
+            bb = b.clone().requires_grad_(True)
+            rm = torch.zeros(x.shape[1], device="cuda")
+            rv = torch.ones(x.shape[1], device="cuda")
+            y = F.batch_norm(xx, rm, rv, ww, bb, training=True, momentum=0.1, eps=1e-5)
+            y.backward(torch.cos(y.detach()))
+            yi = F.batch_norm(x, rm, rv, wgt, b, training=False, eps=1e-5)
+            res.append((y.detach(), xx.grad, ww.grad, bb.grad, rm, rv, yi))
+        return res
+
+    assert orion.orion_init_scheduler(1) == 0
+    orion.orion_set_capture(0)
+    refs = run()
+    torch.cuda.synchronize()
+    orion.orion_start_scheduler_thread()
+    orion.orion_set_capture(1)
+    outs = run_on_client(orion, 0, run)
+    orion.orion_set_capture(0)
+    stats = orion.stats(0)
+    orion.orion_stop_scheduler()
+    names = ("y", "dx", "dscale", "dbias", "running_mean", "running_var", "y_inference")
+    errs = {}
+    for i, (o, r) in enumerate(zip(outs, refs)):
+        for nm, a, b in zip(names, o, r):
+            errs[f"{nm}_{i}"] = rel(a, b)
+    return {"errors": errs, "stats": stats}
+
+
+def scenario_gpt(orion):
+    """End-to-end: the GPT decoder forward (fp32, batch 2 x seq 256) captured
+    on client 0 vs the same forward through the real libraries."""
+    import torch
+
+    from kernel_intercept_b200 import harness
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.manual_seed(0)
+    m = harness.make_gpt(device="cuda").eval()
+    tok = torch.randint(0, 32000, (2, 256), device="cuda")
+    assert orion.orion_init_scheduler(1) == 0
+    orion.orion_set_capture(0)
+    with torch.no_grad():
+        ref = m(tok)
+    torch.cuda.synchronize()
+    orion.orion_start_scheduler_thread()
+    orion.orion_set_capture(1)
+
+    def fwd():
+        with torch.no_grad():
+            return m(tok)
+
+    out = run_on_client(orion, 0, fwd)
+    orion.orion_set_capture(0)
+    stats = orion.stats(0)
+    orion.orion_stop_scheduler()
+    return {"errors": {"logits": rel(out, ref)}, "stats": stats}
+
+
+def scenario_hpbe(orion):
+    """HP (small GEMMs) and BE (large GEMMs) clients at once: both finish,
+    results stay exact, the BE client saw yields or blocking."""
+    import torch
+
+    from kernel_intercept_b200 import harness
+    torch.backends.cuda.matmul.allow_tf32 = False
+    g = torch.Generator(device="cuda").manual_seed(3)
+    a = torch.randn(256, 1024, device="cuda", generator=g)
+    b = torch.randn(1024, 1024, device="cuda", generator=g)
+    A = torch.randn(4096, 4096, device="cuda", generator=g)
+    B = torch.randn(4096, 4096, device="cuda", generator=g)
+    assert orion.orion_init_scheduler(2) == 0
+    orion.orion_set_capture(0)
+    ref_hp = a @ b
+    ref_be = A @ B
+    torch.cuda.synchronize()
+    orion.orion_start_scheduler_thread()
+    orion.orion_set_capture(1)
+    hp_out, be_out = [], []
+
+    def hp_step():
+        hp_out.append(a @ b)
+
+    def be_step():
+        be_out.append(A @ B)
+
+    hp, be = harness.run_clients(orion, hp_step, be_step, hp_steps=40, hp_warmup=2)
+    orion.orion_set_capture(0)
+    stats = {c: orion.stats(c) for c in (0, 1)}
+    orion.orion_stop_scheduler()
+    torch.cuda.synchronize()
+    err_hp = max(rel(o, ref_hp) for o in hp_out)
+    err_be = max(rel(o, ref_be) for o in be_out)
+    return {"errors": {"hp": err_hp, "be": err_be}, "stats": stats,
+            "hp_p50_ms": harness.percentile(hp.latencies_ms, 0.5), "be_iters": be.iters}
+
+
+def main():
+    scenario = sys.argv[1]
+    from kernel_intercept_b200 import harness
+    if not harness.preloaded():
+        print(json.dumps({"error": "not preloaded"}))
+        return 2
+    orion = harness.Orion()
+    res = globals()["scenario_" + scenario](orion)
+    print(json.dumps(res), flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    rc = main()
+    sys.stdout.flush()
+    os._exit(rc)

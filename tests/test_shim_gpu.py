@@ -1,0 +1,86 @@
+"""Interposer (libgpu_scheduler.so) parity on the GPU.
+
+Each test starts tests/shim_child.py under LD_PRELOAD, the way the
+reference's drivers run (run.sh under LD_PRELOAD; python/test_orion_blocking.py
+``run_test``), so PyTorch's own cuBLAS / cuBLASLt / cuDNN calls are the ones
+intercepted.  The child compares each captured op (executed by the worker on
+the kx kernels) with the same op through the real libraries with capture off
+and TF32 disabled.  Tolerances: fp32 max normwise relative error 1e-5; bf16
+1e-2 against the real library's fp32-accumulated result.
+"""
+import json
+import os
+import subprocess
+import sys
+
+import pytest
+
+from kernel_intercept_b200 import LIBKX, LIBSHIM
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+CHILD = os.path.join(ROOT, "tests", "shim_child.py")
+
+pytestmark = pytest.mark.gpu
+
+F32_TOL = 1e-5
+BF16_TOL = 1e-2
+
+
+def run_child(scenario, timeout=900, extra_env=None):
+    if not (os.path.exists(LIBSHIM) and os.path.exists(LIBKX)):
+        pytest.fail("libgpu_scheduler.so / libkx.so not built")
+    env = dict(os.environ)
+    env["LD_PRELOAD"] = LIBSHIM
+    env.setdefault("ORION_LOG_LEVEL", "WARN")
+    if extra_env:
+        env.update(extra_env)
+    p = subprocess.run([sys.executable, CHILD, scenario], env=env, cwd=ROOT,
+                       capture_output=True, text=True, timeout=timeout)
+    lines = [ln for ln in p.stdout.splitlines() if ln.startswith("{")]
+    assert p.returncode == 0 and lines, (
+        f"child {scenario} rc={p.returncode}\nstdout:\n{p.stdout[-3000:]}\n"
+        f"stderr:\n{p.stderr[-3000:]}")
+    return json.loads(lines[-1])
+
+
+def test_gemm_ops_through_interposer():
+    res = run_child("gemm")
+    st = res["stats"]
+    assert st["errors"] == 0, st
+    assert st["kx_ops"] >= len(res["errors"]), st
+    for name, err in res["errors"].items():
+        tol = BF16_TOL if res["dtypes"][name] == "bf16" else F32_TOL
+        assert err <= tol, (name, err)
+
+
+def test_conv_fwd_dgrad_wgrad_through_interposer():
+    res = run_child("conv")
+    st = res["stats"]
+    assert st["errors"] == 0, st
+    assert st["kx_ops"] >= 15, st  # 5 shapes x (fwd, dgrad, wgrad)
+    for name, err in res["errors"].items():
+        assert err <= F32_TOL, (name, err)
+
+
+def test_batchnorm_through_interposer():
+    res = run_child("bn")
+    st = res["stats"]
+    assert st["errors"] == 0, st
+    for name, err in res["errors"].items():
+        assert err <= F32_TOL, (name, err)
+
+
+def test_gpt_forward_through_interposer():
+    res = run_child("gpt")
+    st = res["stats"]
+    assert st["errors"] == 0, st
+    assert st["kx_ops"] > 200, st  # 144 per-head GEMMs + 96 batched + Lt per forward
+    assert res["errors"]["logits"] <= F32_TOL, res
+
+
+def test_hp_be_clients_contend():
+    res = run_child("hpbe")
+    for c in ("0", "1"):
+        assert res["stats"][c]["errors"] == 0, res
+    assert res["errors"]["hp"] <= F32_TOL and res["errors"]["be"] <= F32_TOL, res
+    assert res["be_iters"] >= 1
