@@ -196,7 +196,7 @@ class Clocks:
         sm = sorted(float(r[0]) for r in rows if r[0].replace(".", "").isdigit())
         mx = max(float(r[1]) for r in rows if r[1].replace(".", "").isdigit())
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if "Active" in r[3 + i]})
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[3 + i] == "Active"})
         return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": reasons}
 
 
@@ -420,6 +420,30 @@ def roofline(recs, peaks, peak_src, tf32, sustained):
             "op": f"{client}:{op}", "kernel": top, "launches": agg["n"],
             "avg_ms": round(avg_ms, 4), "share_of_captured_ms":
             round(agg["ms"] / sum(v["ms"] for v in by_op.values()), 4)}
+
+
+def measure_tf32_peak(dev):
+    """cuBLAS TF32 rate on 8192^3 (burst, best of 5), the denominator of the
+    3xTF32 ceiling.  Called with capture off, so cuBLAS itself runs."""
+    import torch
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = True
+    a = torch.randn(8192, 8192, device=dev)
+    b = torch.randn(8192, 8192, device=dev)
+    c = torch.empty(8192, 8192, device=dev)
+    for _ in range(2):
+        torch.matmul(a, b, out=c)
+    best = 1e9
+    for _ in range(5):
+        s, e = torch.cuda.Event(True), torch.cuda.Event(True)
+        s.record()
+        torch.matmul(a, b, out=c)
+        e.record()
+        e.synchronize()
+        best = min(best, s.elapsed_time(e))
+    torch.backends.cuda.matmul.allow_tf32 = prev
+    del a, b, c
+    return 2 * 8192 ** 3 / (best * 1e-3) / 1e12
 
 
 def torch_cpu_vgg16_images_per_s(sample_images=2):

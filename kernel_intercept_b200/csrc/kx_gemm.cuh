@@ -73,6 +73,12 @@ struct GemmParams {
   int max_tiles;
   unsigned long long timeout_ns;
   int* err_word;
+  // split-K: each output tile is computed as `splits` K slices of
+  // `kb_per_split` k-blocks whose fp32 partials go to ws
+  // ([batch][splits][n][m], column-major per slice); kx_splitk_reduce then
+  // applies alpha / beta / bias / activation.  splits == 1: direct epilogue.
+  int splits, kb_per_split;
+  float* ws;
 };
 
 template <int BN_, Arith AR_, bool A_MN_, bool B_MN_>
@@ -158,9 +164,14 @@ KX_DEV float gelu_tanh(float x) {
   return 0.5f * x * (1.0f + tanhf(k0 * (x + 0.044715f * x * x * x)));
 }
 
-KX_DEV void decode_tile(int tile, const GemmParams& p, int& b, int& mb, int& nb) {
+// Tile id -> (batch, K slice, M block, N block).  Slices are outermost within
+// a batch so that concurrently running CTAs share A/B rows in L2.
+KX_DEV void decode_tile(int tile, const GemmParams& p, int& b, int& ks, int& mb, int& nb) {
   b = tile / p.tiles_per_batch;
   int t = tile - b * p.tiles_per_batch;
+  const int per_split = p.num_mb * p.num_nb;
+  ks = t / per_split;
+  t -= ks * per_split;
   // grouped raster: 8 M-blocks share each sweep over N for L2 reuse of B
   constexpr int G = 8;
   int group_span = G * p.num_nb;
@@ -170,6 +181,43 @@ KX_DEV void decode_tile(int tile, const GemmParams& p, int& b, int& mb, int& nb)
   int r = t - g * group_span;
   mb = first_mb + r % gsize;
   nb = r / gsize;
+}
+
+// First k-block and k-block count of a tile's K slice.
+KX_DEV void tile_k_range(int tile, const GemmParams& p, int& kb0, int& nkb) {
+  const int ks = (tile % p.tiles_per_batch) / (p.num_mb * p.num_nb);
+  kb0 = ks * p.kb_per_split;
+  const int end = kb0 + p.kb_per_split < p.num_kb ? kb0 + p.kb_per_split : p.num_kb;
+  nkb = end - kb0;
+}
+
+// Sums the split-K partials of every output element and applies the
+// epilogue.  Runs after the GEMM kernel on the same stream; does nothing when
+// that launch stopped early (yield or tile budget), in which case the
+// relaunch that completes the tiles is followed by another reduce.
+static __global__ void __launch_bounds__(256) kx_splitk_reduce(const GemmParams p, int batch) {
+  if (p.work->status != 1) return;
+  const float alpha = p.alpha_dev ? *p.alpha_dev : p.alpha;
+  const float beta = p.beta_dev ? *p.beta_dev : p.beta;
+  const long long mn = static_cast<long long>(p.m) * p.n;
+  const long long total = mn * batch;
+  for (long long e = blockIdx.x * 256LL + threadIdx.x; e < total;
+       e += static_cast<long long>(gridDim.x) * 256) {
+    const long long b = e / mn;
+    const long long r = e - b * mn;
+    const int col = static_cast<int>(r / p.m);
+    const int row = static_cast<int>(r - static_cast<long long>(col) * p.m);
+    const float* src = p.ws + b * p.splits * mn + r;
+    float acc = 0.f;
+    for (int s = 0; s < p.splits; ++s) acc += src[s * mn];
+    float o = alpha * acc;
+    if (beta != 0.f)
+      o += beta * load_scalar(p.C, p.c_type, b * p.strideC + static_cast<long long>(col) * p.ldc + row);
+    if (p.bias != nullptr) o += load_scalar(p.bias, p.bias_type, row);
+    if (p.relu) o = fmaxf(o, 0.f);
+    if (p.gelu) o = gelu_tanh(o);
+    store_scalar(p.D, p.d_type, b * p.strideD + static_cast<long long>(col) * p.ldd + row, o);
+  }
 }
 
 template <class Cfg>
@@ -250,12 +298,13 @@ __global__ void __launch_bounds__(256, 1)
         mbar_arrive(smem_addr(&sb->ring_full[r]));
         if (tile < 0) break;
         ++taken;
-        int b, mb, nb;
-        decode_tile(tile, p, b, mb, nb);
+        int b, ks, mb, nb, kb0, nkb;
+        decode_tile(tile, p, b, ks, mb, nb);
+        tile_k_range(tile, p, kb0, nkb);
         const int ba = p.a_bcast ? 0 : b;
         const int bb = p.b_bcast ? 0 : b;
         bool ok = true;
-        for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+        for (int kb = kb0; kb < kb0 + nkb; ++kb, ++it) {
           const uint32_t s = it % S;
           if (!mbar_wait(smem_addr(&sb->empty[s]), ((it / S) & 1) ^ 1, wc)) { ok = false; break; }
           const uint32_t fb = smem_addr(&sb->full[s]);
@@ -302,12 +351,14 @@ __global__ void __launch_bounds__(256, 1)
         const int tile = sb->ring[r];
         mbar_arrive(smem_addr(&sb->ring_empty[r]));
         if (tile < 0) break;
-        for (int kb = 0; kb < p.num_kb && ok; ++sc) {
+        int kb0, nkb;
+        tile_k_range(tile, p, kb0, nkb);
+        for (int kb = 0; kb < nkb && ok; ++sc) {
           const uint32_t a = sc & 1;
           if (!mbar_wait(smem_addr(&sb->tempty[a]), ((sc >> 1) & 1) ^ 1, wc)) { ok = false; break; }
           tc_fence_after();
           const uint32_t d_tmem = tmem + a * Cfg::BN;
-          const int kend = (p.num_kb - kb > Cfg::SEG) ? kb + Cfg::SEG : p.num_kb;
+          const int kend = (nkb - kb > Cfg::SEG) ? kb + Cfg::SEG : nkb;
           const int kfirst = kb;
           for (; kb < kend; ++kb, ++it) {
             const uint32_t s = it % S;
@@ -365,7 +416,9 @@ __global__ void __launch_bounds__(256, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_addr(&sb->ring_empty[r]));
         if (tile < 0) break;
-        for (int kb = 0; kb < p.num_kb; ++kb, ++it) {
+        int kb0, nkb;
+        tile_k_range(tile, p, kb0, nkb);
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
           const uint32_t s = it % S;
           ok = mbar_wait(smem_addr(&sb->full[s]), (it / S) & 1, wc);
           ok = __all_sync(0xffffffffu, ok);
@@ -397,8 +450,8 @@ __global__ void __launch_bounds__(256, 1)
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     const float alpha = p.alpha_dev ? *p.alpha_dev : p.alpha;
     const float beta = p.beta_dev ? *p.beta_dev : p.beta;
-    const int nseg = Cfg::PROMOTE ? (p.num_kb + Cfg::SEG - 1) / Cfg::SEG : 1;
     const uint32_t lane_off = (q * 32u) << 16;
+    const bool split = p.splits > 1;
     uint32_t sc = 0;
     for (uint32_t slot = 0;; ++slot) {
       const uint32_t r = slot % R;
@@ -409,17 +462,29 @@ __global__ void __launch_bounds__(256, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_addr(&sb->ring_empty[r]));
       if (tile < 0) break;
-      int b, mb, nb;
-      decode_tile(tile, p, b, mb, nb);
+      int b, ks, mb, nb, kb0, nkb;
+      decode_tile(tile, p, b, ks, mb, nb);
+      tile_k_range(tile, p, kb0, nkb);
+      const int nseg = Cfg::PROMOTE ? (nkb + Cfg::SEG - 1) / Cfg::SEG : 1;
       const int row = mb * Cfg::BM + q * 32 + static_cast<int>(lane);
       const bool row_ok = row < p.m;
-      const float bias_v = (p.bias != nullptr && row_ok) ? load_scalar(p.bias, p.bias_type, row) : 0.f;
+      const float bias_v = (p.bias != nullptr && row_ok && !split) ? load_scalar(p.bias, p.bias_type, row) : 0.f;
       const size_t d_base = static_cast<size_t>(b) * p.strideD + row;
       const size_t c_base = static_cast<size_t>(b) * p.strideC + row;
+      // split-K slice: raw fp32 partial, column-major with ld m
+      float* ws_tile = split ? p.ws + (static_cast<size_t>(b) * p.splits + ks) *
+                                          static_cast<size_t>(p.m) * p.n + row
+                             : nullptr;
       // alpha/beta/bias/activation for 32 consecutive columns of this row
       auto emit = [&](int c0, const float* acc) {
         const int col0 = nb * Cfg::BN + c0;
         if (!row_ok) return;
+        if (split) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (col0 + j < p.n) ws_tile[static_cast<size_t>(col0 + j) * p.m] = acc[j];
+          return;
+        }
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
           const int col = col0 + j;

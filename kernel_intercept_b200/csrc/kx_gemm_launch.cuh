@@ -74,9 +74,43 @@ int launch_gemm_tc(const Exec& e, const TcProblem& pr, GemmParams p) {
       return KX_ERR_DEVICE;
     attr_set[di.device & 63] = true;
   }
+  // Split-K when the output tiles cannot fill the CTAs the launch may use and
+  // K is long: slices of at least MIN_KB k-blocks (256 of K), at most 32.
+  constexpr int MIN_KB = 256 / Cfg::BK;
+  const int cap = persistent_grid(e, 1 << 30);
+  p.splits = 1;
+  p.kb_per_split = p.num_kb;
+  if (tiles * 2 <= cap && p.num_kb >= 2 * MIN_KB && !split_k_disabled()) {
+    long long want = cap / tiles;
+    const long long by_k = p.num_kb / MIN_KB;
+    if (want > by_k) want = by_k;
+    if (want > 32) want = 32;
+    if (want >= 2) {
+      const int kbps = static_cast<int>((p.num_kb + want - 1) / want);
+      const int splits = (p.num_kb + kbps - 1) / kbps;
+      const size_t ws_bytes = sizeof(float) * static_cast<size_t>(splits) * pr.batch *
+                              static_cast<size_t>(pr.m) * pr.n;
+      float* ws = static_cast<float*>(scratch_for(e.stream, ws_bytes, 1));
+      if (ws != nullptr && tiles * splits <= 0x7fffffffLL) {
+        p.splits = splits;
+        p.kb_per_split = kbps;
+        p.ws = ws;
+        p.tiles_per_batch *= splits;
+        p.num_tiles = static_cast<int>(tiles * splits);
+      }
+    }
+  }
   const int grid = persistent_grid(e, p.num_tiles);
   note_launch();
   kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, e.stream>>>(ma, mb, p);
+  if (p.splits > 1) {
+    const long long total = static_cast<long long>(pr.m) * pr.n * pr.batch;
+    long long rgrid = (total + 255) / 256;
+    const long long rcap = 8LL * device_info().num_sms;
+    if (rgrid > rcap) rgrid = rcap;
+    note_launch();
+    kx_splitk_reduce<<<static_cast<int>(rgrid), 256, 0, e.stream>>>(p, pr.batch);
+  }
   static char name[96];
   if (name[0] == 0)
     snprintf(name, sizeof(name), "kx_gemm_tc<bn%d,%s,A%s,B%s>", BN, arith_name<AR>(),

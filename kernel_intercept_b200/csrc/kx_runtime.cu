@@ -90,16 +90,17 @@ struct Scratch {
   void* ptr = nullptr;
   size_t bytes = 0;
 };
-std::unordered_map<cudaStream_t, Scratch> g_scratch[64];
+std::unordered_map<cudaStream_t, Scratch> g_scratch[64][2];
 }  // namespace
 
-void* scratch_for(cudaStream_t stream, size_t bytes) {
+void* scratch_for(cudaStream_t stream, size_t bytes, int slot) {
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) dev = 0;
+  if (slot < 0 || slot > 1) return nullptr;
   if (bytes == 0) bytes = 256;
   std::lock_guard<std::mutex> lk(g_mu);
-  Scratch& s = g_scratch[dev][stream];
+  Scratch& s = g_scratch[dev][slot][stream];
   if (s.bytes >= bytes) return s.ptr;
   if (s.ptr != nullptr) {
     cudaFree(s.ptr);

@@ -7,6 +7,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <cstdlib>
 #include <mutex>
 #include <unordered_map>
 
@@ -34,7 +35,19 @@ WorkSlot* work_slot_for(cudaStream_t stream);
 // `bytes` long.  Growing it frees the previous buffer (cudaFree waits for the
 // device), so ops on one stream may reuse it back to back; ops on different
 // streams get different buffers.  Returns nullptr on allocation failure.
-void* scratch_for(cudaStream_t stream, size_t bytes);
+// Slot 0 serves the operator entry points (im2col buffers, batch-norm
+// statistics); slot 1 is the GEMM's own split-K workspace, so a GEMM issued
+// by an operator never overwrites the operator's buffer.
+void* scratch_for(cudaStream_t stream, size_t bytes, int slot = 0);
+
+// KX_SPLITK=0 turns split-K off (every output tile then runs its whole K).
+inline bool split_k_disabled() {
+  static const bool off = [] {
+    const char* s = std::getenv("KX_SPLITK");
+    return s != nullptr && s[0] == '0';
+  }();
+  return off;
+}
 
 // Resolved execution controls.
 struct Exec {

@@ -18,9 +18,13 @@
 // Calls kx does not implement (non-float data, grouped or 3-D convolutions,
 // non-packed NCHW tensors) go to the real cuDNN after the client's queue has
 // drained.
+#include <algorithm>
+#include <atomic>
+#include <vector>
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <string>
 #include <thread>
 #include <unordered_map>
 
@@ -134,6 +138,9 @@ cudnnStatus_t submit_op(OperationType type, void* handle, Params p, bool support
   const Route r = route_for(handle, p.stream, &client);
   if (r == Route::kReal) return real();
   if (!supported) {
+    static std::atomic<int> reported{0};
+    if (reported.fetch_add(1) < 8)
+      LOG_WARN("%s: arguments not handled by kx; running on cuDNN", op_type_name(type));
     drain_client(client);
     g_scheduler.stats(client < 0 ? 0 : client).passthrough_ops.fetch_add(1);
     return real();
@@ -546,70 +553,130 @@ cudnnStatus_t cudnnSetStream(void* handle, cudaStream_t streamId) {
 // ------------------------------------------------------- backend graph API --
 //
 // PyTorch 2.x reaches cuDNN convolutions only through the graph API: it
-// finalizes an execution plan for a one-operation graph and calls
-// cudnnBackendExecute(handle, plan, variantPack).  The plan is decoded with
-// cuDNN's public getters (plan -> engine config -> engine -> operation graph
-// -> convolution operation -> X/W/Y tensors + convolution descriptor) and
-// cached per plan (cudnnBackendDestroyDescriptor evicts).  Data pointers come
-// from the variant pack by tensor UID.  Anything that does not decode to a
-// single packed-NCHW fp32 2-D convolution runs on the real cuDNN.
+// builds a one-operation graph, finalizes an execution plan for it and calls
+// cudnnBackendExecute(handle, plan, variantPack).  cuDNN does not hand the
+// operations of a finalized graph back (getting CUDNN_ATTR_OPERATIONGRAPH_OPS
+// answers CUDNN_STATUS_NOT_SUPPORTED), so the interposer keeps a shadow of
+// the descriptors as the caller builds them: cudnnBackendCreateDescriptor
+// records each descriptor's type, cudnnBackendSetAttribute the attributes
+// that describe a convolution (tensor dims / strides / UID / type, the
+// convolution descriptor, the operation's tensors and scalars, graph ops,
+// engine -> graph, engine config -> engine, plan -> engine config) and
+// cudnnBackendGetAttribute the engine configs that heuristics return for a
+// graph.  When a plan is finalized its chain is resolved (all descriptors are
+// still alive then) and the decoded convolution is cached per plan;
+// cudnnBackendDestroyDescriptor drops shadows and cached plans.  Data
+// pointers come from the variant pack by tensor UID.  A plan that does not
+// decode to a single packed-NCHW fp32 2-D convolution runs on the real cuDNN.
 
 namespace {
 
 using BDesc = void*;
 using GetAttr = int (*)(BDesc, int, int, int64_t, int64_t*, void*);
-using CreateDesc = int (*)(int, BDesc*);
-using DestroyDesc = int (*)(BDesc);
 
 constexpr int kTypeDataType = 1, kTypeInt64 = 3, kTypeFloat = 4, kTypeDouble = 5,
               kTypeVoidPtr = 6, kTypeConvMode = 7, kTypeBackendDesc = 15;
-constexpr int kDescConvolution = 1, kDescEngine = 2, kDescEngineCfg = 3,
-              kDescConvFwd = 10, kDescConvBwdFilter = 11, kDescConvBwdData = 12,
-              kDescOpGraph = 15, kDescTensor = 17;
+constexpr int kDescPlan = 5, kDescConvFwd = 10, kDescConvBwdFilter = 11, kDescConvBwdData = 12;
+// attribute names (cudnnBackendAttributeName_t)
+constexpr int kAttrConvCompType = 100, kAttrConvMode = 101, kAttrConvDilations = 102,
+              kAttrConvStrides = 103, kAttrConvPostPad = 104, kAttrConvPrePad = 105,
+              kAttrConvSpatialDims = 106, kAttrHeurGraph = 201, kAttrHeurResults = 202,
+              kAttrCfgEngine = 300, kAttrPlanCfg = 401, kAttrGraphOps = 801,
+              kAttrTensorType = 901, kAttrTensorDims = 902, kAttrTensorStrides = 903,
+              kAttrTensorUid = 906, kAttrPackUids = 1000, kAttrPackPtrs = 1001,
+              kAttrEngineGraph = 1300;
+constexpr int kSynthCfgGraph = -1;  // graph of the heuristics query a config came from
 
-struct Getters {
-  GetAttr get = reinterpret_cast<GetAttr>(real::cudnn("cudnnBackendGetAttribute"));
-  CreateDesc create = reinterpret_cast<CreateDesc>(real::cudnn("cudnnBackendCreateDescriptor"));
-  DestroyDesc destroy = reinterpret_cast<DestroyDesc>(real::cudnn("cudnnBackendDestroyDescriptor"));
-  bool ok() const { return get && create && destroy; }
-};
-
-const Getters& getters() {
-  static Getters g;
-  return g;
+bool recorded_attr(int a) {
+  return (a >= kAttrConvCompType && a <= kAttrConvSpatialDims) || a == kAttrHeurGraph ||
+         a == kAttrCfgEngine || a == kAttrPlanCfg || (a >= 700 && a <= 717) ||
+         a == kAttrGraphOps || a == kAttrTensorType || a == kAttrTensorDims ||
+         a == kAttrTensorStrides || a == kAttrTensorUid || a == kAttrEngineGraph;
 }
 
-// RAII for descriptors created to receive attribute copies.
-struct Owned {
-  BDesc d = nullptr;
-  explicit Owned(int type) { getters().create(type, &d); }
-  ~Owned() {
-    if (d) getters().destroy(d);
-  }
+struct Shadow {
+  int type = -1;
+  std::unordered_map<int, std::vector<int64_t>> ints;  // INT64 and enum attributes
+  std::unordered_map<int, std::vector<BDesc>> descs;   // descriptor attributes
+  std::unordered_map<int, double> scalars;             // FLOAT / DOUBLE attributes
 };
 
-bool get_desc_attr(BDesc from, int attr, BDesc into) {
-  int64_t n = 0;
-  return into && getters().get(from, attr, kTypeBackendDesc, 1, &n, &into) == 0 && n == 1;
+std::mutex g_shadow_mu;
+std::unordered_map<BDesc, Shadow> g_shadow;
+
+void record_set(BDesc d, int attr, int type, int64_t count, const void* elems) {
+  if (!recorded_attr(attr) || elems == nullptr || count < 0 || count > 64) return;
+  std::lock_guard<std::mutex> lk(g_shadow_mu);
+  Shadow& s = g_shadow[d];
+  switch (type) {
+    case kTypeInt64: {
+      const int64_t* v = static_cast<const int64_t*>(elems);
+      s.ints[attr].assign(v, v + count);
+      break;
+    }
+    case kTypeDataType:
+    case kTypeConvMode: {
+      const int* v = static_cast<const int*>(elems);
+      s.ints[attr].assign(v, v + count);
+      break;
+    }
+    case kTypeBackendDesc: {
+      const BDesc* v = static_cast<const BDesc*>(elems);
+      s.descs[attr].assign(v, v + count);
+      break;
+    }
+    case kTypeFloat:
+      if (count == 1) s.scalars[attr] = *static_cast<const float*>(elems);
+      break;
+    case kTypeDouble:
+      if (count == 1) s.scalars[attr] = *static_cast<const double*>(elems);
+      break;
+    default:
+      break;
+  }
+}
+
+// Reads from the shadow map (caller holds g_shadow_mu).
+const Shadow* shadow_of(BDesc d) {
+  auto it = g_shadow.find(d);
+  return it == g_shadow.end() ? nullptr : &it->second;
+}
+
+BDesc first_desc(const Shadow* s, int attr) {
+  if (s == nullptr) return nullptr;
+  auto it = s->descs.find(attr);
+  return it == s->descs.end() || it->second.empty() ? nullptr : it->second[0];
+}
+
+const std::vector<int64_t>* ints_of(const Shadow* s, int attr) {
+  if (s == nullptr) return nullptr;
+  auto it = s->ints.find(attr);
+  return it == s->ints.end() ? nullptr : &it->second;
 }
 
 struct TensorInfo {
   int64_t uid = -1;
-  int64_t dims[8] = {0};
-  int64_t strides[8] = {0};
-  int64_t nd = 0;
+  int64_t dims[4] = {0};
+  int64_t strides[4] = {0};
   int dtype = -1;
 };
 
-bool read_backend_tensor(BDesc t, TensorInfo& ti) {
-  const Getters& g = getters();
-  int64_t n = 0;
-  if (g.get(t, 906, kTypeInt64, 1, &n, &ti.uid) != 0) return false;
-  if (g.get(t, 902, kTypeInt64, 8, &ti.nd, ti.dims) != 0) return false;
-  int64_t ns = 0;
-  if (g.get(t, 903, kTypeInt64, 8, &ns, ti.strides) != 0 || ns != ti.nd) return false;
-  g.get(t, 901, kTypeDataType, 1, &n, &ti.dtype);
-  return ti.nd == 4;
+bool shadow_tensor(BDesc t, TensorInfo& ti) {
+  const Shadow* s = shadow_of(t);
+  const auto* dims = ints_of(s, kAttrTensorDims);
+  const auto* str = ints_of(s, kAttrTensorStrides);
+  const auto* uid = ints_of(s, kAttrTensorUid);
+  const auto* dt = ints_of(s, kAttrTensorType);
+  if (!dims || !str || !uid || !dt || dims->size() != 4 || str->size() != 4 || uid->empty() ||
+      dt->empty())
+    return false;
+  for (int i = 0; i < 4; ++i) {
+    ti.dims[i] = (*dims)[i];
+    ti.strides[i] = (*str)[i];
+  }
+  ti.uid = (*uid)[0];
+  ti.dtype = static_cast<int>((*dt)[0]);
+  return true;
 }
 
 bool packed_nchw(const TensorInfo& t) {
@@ -620,105 +687,145 @@ bool packed_nchw(const TensorInfo& t) {
 // Decoded plan: which convolution, geometry, the three UIDs and the scalars.
 struct PlanInfo {
   bool ok = false;
+  const char* why = "not decoded";  // first check that failed
   OperationType type = OperationType::UNKNOWN;
   ConvGeometry geom;
-  int64_t uid_x = -1, uid_w = -1, uid_y = -1;  // forward roles: x (input), w, y (output)
+  int64_t uid_x = -1, uid_w = -1, uid_y = -1;  // forward roles: input, filter, output
   float alpha = 1.f, beta = 0.f;
 };
 
-float read_scalar(BDesc op, int attr, float dflt) {
-  const Getters& g = getters();
-  int64_t n = 0;
-  float f = 0.f;
-  if (g.get(op, attr, kTypeFloat, 1, &n, &f) == 0 && n == 1) return f;
-  double d = 0.0;
-  if (g.get(op, attr, kTypeDouble, 1, &n, &d) == 0 && n == 1) return static_cast<float>(d);
-  return dflt;
-}
-
-PlanInfo decode_plan(BDesc plan) {
+// Resolves plan -> engine config -> (engine ->) graph -> the single
+// convolution operation from the shadow records.  Caller holds g_shadow_mu.
+PlanInfo decode_shadow(BDesc plan) {
   PlanInfo info;
-  const Getters& g = getters();
-  if (!g.ok()) return info;
-  Owned cfg(kDescEngineCfg), eng(kDescEngine), graph(kDescOpGraph);
-  if (!get_desc_attr(plan, 401, cfg.d) || !get_desc_attr(cfg.d, 300, eng.d) ||
-      !get_desc_attr(eng.d, 1300, graph.d))
+  auto fail = [&info](const char* why) {
+    info.why = why;
     return info;
-  int64_t nops = 0;
-  // one-operation graphs only; try each convolution flavour for the op's type
-  const struct { int desc; OperationType t; int x, w, y, conv, alpha, beta; } kinds[] = {
-      {kDescConvFwd, OperationType::CUDNN_CONV_FWD, 704, 703, 705, 702, 700, 701},
-      {kDescConvBwdData, OperationType::CUDNN_CONV_BWD_DATA, 710, 709, 711, 708, 706, 707},
-      {kDescConvBwdFilter, OperationType::CUDNN_CONV_BWD_FILTER, 716, 715, 717, 714, 712, 713},
   };
-  for (const auto& k : kinds) {
-    Owned op(k.desc);
-    BDesc arr[1] = {op.d};
-    if (g.get(graph.d, 801, kTypeBackendDesc, 1, &nops, arr) != 0 || nops != 1) continue;
-    Owned tx(kDescTensor), tw(kDescTensor), ty(kDescTensor), cd(kDescConvolution);
-    if (!get_desc_attr(op.d, k.x, tx.d) || !get_desc_attr(op.d, k.w, tw.d) ||
-        !get_desc_attr(op.d, k.y, ty.d) || !get_desc_attr(op.d, k.conv, cd.d))
-      continue;
-    // For bwd-data the attributes are (dx, w, dy); for bwd-filter (x, dw, dy):
-    // map them to the forward roles input / filter / output.
-    TensorInfo a, b, c;
-    if (!read_backend_tensor(tx.d, a) || !read_backend_tensor(tw.d, b) ||
-        !read_backend_tensor(ty.d, c))
-      return info;
-    TensorInfo in = a, filt = b, out = c;
-    if (k.t == OperationType::CUDNN_CONV_BWD_FILTER) {  // (x, dw, dy): a = x, b = dw, c = dy
-      in = a;
-      filt = b;
-      out = c;
-    }
-    int64_t n = 0, sd = 0;
-    int64_t pre[4] = {0}, post[4] = {0}, dil[4] = {0}, str[4] = {0};
-    int mode = 1, ctype = -1;
-    if (g.get(cd.d, 106, kTypeInt64, 1, &n, &sd) != 0 || sd != 2) return info;
-    if (g.get(cd.d, 105, kTypeInt64, 4, &n, pre) != 0 || n != 2) return info;
-    if (g.get(cd.d, 104, kTypeInt64, 4, &n, post) != 0 || n != 2) return info;
-    if (g.get(cd.d, 102, kTypeInt64, 4, &n, dil) != 0 || n != 2) return info;
-    if (g.get(cd.d, 103, kTypeInt64, 4, &n, str) != 0 || n != 2) return info;
-    g.get(cd.d, 101, kTypeConvMode, 1, &n, &mode);
-    g.get(cd.d, 100, kTypeDataType, 1, &n, &ctype);
-    ConvGeometry& G = info.geom;
-    std::memset(&G, 0, sizeof(G));
-    G.n = static_cast<int>(in.dims[0]);
-    G.c = static_cast<int>(in.dims[1]);
-    G.h = static_cast<int>(in.dims[2]);
-    G.w = static_cast<int>(in.dims[3]);
-    G.k = static_cast<int>(filt.dims[0]);
-    G.r = static_cast<int>(filt.dims[2]);
-    G.s = static_cast<int>(filt.dims[3]);
-    G.pad_h = static_cast<int>(pre[0]);
-    G.pad_w = static_cast<int>(pre[1]);
-    G.stride_h = static_cast<int>(str[0]);
-    G.stride_w = static_cast<int>(str[1]);
-    G.dil_h = static_cast<int>(dil[0]);
-    G.dil_w = static_cast<int>(dil[1]);
-    G.cross_correlation = mode == 1 ? 1 : 0;
-    G.data_type = in.dtype;
-    const bool geom_ok =
-        pre[0] == post[0] && pre[1] == post[1] && filt.dims[1] == in.dims[1] &&
-        out.dims[0] == in.dims[0] && out.dims[1] == filt.dims[0] && in.dtype == 0 &&
-        filt.dtype == 0 && out.dtype == 0 && (ctype == 0 || ctype == -1) && packed_nchw(in) &&
-        packed_nchw(filt) && packed_nchw(out) && G.stride_h > 0 && G.stride_w > 0;
-    if (!geom_ok) return info;
-    G.packed_nchw = 1;
-    info.type = k.t;
-    info.uid_x = in.uid;
-    info.uid_w = filt.uid;
-    info.uid_y = out.uid;
-    info.alpha = read_scalar(op.d, k.alpha, 1.f);
-    info.beta = read_scalar(op.d, k.beta, 0.f);
-    info.ok = true;
-    return info;
-  }
+  BDesc cfg = first_desc(shadow_of(plan), kAttrPlanCfg);
+  if (!cfg) return fail("plan has no recorded engine config");
+  const Shadow* scfg = shadow_of(cfg);
+  BDesc graph = first_desc(scfg, kSynthCfgGraph);
+  if (!graph) graph = first_desc(shadow_of(first_desc(scfg, kAttrCfgEngine)), kAttrEngineGraph);
+  if (!graph) return fail("engine config without a recorded operation graph");
+  const Shadow* sg = shadow_of(graph);
+  if (!sg || !sg->descs.count(kAttrGraphOps)) return fail("graph without recorded operations");
+  const auto& ops = sg->descs.at(kAttrGraphOps);
+  if (ops.size() != 1) return fail("graph is not a single operation");
+  const Shadow* op = shadow_of(ops[0]);
+  if (!op) return fail("operation not recorded");
+  struct Kind { int desc; OperationType t; int alpha, beta, conv, in, filt, out; };
+  // attribute numbers in forward roles: input, filter, output
+  static const Kind kinds[] = {
+      {kDescConvFwd, OperationType::CUDNN_CONV_FWD, 700, 701, 702, 704, 703, 705},
+      {kDescConvBwdData, OperationType::CUDNN_CONV_BWD_DATA, 706, 707, 708, 710, 709, 711},
+      {kDescConvBwdFilter, OperationType::CUDNN_CONV_BWD_FILTER, 712, 713, 714, 716, 715, 717},
+  };
+  const Kind* k = nullptr;
+  for (const auto& c : kinds)
+    if (op->type == c.desc) k = &c;
+  if (!k) return fail("operation is not a convolution");
+  TensorInfo in, filt, out;
+  if (!shadow_tensor(first_desc(op, k->in), in) || !shadow_tensor(first_desc(op, k->filt), filt) ||
+      !shadow_tensor(first_desc(op, k->out), out))
+    return fail("convolution tensors are not 4-D or not recorded");
+  const Shadow* cd = shadow_of(first_desc(op, k->conv));
+  const auto* sd = ints_of(cd, kAttrConvSpatialDims);
+  const auto* pre = ints_of(cd, kAttrConvPrePad);
+  const auto* post = ints_of(cd, kAttrConvPostPad);
+  const auto* dil = ints_of(cd, kAttrConvDilations);
+  const auto* str = ints_of(cd, kAttrConvStrides);
+  const auto* mode = ints_of(cd, kAttrConvMode);
+  const auto* comp = ints_of(cd, kAttrConvCompType);
+  if (!sd || sd->empty() || (*sd)[0] != 2 || !pre || pre->size() != 2 || !post ||
+      post->size() != 2 || !dil || dil->size() != 2 || !str || str->size() != 2)
+    return fail("convolution descriptor is not 2-D");
+  ConvGeometry& G = info.geom;
+  std::memset(&G, 0, sizeof(G));
+  G.n = static_cast<int>(in.dims[0]);
+  G.c = static_cast<int>(in.dims[1]);
+  G.h = static_cast<int>(in.dims[2]);
+  G.w = static_cast<int>(in.dims[3]);
+  G.k = static_cast<int>(filt.dims[0]);
+  G.r = static_cast<int>(filt.dims[2]);
+  G.s = static_cast<int>(filt.dims[3]);
+  G.pad_h = static_cast<int>((*pre)[0]);
+  G.pad_w = static_cast<int>((*pre)[1]);
+  G.dil_h = static_cast<int>((*dil)[0]);
+  G.dil_w = static_cast<int>((*dil)[1]);
+  G.stride_h = static_cast<int>((*str)[0]);
+  G.stride_w = static_cast<int>((*str)[1]);
+  G.cross_correlation = (mode && !mode->empty() && (*mode)[0] == 0) ? 0 : 1;
+  G.data_type = in.dtype;
+  const bool float_math = !comp || comp->empty() || (*comp)[0] == 0;
+  const bool geom_ok = (*pre)[0] == (*post)[0] && (*pre)[1] == (*post)[1] &&
+                       filt.dims[1] == in.dims[1] && out.dims[0] == in.dims[0] &&
+                       out.dims[1] == filt.dims[0] && in.dtype == 0 && filt.dtype == 0 &&
+                       out.dtype == 0 && float_math && packed_nchw(in) && packed_nchw(filt) &&
+                       packed_nchw(out) && G.stride_h > 0 && G.stride_w > 0 && G.dil_h > 0 &&
+                       G.dil_w > 0;
+  if (!geom_ok) return fail("data type / grouping / layout not handled by kx");
+  G.packed_nchw = 1;
+  info.type = k->t;
+  info.uid_x = in.uid;
+  info.uid_w = filt.uid;
+  info.uid_y = out.uid;
+  auto sa = op->scalars.find(k->alpha);
+  auto sb = op->scalars.find(k->beta);
+  info.alpha = sa == op->scalars.end() ? 1.f : static_cast<float>(sa->second);
+  info.beta = sb == op->scalars.end() ? 0.f : static_cast<float>(sb->second);
+  info.ok = true;
+  info.why = "";
   return info;
 }
 
 std::mutex g_plan_mu;
 std::unordered_map<BDesc, PlanInfo> g_plans;
+
+// Calls seen per attribute name (diagnostics for undecodable plans).
+std::atomic<int> g_set_calls[2048], g_get_calls[2048];
+
+std::string describe(BDesc d) {
+  const Shadow* s = shadow_of(d);
+  if (!s) return "unrecorded";
+  std::string out = "type " + std::to_string(s->type) + " attrs";
+  for (const auto& kv : s->ints) out += " " + std::to_string(kv.first);
+  for (const auto& kv : s->descs) out += " " + std::to_string(kv.first) + "(d" + std::to_string(kv.second.size()) + ")";
+  for (const auto& kv : s->scalars) out += " " + std::to_string(kv.first) + "(f)";
+  return out;
+}
+
+void dump_chain(BDesc plan) {
+  std::string msg;
+  {
+    std::lock_guard<std::mutex> lk(g_shadow_mu);
+    BDesc cfg = first_desc(shadow_of(plan), kAttrPlanCfg);
+    BDesc synth = first_desc(shadow_of(cfg), kSynthCfgGraph);
+    BDesc eng = first_desc(shadow_of(cfg), kAttrCfgEngine);
+    BDesc eg = first_desc(shadow_of(eng), kAttrEngineGraph);
+    char buf[160];
+    snprintf(buf, sizeof(buf), "plan %p cfg %p synth-graph %p engine %p engine-graph %p; ", plan,
+             cfg, synth, eng, eg);
+    msg = buf;
+    msg += "plan: " + describe(plan) + "; cfg: " + describe(cfg) + "; graph: " +
+           describe(synth ? synth : eg) + "; set calls:";
+  }
+  for (int a = 0; a < 2048; ++a)
+    if (g_set_calls[a].load()) msg += " " + std::to_string(a) + "x" + std::to_string(g_set_calls[a].load());
+  msg += "; get calls:";
+  for (int a = 0; a < 2048; ++a)
+    if (g_get_calls[a].load()) msg += " " + std::to_string(a) + "x" + std::to_string(g_get_calls[a].load());
+  LOG_WARN("%s", msg.c_str());
+}
+
+void note_plan(BDesc plan, const PlanInfo& info) {
+  static std::atomic<int> reported{0};
+  const int nrep = reported.fetch_add(1);
+  if (!info.ok && nrep < 8) LOG_WARN("cudnn plan %p will run on cuDNN (%s)", plan, info.why);
+  if (!info.ok && nrep < 2 && std::getenv("KX_CUDNN_DEBUG") != nullptr) dump_chain(plan);
+  std::lock_guard<std::mutex> lk(g_plan_mu);
+  g_plans[plan] = info;
+}
 
 PlanInfo plan_info(BDesc plan) {
   {
@@ -726,20 +833,25 @@ PlanInfo plan_info(BDesc plan) {
     auto it = g_plans.find(plan);
     if (it != g_plans.end()) return it->second;
   }
-  PlanInfo info = decode_plan(plan);
-  std::lock_guard<std::mutex> lk(g_plan_mu);
-  g_plans[plan] = info;
+  // finalized before the interposer saw it (not expected under LD_PRELOAD)
+  PlanInfo info;
+  {
+    std::lock_guard<std::mutex> lk(g_shadow_mu);
+    info = decode_shadow(plan);
+  }
+  note_plan(plan, info);
   return info;
 }
 
 bool variant_pointers(BDesc vp, const PlanInfo& info, void** px, void** pw, void** py) {
-  const Getters& g = getters();
+  static GetAttr get = reinterpret_cast<GetAttr>(real::cudnn("cudnnBackendGetAttribute"));
+  if (!get) return false;
   int64_t uids[16], n = 0, np = 0;
   void* ptrs[16];
-  if (g.get(vp, 1000, kTypeInt64, 16, &n, uids) != 0) return false;
-  if (g.get(vp, 1001, kTypeVoidPtr, 16, &np, ptrs) != 0 || np != n) return false;
+  if (get(vp, kAttrPackUids, kTypeInt64, 16, &n, uids) != 0) return false;
+  if (get(vp, kAttrPackPtrs, kTypeVoidPtr, 16, &np, ptrs) != 0 || np != n) return false;
   *px = *pw = *py = nullptr;
-  for (int64_t i = 0; i < n; ++i) {
+  for (int64_t i = 0; i < n && i < 16; ++i) {
     if (uids[i] == info.uid_x) *px = ptrs[i];
     if (uids[i] == info.uid_w) *pw = ptrs[i];
     if (uids[i] == info.uid_y) *py = ptrs[i];
@@ -750,6 +862,74 @@ bool variant_pointers(BDesc vp, const PlanInfo& info, void** px, void** pw, void
 }  // namespace
 
 extern "C" {
+
+cudnnStatus_t cudnnBackendCreateDescriptor(int descriptorType, void** descriptor) {
+  using Fn = cudnnStatus_t (*)(int, void**);
+  static Fn real = reinterpret_cast<Fn>(orion::real::cudnn("cudnnBackendCreateDescriptor"));
+  if (!real) return 1;
+  const cudnnStatus_t st = real(descriptorType, descriptor);
+  if (st == 0 && descriptor && *descriptor) {
+    std::lock_guard<std::mutex> lk(g_shadow_mu);
+    Shadow& s = g_shadow[*descriptor];
+    s = Shadow();
+    s.type = descriptorType;
+  }
+  return st;
+}
+
+cudnnStatus_t cudnnBackendSetAttribute(void* descriptor, int attributeName, int attributeType,
+                                       int64_t elementCount, const void* arrayOfElements) {
+  using Fn = cudnnStatus_t (*)(void*, int, int, int64_t, const void*);
+  static Fn real = reinterpret_cast<Fn>(orion::real::cudnn("cudnnBackendSetAttribute"));
+  if (!real) return 1;
+  const cudnnStatus_t st = real(descriptor, attributeName, attributeType, elementCount,
+                                arrayOfElements);
+  if (attributeName >= 0 && attributeName < 2048) g_set_calls[attributeName].fetch_add(1);
+  if (st == 0) record_set(descriptor, attributeName, attributeType, elementCount, arrayOfElements);
+  return st;
+}
+
+cudnnStatus_t cudnnBackendGetAttribute(void* descriptor, int attributeName, int attributeType,
+                                       int64_t requestedElementCount, int64_t* elementCount,
+                                       void* arrayOfElements) {
+  using Fn = cudnnStatus_t (*)(void*, int, int, int64_t, int64_t*, void*);
+  static Fn real = reinterpret_cast<Fn>(orion::real::cudnn("cudnnBackendGetAttribute"));
+  if (!real) return 1;
+  const cudnnStatus_t st = real(descriptor, attributeName, attributeType, requestedElementCount,
+                                elementCount, arrayOfElements);
+  if (attributeName >= 0 && attributeName < 2048) g_get_calls[attributeName].fetch_add(1);
+  if (st == 0 && attributeName == kAttrHeurResults && attributeType == kTypeBackendDesc &&
+      arrayOfElements && elementCount) {
+    // engine configs returned by heuristics belong to the heuristics' graph
+    std::lock_guard<std::mutex> lk(g_shadow_mu);
+    BDesc graph = first_desc(shadow_of(descriptor), kAttrHeurGraph);
+    const int64_t n = std::min<int64_t>(*elementCount, requestedElementCount);
+    BDesc* cfgs = static_cast<BDesc*>(arrayOfElements);
+    if (graph)
+      for (int64_t i = 0; i < n; ++i) g_shadow[cfgs[i]].descs[kSynthCfgGraph] = {graph};
+  }
+  return st;
+}
+
+cudnnStatus_t cudnnBackendFinalize(void* descriptor) {
+  using Fn = cudnnStatus_t (*)(void*);
+  static Fn real = reinterpret_cast<Fn>(orion::real::cudnn("cudnnBackendFinalize"));
+  if (!real) return 1;
+  const cudnnStatus_t st = real(descriptor);
+  if (st != 0) return st;
+  PlanInfo info;
+  bool is_plan = false;
+  {
+    std::lock_guard<std::mutex> lk(g_shadow_mu);
+    const Shadow* s = shadow_of(descriptor);
+    if (s && s->type == kDescPlan) {
+      is_plan = true;
+      info = decode_shadow(descriptor);
+    }
+  }
+  if (is_plan) note_plan(descriptor, info);
+  return st;
+}
 
 cudnnStatus_t cudnnBackendExecute(void* handle, void* executionPlan, void* variantPack) {
   using Fn = cudnnStatus_t (*)(void*, void*, void*);
@@ -765,6 +945,7 @@ cudnnStatus_t cudnnBackendExecute(void* handle, void* executionPlan, void* varia
   const PlanInfo info = plan_info(executionPlan);
   void *px = nullptr, *pw = nullptr, *py = nullptr;
   const bool ok = info.ok && variant_pointers(variantPack, info, &px, &pw, &py);
+  if (info.ok && !ok) LOG_WARN("cudnnBackendExecute: variant pack lacks the plan's tensor UIDs");
   CudnnConvParams p;
   std::memset(&p, 0, sizeof(p));
   p.handle = handle;
@@ -802,6 +983,10 @@ cudnnStatus_t cudnnBackendDestroyDescriptor(void* descriptor) {
   {
     std::lock_guard<std::mutex> lk(g_plan_mu);
     g_plans.erase(descriptor);
+  }
+  {
+    std::lock_guard<std::mutex> lk(g_shadow_mu);
+    g_shadow.erase(descriptor);
   }
   return real ? real(descriptor) : 1;
 }

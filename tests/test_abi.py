@@ -43,7 +43,8 @@ orion_end_profiling
 ADDED_EXPORTS = """
 block cudnnBatchNormalizationForwardInference cudnnBatchNormalizationBackward
 cudnnBatchNormalizationForwardTrainingEx cudnnBatchNormalizationBackwardEx cudnnBackendExecute
-cudnnBackendDestroyDescriptor cudaEventRecord cudaEventRecordWithFlags cudaStreamWaitEvent
+cudnnBackendDestroyDescriptor cudnnBackendCreateDescriptor cudnnBackendSetAttribute
+cudnnBackendGetAttribute cudnnBackendFinalize cudaEventRecord cudaEventRecordWithFlags cudaStreamWaitEvent
 cudaEventSynchronize cudaEventQuery cudaStreamQuery orion_set_be_keep_sms orion_get_be_keep_sms
 orion_set_sm_budgets orion_get_client_stats
 """.split()

@@ -111,6 +111,56 @@ def test_sgemm_vgg_fc(cuda):
     assert err <= TOL_F32, err
 
 
+@pytest.mark.parametrize("ta,tb", [(0, 0), (0, 1), (1, 0), (1, 1)])
+@pytest.mark.parametrize("m,n,k,alpha,beta,pads", [
+    (512, 64, 4096, 1.0, 0.0, (0, 0, 0)),      # GPT per-head weight gradient: split-K
+    (100, 50, 3000, 0.75, 0.5, (3, 5, 7)),     # ragged K and tiles, padded ld, beta
+    (27, 64, 20000, 1.0, 1.0, (0, 0, 0)),      # first-layer conv weight gradient shape
+])
+def test_sgemm_split_k(cuda, ta, tb, m, n, k, alpha, beta, pads):
+    # few output tiles, long K: partials of K slices are reduced in a second kernel
+    err = _sgemm_case(ta, tb, m, n, k, pads=pads, alpha=alpha, beta=beta, seed=m + n)
+    assert err <= TOL_F32, err
+
+
+def test_split_k_epilogue_and_batch(cuda):
+    """Split-K with the Lt bias+GELU epilogue, and a strided batch whose
+    per-matrix tile count is small."""
+    kx = _kx()
+    import torch
+    rng = np.random.default_rng(31)
+    m, n, k = 256, 48, 6144
+    A = rng.standard_normal(k * m).astype(np.float32)
+    B = rng.standard_normal(k * n).astype(np.float32)
+    bias = rng.standard_normal(m).astype(np.float32)
+    ref = np.zeros(m * n, np.float32)
+    o.gemm_ex(1, 0, m, n, k, 0.5, A, o.R_32F, k, B, o.R_32F, k, 0.0, None, o.R_32F, m, D=ref,
+              Dtype=o.R_32F, ldd=m, epilogue=36, bias=bias)
+    dA, dB, db = _dev(A), _dev(B), _dev(bias)
+    dD = torch.zeros(m * n, device="cuda")
+    kx.matmul(kx.current_exec(), 1, 0, m, n, k, 0.5, dA.data_ptr(), kx.R_32F, k, 0,
+              dB.data_ptr(), kx.R_32F, k, 0, 0.0, None, kx.R_32F, m, 0, dD.data_ptr(), kx.R_32F,
+              m, 0, 1, 36, db.data_ptr(), kx.R_32F)
+    torch.cuda.synchronize()
+    assert o.normwise_rel_err(dD.cpu().numpy(), ref) <= TOL_F32
+
+    batch, m, n, k = 3, 96, 80, 2048
+    sA, sB, sC = m * k, k * n, m * n
+    A = rng.standard_normal(sA * batch).astype(np.float32)
+    B = rng.standard_normal(sB * batch).astype(np.float32)
+    C = rng.standard_normal(sC * batch).astype(np.float32)
+    ref = C.copy()
+    o.sgemm_strided_batched(0, 0, m, n, k, 1.0, A, m, sA, B, k, sB, -1.0, ref, m, sC, batch)
+    dA, dB, dC = _dev(A), _dev(B), _dev(C)
+    kx.sgemm_strided_batched(kx.current_exec(), 0, 0, m, n, k, 1.0, dA.data_ptr(), m, sA,
+                             dB.data_ptr(), k, sB, -1.0, dC.data_ptr(), m, sC, batch)
+    torch.cuda.synchronize()
+    got = dC.cpu().numpy()
+    for b in range(batch):
+        seg = slice(b * sC, (b + 1) * sC)
+        assert o.normwise_rel_err(got[seg], ref[seg]) <= TOL_F32, b
+
+
 def test_sgemm_lm_head(cuda):
     # vocab 32000 x tokens 2048 x emb 512; oracle on 48 sampled token columns
     cols = np.random.default_rng(1).choice(2048, 48, replace=False)
