@@ -215,8 +215,13 @@ int choose_bn(int m, int n, int batch, int sms, int max_bn) {
   }
   const long long mb = (m + 127) / 128;
   auto tiles = [&](int bn) { return mb * ((n + bn - 1) / bn) * batch; };
-  if (max_bn >= 256 && tiles(256) >= sms) return 256;
-  if (tiles(128) >= sms) return 128;
+  // share of a tile row that falls beyond n (computed, then thrown away)
+  auto waste = [&](int bn) {
+    const long long padded = (static_cast<long long>(n) + bn - 1) / bn * bn;
+    return static_cast<double>(padded - n) / static_cast<double>(padded);
+  };
+  if (max_bn >= 256 && tiles(256) >= sms && waste(256) <= 0.125) return 256;
+  if (tiles(128) >= sms && waste(128) <= 0.125) return 128;
   return 64;
 }
 

@@ -424,19 +424,22 @@ __global__ void __launch_bounds__(256, 1)
           ok = __all_sync(0xffffffffu, ok);
           if (!ok) break;
           // A and B (and their lo buffers) are contiguous: [A | B] and [Alo | Blo].
-          float4* hi = reinterpret_cast<float4*>(stageA(s));
+          // hi is the fp32 value itself: a kind::tf32 MMA reads only the
+          // sign, exponent and top 10 mantissa bits of each 32-bit element,
+          // i.e. the value truncated to tf32.  lo = x - trunc_tf32(x) is
+          // exact in fp32, so only lo is written (half the shared-memory
+          // traffic of a split that also rewrites hi).
+          const float4* hi = reinterpret_cast<const float4*>(stageA(s));
           float4* lo = reinterpret_cast<float4*>(stageAlo(s));
           constexpr int NV = Cfg::LOAD_BYTES / 16;
 #pragma unroll 4
           for (int v = ct; v < NV; v += 64) {
-            float4 x = hi[v];
-            float4 h, l;
-            h.x = tf32_rna(x.x); h.y = tf32_rna(x.y); h.z = tf32_rna(x.z); h.w = tf32_rna(x.w);
-            l.x = isfinite(h.x) ? x.x - h.x : 0.f;
-            l.y = isfinite(h.y) ? x.y - h.y : 0.f;
-            l.z = isfinite(h.z) ? x.z - h.z : 0.f;
-            l.w = isfinite(h.w) ? x.w - h.w : 0.f;
-            hi[v] = h;
+            const float4 x = hi[v];
+            float4 l;
+            l.x = tf32_lo(x.x);
+            l.y = tf32_lo(x.y);
+            l.z = tf32_lo(x.z);
+            l.w = tf32_lo(x.w);
             lo[v] = l;
           }
           fence_proxy_async_smem();

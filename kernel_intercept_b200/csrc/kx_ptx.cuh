@@ -238,4 +238,12 @@ KX_DEV float tf32_rna(float x) {
   return __uint_as_float(r);
 }
 
+// Low part of the 3xTF32 split with a truncated high part:
+// x - (x with its low 13 mantissa bits cleared), exact in fp32.  Inf / NaN
+// have no low part (their high part carries them).
+KX_DEV float tf32_lo(float x) {
+  const float t = __uint_as_float(__float_as_uint(x) & 0xffffe000u);
+  return isfinite(x) ? x - t : 0.f;
+}
+
 }  // namespace kx

@@ -23,6 +23,7 @@
 #include <vector>
 #include <cstdlib>
 #include <cstring>
+#include <memory>
 #include <mutex>
 #include <string>
 #include <thread>
@@ -576,7 +577,8 @@ using GetAttr = int (*)(BDesc, int, int, int64_t, int64_t*, void*);
 
 constexpr int kTypeDataType = 1, kTypeInt64 = 3, kTypeFloat = 4, kTypeDouble = 5,
               kTypeVoidPtr = 6, kTypeConvMode = 7, kTypeBackendDesc = 15;
-constexpr int kDescPlan = 5, kDescConvFwd = 10, kDescConvBwdFilter = 11, kDescConvBwdData = 12;
+constexpr int kDescPlan = 5, kDescConvFwd = 10, kDescConvBwdFilter = 11, kDescConvBwdData = 12,
+              kDescOpGraph = 15;
 // attribute names (cudnnBackendAttributeName_t)
 constexpr int kAttrConvCompType = 100, kAttrConvMode = 101, kAttrConvDilations = 102,
               kAttrConvStrides = 103, kAttrConvPostPad = 104, kAttrConvPrePad = 105,
@@ -591,15 +593,24 @@ bool recorded_attr(int a) {
   return (a >= kAttrConvCompType && a <= kAttrConvSpatialDims) || a == kAttrHeurGraph ||
          a == kAttrCfgEngine || a == kAttrPlanCfg || (a >= 700 && a <= 717) ||
          a == kAttrGraphOps || a == kAttrTensorType || a == kAttrTensorDims ||
-         a == kAttrTensorStrides || a == kAttrTensorUid || a == kAttrEngineGraph;
+         a == kAttrTensorStrides || a == kAttrTensorUid || a == kAttrEngineGraph ||
+         a == kAttrPackUids || a == kAttrPackPtrs;
 }
+
+struct PlanInfo;
 
 struct Shadow {
   int type = -1;
   std::unordered_map<int, std::vector<int64_t>> ints;  // INT64 and enum attributes
   std::unordered_map<int, std::vector<BDesc>> descs;   // descriptor attributes
   std::unordered_map<int, double> scalars;             // FLOAT / DOUBLE attributes
+  // Heuristics, engine and engine-config descriptors: the convolution their
+  // operation graph holds, decoded while that graph was alive (callers may
+  // destroy the graph before they finalize the plan).
+  std::shared_ptr<const PlanInfo> conv;
 };
+
+std::shared_ptr<const PlanInfo> decode_graph_shared(BDesc graph);
 
 std::mutex g_shadow_mu;
 std::unordered_map<BDesc, Shadow> g_shadow;
@@ -620,9 +631,20 @@ void record_set(BDesc d, int attr, int type, int64_t count, const void* elems) {
       s.ints[attr].assign(v, v + count);
       break;
     }
+    case kTypeVoidPtr: {
+      const BDesc* v = static_cast<const BDesc*>(elems);
+      s.descs[attr].assign(v, v + count);
+      break;
+    }
     case kTypeBackendDesc: {
       const BDesc* v = static_cast<const BDesc*>(elems);
       s.descs[attr].assign(v, v + count);
+      if (count == 1 && (attr == kAttrHeurGraph || attr == kAttrEngineGraph)) {
+        s.conv = decode_graph_shared(v[0]);
+      } else if (count == 1 && attr == kAttrCfgEngine) {
+        auto it = g_shadow.find(v[0]);
+        s.conv = it == g_shadow.end() ? nullptr : it->second.conv;
+      }
       break;
     }
     case kTypeFloat:
@@ -694,25 +716,37 @@ struct PlanInfo {
   float alpha = 1.f, beta = 0.f;
 };
 
-// Resolves plan -> engine config -> (engine ->) graph -> the single
-// convolution operation from the shadow records.  Caller holds g_shadow_mu.
-PlanInfo decode_shadow(BDesc plan) {
+// Decodes the single convolution of an operation graph from the shadow
+// records.  Caller holds g_shadow_mu.
+PlanInfo decode_op(BDesc op_desc);
+
+PlanInfo decode_graph(BDesc graph) {
+  PlanInfo info;
+  const Shadow* sg = shadow_of(graph);
+  if (sg && sg->conv) return *sg->conv;  // decoded when the graph was finalized
+  if (!sg || !sg->descs.count(kAttrGraphOps)) {
+    info.why = "graph without recorded operations";
+    return info;
+  }
+  const auto& ops = sg->descs.at(kAttrGraphOps);
+  if (ops.size() != 1) {
+    info.why = "graph is not a single operation";
+    return info;
+  }
+  const Shadow* op = shadow_of(ops[0]);
+  if (op && op->conv) return *op->conv;  // decoded when the operation was finalized
+  return decode_op(ops[0]);
+}
+
+// Decodes one convolution operation descriptor (its tensors and convolution
+// descriptor must still be recorded).  Caller holds g_shadow_mu.
+PlanInfo decode_op(BDesc op_desc) {
   PlanInfo info;
   auto fail = [&info](const char* why) {
     info.why = why;
     return info;
   };
-  BDesc cfg = first_desc(shadow_of(plan), kAttrPlanCfg);
-  if (!cfg) return fail("plan has no recorded engine config");
-  const Shadow* scfg = shadow_of(cfg);
-  BDesc graph = first_desc(scfg, kSynthCfgGraph);
-  if (!graph) graph = first_desc(shadow_of(first_desc(scfg, kAttrCfgEngine)), kAttrEngineGraph);
-  if (!graph) return fail("engine config without a recorded operation graph");
-  const Shadow* sg = shadow_of(graph);
-  if (!sg || !sg->descs.count(kAttrGraphOps)) return fail("graph without recorded operations");
-  const auto& ops = sg->descs.at(kAttrGraphOps);
-  if (ops.size() != 1) return fail("graph is not a single operation");
-  const Shadow* op = shadow_of(ops[0]);
+  const Shadow* op = shadow_of(op_desc);
   if (!op) return fail("operation not recorded");
   struct Kind { int desc; OperationType t; int alpha, beta, conv, in, filt, out; };
   // attribute numbers in forward roles: input, filter, output
@@ -727,8 +761,25 @@ PlanInfo decode_shadow(BDesc plan) {
   if (!k) return fail("operation is not a convolution");
   TensorInfo in, filt, out;
   if (!shadow_tensor(first_desc(op, k->in), in) || !shadow_tensor(first_desc(op, k->filt), filt) ||
-      !shadow_tensor(first_desc(op, k->out), out))
+      !shadow_tensor(first_desc(op, k->out), out)) {
+    if (std::getenv("KX_CUDNN_DEBUG") != nullptr) {
+      for (int a : {k->in, k->filt, k->out}) {
+        BDesc t = first_desc(op, a);
+        const Shadow* st = shadow_of(t);
+        std::string d = "tensor attr " + std::to_string(a) + " desc " +
+                        std::to_string(reinterpret_cast<uintptr_t>(t)) +
+                        (st ? " type " + std::to_string(st->type) : std::string(" unrecorded"));
+        if (st)
+          for (const auto& kv : st->ints) {
+            d += " [" + std::to_string(kv.first) + ":";
+            for (int64_t v : kv.second) d += " " + std::to_string(v);
+            d += "]";
+          }
+        LOG_WARN("%s", d.c_str());
+      }
+    }
     return fail("convolution tensors are not 4-D or not recorded");
+  }
   const Shadow* cd = shadow_of(first_desc(op, k->conv));
   const auto* sd = ints_of(cd, kAttrConvSpatialDims);
   const auto* pre = ints_of(cd, kAttrConvPrePad);
@@ -776,6 +827,26 @@ PlanInfo decode_shadow(BDesc plan) {
   info.beta = sb == op->scalars.end() ? 0.f : static_cast<float>(sb->second);
   info.ok = true;
   info.why = "";
+  return info;
+}
+
+std::shared_ptr<const PlanInfo> decode_graph_shared(BDesc graph) {
+  return std::make_shared<const PlanInfo>(decode_graph(graph));
+}
+
+// Resolves plan -> engine config -> decoded convolution (recorded when the
+// config came from heuristics or was built on an engine).  Caller holds
+// g_shadow_mu.
+PlanInfo decode_shadow(BDesc plan) {
+  PlanInfo info;
+  BDesc cfg = first_desc(shadow_of(plan), kAttrPlanCfg);
+  if (!cfg) {
+    info.why = "plan has no recorded engine config";
+    return info;
+  }
+  const Shadow* scfg = shadow_of(cfg);
+  if (scfg && scfg->conv) return *scfg->conv;
+  info.why = "engine config without a recorded operation graph";
   return info;
 }
 
@@ -843,13 +914,30 @@ PlanInfo plan_info(BDesc plan) {
   return info;
 }
 
+// Data pointers of the plan's three tensors, by UID, from the variant pack
+// (recorded as the caller set it; cuDNN's getter as a fallback).
 bool variant_pointers(BDesc vp, const PlanInfo& info, void** px, void** pw, void** py) {
-  static GetAttr get = reinterpret_cast<GetAttr>(real::cudnn("cudnnBackendGetAttribute"));
-  if (!get) return false;
   int64_t uids[16], n = 0, np = 0;
   void* ptrs[16];
-  if (get(vp, kAttrPackUids, kTypeInt64, 16, &n, uids) != 0) return false;
-  if (get(vp, kAttrPackPtrs, kTypeVoidPtr, 16, &np, ptrs) != 0 || np != n) return false;
+  {
+    std::lock_guard<std::mutex> lk(g_shadow_mu);
+    const Shadow* s = shadow_of(vp);
+    const auto* u = ints_of(s, kAttrPackUids);
+    auto pit = s ? s->descs.find(kAttrPackPtrs) : decltype(s->descs.end()){};
+    if (u && s && pit != s->descs.end() && u->size() == pit->second.size() && u->size() <= 16) {
+      n = np = static_cast<int64_t>(u->size());
+      for (int64_t i = 0; i < n; ++i) {
+        uids[i] = (*u)[i];
+        ptrs[i] = pit->second[i];
+      }
+    }
+  }
+  if (n == 0) {
+    static GetAttr get = reinterpret_cast<GetAttr>(real::cudnn("cudnnBackendGetAttribute"));
+    if (!get) return false;
+    if (get(vp, kAttrPackUids, kTypeInt64, 16, &n, uids) != 0) return false;
+    if (get(vp, kAttrPackPtrs, kTypeVoidPtr, 16, &np, ptrs) != 0 || np != n) return false;
+  }
   *px = *pw = *py = nullptr;
   for (int64_t i = 0; i < n && i < 16; ++i) {
     if (uids[i] == info.uid_x) *px = ptrs[i];
@@ -902,11 +990,18 @@ cudnnStatus_t cudnnBackendGetAttribute(void* descriptor, int attributeName, int 
       arrayOfElements && elementCount) {
     // engine configs returned by heuristics belong to the heuristics' graph
     std::lock_guard<std::mutex> lk(g_shadow_mu);
-    BDesc graph = first_desc(shadow_of(descriptor), kAttrHeurGraph);
+    const Shadow* heur = shadow_of(descriptor);
+    BDesc graph = first_desc(heur, kAttrHeurGraph);
+    std::shared_ptr<const PlanInfo> conv = heur ? heur->conv : nullptr;
     const int64_t n = std::min<int64_t>(*elementCount, requestedElementCount);
     BDesc* cfgs = static_cast<BDesc*>(arrayOfElements);
-    if (graph)
-      for (int64_t i = 0; i < n; ++i) g_shadow[cfgs[i]].descs[kSynthCfgGraph] = {graph};
+    if (graph) {
+      for (int64_t i = 0; i < n; ++i) {
+        Shadow& c = g_shadow[cfgs[i]];
+        c.descs[kSynthCfgGraph] = {graph};
+        c.conv = conv;
+      }
+    }
   }
   return st;
 }
@@ -917,14 +1012,23 @@ cudnnStatus_t cudnnBackendFinalize(void* descriptor) {
   if (!real) return 1;
   const cudnnStatus_t st = real(descriptor);
   if (st != 0) return st;
+  // Decode as early as possible: callers may destroy tensors once the
+  // operation is finalized, and operations once the graph is.
   PlanInfo info;
   bool is_plan = false;
   {
     std::lock_guard<std::mutex> lk(g_shadow_mu);
-    const Shadow* s = shadow_of(descriptor);
-    if (s && s->type == kDescPlan) {
-      is_plan = true;
-      info = decode_shadow(descriptor);
+    auto it = g_shadow.find(descriptor);
+    if (it != g_shadow.end()) {
+      Shadow& sd = it->second;
+      if (sd.type == kDescConvFwd || sd.type == kDescConvBwdData || sd.type == kDescConvBwdFilter) {
+        sd.conv = std::make_shared<const PlanInfo>(decode_op(descriptor));
+      } else if (sd.type == kDescOpGraph) {
+        sd.conv = std::make_shared<const PlanInfo>(decode_graph(descriptor));
+      } else if (sd.type == kDescPlan) {
+        is_plan = true;
+        info = decode_shadow(descriptor);
+      }
     }
   }
   if (is_plan) note_plan(descriptor, info);
