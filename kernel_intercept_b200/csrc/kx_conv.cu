@@ -175,6 +175,15 @@ int finish_done(const Exec& e) {
 
 int round4(int v) { return (v + 3) & ~3; }
 
+// KX_CONV_IMPLICIT=0 lowers forward convolutions through im2col instead.
+bool implicit_conv_enabled() {
+  static const bool on = [] {
+    const char* s = std::getenv("KX_CONV_IMPLICIT");
+    return s == nullptr || s[0] != '0';
+  }();
+  return on;
+}
+
 }  // namespace
 }  // namespace kx
 
@@ -193,6 +202,13 @@ extern "C" int kx_conv_fwd(const kx_exec* ex, const kx_conv_desc* d, const float
   ConvGeom g;
   if (!make_geom(d, g) || !x || !w || !y || !alpha || !beta) return KX_ERR_INVALID;
   Exec e = resolve_exec(ex);
+  if (implicit_conv_enabled()) {
+    // one persistent implicit-GEMM launch (preemptible like any kx GEMM)
+    const ConvShape cs{g.N, g.C, g.H, g.W, g.K, g.R, g.S, g.ph, g.pw, g.sh,
+                       g.sw, g.dh, g.dw, g.P, g.Q, g.xcorr == 0};
+    const int rc = conv_fwd_implicit(e, cs, x, w, y, *alpha, *beta);
+    if (rc != KX_ERR_UNSUPPORTED) return rc;
+  }
   const int nb = images_per_chunk(g);
   const size_t col_elems = static_cast<size_t>(nb) * g.CRS * g.ldpq;
   const bool repack = !g.xcorr || (g.CRS & 3) != 0;

@@ -1,0 +1,313 @@
+// kx_conv_tc.cu — forward convolution as an implicit GEMM on the persistent
+// tcgen05 kernel (kx_gemm_tc_kernel with CONV = true), 3xTF32.
+//
+//   y_n (pixels x K) = A_n (pixels x Kd) * Wp^T (Kd x K)
+//
+// A is never materialised per tap.  One staging pass copies x to NHWC with
+// the channels padded to a multiple of 32 (and writes the 3xTF32 low part
+// beside it); the GEMM's producer then loads, for k-block (tap r,s; channel
+// block c0), the 4-D TMA box {32 channels, wbox columns, hbox rows, 1 image}
+// starting at the tap's offset (q0*sw - pw + s*dw, p0*sh - ph + r*dh).  The
+// box lands as 128 rows of 128 bytes, exactly the K-major 128-byte-swizzled
+// A tile, and TMA's zero fill supplies the padding border.  Strides use the
+// tensor map's element strides.  When C*R*S is small (the first layer of a
+// CNN: C = 3), taps are folded into the channel dimension instead: the
+// staging holds [N][P][Q][round32(C*R*S)] and the GEMM is a 1x1 convolution.
+//
+// Wp[k][(r*S + s)*Cp + c] is the filter repacked tap-major (flipped for
+// CUDNN_CONVOLUTION), streamed by TMA as a K-major B operand, with its low
+// part beside it.  Replaces the im2col lowering for the forward pass
+// (cudnnConvolutionForward, src/cudnn_intercept.cpp:433-489 of the reference).
+#include <cstdio>
+#include <cstring>
+
+#include "kx_gemm_launch.cuh"
+
+namespace kx {
+namespace {
+
+// NCHW -> NHWC with channels padded to cp; hi = x, lo = x - trunc_tf32(x).
+// 32 channels x 32 pixels per block through shared memory so both the read
+// (along pixels) and the write (along channels) coalesce.
+__global__ void __launch_bounds__(256) stage_nhwc_split(const float* __restrict__ x,
+                                                        float* __restrict__ xh,
+                                                        float* __restrict__ xl, int C, int HW,
+                                                        int cp) {
+  __shared__ float tile[32][33];
+  const int n = blockIdx.z;
+  const int c0 = blockIdx.y * 32;
+  const int p0 = blockIdx.x * 32;
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
+  const float* xn = x + static_cast<size_t>(n) * C * HW;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int c = c0 + ty + 8 * j;
+    const int px = p0 + tx;
+    tile[ty + 8 * j][tx] = (c < C && px < HW) ? __ldg(xn + static_cast<size_t>(c) * HW + px) : 0.f;
+  }
+  __syncthreads();
+  const size_t base = static_cast<size_t>(n) * HW * cp;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int px = p0 + ty + 8 * j;
+    if (px < HW) {
+      const float v = tile[tx][ty + 8 * j];
+      const size_t o = base + static_cast<size_t>(px) * cp + c0 + tx;
+      xh[o] = v;
+      xl[o] = tf32_lo(v);
+    }
+  }
+}
+
+// Taps folded into channels: st[n][p][q][kk], kk = (c*R + r)*S + s < C*R*S,
+// zero up to kf; hi and lo as above.
+__global__ void __launch_bounds__(256) stage_folded_split(const float* __restrict__ x,
+                                                          float* __restrict__ xh,
+                                                          float* __restrict__ xl, ConvShape g,
+                                                          int kf) {
+  const size_t total = static_cast<size_t>(g.N) * g.P * g.Q * kf;
+  const int crs = g.C * g.R * g.S;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const int kk = static_cast<int>(i % kf);
+    const size_t pix = i / kf;  // (n, p, q)
+    const int q = static_cast<int>(pix % g.Q);
+    const int p = static_cast<int>((pix / g.Q) % g.P);
+    const int n = static_cast<int>(pix / (static_cast<size_t>(g.Q) * g.P));
+    float v = 0.f;
+    if (kk < crs) {
+      const int c = kk / (g.R * g.S);
+      const int rs = kk - c * g.R * g.S;
+      const int r = rs / g.S, s = rs - (rs / g.S) * g.S;
+      const int h = p * g.sh - g.ph + r * g.dh;
+      const int w = q * g.sw - g.pw + s * g.dw;
+      if (h >= 0 && h < g.H && w >= 0 && w < g.W)
+        v = __ldg(x + ((static_cast<size_t>(n) * g.C + c) * g.H + h) * g.W + w);
+    }
+    xh[i] = v;
+    xl[i] = tf32_lo(v);
+  }
+}
+
+// Filter for the tap-major K order (folded = false: Wp[k][(r*S+s)*cp + c])
+// or the folded order (folded = true: Wp[k][(c*R + r)*S + s], padded to cp).
+__global__ void pack_filter(const float* __restrict__ w, float* __restrict__ wp,
+                            float* __restrict__ wp_lo, int K, int C, int R, int S, int cp,
+                            int folded, int flip) {
+  const int RS = R * S;
+  const size_t row = folded ? static_cast<size_t>(cp) : static_cast<size_t>(RS) * cp;
+  const size_t total = static_cast<size_t>(K) * row;
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
+    const size_t k = i / row;
+    const int rem = static_cast<int>(i - k * row);
+    int c, r, s;
+    bool valid;
+    if (folded) {
+      c = rem / RS;
+      const int rs = rem - c * RS;
+      r = rs / S;
+      s = rs - r * S;
+      valid = rem < C * RS;
+    } else {
+      const int tap = rem / cp;
+      c = rem - tap * cp;
+      r = tap / S;
+      s = tap - r * S;
+      valid = c < C;
+    }
+    float v = 0.f;
+    if (valid) {
+      if (flip) {
+        r = R - 1 - r;
+        s = S - 1 - s;
+      }
+      v = w[((k * C + c) * R + r) * S + s];
+    }
+    wp[i] = v;
+    wp_lo[i] = tf32_lo(v);
+  }
+}
+
+// Output tile = hbox rows x wbox columns of output pixels (wbox * hbox =
+// 128, powers of two), chosen to waste the fewest MMA rows.
+void choose_box(int P, int Q, int sw, int sh, int& wbox, int& hbox) {
+  long long best = -1;
+  wbox = 128;
+  hbox = 1;
+  for (int wb = 1; wb <= 128; wb *= 2) {
+    const int hb = 128 / wb;
+    if (wb * sw > 256 || hb * sh > 256) continue;
+    const long long tiles = static_cast<long long>((Q + wb - 1) / wb) * ((P + hb - 1) / hb);
+    if (best < 0 || tiles < best) {
+      best = tiles;
+      wbox = wb;
+      hbox = hb;
+    }
+  }
+}
+
+template <int BN>
+int launch_conv_tc(const Exec& e, const ConvShape& g, const ConvShape& t, const float* xh,
+                   const float* xl, int cp, const float* wp, const float* wp_lo, float* y,
+                   float alpha, float beta) {
+  // t: the geometry the kernel sees (g itself, or the folded 1x1 problem)
+  using Cfg = GemmCfg<BN, Arith::F32x3, false, false>;
+  const long long kd = static_cast<long long>(t.R) * t.S * cp;
+  const long long pq = static_cast<long long>(g.P) * g.Q;
+  int wbox, hbox;
+  choose_box(g.P, g.Q, t.sw, t.sh, wbox, hbox);
+  // A: NHWC staging {cp, W, H, N}
+  const uint64_t dims[4] = {static_cast<uint64_t>(cp), static_cast<uint64_t>(t.W),
+                            static_cast<uint64_t>(t.H), static_cast<uint64_t>(t.N)};
+  const uint64_t strides[3] = {static_cast<uint64_t>(cp) * 4,
+                               static_cast<uint64_t>(cp) * t.W * 4,
+                               static_cast<uint64_t>(cp) * t.W * t.H * 4};
+  const uint32_t box[4] = {32u, static_cast<uint32_t>(wbox * t.sw),
+                           static_cast<uint32_t>(hbox * t.sh), 1u};
+  const uint32_t es[4] = {1u, static_cast<uint32_t>(t.sw), static_cast<uint32_t>(t.sh), 1u};
+  CUtensorMap ma, malo, mb, mblo;
+  if (!encode_map(&ma, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, xh, dims, strides, box,
+                  CU_TENSOR_MAP_SWIZZLE_128B, es) ||
+      !encode_map(&malo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, xl, dims, strides, box,
+                  CU_TENSOR_MAP_SWIZZLE_128B, es))
+    return KX_ERR_UNSUPPORTED;
+  if (!encode_map_3d(&mb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, wp, kd, g.K, 1, kd, 0, Cfg::BK, BN) ||
+      !encode_map_3d(&mblo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, wp_lo, kd, g.K, 1, kd, 0, Cfg::BK,
+                     BN))
+    return KX_ERR_UNSUPPORTED;
+  GemmParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.m = static_cast<int>(pq);
+  p.n = g.K;
+  p.k = static_cast<int>(kd);
+  p.alpha = alpha;
+  p.beta = beta;
+  p.D = y;
+  p.ldd = pq;
+  p.strideD = pq * g.K;
+  p.d_type = DT_F32;
+  p.C = y;
+  p.ldc = pq;
+  p.strideC = pq * g.K;
+  p.c_type = DT_F32;
+  p.work = work_slot_for(e.stream);
+  if (p.work == nullptr) return KX_ERR_NOMEM;
+  p.yield_flag = e.yield_flag;
+  p.done_flag = e.done_flag;
+  p.max_tiles = e.max_tiles;
+  p.timeout_ns = e.timeout_ns;
+  p.err_word = e.err_word ? e.err_word : &p.work->err;
+  p.presplit = 1;
+  p.cv_p = g.P;
+  p.cv_q = g.Q;
+  p.cv_wbox = wbox;
+  p.cv_hbox = hbox;
+  p.cv_tiles_w = (g.Q + wbox - 1) / wbox;
+  p.cv_s = t.S;
+  p.cv_cb = cp / 32;
+  p.cv_pad_h = t.ph;
+  p.cv_pad_w = t.pw;
+  p.cv_str_h = t.sh;
+  p.cv_str_w = t.sw;
+  p.cv_dil_h = t.dh;
+  p.cv_dil_w = t.dw;
+  p.num_mb = p.cv_tiles_w * ((g.P + hbox - 1) / hbox);
+  p.num_nb = (g.K + BN - 1) / BN;
+  p.num_kb = static_cast<int>(kd / Cfg::BK);
+  p.tiles_per_batch = p.num_mb * p.num_nb;
+  const long long tiles = static_cast<long long>(p.tiles_per_batch) * g.N;
+  if (tiles <= 0 || tiles > 0x7fffffffLL) return KX_ERR_UNSUPPORTED;
+  p.num_tiles = static_cast<int>(tiles);
+  p.splits = 1;
+  p.kb_per_split = p.num_kb;
+  p.a_bcast = 0;
+  p.b_bcast = 1;
+
+  auto kern = kx_gemm_tc_kernel<Cfg, true>;
+  static bool attr_set[64] = {false};
+  const DeviceInfo& di = device_info();
+  if (!attr_set[di.device & 63]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             Cfg::SMEM_BYTES) != cudaSuccess)
+      return KX_ERR_DEVICE;
+    attr_set[di.device & 63] = true;
+  }
+  const int grid = persistent_grid(e, p.num_tiles);
+  note_launch();
+  kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, e.stream>>>(ma, mb, malo, mblo, p);
+  static char name[64];
+  if (name[0] == 0) snprintf(name, sizeof(name), "kx_conv_fwd_tc<bn%d,f32x3>", BN);
+  set_last_kernel_name(name);
+  return launch_status();
+}
+
+size_t round256(size_t elems) { return (elems + 63) & ~static_cast<size_t>(63); }
+
+int grid_for(size_t total) {
+  size_t b = (total + 255) / 256;
+  const size_t cap = 8ull * device_info().num_sms;
+  return static_cast<int>(b < 1 ? 1 : (b > cap ? cap : b));
+}
+
+}  // namespace
+
+int conv_fwd_implicit(const Exec& e, const ConvShape& g, const float* x, const float* w, float* y,
+                      float alpha, float beta) {
+  if (e.fp32_mode != KX_FP32_3XTF32) return KX_ERR_UNSUPPORTED;
+  const int crs = g.C * g.R * g.S;
+  const int cp_taps = (g.C + 31) / 32 * 32;
+  const int kf = (crs + 31) / 32 * 32;
+  // fold the taps into channels when that at least halves the K extent
+  const bool folded = static_cast<long long>(kf) * 2 <= static_cast<long long>(cp_taps) * g.R * g.S;
+  ConvShape t = g;  // geometry seen by the kernel
+  int cp = cp_taps;
+  if (folded) {
+    t.C = kf;
+    t.H = g.P;
+    t.W = g.Q;
+    t.R = t.S = 1;
+    t.ph = t.pw = 0;
+    t.sh = t.sw = 1;
+    t.dh = t.dw = 1;
+    cp = kf;
+  }
+  if (t.sw > 8 || t.sh > 8) return KX_ERR_UNSUPPORTED;
+  const size_t stage_elems = static_cast<size_t>(t.N) * t.H * t.W * cp;
+  const size_t wp_elems = static_cast<size_t>(g.K) * t.R * t.S * cp;
+  if (stage_elems > (1ull << 36) || static_cast<long long>(t.R) * t.S * cp > 0x7fffffffLL ||
+      static_cast<long long>(g.P) * g.Q * g.K > (1LL << 40))
+    return KX_ERR_UNSUPPORTED;
+  const size_t s_pad = round256(stage_elems), w_pad = round256(wp_elems);
+  float* base = static_cast<float*>(
+      scratch_for(e.stream, (2 * s_pad + 2 * w_pad) * sizeof(float)));
+  if (base == nullptr) return KX_ERR_NOMEM;
+  float* xh = base;
+  float* xl = base + s_pad;
+  float* wp = base + 2 * s_pad;
+  float* wp_lo = wp + w_pad;
+  note_launch();
+  if (folded) {
+    stage_folded_split<<<grid_for(stage_elems), 256, 0, e.stream>>>(x, xh, xl, g, kf);
+  } else {
+    const int hw = g.H * g.W;
+    dim3 grid((hw + 31) / 32, cp / 32, g.N);
+    if (grid.y > 65535 || grid.z > 65535) return KX_ERR_UNSUPPORTED;
+    stage_nhwc_split<<<grid, 256, 0, e.stream>>>(x, xh, xl, g.C, hw, cp);
+  }
+  note_launch();
+  pack_filter<<<grid_for(wp_elems), 256, 0, e.stream>>>(w, wp, wp_lo, g.K, g.C, g.R, g.S, cp,
+                                                        folded ? 1 : 0, g.flip ? 1 : 0);
+  if (launch_status() != KX_OK) return KX_ERR_DEVICE;
+  // 128-wide channel tiles when they fill the GPU and waste nothing
+  const int sms = persistent_grid(e, 1 << 30);
+  int wbox, hbox;
+  choose_box(g.P, g.Q, t.sw, t.sh, wbox, hbox);
+  const long long mtiles =
+      static_cast<long long>((g.Q + wbox - 1) / wbox) * ((g.P + hbox - 1) / hbox) * g.N;
+  if (g.K % 128 == 0 && mtiles * (g.K / 128) >= sms)
+    return launch_conv_tc<128>(e, g, t, xh, xl, cp, wp, wp_lo, y, alpha, beta);
+  return launch_conv_tc<64>(e, g, t, xh, xl, cp, wp, wp_lo, y, alpha, beta);
+}
+
+}  // namespace kx

@@ -121,7 +121,47 @@ __global__ void __launch_bounds__(256) kx_gemm_simt_kernel(const SimtGemmParams 
   }
 }
 
+// lo[i] = src[i] - trunc_tf32(src[i]) over two spans (the 3xTF32 low parts
+// of both GEMM operands in one launch).
+__global__ void __launch_bounds__(256) tf32_split_lo(const float* __restrict__ a, float* __restrict__ alo,
+                                                     size_t na, const float* __restrict__ b,
+                                                     float* __restrict__ blo, size_t nb) {
+  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+  const size_t t0 = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x;
+  // both spans start 16-byte aligned (TMA-addressable operands)
+  const size_t na4 = na / 4, nb4 = nb / 4;
+  for (size_t i = t0; i < na4 + nb4; i += stride) {
+    const bool in_a = i < na4;
+    const float4 x = in_a ? reinterpret_cast<const float4*>(a)[i]
+                          : reinterpret_cast<const float4*>(b)[i - na4];
+    const float4 l = make_float4(tf32_lo(x.x), tf32_lo(x.y), tf32_lo(x.z), tf32_lo(x.w));
+    if (in_a)
+      reinterpret_cast<float4*>(alo)[i] = l;
+    else
+      reinterpret_cast<float4*>(blo)[i - na4] = l;
+  }
+  if (t0 < na - na4 * 4) alo[na4 * 4 + t0] = tf32_lo(a[na4 * 4 + t0]);
+  if (t0 < nb - nb4 * 4) blo[nb4 * 4 + t0] = tf32_lo(b[nb4 * 4 + t0]);
+}
+
 namespace {
+
+// KX_PRESPLIT=0 keeps the 3xTF32 split inside the GEMM kernel.
+bool presplit_disabled() {
+  static const bool off = [] {
+    const char* s = std::getenv("KX_PRESPLIT");
+    return s != nullptr && s[0] == '0';
+  }();
+  return off;
+}
+
+// Elements from the first to the last one a (possibly batched, padded)
+// column-major operand touches.
+size_t operand_span(long long rows, long long cols, long long ld, long long stride, int batch) {
+  long long span = (cols - 1) * ld + rows;
+  if (batch > 1 && stride > 0) span += (batch - 1) * stride;
+  return span > 0 ? static_cast<size_t>(span) : 0;
+}
 
 struct GemmCall {
   int transa, transb, m, n, k, batch;
@@ -300,7 +340,34 @@ int run_gemm(const kx_exec* ex, const GemmCall& g) {
   p.timeout_ns = e.timeout_ns;
   p.err_word = e.err_word ? e.err_word : &p.work->err;
 
-  TcProblem pr{g.m, g.n, g.k, g.batch, g.A, g.lda, g.strideA, g.B, g.ldb, g.strideB};
+  TcProblem pr{g.m, g.n, g.k, g.batch, g.A, g.lda, g.strideA, g.B, g.ldb, g.strideB,
+               nullptr, nullptr};
+  // 3xTF32 low parts: split off in global memory when every operand element
+  // is reused by enough output tiles to amortise the extra pass; skinny
+  // problems (m or n small: few reuses, large operand) split in the kernel.
+  p.presplit = (ar == Arith::F32x3 && g.m >= 256 && g.n >= 256 &&
+                static_cast<long long>(g.m) * g.n >= (1LL << 20) && !presplit_disabled())
+                   ? 1
+                   : 0;
+  if (p.presplit) {
+    // low parts of both operands, laid out exactly like the operands
+    const size_t na = operand_span(ta == 0 ? g.m : g.k, ta == 0 ? g.k : g.m, g.lda, g.strideA,
+                                   g.batch);
+    const size_t nb = operand_span(tb == 0 ? g.k : g.n, tb == 0 ? g.n : g.k, g.ldb, g.strideB,
+                                   g.batch);
+    const size_t na_pad = (na + 63) & ~static_cast<size_t>(63);
+    float* lo = static_cast<float*>(scratch_for(e.stream, (na_pad + nb) * sizeof(float), 2));
+    if (lo == nullptr) return KX_ERR_NOMEM;
+    size_t blocks = (na / 4 + nb / 4 + 255) / 256;
+    const size_t cap = 8ull * device_info().num_sms;
+    if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
+    note_launch();
+    tf32_split_lo<<<static_cast<int>(blocks), 256, 0, e.stream>>>(
+        static_cast<const float*>(g.A), lo, na, static_cast<const float*>(g.B), lo + na_pad, nb);
+    pr.Alo = lo;
+    pr.Blo = lo + na_pad;
+  }
   const int sms = persistent_grid(e, 1 << 30);
   const int bn = choose_bn(g.m, g.n, g.batch, sms, ar == Arith::F32x3 ? 128 : 256);
   const bool amn = ta == 0, bmn = tb == 1;

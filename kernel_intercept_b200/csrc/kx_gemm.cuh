@@ -19,9 +19,13 @@
 //   warp 0      TMA producer: takes tiles from the global tile queue,
 //               publishes them to the other roles, streams A/B k-blocks.
 //   warp 1      allocates TMEM; lane 0 issues tcgen05.mma.
-//   warps 2-3   fp32 path only: split each fp32 k-block into tf32 hi (in
-//               place) and lo (separate buffer) for 3xTF32.
+//   warps 2-3   3xTF32 with in-kernel split only: compute the low parts.
 //   warps 4-7   epilogue: TMEM -> registers -> alpha/beta/bias/act -> HBM.
+// fp32 (3xTF32): each operand x is used as hi (a kind::tf32 MMA reads only
+// its top 19 bits, i.e. trunc_tf32(x)) and lo = x - trunc_tf32(x); three
+// MMAs per k-step accumulate lo*hi + hi*lo + hi*hi.  When both operands are
+// reused enough, a split kernel writes lo to global memory before the launch
+// and TMA brings it beside hi; otherwise warps 2-3 compute it per k-block.
 // The accumulator is double-buffered in TMEM so the epilogue of tile t
 // overlaps the MMAs of tile t+1.
 //
@@ -79,6 +83,18 @@ struct GemmParams {
   // applies alpha / beta / bias / activation.  splits == 1: direct epilogue.
   int splits, kb_per_split;
   float* ws;
+  // 3xTF32: 1 = the low parts of A and B were written to global memory
+  // before the launch and arrive by TMA (maps tmAlo / tmBlo); 0 = warps 2-3
+  // compute them in shared memory from each k-block.
+  int presplit;
+  // Implicit-GEMM convolution (kernel instantiated with CONV = true).  The A
+  // operand is a 4-D TMA box (32 channels x cv_wbox x cv_hbox output pixels
+  // of one image) of an NHWC staging copy of x whose channels are padded to
+  // cv_cb blocks of 32; K runs over (filter tap, channel block).  An output
+  // tile is cv_hbox rows x cv_wbox columns of output pixels (cv_tiles_w tiles
+  // across a row); batch = image; D is NCHW (ld = P*Q).
+  int cv_p, cv_q, cv_wbox, cv_hbox, cv_tiles_w, cv_s, cv_cb;
+  int cv_pad_h, cv_pad_w, cv_str_h, cv_str_w, cv_dil_h, cv_dil_w;
 };
 
 template <int BN_, Arith AR_, bool A_MN_, bool B_MN_>
@@ -102,7 +118,7 @@ struct GemmCfg {
   static constexpr int RING = 4;  // depth of the tile-id broadcast ring
   static constexpr int TMEM_COLS = (2 * BN) <= 32 ? 32 : (2 * BN) <= 64 ? 64 : (2 * BN) <= 128 ? 128 : (2 * BN) <= 256 ? 256 : 512;
   static constexpr int THREADS = 256;
-  static constexpr int NUM_CONS = 1 + (SPLIT ? 2 : 0) + 4;  // ring consumers (arrivals)
+  static constexpr int NUM_CONS = 1 + 4;  // ring consumers: MMA issuer + epilogue warps
   // 3xTF32: the tensor core's fp32 accumulation does not round to nearest, so
   // the error of one TMEM accumulator grows linearly with its K length.  The
   // K loop is therefore cut into segments of SEG k-blocks (256 of K); each
@@ -220,12 +236,22 @@ static __global__ void __launch_bounds__(256) kx_splitk_reduce(const GemmParams 
   }
 }
 
-template <class Cfg>
+// CONV = true: implicit-GEMM convolution (see GemmParams::cv_*): the A tile
+// of k-block (tap, channel block) is the 4-D box of the NHWC staging copy
+// shifted by the tap's offset, so TMA zero-fills the padding border.
+template <class Cfg, bool CONV = false>
 __global__ void __launch_bounds__(256, 1)
     kx_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
-                      const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
+                      const __grid_constant__ CUtensorMap tmB,
+                      const __grid_constant__ CUtensorMap tmAlo,
+                      const __grid_constant__ CUtensorMap tmBlo, const GemmParams p) {
+  static_assert(!CONV || (Cfg::AR == Arith::F32x3 && !Cfg::A_MN),
+                "implicit convolution: 3xTF32 with a K-major A tile");
   constexpr int S = Cfg::STAGES;
   constexpr int R = Cfg::RING;
+  // in-kernel 3xTF32 split (warps 2-3) unless the low parts come by TMA
+  const bool convert = Cfg::SPLIT && !CONV && p.presplit == 0;
+  const bool lo_by_tma = Cfg::SPLIT && !convert;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
@@ -244,7 +270,7 @@ __global__ void __launch_bounds__(256, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(smem_addr(&sb->full[s]), 1);
-      mbar_init(smem_addr(&sb->conv[s]), 64);
+      mbar_init(smem_addr(&sb->conv[s]), convert ? 64 : 1);
       mbar_init(smem_addr(&sb->empty[s]), 1);
     }
     for (int a = 0; a < 2; ++a) {
@@ -253,7 +279,7 @@ __global__ void __launch_bounds__(256, 1)
     }
     for (int r = 0; r < R; ++r) {
       mbar_init(smem_addr(&sb->ring_full[r]), 1);
-      mbar_init(smem_addr(&sb->ring_empty[r]), Cfg::NUM_CONS);
+      mbar_init(smem_addr(&sb->ring_empty[r]), Cfg::NUM_CONS + (convert ? 2 : 0));
     }
     mbar_init(smem_addr(&sb->final_mma), 1);
     sb->abort_flag = 0;
@@ -262,6 +288,10 @@ __global__ void __launch_bounds__(256, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (lo_by_tma) {
+      tma_prefetch_desc(&tmAlo);
+      tma_prefetch_desc(&tmBlo);
+    }
   }
   if (warp == 1) {
     tmem_alloc(smem_addr(&sb->tmem_base), Cfg::TMEM_COLS);
@@ -308,24 +338,44 @@ __global__ void __launch_bounds__(256, 1)
           const uint32_t s = it % S;
           if (!mbar_wait(smem_addr(&sb->empty[s]), ((it / S) & 1) ^ 1, wc)) { ok = false; break; }
           const uint32_t fb = smem_addr(&sb->full[s]);
-          mbar_arrive_expect_tx(fb, Cfg::LOAD_BYTES);
-          const uint32_t sa = smem_addr(stageA(s));
-          const uint32_t sbb = smem_addr(stageB(s));
-          if (!Cfg::A_MN) {
-            tma_load_3d(sa, &tmA, fb, kb * Cfg::BK, mb * Cfg::BM, ba);
-          } else {
+          // 3xTF32 with pre-split operands: the low parts arrive by TMA beside
+          // the high parts.
+          mbar_arrive_expect_tx(fb, Cfg::LOAD_BYTES * (lo_by_tma ? 2 : 1));
+          auto load_a = [&](uint32_t sa, const CUtensorMap* map) {
+            if constexpr (CONV) {
+              const int tap = kb / p.cv_cb;
+              const int c0 = (kb - tap * p.cv_cb) * 32;
+              const int rr = tap / p.cv_s;
+              const int ss = tap - rr * p.cv_s;
+              const int th = mb / p.cv_tiles_w;
+              const int tw = mb - th * p.cv_tiles_w;
+              const int w0 = tw * p.cv_wbox * p.cv_str_w - p.cv_pad_w + ss * p.cv_dil_w;
+              const int h0 = th * p.cv_hbox * p.cv_str_h - p.cv_pad_h + rr * p.cv_dil_h;
+              tma_load_4d(sa, map, fb, c0, w0, h0, b);
+            } else if (!Cfg::A_MN) {
+              tma_load_3d(sa, map, fb, kb * Cfg::BK, mb * Cfg::BM, ba);
+            } else {
 #pragma unroll
-            for (int c = 0; c < Cfg::BM / Cfg::CHUNK; ++c)
-              tma_load_3d(sa + c * Cfg::BK * 128, &tmA, fb, mb * Cfg::BM + c * Cfg::CHUNK,
-                          kb * Cfg::BK, ba);
-          }
-          if (!Cfg::B_MN) {
-            tma_load_3d(sbb, &tmB, fb, kb * Cfg::BK, nb * Cfg::BN, bb);
-          } else {
+              for (int c = 0; c < Cfg::BM / Cfg::CHUNK; ++c)
+                tma_load_3d(sa + c * Cfg::BK * 128, map, fb, mb * Cfg::BM + c * Cfg::CHUNK,
+                            kb * Cfg::BK, ba);
+            }
+          };
+          auto load_b = [&](uint32_t sbb, const CUtensorMap* map) {
+            if (!Cfg::B_MN) {
+              tma_load_3d(sbb, map, fb, kb * Cfg::BK, nb * Cfg::BN, bb);
+            } else {
 #pragma unroll
-            for (int c = 0; c < Cfg::BN / Cfg::CHUNK; ++c)
-              tma_load_3d(sbb + c * Cfg::BK * 128, &tmB, fb, nb * Cfg::BN + c * Cfg::CHUNK,
-                          kb * Cfg::BK, bb);
+              for (int c = 0; c < Cfg::BN / Cfg::CHUNK; ++c)
+                tma_load_3d(sbb + c * Cfg::BK * 128, map, fb, nb * Cfg::BN + c * Cfg::CHUNK,
+                            kb * Cfg::BK, bb);
+            }
+          };
+          load_a(smem_addr(stageA(s)), &tmA);
+          load_b(smem_addr(stageB(s)), &tmB);
+          if (lo_by_tma) {
+            load_a(smem_addr(stageAlo(s)), &tmAlo);
+            load_b(smem_addr(stageBlo(s)), &tmBlo);
           }
         }
         if (!ok) break;
@@ -362,7 +412,7 @@ __global__ void __launch_bounds__(256, 1)
           const int kfirst = kb;
           for (; kb < kend; ++kb, ++it) {
             const uint32_t s = it % S;
-            const uint32_t wb = Cfg::SPLIT ? smem_addr(&sb->conv[s]) : smem_addr(&sb->full[s]);
+            const uint32_t wb = convert ? smem_addr(&sb->conv[s]) : smem_addr(&sb->full[s]);
             if (!mbar_wait(wb, (it / S) & 1, wc)) { ok = false; break; }
             tc_fence_after();
             const uint32_t a_hi = smem_addr(stageA(s));
@@ -403,8 +453,11 @@ __global__ void __launch_bounds__(256, 1)
       mbar_wait(smem_addr(&sb->final_mma), 0, drain);
     }
   } else if (warp < 4) {
-    // ------------------------------------------- 3xTF32 split (fp32 only) --
-    if constexpr (Cfg::SPLIT) {
+    // -------------------------- 3xTF32 low parts in shared memory (warps 2-3) --
+    // Only when they were not split off before the launch.  hi is the fp32
+    // value itself (a kind::tf32 MMA reads trunc_tf32(x)); lo = x -
+    // trunc_tf32(x) is exact in fp32 and goes to the stage's lo buffers.
+    if (convert) {
       const int ct = threadIdx.x - 64;  // 0..63
       uint32_t it = 0;
       for (uint32_t slot = 0;; ++slot) {
@@ -424,23 +477,13 @@ __global__ void __launch_bounds__(256, 1)
           ok = __all_sync(0xffffffffu, ok);
           if (!ok) break;
           // A and B (and their lo buffers) are contiguous: [A | B] and [Alo | Blo].
-          // hi is the fp32 value itself: a kind::tf32 MMA reads only the
-          // sign, exponent and top 10 mantissa bits of each 32-bit element,
-          // i.e. the value truncated to tf32.  lo = x - trunc_tf32(x) is
-          // exact in fp32, so only lo is written (half the shared-memory
-          // traffic of a split that also rewrites hi).
           const float4* hi = reinterpret_cast<const float4*>(stageA(s));
           float4* lo = reinterpret_cast<float4*>(stageAlo(s));
           constexpr int NV = Cfg::LOAD_BYTES / 16;
 #pragma unroll 4
           for (int v = ct; v < NV; v += 64) {
             const float4 x = hi[v];
-            float4 l;
-            l.x = tf32_lo(x.x);
-            l.y = tf32_lo(x.y);
-            l.z = tf32_lo(x.z);
-            l.w = tf32_lo(x.w);
-            lo[v] = l;
+            lo[v] = make_float4(tf32_lo(x.x), tf32_lo(x.y), tf32_lo(x.z), tf32_lo(x.w));
           }
           fence_proxy_async_smem();
           mbar_arrive(smem_addr(&sb->conv[s]));
@@ -448,7 +491,7 @@ __global__ void __launch_bounds__(256, 1)
         if (!ok) break;
       }
     }
-  } else {
+  } else if (warp < 8) {
     // ------------------------------------------------------- epilogue -----
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     const float alpha = p.alpha_dev ? *p.alpha_dev : p.alpha;
@@ -469,8 +512,18 @@ __global__ void __launch_bounds__(256, 1)
       decode_tile(tile, p, b, ks, mb, nb);
       tile_k_range(tile, p, kb0, nkb);
       const int nseg = Cfg::PROMOTE ? (nkb + Cfg::SEG - 1) / Cfg::SEG : 1;
-      const int row = mb * Cfg::BM + q * 32 + static_cast<int>(lane);
-      const bool row_ok = row < p.m;
+      int row = mb * Cfg::BM + q * 32 + static_cast<int>(lane);
+      bool row_ok = row < p.m;
+      if constexpr (CONV) {
+        // tile row i = output pixel (th*hbox + i / wbox, tw*wbox + i % wbox)
+        const int i = q * 32 + static_cast<int>(lane);
+        const int th = mb / p.cv_tiles_w;
+        const int tw = mb - th * p.cv_tiles_w;
+        const int op = th * p.cv_hbox + i / p.cv_wbox;
+        const int oq = tw * p.cv_wbox + (i - (i / p.cv_wbox) * p.cv_wbox);
+        row_ok = op < p.cv_p && oq < p.cv_q;
+        row = op * p.cv_q + oq;
+      }
       const float bias_v = (p.bias != nullptr && row_ok && !split) ? load_scalar(p.bias, p.bias_type, row) : 0.f;
       const size_t d_base = static_cast<size_t>(b) * p.strideD + row;
       const size_t c_base = static_cast<size_t>(b) * p.strideC + row;

@@ -15,6 +15,9 @@ struct TcProblem {
   long long lda, strideA;
   const void* B;
   long long ldb, strideB;
+  // 3xTF32 only: x - trunc_tf32(x) of A and B, same layout as A and B
+  const void* Alo;
+  const void* Blo;
 };
 
 template <Arith AR>
@@ -33,27 +36,32 @@ template <int BN, Arith AR, bool AMN, bool BMN>
 int launch_gemm_tc(const Exec& e, const TcProblem& pr, GemmParams p) {
   using Cfg = GemmCfg<BN, AR, AMN, BMN>;
   constexpr CUtensorMapDataType dt = map_dtype<AR>();
-  CUtensorMap ma, mb;
-  bool ok;
+  CUtensorMap ma, mb, malo, mblo;
   // M/N-major tf32 operands need the 32-byte-atom variant of the 128-byte swizzle
   constexpr CUtensorMapSwizzle swzA =
       Cfg::A_MN32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B;
   constexpr CUtensorMapSwizzle swzB =
       Cfg::B_MN32 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B;
-  if (AMN)
-    ok = encode_map_3d(&ma, dt, Cfg::ESIZE, pr.A, pr.m, pr.k, pr.batch, pr.lda, pr.strideA,
-                       Cfg::CHUNK, Cfg::BK, swzA);
-  else
-    ok = encode_map_3d(&ma, dt, Cfg::ESIZE, pr.A, pr.k, pr.m, pr.batch, pr.lda, pr.strideA,
-                       Cfg::BK, Cfg::BM);
-  if (!ok) return KX_ERR_UNSUPPORTED;
-  if (BMN)
-    ok = encode_map_3d(&mb, dt, Cfg::ESIZE, pr.B, pr.n, pr.k, pr.batch, pr.ldb, pr.strideB,
-                       Cfg::CHUNK, Cfg::BK, swzB);
-  else
-    ok = encode_map_3d(&mb, dt, Cfg::ESIZE, pr.B, pr.k, pr.n, pr.batch, pr.ldb, pr.strideB,
-                       Cfg::BK, BN);
-  if (!ok) return KX_ERR_UNSUPPORTED;
+  auto map_a = [&](CUtensorMap* m, const void* base) {
+    return AMN ? encode_map_3d(m, dt, Cfg::ESIZE, base, pr.m, pr.k, pr.batch, pr.lda, pr.strideA,
+                               Cfg::CHUNK, Cfg::BK, swzA)
+               : encode_map_3d(m, dt, Cfg::ESIZE, base, pr.k, pr.m, pr.batch, pr.lda, pr.strideA,
+                               Cfg::BK, Cfg::BM);
+  };
+  auto map_b = [&](CUtensorMap* m, const void* base) {
+    return BMN ? encode_map_3d(m, dt, Cfg::ESIZE, base, pr.n, pr.k, pr.batch, pr.ldb, pr.strideB,
+                               Cfg::CHUNK, Cfg::BK, swzB)
+               : encode_map_3d(m, dt, Cfg::ESIZE, base, pr.k, pr.n, pr.batch, pr.ldb, pr.strideB,
+                               Cfg::BK, BN);
+  };
+  if (!map_a(&ma, pr.A) || !map_b(&mb, pr.B)) return KX_ERR_UNSUPPORTED;
+  if (Cfg::SPLIT && p.presplit) {
+    if (pr.Alo == nullptr || pr.Blo == nullptr) return KX_ERR_INVALID;
+    if (!map_a(&malo, pr.Alo) || !map_b(&mblo, pr.Blo)) return KX_ERR_UNSUPPORTED;
+  } else {
+    malo = ma;
+    mblo = mb;
+  }
 
   p.num_mb = (pr.m + Cfg::BM - 1) / Cfg::BM;
   p.num_nb = (pr.n + BN - 1) / BN;
@@ -102,7 +110,7 @@ int launch_gemm_tc(const Exec& e, const TcProblem& pr, GemmParams p) {
   }
   const int grid = persistent_grid(e, p.num_tiles);
   note_launch();
-  kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, e.stream>>>(ma, mb, p);
+  kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, e.stream>>>(ma, mb, malo, mblo, p);
   if (p.splits > 1) {
     const long long total = static_cast<long long>(pr.m) * pr.n * pr.batch;
     long long rgrid = (total + 255) / 256;

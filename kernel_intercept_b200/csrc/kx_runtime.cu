@@ -90,14 +90,14 @@ struct Scratch {
   void* ptr = nullptr;
   size_t bytes = 0;
 };
-std::unordered_map<cudaStream_t, Scratch> g_scratch[64][2];
+std::unordered_map<cudaStream_t, Scratch> g_scratch[64][3];
 }  // namespace
 
 void* scratch_for(cudaStream_t stream, size_t bytes, int slot) {
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) dev = 0;
-  if (slot < 0 || slot > 1) return nullptr;
+  if (slot < 0 || slot > 2) return nullptr;
   if (bytes == 0) bytes = 256;
   std::lock_guard<std::mutex> lk(g_mu);
   Scratch& s = g_scratch[dev][slot][stream];
@@ -142,7 +142,7 @@ int persistent_grid(const Exec& e, int tiles) {
 
 bool encode_map(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* base,
                 const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
-                CUtensorMapSwizzle swz) {
+                CUtensorMapSwizzle swz, const uint32_t* elem_strides) {
   EncodeTiledFn fn = encode_fn();
   if (fn == nullptr) return false;
   if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0) return false;
@@ -152,8 +152,13 @@ bool encode_map(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* 
   cuuint32_t es[5] = {1, 1, 1, 1, 1};
   for (int i = 0; i < rank; ++i) {
     if (dims[i] == 0 || dims[i] > (1ull << 32)) return false;
+    if (box[i] == 0 || box[i] > 256) return false;
     d[i] = dims[i];
     b[i] = box[i];
+    if (elem_strides != nullptr) {
+      if (elem_strides[i] == 0 || elem_strides[i] > 8) return false;
+      es[i] = elem_strides[i];
+    }
   }
   for (int i = 0; i + 1 < rank; ++i) {
     if ((strides_bytes[i] & 15u) != 0 || strides_bytes[i] >= (1ull << 40)) return false;

@@ -36,8 +36,9 @@ WorkSlot* work_slot_for(cudaStream_t stream);
 // device), so ops on one stream may reuse it back to back; ops on different
 // streams get different buffers.  Returns nullptr on allocation failure.
 // Slot 0 serves the operator entry points (im2col buffers, batch-norm
-// statistics); slot 1 is the GEMM's own split-K workspace, so a GEMM issued
-// by an operator never overwrites the operator's buffer.
+// statistics); slot 1 is the GEMM's own split-K workspace and slot 2 holds
+// the 3xTF32 low parts of its operands, so a GEMM issued by an operator never
+// overwrites the operator's buffer.
 void* scratch_for(cudaStream_t stream, size_t bytes, int slot = 0);
 
 // KX_SPLITK=0 turns split-K off (every output tile then runs its whole K).
@@ -66,6 +67,20 @@ Exec resolve_exec(const kx_exec* ex);
 // Grid size for a persistent launch with `tiles` work items.
 int persistent_grid(const Exec& e, int tiles);
 
+// Convolution problem in the form the implicit-GEMM kernel takes.
+struct ConvShape {
+  int N, C, H, W, K, R, S, ph, pw, sh, sw, dh, dw, P, Q;
+  bool flip;  // CUDNN_CONVOLUTION (true convolution) rather than cross-correlation
+};
+
+// Forward convolution on the implicit-GEMM tcgen05 kernel (3xTF32):
+// y = alpha * conv(x, w) + beta * y.  Returns KX_ERR_UNSUPPORTED when the
+// shape is outside what the kernel addresses (the caller then lowers
+// through im2col).  Defined in kx_conv_tc.cu.
+int conv_fwd_implicit(const Exec& e, const ConvShape& g, const float* x, const float* w, float* y,
+                      float alpha, float beta);
+
+
 // cuTensorMapEncodeTiled through cudaGetDriverEntryPoint (no libcuda link).
 // 3-D map {inner, outer, batch} with 128-byte swizzle.  Returns false when the
 // driver rejects the geometry (caller falls back to the SIMT kernel).
@@ -76,9 +91,12 @@ bool encode_map_3d(CUtensorMap* map, CUtensorMapDataType dt, int esize, const vo
 
 // Generic tiled map of rank 2..5 (dims/strides in elements / bytes as the
 // driver expects), 128-byte swizzle, zero OOB fill.
+// elem_strides (nullable): traversal stride per dimension (a box of b
+// elements with stride t loads b / t of them).
 bool encode_map(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* base,
                 const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
-                CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B);
+                CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B,
+                const uint32_t* elem_strides = nullptr);
 
 void set_last_kernel_name(const char* name);
 

@@ -56,6 +56,37 @@ def test_conv_fwd(cuda, case):
     assert o.normwise_rel_err(dy.cpu().numpy(), ref) <= TOL_F32
 
 
+IMPLICIT_CASES = [
+    (8, 32, 56, 56, 128, 3, 3, (1, 1), (1, 1), (1, 1), True),   # 128-wide channel tiles
+    (2, 40, 17, 19, 72, 3, 3, (1, 1), (1, 1), (1, 1), True),    # partial channel block, ragged K
+    (2, 96, 15, 15, 64, 1, 1, (0, 0), (1, 1), (1, 1), True),    # 1x1
+    (2, 16, 30, 30, 32, 5, 5, (2, 2), (2, 2), (1, 1), False),   # 5x5 strided, flipped
+    (2, 64, 28, 28, 128, 3, 3, (1, 1), (2, 2), (1, 1), True),   # stride 2 (TMA element strides)
+    (2, 32, 20, 22, 64, 3, 3, (2, 2), (1, 1), (2, 2), True),    # dilated taps
+    (4, 3, 64, 64, 64, 3, 3, (1, 1), (1, 1), (1, 1), True),     # C = 3: taps folded into K
+]
+
+
+@pytest.mark.parametrize("case", IMPLICIT_CASES)
+def test_conv_fwd_implicit_gemm(cuda, case):
+    """Forward convolution on the implicit-GEMM kernel (A tiles by 4-D TMA
+    from the NHWC staging copy; folded taps for small C*R*S)."""
+    kx = _kx()
+    import torch
+    kd, od = _desc(case)
+    rng = np.random.default_rng(3 + sum(case[:7]))
+    x = rng.standard_normal((od.n, od.c, od.h, od.w)).astype(np.float32)
+    w = rng.standard_normal((od.k, od.c, od.r, od.s)).astype(np.float32)
+    p, q = o.conv_out_dims(od)
+    y0 = rng.standard_normal((od.n, od.k, p, q)).astype(np.float32)
+    ref = o.conv_fwd(od, 0.5, x, w, beta=-0.25, y=y0.copy())
+    dx, dw, dy = _dev(x), _dev(w), _dev(y0)
+    kx.conv_fwd(kx.current_exec(), kd, 0.5, dx.data_ptr(), dw.data_ptr(), -0.25, dy.data_ptr())
+    torch.cuda.synchronize()
+    assert kx.last_kernel_name().startswith("kx_conv_fwd_tc<")
+    assert o.normwise_rel_err(dy.cpu().numpy(), ref) <= TOL_F32
+
+
 @pytest.mark.parametrize("case", CONV_CASES)
 def test_conv_bwd_data(cuda, case):
     kx = _kx()
