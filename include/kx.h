@@ -199,6 +199,20 @@ int kx_bn_fwd_training(const kx_exec* ex, int mode, const float* alpha, const fl
                        float* running_mean, float* running_var, double eps,
                        float* save_mean, float* save_inv_var);
 
+/* Allocation-free kx_bn_fwd_training (no counterpart in the reference: an
+ * addition for callers that cannot allocate device memory).  Same arguments
+ * and results; its statistics scratch is one file-scope device array of
+ * 4 MiB per device, so it calls no cudaMalloc / cudaFree.  Returns
+ * KX_ERR_INVALID when the call needs more scratch than that: 16 bytes per
+ * channel-split partial plus 8 bytes per channel (modes 1, 2), 8 bytes per
+ * activation c*h*w (mode 0).  All calls share the array: calls that overlap
+ * on the GPU race and must be serialised by the caller. */
+int kx_bn_fwd_training_noalloc(const kx_exec* ex, int mode, const float* alpha,
+                               const float* beta, int n, int c, int h, int w, const float* x,
+                               float* y, const float* scale, const float* bias,
+                               double exp_avg_factor, float* running_mean, float* running_var,
+                               double eps, float* save_mean, float* save_inv_var);
+
 int kx_bn_fwd_inference(const kx_exec* ex, int mode, const float* alpha, const float* beta,
                         int n, int c, int h, int w, const float* x, float* y,
                         const float* scale, const float* bias, const float* est_mean,

@@ -493,3 +493,95 @@ extern "C" int kx_bn_bwd(const kx_exec* ex, int mode, const float* alpha_data,
   set_last_kernel_name("kx_bn_bwd");
   return launch_status();
 }
+
+// ------------------------------------------------ allocation-free variant --
+//
+// kx_bn_fwd_training_noalloc: the same computation as kx_bn_fwd_training, for
+// callers that cannot allocate device memory.  Its statistics scratch is the
+// file-scope array below (kNoAllocScratchBytes = 4 MiB per device) instead of
+// the stream's scratch arena; nothing in this path calls cudaMalloc,
+// cudaFree or any allocating routine.  Every call shares the one array, so
+// calls whose kernels overlap on the GPU (other streams, other host threads)
+// race on it; callers serialise them.  No part of the array has to start at
+// zero: every call writes all the scratch it reads (per-block partial sums,
+// then per-channel coefficients) before reading it.
+
+namespace kx {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = 4u << 20;
+__device__ __align__(256) unsigned char g_bn_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[64] = {nullptr};
+
+// Device address of the array for the current device, looked up once per
+// device (with that device current).
+void* noalloc_scratch() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_bn_noalloc_scratch) != cudaSuccess) {
+      cudaGetLastError();
+      return nullptr;
+    }
+    g_noalloc_ptr[dev] = p;
+  }
+  return g_noalloc_ptr[dev];
+}
+
+}  // namespace
+}  // namespace kx
+
+extern "C" int kx_bn_fwd_training_noalloc(const kx_exec* ex, int mode, const float* alpha,
+                                          const float* beta, int n, int c, int h, int w,
+                                          const float* x, float* y, const float* scale,
+                                          const float* bias, double exp_avg_factor,
+                                          float* running_mean, float* running_var, double eps,
+                                          float* save_mean, float* save_inv_var) {
+  if (bad_dims(n, c, h, w) || !x || !y || !scale || !bias || !alpha || !beta) return KX_ERR_INVALID;
+  if (mode != 0 && mode != 1 && mode != 2) return KX_ERR_UNSUPPORTED;
+  Exec e = resolve_exec(ex);
+  const int HW = h * w;
+  // scratch this call needs; more than the array holds is rejected
+  const int S = mode == 0 ? 0 : split_for(static_cast<long long>(n) * HW, c);
+  const size_t part_bytes = sizeof(double) * 2 * static_cast<size_t>(c) * S;
+  const size_t coef_off = (part_bytes + 255) & ~static_cast<size_t>(255);
+  const size_t need = mode == 0 ? sizeof(float2) * static_cast<size_t>(c) * HW
+                                : coef_off + sizeof(float2) * static_cast<size_t>(c);
+  if (need > kNoAllocScratchBytes) return KX_ERR_INVALID;
+  char* base = static_cast<char*>(noalloc_scratch());
+  if (base == nullptr) return KX_ERR_DEVICE;
+  if (mode == 0) {
+    const int G = c * HW;
+    float2* coef = reinterpret_cast<float2*>(base);
+    note_launch();
+    bn_stats_per_activation<<<(G + 255) / 256, 256, 0, e.stream>>>(
+        x, n, G, scale, bias, exp_avg_factor, running_mean, running_var, eps, save_mean,
+        save_inv_var, coef, nullptr, nullptr);
+    const size_t total = static_cast<size_t>(n) * G;
+    const size_t cap = 8u * device_info().num_sms;
+    const int blocks = static_cast<int>((total + 255) / 256 < cap ? (total + 255) / 256 : cap);
+    note_launch();
+    bn_apply_per_activation<<<blocks, 256, 0, e.stream>>>(x, y, n, G, coef, *alpha, *beta);
+    set_last_kernel_name("kx_bn_apply_per_activation");
+    return launch_status();
+  }
+  double* part = reinterpret_cast<double*>(base);
+  float2* coef = reinterpret_cast<float2*>(base + coef_off);
+  note_launch();
+  bn_stats_spatial<<<dim3(c, S), kThreads, 0, e.stream>>>(x, n, c, HW, S, part);
+  note_launch();
+  bn_finalize_spatial<<<(c + 127) / 128, 128, 0, e.stream>>>(x, n, c, HW, S, part, scale, bias,
+                                                             exp_avg_factor, running_mean,
+                                                             running_var, eps, save_mean,
+                                                             save_inv_var, coef);
+  const long long rows = static_cast<long long>(n) * c;
+  note_launch();
+  bn_apply_spatial<<<apply_grid(rows, HW), kThreads, 0, e.stream>>>(x, y, c, HW, rows, coef,
+                                                                   *alpha, *beta);
+  set_last_kernel_name("kx_bn_apply_spatial");
+  return launch_status();
+}

@@ -79,6 +79,8 @@ _SIGNATURES = {
     "kx_conv_bwd_filter": [_EP, _CD, _P, _P, _P, _P, _P],
     "kx_bn_fwd_training": [_EP, _I, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P, _D, _P, _P, _D, _P,
                            _P],
+    "kx_bn_fwd_training_noalloc": [_EP, _I, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P, _D, _P, _P,
+                                   _D, _P, _P],
     "kx_bn_fwd_inference": [_EP, _I, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _D],
     "kx_bn_bwd": [_EP, _I, _P, _P, _P, _P, _I, _I, _I, _I, _P, _P, _P, _P, _P, _P, _D, _P, _P],
     "kx_host_flags_alloc": [_I, ctypes.POINTER(_P), ctypes.POINTER(_P)],
