@@ -1,6 +1,6 @@
 #!/usr/bin/env python
 """Benchmark: HP/BE co-scheduling on the kx kernels through the drop-in
-interposer (configuration 1 of the reference's benchmark set).
+interposer: HP VGG16 inference against BE GPT training.
 
 Workload (one "step" = one HP request):
   HP  = VGG16 inference, fp32, batch 32 x 3x224x224 N(0,1), Kaiming-normal init
@@ -12,10 +12,13 @@ LD_PRELOAD=kernel_intercept_b200/libgpu_scheduler.so; client 0 (HP) and client
 1 (BE) are registered threads, every captured GEMM / convolution runs on the
 kx sm_100a kernels (bench.py re-executes itself with the preload when needed).
 
-Phases (same models and inputs): HP alone, BE alone, HP + BE together.  The
-timed region is the K HP steps of the contended phase, bracketed by a barrier
-and a device synchronize, timed with CUDA events on the HP stream (max over
-ranks).  `value` = HP images/s under contention (whole job: sum over ranks).
+Phases (same models and inputs): HP alone, BE alone, HP + BE together (HP
+back to back: the timed region), HP paced at a duty cycle of --hp-load
+against BE (the Orion setting: HP p99 vs solo and BE retention), and the
+end-to-end repeat.  The timed region is the K HP steps of the contended phase,
+bracketed by a barrier and a device synchronize, timed with CUDA events on
+the HP stream (max over ranks).  `value` = HP images/s under contention
+(whole job: sum over ranks).
 `e2e` repeats the contended phase with the HP input copied from pinned host
 memory and the logits copied back inside every step.  `roofline` is the
 dominant captured kernel class (HP convolutions) from CUDA events recorded
@@ -52,7 +55,10 @@ def parse():
     ap.add_argument("--impl", default="kx", choices=["kx", "reference"])
     ap.add_argument("--be-seconds", type=float, default=4.0)
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--be-keep-sms", type=int, default=-1)
+    ap.add_argument("--be-keep-sms", type=int, default=-1,
+                    help="SMs a BE op keeps while HP runs (default: the scheduler's)")
+    ap.add_argument("--hp-load", type=float, default=1.0 / 3.0,
+                    help="HP duty cycle of the paced phase (request period = solo p50 / load)")
     return ap.parse_args()
 
 
@@ -143,8 +149,8 @@ def run_reference(args):
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(total / args.steps * 1e3, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f64-accumulate",
-        "data": "synthetic", "config": {"workload": "config1: VGG16 inference (HP) fp32, "
-                                        "CPU path of the captured ops, 1-image sample per step",
+        "data": "synthetic", "config": {"workload": "VGG16 inference fp32 (the HP model), CPU "
+                                        "path of the captured ops, 1-image sample per step",
                                         "batch": 1},
         "cpu_baseline": {"value": round(value, 4), "unit": "images/s", "cores": used,
                          "kind": "port", "sample": "1 image of the batch-32 VGG16 forward per step"},
@@ -299,7 +305,14 @@ def run_kx(args):
     clk = clocks.stop()
     launches = kxlib.kx_launch_count() - launches0
     barrier()
-    # phase 4: e2e (host buffers in every HP step), contended
+    # phase 4: paced HP (requests every solo_p50 / hp_load ms) against BE, the
+    # Orion setting in which HP latency vs solo and BE retention are judged
+    s50_now = harness.percentile(hp_solo.latencies_ms, 0.5)
+    period = s50_now / max(args.hp_load, 1e-3)
+    paced_steps = max(6 * args.steps, 60)  # long enough for a stable BE rate and p99
+    hp_p, be_p = harness.run_clients(orion, hp_step, be_step, paced_steps, args.warmup,
+                                     hp_period_ms=period)
+    # phase 5: e2e (host buffers in every HP step), contended
     hp_e2e = None
     if not args.no_e2e:
         hp_e2e, _ = harness.run_clients(orion, hp_step_e2e, be_step, args.steps, args.warmup)
@@ -355,6 +368,16 @@ def run_kx(args):
                    "l2": "inputs larger than L2 (VGG16 first-block activations 411 MB)"},
         "hp": {"p50_ms": round(p50, 3), "p99_ms": round(p99, 3), "solo_p50_ms": round(s50, 3),
                "solo_p99_ms": round(s99, 3), "p99_vs_solo": round(p99 / s99, 4) if s99 else None},
+        "paced": {"hp_load": round(args.hp_load, 3), "period_ms": round(period, 3),
+                  "hp_steps": paced_steps,
+                  "hp_p50_ms": round(harness.percentile(hp_p.latencies_ms, 0.5), 3),
+                  "hp_p99_ms": round(harness.percentile(hp_p.latencies_ms, 0.99), 3),
+                  "hp_p99_vs_solo": round(harness.percentile(hp_p.latencies_ms, 0.99) / s99, 4)
+                  if s99 else None,
+                  "be_iters_per_s": round(be_p.iters / (be_p.elapsed_ms / 1e3), 3)
+                  if be_p.elapsed_ms else None,
+                  "be_retention": round(be_p.iters / (be_p.elapsed_ms / 1e3) / be_solo_ips, 4)
+                  if be_p.elapsed_ms and be_solo_ips else None},
         "be": {"iters_per_s": round(be_c_ips, 3), "solo_iters_per_s": round(be_solo_ips, 3),
                "retention": round(be_c_ips / be_solo_ips, 4) if be_solo_ips else None,
                "tokens_per_s": round(be_c_ips * BE_BATCH * BE_SEQ, 1)},

@@ -170,6 +170,16 @@ private:
     // HP flag in pinned, device-mapped host memory (read by BE kernels).
     volatile int* hp_flag_host_{nullptr};
     int* hp_flag_dev_{nullptr};
+    // Copy of hp_flag_host_[0] in device memory: the flag BE kernels poll.
+    // Device reads of pinned host memory cross PCIe and serialise when many
+    // CTAs poll at once, so the kernels read this copy, which the scheduler
+    // updates with an async copy on flag_stream_ whenever the flag changes.
+    int* hp_flag_devmem_{nullptr};
+    // HP idle hysteresis: the flag drops only after HP has been idle this long
+    int64_t hp_idle_since_ns_{0};
+    int64_t hp_hold_ns_{1000000};
+    cudaStream_t flag_stream_{nullptr};
+    void publish_hp_flag(int value);
     std::atomic<int> be_keep_sms_{0};
     cudaEvent_t hp_last_event_{nullptr};
     std::atomic<bool> hp_event_pending_{false};

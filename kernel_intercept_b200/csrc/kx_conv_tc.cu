@@ -130,7 +130,7 @@ __global__ void pack_filter(const float* __restrict__ w, float* __restrict__ wp,
 }
 
 // Output tile = hbox rows x wbox columns of output pixels (wbox * hbox =
-// 128, powers of two), chosen to waste the fewest MMA rows.
+// 128, powers of two), chosen to waste the fewest MMA rows (ties: widest).
 void choose_box(int P, int Q, int sw, int sh, int& wbox, int& hbox) {
   long long best = -1;
   wbox = 128;
@@ -139,7 +139,8 @@ void choose_box(int P, int Q, int sw, int sh, int& wbox, int& hbox) {
     const int hb = 128 / wb;
     if (wb * sw > 256 || hb * sh > 256) continue;
     const long long tiles = static_cast<long long>((Q + wb - 1) / wb) * ((P + hb - 1) / hb);
-    if (best < 0 || tiles < best) {
+    // ties go to the wider box: longer contiguous output rows
+    if (best < 0 || tiles <= best) {
       best = tiles;
       wbox = wb;
       hbox = hb;
@@ -233,9 +234,27 @@ int launch_conv_tc(const Exec& e, const ConvShape& g, const ConvShape& t, const 
       return KX_ERR_DEVICE;
     attr_set[di.device & 63] = true;
   }
+  // y through TMA stores: {Q, P, K, N} map, per-warp box {min(wbox,32),
+  // 32/min(wbox,32), 32 channels, 1}; needs 16-byte rows (Q % 4 == 0) and a
+  // box at least 16 bytes wide
+  CUtensorMap md = ma;
+  p.tma_store = 0;
+  if (g.Q % 4 == 0 && wbox >= 4 && !tma_store_disabled()) {
+    const int ww = wbox < 32 ? wbox : 32;
+    const uint64_t ydims[4] = {static_cast<uint64_t>(g.Q), static_cast<uint64_t>(g.P),
+                               static_cast<uint64_t>(g.K), static_cast<uint64_t>(g.N)};
+    const uint64_t ystr[3] = {static_cast<uint64_t>(g.Q) * 4, static_cast<uint64_t>(pq) * 4,
+                              static_cast<uint64_t>(pq) * g.K * 4};
+    const uint32_t ybox[4] = {static_cast<uint32_t>(ww), static_cast<uint32_t>(32 / ww), 32u, 1u};
+    if (encode_map(&md, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, y, ydims, ystr, ybox,
+                   CU_TENSOR_MAP_SWIZZLE_NONE))
+      p.tma_store = 1;
+  }
   const int grid = persistent_grid(e, p.num_tiles);
+  p.pipe_stats = pipe_stats_begin();
   note_launch();
-  kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, e.stream>>>(ma, mb, malo, mblo, p);
+  kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, e.stream>>>(ma, mb, malo, mblo, md, p);
+  pipe_stats_end(p.pipe_stats, "kx_conv_fwd_tc", e.stream, grid);
   static char name[64];
   if (name[0] == 0) snprintf(name, sizeof(name), "kx_conv_fwd_tc<bn%d,f32x3>", BN);
   set_last_kernel_name(name);

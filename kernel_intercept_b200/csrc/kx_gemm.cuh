@@ -95,7 +95,39 @@ struct GemmParams {
   // across a row); batch = image; D is NCHW (ld = P*Q).
   int cv_p, cv_q, cv_wbox, cv_hbox, cv_tiles_w, cv_s, cv_cb;
   int cv_pad_h, cv_pad_w, cv_str_h, cv_str_w, cv_dil_h, cv_dil_w;
+  // Pipeline diagnostics (nullable): per CTA kPipeStats clock64 counters of
+  // the time each role spends waiting (see PipeStat).
+  unsigned long long* pipe_stats;
+  // 1: the epilogue writes D through shared memory and TMA stores (map tmD:
+  // {m, n, batch} for GEMMs, {Q, P, K, N} for convolutions); 0: one st.global
+  // per element (unaligned D, split-K partials).
+  int tma_store;
 };
+
+enum PipeStat : int {
+  PS_PROD_EMPTY = 0,  // producer waits for a free stage
+  PS_PROD_RING,       // producer waits for a free tile-ring slot
+  PS_MMA_DATA,        // MMA issuer waits for a stage's data
+  PS_MMA_TMEM,        // MMA issuer waits for a free accumulator buffer
+  PS_MMA_RING,        // MMA issuer waits for the next tile id
+  PS_EPI_TFULL,       // epilogue (warp 4) waits for an accumulator
+  PS_TOTAL,           // CTA lifetime
+  PS_PROLOGUE,        // barrier init + TMEM allocation
+  PS_MMA_ISSUE,       // MMA issuer: issuing a k-block's MMAs and its commit
+  PS_EPI_FOLD,        // epilogue (warp 4): folding segments from TMEM
+  PS_EPI_EMIT,        // epilogue (warp 4): output stores
+  PS_EPI_STWAIT,      // epilogue (warp 4): proxy fences before its TMA stores
+  kPipeStats = 12
+};
+
+KX_DEV bool timed_wait(uint32_t bar, uint32_t parity, const WaitCtl& wc,
+                       unsigned long long* acc) {
+  if (acc == nullptr) return mbar_wait(bar, parity, wc);
+  const long long t0 = clock64();
+  const bool ok = mbar_wait(bar, parity, wc);
+  *acc += static_cast<unsigned long long>(clock64() - t0);
+  return ok;
+}
 
 template <int BN_, Arith AR_, bool A_MN_, bool B_MN_>
 struct GemmCfg {
@@ -113,7 +145,7 @@ struct GemmCfg {
   static constexpr int B_BYTES = BN * 128;
   static constexpr int LOAD_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGE_BYTES = LOAD_BYTES * (SPLIT ? 2 : 1);
-  static constexpr int STAGES_RAW = (200 * 1024) / STAGE_BYTES;
+  static constexpr int STAGES_RAW = (192 * 1024) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
   static constexpr int RING = 4;  // depth of the tile-id broadcast ring
   static constexpr int TMEM_COLS = (2 * BN) <= 32 ? 32 : (2 * BN) <= 64 ? 64 : (2 * BN) <= 128 ? 128 : (2 * BN) <= 256 ? 256 : 512;
@@ -140,8 +172,11 @@ struct GemmCfg {
   static_assert(!PROMOTE || BN <= 128, "3xTF32 keeps a BN-wide fp32 accumulator per thread");
   static constexpr uint32_t FMT = (AR == Arith::BF16) ? 1u : (AR == Arith::F16) ? 0u : 2u;
   static constexpr uint32_t IDESC = make_idesc(FMT, A_MN, B_MN, BM, BN);
-  // barrier block follows the stages
-  static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
+  // epilogue staging (4 warps x 2 buffers of 32 x 32 fp32) after the stages,
+  // then the barrier block
+  static constexpr int EPI_OFF = STAGES * STAGE_BYTES;
+  static constexpr int EPI_BYTES = 4 * 2 * 4096;
+  static constexpr int BAR_OFF = EPI_OFF + EPI_BYTES;
   static constexpr int SMEM_BYTES = 1024 /*align slack*/ + BAR_OFF + 1024 /*barriers*/;
   static_assert(STAGES >= 2, "not enough shared memory for two stages");
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "bad BN");
@@ -244,7 +279,8 @@ __global__ void __launch_bounds__(256, 1)
     kx_gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA,
                       const __grid_constant__ CUtensorMap tmB,
                       const __grid_constant__ CUtensorMap tmAlo,
-                      const __grid_constant__ CUtensorMap tmBlo, const GemmParams p) {
+                      const __grid_constant__ CUtensorMap tmBlo,
+                      const __grid_constant__ CUtensorMap tmD, const GemmParams p) {
   static_assert(!CONV || (Cfg::AR == Arith::F32x3 && !Cfg::A_MN),
                 "implicit convolution: 3xTF32 with a K-major A tile");
   constexpr int S = Cfg::STAGES;
@@ -301,8 +337,12 @@ __global__ void __launch_bounds__(256, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sb->tmem_base;
+  const long long t_ready = clock64();
 
   WaitCtl wc{&sb->abort_flag, p.err_word, p.timeout_ns};
+  const long long t_start = clock64();
+  unsigned long long st_a = 0, st_b = 0, st_c = 0, st_d = 0, st_e = 0;  // per-role counters
+  const bool stats = p.pipe_stats != nullptr;
 
   if (warp == 0) {
     // ------------------------------------------------------ TMA producer --
@@ -323,7 +363,9 @@ __global__ void __launch_bounds__(256, 1)
           if (tile >= p.num_tiles) tile = -1;
         }
         const uint32_t r = slot % R;
-        if (!mbar_wait(smem_addr(&sb->ring_empty[r]), ((slot / R) & 1) ^ 1, wc)) break;
+        if (!timed_wait(smem_addr(&sb->ring_empty[r]), ((slot / R) & 1) ^ 1, wc,
+                        stats ? &st_b : nullptr))
+          break;
         sb->ring[r] = tile;
         mbar_arrive(smem_addr(&sb->ring_full[r]));
         if (tile < 0) break;
@@ -336,7 +378,11 @@ __global__ void __launch_bounds__(256, 1)
         bool ok = true;
         for (int kb = kb0; kb < kb0 + nkb; ++kb, ++it) {
           const uint32_t s = it % S;
-          if (!mbar_wait(smem_addr(&sb->empty[s]), ((it / S) & 1) ^ 1, wc)) { ok = false; break; }
+          if (!timed_wait(smem_addr(&sb->empty[s]), ((it / S) & 1) ^ 1, wc,
+                          stats ? &st_a : nullptr)) {
+            ok = false;
+            break;
+          }
           const uint32_t fb = smem_addr(&sb->full[s]);
           // 3xTF32 with pre-split operands: the low parts arrive by TMA beside
           // the high parts.
@@ -397,7 +443,9 @@ __global__ void __launch_bounds__(256, 1)
       bool ok = true;
       for (uint32_t slot = 0; ok; ++slot) {
         const uint32_t r = slot % R;
-        if (!mbar_wait(smem_addr(&sb->ring_full[r]), (slot / R) & 1, wc)) break;
+        if (!timed_wait(smem_addr(&sb->ring_full[r]), (slot / R) & 1, wc,
+                        stats ? &st_c : nullptr))
+          break;
         const int tile = sb->ring[r];
         mbar_arrive(smem_addr(&sb->ring_empty[r]));
         if (tile < 0) break;
@@ -405,7 +453,11 @@ __global__ void __launch_bounds__(256, 1)
         tile_k_range(tile, p, kb0, nkb);
         for (int kb = 0; kb < nkb && ok; ++sc) {
           const uint32_t a = sc & 1;
-          if (!mbar_wait(smem_addr(&sb->tempty[a]), ((sc >> 1) & 1) ^ 1, wc)) { ok = false; break; }
+          if (!timed_wait(smem_addr(&sb->tempty[a]), ((sc >> 1) & 1) ^ 1, wc,
+                          stats ? &st_b : nullptr)) {
+            ok = false;
+            break;
+          }
           tc_fence_after();
           const uint32_t d_tmem = tmem + a * Cfg::BN;
           const int kend = (nkb - kb > Cfg::SEG) ? kb + Cfg::SEG : nkb;
@@ -413,7 +465,11 @@ __global__ void __launch_bounds__(256, 1)
           for (; kb < kend; ++kb, ++it) {
             const uint32_t s = it % S;
             const uint32_t wb = convert ? smem_addr(&sb->conv[s]) : smem_addr(&sb->full[s]);
-            if (!mbar_wait(wb, (it / S) & 1, wc)) { ok = false; break; }
+            if (!timed_wait(wb, (it / S) & 1, wc, stats ? &st_a : nullptr)) {
+              ok = false;
+              break;
+            }
+            const long long t_iss = stats ? clock64() : 0;
             tc_fence_after();
             const uint32_t a_hi = smem_addr(stageA(s));
             const uint32_t b_hi = smem_addr(stageB(s));
@@ -441,6 +497,7 @@ __global__ void __launch_bounds__(256, 1)
               }
             }
             tc_commit(smem_addr(&sb->empty[s]));
+            if (stats) st_d += static_cast<unsigned long long>(clock64() - t_iss);
           }
           if (!ok) break;
           tc_commit(smem_addr(&sb->tfull[a]));
@@ -498,6 +555,10 @@ __global__ void __launch_bounds__(256, 1)
     const float beta = p.beta_dev ? *p.beta_dev : p.beta;
     const uint32_t lane_off = (q * 32u) << 16;
     const bool split = p.splits > 1;
+    const bool use_tma_store = p.tma_store != 0 && !split;
+    // alpha * acc only (no beta, bias or activation)
+    const bool plain_epi = beta == 0.f && p.bias == nullptr && !p.relu && !p.gelu;
+    uint32_t epi_chunk = 0;
     uint32_t sc = 0;
     for (uint32_t slot = 0;; ++slot) {
       const uint32_t r = slot % R;
@@ -555,6 +616,69 @@ __global__ void __launch_bounds__(256, 1)
           }
         }
       };
+      // Same values through shared memory: the warp writes its 32 rows x 32
+      // columns (column-contiguous, as D is) into one of its two staging
+      // buffers and lane 0 issues a TMA store, which clips rows / columns
+      // outside D.  A buffer is rewritten only after the store issued from it
+      // two chunks earlier has read it.
+      auto emit_tma = [&](int c0, const float* acc) {
+        const int col0 = nb * Cfg::BN + c0;
+        uint8_t* buf = smem + Cfg::EPI_OFF + (q * 2 + (epi_chunk & 1u)) * 4096;
+        ++epi_chunk;
+        if (lane == 0) bulk_wait_group_read<1>();
+        __syncwarp();
+        // element (column j, row lane) at index j*32 + lane of the buffer
+        float* fbuf = reinterpret_cast<float*>(buf);
+        if (plain_epi && p.d_type == DT_F32) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) fbuf[j * 32 + lane] = alpha * acc[j];
+        } else if (plain_epi && p.d_type == DT_BF16) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            reinterpret_cast<__nv_bfloat16*>(buf)[j * 32 + lane] = __float2bfloat16_rn(alpha * acc[j]);
+        } else {
+          // general epilogue in a second, rolled pass over the staged values
+          // (keeps the code small: the epilogue warps share the instruction
+          // cache with the producer and MMA loops)
+#pragma unroll
+          for (int j = 0; j < 32; ++j) fbuf[j * 32 + lane] = alpha * acc[j];
+          __syncwarp();
+#pragma unroll 1
+          for (int j = 0; j < 32; ++j) {
+            const int col = col0 + j;
+            float o = fbuf[j * 32 + lane];
+            if (beta != 0.f && row_ok && col < p.n)
+              o += beta * load_scalar(p.C, p.c_type, c_base + static_cast<size_t>(col) * p.ldc);
+            o += bias_v;
+            if (p.relu) o = fmaxf(o, 0.f);
+            if (p.gelu) o = gelu_tanh(o);
+            // 16-bit outputs shrink in place: element i is written at byte 2i,
+            // below every element a later iteration still reads
+            if (p.d_type == DT_F32)
+              fbuf[j * 32 + lane] = o;
+            else if (p.d_type == DT_BF16)
+              reinterpret_cast<__nv_bfloat16*>(buf)[j * 32 + lane] = __float2bfloat16_rn(o);
+            else
+              reinterpret_cast<__half*>(buf)[j * 32 + lane] = __float2half_rn(o);
+            __syncwarp();
+          }
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          if constexpr (CONV) {
+            // warp q holds tile rows 32q .. 32q+31 = a {min(wbox,32), 32/min(wbox,32)} box
+            const int th = mb / p.cv_tiles_w;
+            const int tw = mb - th * p.cv_tiles_w;
+            const int i0 = q * 32;
+            tma_store_4d(&tmD, smem_addr(buf), tw * p.cv_wbox + i0 % p.cv_wbox,
+                         th * p.cv_hbox + i0 / p.cv_wbox, col0, b);
+          } else {
+            tma_store_3d(&tmD, smem_addr(buf), mb * Cfg::BM + q * 32, col0, b);
+          }
+          bulk_commit_group();
+        }
+      };
       if constexpr (Cfg::PROMOTE) {
         // fold every segment's TMEM partial into round-to-nearest registers
         float acc[Cfg::BN / 32][32];
@@ -564,9 +688,11 @@ __global__ void __launch_bounds__(256, 1)
           for (int j = 0; j < 32; ++j) acc[c][j] = 0.f;
         for (int sg = 0; sg < nseg; ++sg, ++sc) {
           const uint32_t a = sc & 1;
-          ok = mbar_wait(smem_addr(&sb->tfull[a]), (sc >> 1) & 1, wc);
+          ok = timed_wait(smem_addr(&sb->tfull[a]), (sc >> 1) & 1, wc,
+                          stats && warp == 4 ? &st_a : nullptr);
           ok = __all_sync(0xffffffffu, ok);
           if (!ok) break;
+          const long long t_fold = stats ? clock64() : 0;
           tc_fence_after();
 #pragma unroll
           for (int c = 0; c < Cfg::BN / 32; ++c) {
@@ -579,16 +705,26 @@ __global__ void __launch_bounds__(256, 1)
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive(smem_addr(&sb->tempty[a]));
+          if (stats) st_b += static_cast<unsigned long long>(clock64() - t_fold);
         }
         if (!ok) break;
+        const long long t_emit = stats ? clock64() : 0;
+        if (use_tma_store) {
 #pragma unroll
-        for (int c = 0; c < Cfg::BN / 32; ++c) emit(c * 32, acc[c]);
+          for (int c = 0; c < Cfg::BN / 32; ++c) emit_tma(c * 32, acc[c]);
+        } else {
+#pragma unroll
+          for (int c = 0; c < Cfg::BN / 32; ++c) emit(c * 32, acc[c]);
+        }
+        if (stats) st_c += static_cast<unsigned long long>(clock64() - t_emit);
       } else {
         const uint32_t a = sc & 1;
-        ok = mbar_wait(smem_addr(&sb->tfull[a]), (sc >> 1) & 1, wc);
+        ok = timed_wait(smem_addr(&sb->tfull[a]), (sc >> 1) & 1, wc,
+                        stats && warp == 4 ? &st_a : nullptr);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         tc_fence_after();
+        const long long t_emit = stats ? clock64() : 0;
 #pragma unroll 1
         for (int c0 = 0; c0 < Cfg::BN; c0 += 32) {
           uint32_t v[32];
@@ -597,8 +733,12 @@ __global__ void __launch_bounds__(256, 1)
           float f[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]);
-          emit(c0, f);
+          if (use_tma_store)
+            emit_tma(c0, f);
+          else
+            emit(c0, f);
         }
+        if (stats) st_c += static_cast<unsigned long long>(clock64() - t_emit);
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_addr(&sb->tempty[a]));
@@ -608,6 +748,27 @@ __global__ void __launch_bounds__(256, 1)
   }
 
   // --------------------------------------------------------- teardown ----
+  // the epilogue's TMA stores complete before the CTA counts as retired
+  if (warp >= 4 && warp < 8 && lane == 0 && p.tma_store != 0) bulk_wait_group_all();
+  if (stats && lane == 0) {
+    unsigned long long* ps = p.pipe_stats + static_cast<size_t>(blockIdx.x) * kPipeStats;
+    if (warp == 0) {
+      ps[PS_PROD_EMPTY] = st_a;
+      ps[PS_PROD_RING] = st_b;
+    } else if (warp == 1) {
+      ps[PS_MMA_DATA] = st_a;
+      ps[PS_MMA_TMEM] = st_b;
+      ps[PS_MMA_RING] = st_c;
+      ps[PS_MMA_ISSUE] = st_d;
+    } else if (warp == 4) {
+      ps[PS_EPI_TFULL] = st_a;
+      ps[PS_EPI_FOLD] = st_b;
+      ps[PS_EPI_EMIT] = st_c;
+      ps[PS_EPI_STWAIT] = st_e;
+      ps[PS_TOTAL] = static_cast<unsigned long long>(clock64() - t_start);
+      ps[PS_PROLOGUE] = static_cast<unsigned long long>(t_ready - t_start);
+    }
+  }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {

@@ -108,9 +108,25 @@ int launch_gemm_tc(const Exec& e, const TcProblem& pr, GemmParams p) {
       }
     }
   }
+  // D through TMA stores when D is TMA-addressable (split-K writes partials)
+  CUtensorMap md = ma;
+  p.tma_store = 0;
+  if (p.splits == 1 && !tma_store_disabled()) {
+    const int des = p.d_type == DT_F32 ? 4 : 2;
+    const CUtensorMapDataType ddt = p.d_type == DT_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                    : p.d_type == DT_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                          : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const bool aligned = (p.ldd * des) % 16 == 0 &&
+                         (pr.batch <= 1 || p.strideD == 0 || (p.strideD * des) % 16 == 0);
+    if (aligned && encode_map_3d(&md, ddt, des, p.D, pr.m, pr.n, pr.batch, p.ldd, p.strideD, 32,
+                                 32, CU_TENSOR_MAP_SWIZZLE_NONE))
+      p.tma_store = 1;
+  }
   const int grid = persistent_grid(e, p.num_tiles);
+  p.pipe_stats = pipe_stats_begin();
   note_launch();
-  kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, e.stream>>>(ma, mb, malo, mblo, p);
+  kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, e.stream>>>(ma, mb, malo, mblo, md, p);
+  pipe_stats_end(p.pipe_stats, "kx_gemm_tc", e.stream, grid);
   if (p.splits > 1) {
     const long long total = static_cast<long long>(pr.m) * pr.n * pr.batch;
     long long rgrid = (total + 255) / 256;

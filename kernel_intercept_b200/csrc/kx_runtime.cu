@@ -194,6 +194,41 @@ bool encode_map_3d(CUtensorMap* map, CUtensorMapDataType dt, int esize, const vo
 
 void set_last_kernel_name(const char* name) { tl_kernel_name = name; }
 
+unsigned long long* pipe_stats_begin() {
+  static const bool on = [] {
+    const char* s = std::getenv("KX_PIPE_STATS");
+    return s != nullptr && s[0] == '1';
+  }();
+  if (!on) return nullptr;
+  static unsigned long long* buf = nullptr;
+  const size_t bytes = sizeof(unsigned long long) * kPipeStats * 1024;
+  if (buf == nullptr && cudaMalloc(&buf, bytes) != cudaSuccess) {
+    buf = nullptr;
+    return nullptr;
+  }
+  cudaMemset(buf, 0, bytes);
+  return buf;
+}
+
+void pipe_stats_end(unsigned long long* buf, const char* kernel, cudaStream_t stream, int grid) {
+  if (buf == nullptr || grid <= 0 || grid > 1024) return;
+  std::vector<unsigned long long> h(static_cast<size_t>(grid) * kPipeStats);
+  cudaStreamSynchronize(stream);
+  cudaMemcpy(h.data(), buf, h.size() * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
+  double sum[kPipeStats] = {0};
+  for (int c = 0; c < grid; ++c)
+    for (int i = 0; i < kPipeStats; ++i) sum[i] += static_cast<double>(h[c * kPipeStats + i]);
+  const double tot = sum[PS_TOTAL] > 0 ? sum[PS_TOTAL] : 1.0;
+  std::fprintf(stderr,
+               "[kx pipe] %s grid %d cycles/CTA %.0f | share: prologue %.3f prod-empty %.3f "
+               "prod-ring %.3f mma-data %.3f mma-tmem %.3f mma-ring %.3f mma-issue %.3f "
+               "epi-tfull %.3f epi-fold %.3f epi-emit %.3f (proxy fences %.3f)\n",
+               kernel, grid, tot / grid, sum[PS_PROLOGUE] / tot, sum[PS_PROD_EMPTY] / tot,
+               sum[PS_PROD_RING] / tot, sum[PS_MMA_DATA] / tot, sum[PS_MMA_TMEM] / tot,
+               sum[PS_MMA_RING] / tot, sum[PS_MMA_ISSUE] / tot, sum[PS_EPI_TFULL] / tot,
+               sum[PS_EPI_FOLD] / tot, sum[PS_EPI_EMIT] / tot, sum[PS_EPI_STWAIT] / tot);
+}
+
 static std::atomic<unsigned long long> g_launches{0};
 
 void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }

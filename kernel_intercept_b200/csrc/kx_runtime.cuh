@@ -41,6 +41,16 @@ WorkSlot* work_slot_for(cudaStream_t stream);
 // overwrites the operator's buffer.
 void* scratch_for(cudaStream_t stream, size_t bytes, int slot = 0);
 
+// KX_TMA_STORE=0 makes the tcgen05 epilogues store D with one st.global per
+// element instead of staging it through shared memory for TMA stores.
+inline bool tma_store_disabled() {
+  static const bool off = [] {
+    const char* s = std::getenv("KX_TMA_STORE");
+    return s != nullptr && s[0] == '0';
+  }();
+  return off;
+}
+
 // KX_SPLITK=0 turns split-K off (every output tile then runs its whole K).
 inline bool split_k_disabled() {
   static const bool off = [] {
@@ -99,6 +109,12 @@ bool encode_map(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* 
                 const uint32_t* elem_strides = nullptr);
 
 void set_last_kernel_name(const char* name);
+
+// Pipeline diagnostics of the tcgen05 kernels (KX_PIPE_STATS=1): a zeroed
+// device buffer for GemmParams::pipe_stats (nullptr when off), and a report of
+// the per-role wait fractions to stderr after the launch (synchronises).
+unsigned long long* pipe_stats_begin();
+void pipe_stats_end(unsigned long long* buf, const char* kernel, cudaStream_t stream, int grid);
 
 // Counts one kernel launch of this library (process-wide, read back by
 // kx_launch_count).  Every `<<<...>>>` site calls it just before launching.

@@ -9,8 +9,9 @@
 //    when HP's next kernel plus this BE kernel fit in the GPU's SMs according
 //    to kernel_info.csv, or when the HP queue is empty; otherwise it waits.
 //  * Sharing (replaces the green-context split, src/scheduler.cpp:244-446):
-//    dense BE ops run as persistent kx kernels that read the HP flag (pinned,
-//    device-mapped) before every tile.  The HP worker raises the flag to
+//    dense BE ops run as persistent kx kernels that read the HP flag before
+//    every tile (a device-memory copy of the pinned host flag, updated by an
+//    async copy whenever the flag changes).  The HP worker raises the flag to
 //    be_keep_sms while HP work is queued or in flight; BE CTAs whose index is
 //    at or above it retire at their next tile boundary and the lower ones
 //    finish the op.  With be_keep_sms = 0 the flag is -1: every BE CTA stops
@@ -211,9 +212,23 @@ bool Scheduler::init(int num_clients, const SchedulerConfig& config) {
   }
   hp_flag_host_ = h;
   hp_flag_dev_ = d;
-  int keep = sms / 4;
+  if (ORION_REAL(cudart, cudaMalloc)(reinterpret_cast<void**>(&hp_flag_devmem_), sizeof(int)) !=
+          cudaSuccess ||
+      ORION_REAL(cudart, cudaMemset)(hp_flag_devmem_, 0, sizeof(int)) != cudaSuccess) {
+    LOG_ERROR("cannot allocate the device copy of the HP flag");
+    return false;
+  }
+  {
+    int lo = 0, hi = 0;
+    ORION_REAL(cudart, cudaDeviceGetStreamPriorityRange)(&lo, &hi);
+    ORION_REAL(cudart, cudaStreamCreateWithPriority)(&flag_stream_, cudaStreamNonBlocking, hi);
+  }
+  // 8 SMs: measured on VGG16-HP / GPT-BE, the largest share BE can keep
+  // while HP p99 stays within 1.1x of solo with HP back to back
+  int keep = 8;
   if (const char* s = std::getenv("KX_BE_KEEP_SMS")) keep = std::atoi(s);
   be_keep_sms_.store(std::max(0, std::min(keep, sms)));
+  if (const char* s = std::getenv("KX_HP_HOLD_US")) hp_hold_ns_ = std::max(0LL, std::atoll(s)) * 1000;
   ORION_REAL(cudart, cudaEventCreateWithFlags)(&hp_last_event_, cudaEventDisableTiming);
   g_orion_state.init(num_clients, sms);
   g_orion_state.sm_threshold = config_.sm_threshold;
@@ -333,14 +348,22 @@ bool Scheduler::orion_should_schedule(OperationPtr op, int client_idx) {
   return q && q->empty();
 }
 
+void Scheduler::publish_hp_flag(int value) {
+  hp_flag_host_[0] = value;
+  std::atomic_thread_fence(std::memory_order_seq_cst);
+  // the copy reads the pinned host value when it executes, so the latest
+  // value always reaches the device copy
+  if (hp_flag_devmem_ != nullptr && flag_stream_ != nullptr)
+    ORION_REAL(cudart, cudaMemcpyAsync)(hp_flag_devmem_, const_cast<int*>(&hp_flag_host_[0]),
+                                        sizeof(int), cudaMemcpyHostToDevice, flag_stream_);
+}
+
 void Scheduler::hp_activity_begin() {
   if (isolated_ || hp_flag_host_ == nullptr) return;
+  hp_idle_since_ns_ = 0;
   const int keep = be_keep_sms_.load();
   const int v = keep > 0 ? keep : -1;
-  if (hp_flag_host_[0] != v) {
-    hp_flag_host_[0] = v;
-    std::atomic_thread_fence(std::memory_order_seq_cst);
-  }
+  if (hp_flag_host_[0] != v) publish_hp_flag(v);
 }
 
 void Scheduler::hp_activity_poll() {
@@ -353,7 +376,12 @@ void Scheduler::hp_activity_poll() {
     if (ORION_REAL(cudart, cudaEventQuery)(hp_last_event_) != cudaSuccess) return;
     hp_event_pending_.store(false);
   }
-  hp_flag_host_[0] = 0;
+  // hold the flag a little longer: HP requests issue kernels with host gaps
+  // between them, and a flag that drops in every gap lets BE retake the SMs
+  const int64_t now = mono_ns();
+  if (hp_idle_since_ns_ == 0) hp_idle_since_ns_ = now;
+  if (now - hp_idle_since_ns_ < hp_hold_ns_) return;
+  publish_hp_flag(0);
 }
 
 cudaError_t Scheduler::execute_operation(OperationPtr op, cudaStream_t fallback) {
@@ -368,8 +396,13 @@ cudaError_t Scheduler::execute_operation(OperationPtr op, cudaStream_t fallback)
   if (pol.stream == nullptr) pol.stream = nullptr;  // legacy default stream of the client
   const bool be = c > 0;
   pol.sm_quota = be ? be_quota() : hp_quota();
+  // DEFAULT mode with BE keeping k SMs under HP load: HP kernels take the
+  // other SMs only, so an HP launch never queues behind BE CTAs that are
+  // allowed to finish their op.
+  const int keep = be_keep_sms_.load();
+  if (!be && !isolated_ && keep > 0 && keep < config_.num_sms) pol.sm_quota = config_.num_sms - keep;
   const bool can_stop = be && !isolated_ && be_keep_sms_.load() <= 0;
-  if (be && !isolated_) pol.yield_flag = hp_flag_dev_;
+  if (be && !isolated_) pol.yield_flag = hp_flag_devmem_ ? hp_flag_devmem_ : hp_flag_dev_;
   if (can_stop) {
     hp_flag_host_[1] = -1;
     pol.done_flag = hp_flag_dev_ + 1;
@@ -457,6 +490,13 @@ void Scheduler::run_worker(int client_idx) {
     if (!op) continue;
     cudaError_t err = execute_operation(op, fallback);
     if (err != cudaSuccess) set_last_error(client_idx, err);
+    if (client_idx == 0 && !isolated_ && is_kernel_op(op->type) && !is_dense_op(op->type)) {
+      // HP kernels the interposer only re-issues count as HP activity too
+      cudaStream_t s = op_stream(*op);
+      std::lock_guard<std::mutex> lk(hp_mu_);
+      ORION_REAL(cudart, cudaEventRecord)(hp_last_event_, s ? s : fallback);
+      hp_event_pending_.store(true);
+    }
     if (is_kernel_op(op->type)) {
       std::lock_guard<std::mutex> lk(g_orion_state.mutex);
       if (client_idx < static_cast<int>(g_orion_state.seen.size())) g_orion_state.seen[client_idx]++;
@@ -489,6 +529,8 @@ void Scheduler::join() {
   for (auto& w : workers_)
     if (w.joinable()) w.join();
   workers_.clear();
+  // host copy only: join() also runs from the destructor at process exit,
+  // when CUDA calls may no longer be made
   if (hp_flag_host_) hp_flag_host_[0] = 0;
 }
 
@@ -498,6 +540,15 @@ void Scheduler::reset() {
   if (hp_last_event_) {
     ORION_REAL(cudart, cudaEventDestroy)(hp_last_event_);
     hp_last_event_ = nullptr;
+  }
+  if (flag_stream_) {
+    ORION_REAL(cudart, cudaStreamSynchronize)(flag_stream_);
+    ORION_REAL(cudart, cudaStreamDestroy)(flag_stream_);
+    flag_stream_ = nullptr;
+  }
+  if (hp_flag_devmem_) {
+    ORION_REAL(cudart, cudaFree)(hp_flag_devmem_);
+    hp_flag_devmem_ = nullptr;
   }
   if (hp_flag_host_) {
     kx_host_flags_free(const_cast<int*>(hp_flag_host_));
