@@ -4,7 +4,7 @@ interposer: HP VGG16 inference against BE GPT training.
 
 Workload (one "step" = one HP request):
   HP  = VGG16 inference, fp32, batch 32 x 3x224x224 N(0,1), Kaiming-normal init
-  BE  = training steps of the config-0 GPT (6 layers, d_model 512, 8 heads,
+  BE  = training steps of a GPT (6 layers, d_model 512, 8 heads,
         FFN 2048, vocab 32000), batch 16 x seq 256, AdamW lr 1e-4,
         cross-entropy against uniform random targets
 Both run as PyTorch models in one process under
@@ -275,23 +275,33 @@ def run_kx(args):
 
     kxlib = kx.lib()
 
-    def profiled(tag, fn):
-        """Runs fn() inside a profiling session; returns (fn's result, records)."""
+    def profiled(tag, run):
+        """Runs run(on_start); the profiling session opens in on_start (after
+        both clients' warm-up, so warm-up launches are not in the records) and
+        closes when run returns.  Returns (run's result, records)."""
         path = tempfile.mktemp(prefix="kx_prof_", suffix=".json")
-        orion.orion_start_profiling(tag.encode())
+        opened = []
+
+        def on_start():
+            orion.orion_start_profiling(tag.encode())
+            opened.append(True)
+
         try:
-            res = fn()
+            res = run(on_start)
         finally:
-            orion.orion_end_profiling(path.encode())
-        with open(path) as f:
-            recs = json.load(f).get("kernels", [])
-        os.unlink(path)
+            if opened:
+                orion.orion_end_profiling(path.encode())
+        recs = []
+        if opened:
+            with open(path) as f:
+                recs = json.load(f).get("kernels", [])
+            os.unlink(path)
         return res, recs
 
     # phase 1: HP alone (per-op timing for the solo roofline)
     barrier()
-    (hp_solo, _), solo_recs = profiled("hp_solo", lambda: harness.run_clients(
-        orion, hp_step, be_step, args.steps, args.warmup, with_be=False))
+    (hp_solo, _), solo_recs = profiled("hp_solo", lambda on_start: harness.run_clients(
+        orion, hp_step, be_step, args.steps, args.warmup, with_be=False, on_start=on_start))
     # phase 2: BE alone
     _, be_solo = harness.run_clients(orion, hp_step, be_step, 0, 0, with_hp=False,
                                      be_seconds=args.be_seconds)
@@ -300,8 +310,8 @@ def run_kx(args):
     barrier()
     launches0 = kxlib.kx_launch_count()
     clocks.start()
-    (hp_c, be_c), cont_recs = profiled("contended", lambda: harness.run_clients(
-        orion, hp_step, be_step, args.steps, args.warmup))
+    (hp_c, be_c), cont_recs = profiled("contended", lambda on_start: harness.run_clients(
+        orion, hp_step, be_step, args.steps, args.warmup, on_start=on_start))
     clk = clocks.stop()
     launches = kxlib.kx_launch_count() - launches0
     barrier()

@@ -1,0 +1,146 @@
+"""Single-workload runners for device profiling of the kx kernels.
+
+    python -m kernel_intercept_b200.cases CASE [--reps R]
+
+Each case allocates its inputs once (seeded N(0,1) data), runs one untimed
+launch, then R more (default 1), synchronizes and prints the kernel name the
+last call ran.  The shapes are the ones the HP/BE co-scheduling benchmark
+exercises, chosen so every input is larger than the 126 MB L2 where the
+workload allows it, while the whole case stays within a few GB of device
+memory (small enough for a multi-pass profiler capture):
+
+  conv3_2     VGG16 conv3_2 forward, batch 32, 256 -> 256 channels, 56x56, 3x3
+              pad 1 (x and y 103 MB each)
+  vgg16_convs the 13 VGG16 convolution layers, batch 32, forward, in order
+  gemm_f32    4096^3 fp32 SGEMM (3xTF32 with pre-split operands)
+  gemm_bf16   2048 x 4096 x 2048 bf16 GemmEx (a LLaMA-7B query projection)
+  bn_train    batch-norm training forward, spatial, 32 x 256 x 56 x 56
+  hp_step     one batch-32 VGG16 inference step (the HP client of the
+              benchmark) through the LD_PRELOAD interposer and the scheduler
+"""
+from __future__ import annotations
+
+import argparse
+import os
+import sys
+
+CASES = ("conv3_2", "vgg16_convs", "gemm_f32", "gemm_bf16", "bn_train", "hp_step")
+
+# VGG16 convolution stack: (in channels, out channels, spatial size)
+VGG16_CONVS = [(3, 64, 224), (64, 64, 224), (64, 128, 112), (128, 128, 112),
+               (128, 256, 56), (256, 256, 56), (256, 256, 56), (256, 512, 28),
+               (512, 512, 28), (512, 512, 28), (512, 512, 14), (512, 512, 14),
+               (512, 512, 14)]
+
+
+def _direct(case, reps):
+    """Cases that call the C-ABI directly (no interposer)."""
+    import torch
+
+    from . import kx
+    torch.manual_seed(0)
+    ex = kx.current_exec()
+    dev = "cuda"
+    calls = []
+    if case in ("conv3_2", "vgg16_convs"):
+        layers = [(256, 256, 56)] if case == "conv3_2" else VGG16_CONVS
+        n = 32
+        for c, k, hw in layers:
+            x = torch.randn(n, c, hw, hw, device=dev)
+            w = torch.randn(k, c, 3, 3, device=dev) * (2.0 / (c * 9)) ** 0.5
+            y = torch.empty(n, k, hw, hw, device=dev)
+            d = kx.ConvDesc(n, c, hw, hw, k, 3, 3, 1, 1, 1, 1, 1, 1, 1)
+            calls.append(lambda d=d, x=x, w=w, y=y: kx.conv_fwd(
+                ex, d, 1.0, x.data_ptr(), w.data_ptr(), 0.0, y.data_ptr()))
+    elif case == "gemm_f32":
+        s = 4096
+        a = torch.randn(s, s, device=dev)
+        b = torch.randn(s, s, device=dev)
+        c_ = torch.empty(s, s, device=dev)
+        calls.append(lambda: kx.sgemm(ex, 1, 0, s, s, s, 1.0, a.data_ptr(), s, b.data_ptr(), s,
+                                      0.0, c_.data_ptr(), s))
+    elif case == "gemm_bf16":
+        m, n_, k = 2048, 4096, 2048
+        a = torch.randn(m, k, device=dev, dtype=torch.bfloat16)
+        b = torch.randn(n_, k, device=dev, dtype=torch.bfloat16)
+        c_ = torch.empty(n_, m, device=dev, dtype=torch.bfloat16)
+        calls.append(lambda: kx.gemm_ex(ex, 1, 0, m, n_, k, 1.0, a.data_ptr(), kx.R_16BF, k,
+                                        b.data_ptr(), kx.R_16BF, k, 0.0, c_.data_ptr(),
+                                        kx.R_16BF, m))
+    elif case == "bn_train":
+        n, c, h, w_ = 32, 256, 56, 56
+        x = torch.randn(n, c, h, w_, device=dev)
+        y = torch.empty_like(x)
+        sc = torch.ones(c, device=dev)
+        bi = torch.zeros(c, device=dev)
+        rm = torch.zeros(c, device=dev)
+        rv = torch.ones(c, device=dev)
+        sm = torch.empty(c, device=dev)
+        si = torch.empty(c, device=dev)
+        calls.append(lambda: kx.bn_fwd_training(
+            ex, 1, 1.0, 0.0, n, c, h, w_, x.data_ptr(), y.data_ptr(), sc.data_ptr(),
+            bi.data_ptr(), 0.1, rm.data_ptr(), rv.data_ptr(), 1e-5, sm.data_ptr(), si.data_ptr()))
+    for _ in range(1 + reps):
+        for f in calls:
+            f()
+    torch.cuda.synchronize()
+    return kx.last_kernel_name()
+
+
+def _hp_step(reps):
+    """One untimed and `reps` more batch-32 VGG16 inference steps as the HP
+    client of the scheduler, with every convolution and GEMM captured."""
+    import torch
+
+    from . import harness, kx
+    dev = torch.device("cuda", 0)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cudnn.allow_tf32 = False
+    torch.backends.cudnn.benchmark = False
+    torch.manual_seed(0)
+    orion = harness.Orion()
+    vgg = harness.make_vgg16(dev).eval()
+    img = torch.randn(32, 3, 224, 224, device=dev)
+
+    def step():
+        with torch.no_grad():
+            vgg(img)
+
+    assert orion.orion_init_scheduler(2) == 0, "orion_init_scheduler failed"
+    orion.orion_set_capture(0)
+    step()
+    torch.cuda.synchronize()
+    orion.orion_start_scheduler_thread()
+    orion.orion_set_capture(1)
+    hp, _ = harness.run_clients(orion, step, None, reps, 1, with_be=False)
+    if hp.error is not None:
+        raise hp.error
+    stats = orion.stats(0)
+    orion.orion_set_capture(0)
+    orion.orion_stop_scheduler()
+    if stats["kx_ops"] == 0 or stats["errors"]:
+        raise RuntimeError(f"HP step not captured by the kx kernels: {stats}")
+    return kx.last_kernel_name()
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
+    ap.add_argument("case", choices=CASES)
+    ap.add_argument("--reps", type=int, default=1)
+    args = ap.parse_args(argv)
+    if args.case == "hp_step":
+        from . import harness
+        if not harness.preloaded():
+            env = harness.preload_env({"ORION_LOG_LEVEL": os.environ.get("ORION_LOG_LEVEL",
+                                                                          "WARN")})
+            os.execve(sys.executable, [sys.executable, "-m", "kernel_intercept_b200.cases"]
+                      + sys.argv[1:], env)
+        name = _hp_step(args.reps)
+    else:
+        name = _direct(args.case, args.reps)
+    print("ok", args.case, name, flush=True)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

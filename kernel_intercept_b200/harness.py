@@ -242,7 +242,7 @@ def make_llama(vocab=32000, hidden=2048, heads=16, layers=12, inter=5504, eps=1e
 
 
 def gpt_flops_forward(batch, seq=256, emb=512, layers=6, vocab=32000, ffn=2048):
-    """Captured-GEMM FLOPs of one config-0 GPT forward."""
+    """Captured-GEMM FLOPs of one forward of the 6-layer d512 GPT."""
     tok = batch * seq
     per_layer = (2 * tok * emb * emb * 3          # q, k, v (all heads)
                  + 2 * batch * seq * seq * emb * 2  # scores + att@v (all heads)
@@ -283,16 +283,19 @@ def percentile(xs, q):
 
 def run_clients(orion: Orion | None, hp_step, be_step, hp_steps: int, hp_warmup: int,
                 be_warmup: int = 1, with_be: bool = True, with_hp: bool = True,
-                be_seconds: float | None = None, hp_period_ms: float = 0.0):
+                be_seconds: float | None = None, hp_period_ms: float = 0.0,
+                on_start=None):
     """Runs the HP loop (hp_warmup + hp_steps timed iterations, CUDA events per
     iteration in the HP client's stream order) and, concurrently, the BE loop
     until HP finishes (or for be_seconds when HP is off).  Client identity:
-    HP = 0, BE = 1, registered on each thread as the reference drivers do."""
+    HP = 0, BE = 1, registered on each thread as the reference drivers do.
+    on_start, when given, runs once after both clients finished their warm-up
+    and before either issues a measured step."""
     import torch
 
     hp_res, be_res = ClientResult(), ClientResult()
     stop = threading.Event()
-    ready = threading.Barrier(2 if (with_hp and with_be) else 1)
+    ready = threading.Barrier(2 if (with_hp and with_be) else 1, action=on_start)
 
     def hp_thread():
         try:
