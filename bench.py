@@ -300,8 +300,10 @@ def run_kx(args):
 
     # phase 1: HP alone (per-op timing for the solo roofline)
     barrier()
+    # latency phases run at least 200 HP steps so that p99 is a percentile
+    lat_steps = max(args.steps, 200)
     (hp_solo, _), solo_recs = profiled("hp_solo", lambda on_start: harness.run_clients(
-        orion, hp_step, be_step, args.steps, args.warmup, with_be=False, on_start=on_start))
+        orion, hp_step, be_step, lat_steps, args.warmup, with_be=False, on_start=on_start))
     # phase 2: BE alone
     _, be_solo = harness.run_clients(orion, hp_step, be_step, 0, 0, with_hp=False,
                                      be_seconds=args.be_seconds)
@@ -319,7 +321,7 @@ def run_kx(args):
     # Orion setting in which HP latency vs solo and BE retention are judged
     s50_now = harness.percentile(hp_solo.latencies_ms, 0.5)
     period = s50_now / max(args.hp_load, 1e-3)
-    paced_steps = max(6 * args.steps, 60)  # long enough for a stable BE rate and p99
+    paced_steps = lat_steps
     hp_p, be_p = harness.run_clients(orion, hp_step, be_step, paced_steps, args.warmup,
                                      hp_period_ms=period)
     # phase 5: e2e (host buffers in every HP step), contended
@@ -377,7 +379,8 @@ def run_kx(args):
                    "parallelism": f"placement x{world} (one HP+BE group per GPU, no collective)",
                    "l2": "inputs larger than L2 (VGG16 first-block activations 411 MB)"},
         "hp": {"p50_ms": round(p50, 3), "p99_ms": round(p99, 3), "solo_p50_ms": round(s50, 3),
-               "solo_p99_ms": round(s99, 3), "p99_vs_solo": round(p99 / s99, 4) if s99 else None},
+               "solo_p99_ms": round(s99, 3), "p99_vs_solo": round(p99 / s99, 4) if s99 else None,
+               "steps": args.steps, "solo_steps": lat_steps},
         "paced": {"hp_load": round(args.hp_load, 3), "period_ms": round(period, 3),
                   "hp_steps": paced_steps,
                   "hp_p50_ms": round(harness.percentile(hp_p.latencies_ms, 0.5), 3),

@@ -60,32 +60,43 @@ __global__ void __launch_bounds__(256) stage_nhwc_split(const float* __restrict_
 }
 
 // Taps folded into channels: st[n][p][q][kk], kk = (c*R + r)*S + s < C*R*S,
-// zero up to kf; hi and lo as above.
+// zero up to kf; hi and lo as above.  Block (blockIdx.x, p, n) covers 32
+// output pixels q of row p of image n; lane = kk within a 32-wide chunk, so
+// every store is one 128-byte row segment, and the (c, r, s) decode runs once
+// per chunk instead of once per element.
+constexpr int kFoldQ = 32;
 __global__ void __launch_bounds__(256) stage_folded_split(const float* __restrict__ x,
                                                           float* __restrict__ xh,
                                                           float* __restrict__ xl, ConvShape g,
                                                           int kf) {
-  const size_t total = static_cast<size_t>(g.N) * g.P * g.Q * kf;
-  const int crs = g.C * g.R * g.S;
-  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
-    const int kk = static_cast<int>(i % kf);
-    const size_t pix = i / kf;  // (n, p, q)
-    const int q = static_cast<int>(pix % g.Q);
-    const int p = static_cast<int>((pix / g.Q) % g.P);
-    const int n = static_cast<int>(pix / (static_cast<size_t>(g.Q) * g.P));
-    float v = 0.f;
-    if (kk < crs) {
-      const int c = kk / (g.R * g.S);
-      const int rs = kk - c * g.R * g.S;
-      const int r = rs / g.S, s = rs - (rs / g.S) * g.S;
-      const int h = p * g.sh - g.ph + r * g.dh;
-      const int w = q * g.sw - g.pw + s * g.dw;
-      if (h >= 0 && h < g.H && w >= 0 && w < g.W)
-        v = __ldg(x + ((static_cast<size_t>(n) * g.C + c) * g.H + h) * g.W + w);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int p = blockIdx.y, n = blockIdx.z;
+  const int q0 = blockIdx.x * kFoldQ;
+  const int crs = g.C * g.R * g.S, rs_n = g.R * g.S;
+  const float* xn = x + static_cast<size_t>(n) * g.C * g.H * g.W;
+  const size_t row0 = (static_cast<size_t>(n) * g.P + p) * g.Q;
+  for (int kb = 0; kb < kf; kb += 32) {
+    const int kk = kb + lane;
+    int c = 0, r = 0, sx = 0;
+    bool valid = kk < crs;
+    if (valid) {
+      c = kk / rs_n;
+      const int rs = kk - c * rs_n;
+      r = rs / g.S;
+      sx = rs - r * g.S;
     }
-    xh[i] = v;
-    xl[i] = tf32_lo(v);
+    const int h = p * g.sh - g.ph + r * g.dh;
+    valid = valid && h >= 0 && h < g.H;
+    const float* xr = xn + (static_cast<size_t>(c) * g.H + (valid ? h : 0)) * g.W;
+    for (int i = warp; i < kFoldQ; i += 8) {
+      const int q = q0 + i;
+      if (q >= g.Q) break;
+      const int w = q * g.sw - g.pw + sx * g.dw;
+      const float v = (valid && w >= 0 && w < g.W) ? __ldg(xr + w) : 0.f;
+      const size_t o = (row0 + q) * kf + kk;
+      xh[o] = v;
+      xl[o] = tf32_lo(v);
+    }
   }
 }
 
@@ -94,13 +105,13 @@ __global__ void __launch_bounds__(256) stage_folded_split(const float* __restric
 __global__ void pack_filter(const float* __restrict__ w, float* __restrict__ wp,
                             float* __restrict__ wp_lo, int K, int C, int R, int S, int cp,
                             int folded, int flip) {
+  // 32-bit index math: the caller keeps K * row below 2^31
   const int RS = R * S;
-  const size_t row = folded ? static_cast<size_t>(cp) : static_cast<size_t>(RS) * cp;
-  const size_t total = static_cast<size_t>(K) * row;
-  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
-    const size_t k = i / row;
-    const int rem = static_cast<int>(i - k * row);
+  const int row = folded ? cp : RS * cp;
+  const int total = K * row;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const int k = i / row;
+    const int rem = i - k * row;
     int c, r, s;
     bool valid;
     if (folded) {
@@ -148,38 +159,115 @@ void choose_box(int P, int Q, int sw, int sh, int& wbox, int& hbox) {
   }
 }
 
+// How one forward convolution runs on the tcgen05 kernel.
+struct ConvPlan {
+  int bn;      // channel tile width (64 or 128)
+  bool im2col; // A tiles by im2col-mode TMA (else wbox x hbox boxes)
+  int splits;  // K slices (partials reduced by kx_splitk_reduce)
+  int wbox, hbox;
+};
+
+// KX_CONV_IM2COL: "0" = always box tiles, "1" = im2col whenever the map
+// can express the geometry, unset = by tile waste (see plan_conv).
+int im2col_mode() {
+  const char* v = std::getenv("KX_CONV_IM2COL");
+  if (v == nullptr || v[0] == 0) return -1;
+  return v[0] == '0' ? 0 : 1;
+}
+
+// Bounding-box corners {w, h} of the im2col map for geometry t.
+void im2col_corners(const ConvShape& t, int lower[2], int upper[2]) {
+  lower[0] = -t.pw;
+  lower[1] = -t.ph;
+  upper[0] = t.pw - t.dw * (t.S - 1);
+  upper[1] = t.ph - t.dh * (t.R - 1);
+}
+
+ConvPlan plan_conv(const ConvShape& g, const ConvShape& t, int cp, int sms) {
+  ConvPlan pl{64, false, 1, 0, 0};
+  choose_box(g.P, g.Q, t.sw, t.sh, pl.wbox, pl.hbox);
+  const long long m = static_cast<long long>(g.N) * g.P * g.Q;
+  int lo[2], up[2];
+  im2col_corners(t, lo, up);
+  bool im2col_ok = m + 128 <= 0x7fffffffLL && t.dw * (t.S - 1) < 65536 &&
+                   t.dh * (t.R - 1) < 65536;
+  for (int i = 0; i < 2; ++i)
+    im2col_ok = im2col_ok && lo[i] >= -128 && up[i] >= -128 && up[i] <= 127;
+  const long long box_mt = static_cast<long long>((g.Q + pl.wbox - 1) / pl.wbox) *
+                           ((g.P + pl.hbox - 1) / pl.hbox) * g.N;
+  // Box tiles stream whole-row TMA boxes and keep the MMA fed best; im2col
+  // tiles waste no rows.  Measured on VGG16: boxes win at 87.5% row use
+  // (28/56/112-wide maps), im2col wins at 77% (14x14).
+  const double box_use = static_cast<double>(m) / (static_cast<double>(box_mt) * 128.0);
+  const int mode = im2col_mode();
+  pl.im2col = im2col_ok && (mode == 1 || (mode < 0 && box_use < 0.85));
+  const long long mt = pl.im2col ? (m + 127) / 128 : box_mt;
+  // 128-wide channel tiles when they fill the GPU and waste nothing
+  if (g.K % 128 == 0 && mt * (g.K / 128) >= sms) pl.bn = 128;
+  if (split_k_disabled()) return pl;
+  // Split K when the tiles leave the last wave mostly empty: per slice count
+  // s, waves x k-blocks per slice (a k-block ~0.55 us per CTA at BN 128),
+  // plus writing and reading s fp32 partial planes (~5 TB/s).
+  const long long tiles = mt * ((g.K + pl.bn - 1) / pl.bn);
+  const int num_kb = t.R * t.S * cp / 32;
+  if (tiles >= 4LL * sms) return pl;
+  const double t_kb = 0.55e-6 * pl.bn / 128.0;
+  double best = -1.0;
+  for (int s = 1; s <= 8; ++s) {
+    const int kbps = (num_kb + s - 1) / s;
+    if (s > 1 && kbps < 8) break;
+    const int real = (num_kb + kbps - 1) / kbps;
+    if (real != s) continue;
+    const long long waves = (tiles * s + sms - 1) / sms;
+    double cost = static_cast<double>(waves) * kbps * t_kb;
+    if (s > 1) cost += 2.0 * s * static_cast<double>(m) * g.K * 4.0 / 5e12;
+    if (best < 0 || cost < best) {
+      best = cost;
+      pl.splits = s;
+    }
+  }
+  return pl;
+}
+
 template <int BN>
 int launch_conv_tc(const Exec& e, const ConvShape& g, const ConvShape& t, const float* xh,
                    const float* xl, int cp, const float* wp, const float* wp_lo, float* y,
-                   float alpha, float beta) {
+                   float alpha, float beta, const ConvPlan& pl) {
   // t: the geometry the kernel sees (g itself, or the folded 1x1 problem)
   using Cfg = GemmCfg<BN, Arith::F32x3, false, false>;
   const long long kd = static_cast<long long>(t.R) * t.S * cp;
   const long long pq = static_cast<long long>(g.P) * g.Q;
-  int wbox, hbox;
-  choose_box(g.P, g.Q, t.sw, t.sh, wbox, hbox);
+  const int wbox = pl.wbox, hbox = pl.hbox;
   // A: NHWC staging {cp, W, H, N}
   const uint64_t dims[4] = {static_cast<uint64_t>(cp), static_cast<uint64_t>(t.W),
                             static_cast<uint64_t>(t.H), static_cast<uint64_t>(t.N)};
   const uint64_t strides[3] = {static_cast<uint64_t>(cp) * 4,
                                static_cast<uint64_t>(cp) * t.W * 4,
                                static_cast<uint64_t>(cp) * t.W * t.H * 4};
-  const uint32_t box[4] = {32u, static_cast<uint32_t>(wbox * t.sw),
-                           static_cast<uint32_t>(hbox * t.sh), 1u};
   const uint32_t es[4] = {1u, static_cast<uint32_t>(t.sw), static_cast<uint32_t>(t.sh), 1u};
   CUtensorMap ma, malo, mb, mblo;
-  if (!encode_map(&ma, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, xh, dims, strides, box,
-                  CU_TENSOR_MAP_SWIZZLE_128B, es) ||
-      !encode_map(&malo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, xl, dims, strides, box,
-                  CU_TENSOR_MAP_SWIZZLE_128B, es))
-    return KX_ERR_UNSUPPORTED;
+  if (pl.im2col) {
+    int lo[2], up[2];
+    im2col_corners(t, lo, up);
+    if (!encode_im2col_map(&ma, xh, dims, strides, lo, up, 32, Cfg::BM, es) ||
+        !encode_im2col_map(&malo, xl, dims, strides, lo, up, 32, Cfg::BM, es))
+      return KX_ERR_UNSUPPORTED;
+  } else {
+    const uint32_t box[4] = {32u, static_cast<uint32_t>(wbox * t.sw),
+                             static_cast<uint32_t>(hbox * t.sh), 1u};
+    if (!encode_map(&ma, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, xh, dims, strides, box,
+                    CU_TENSOR_MAP_SWIZZLE_128B, es) ||
+        !encode_map(&malo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, xl, dims, strides, box,
+                    CU_TENSOR_MAP_SWIZZLE_128B, es))
+      return KX_ERR_UNSUPPORTED;
+  }
   if (!encode_map_3d(&mb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, wp, kd, g.K, 1, kd, 0, Cfg::BK, BN) ||
       !encode_map_3d(&mblo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, wp_lo, kd, g.K, 1, kd, 0, Cfg::BK,
                      BN))
     return KX_ERR_UNSUPPORTED;
   GemmParams p;
   std::memset(&p, 0, sizeof(p));
-  p.m = static_cast<int>(pq);
+  p.m = static_cast<int>(pl.im2col ? pq * g.N : pq);
   p.n = g.K;
   p.k = static_cast<int>(kd);
   p.alpha = alpha;
@@ -213,15 +301,31 @@ int launch_conv_tc(const Exec& e, const ConvShape& g, const ConvShape& t, const 
   p.cv_str_w = t.sw;
   p.cv_dil_h = t.dh;
   p.cv_dil_w = t.dw;
-  p.num_mb = p.cv_tiles_w * ((g.P + hbox - 1) / hbox);
+  p.cv_im2col = pl.im2col ? 1 : 0;
+  p.cv_pq = static_cast<int>(pq);
+  p.num_mb = pl.im2col ? (p.m + Cfg::BM - 1) / Cfg::BM
+                       : p.cv_tiles_w * ((g.P + hbox - 1) / hbox);
   p.num_nb = (g.K + BN - 1) / BN;
   p.num_kb = static_cast<int>(kd / Cfg::BK);
-  p.tiles_per_batch = p.num_mb * p.num_nb;
-  const long long tiles = static_cast<long long>(p.tiles_per_batch) * g.N;
-  if (tiles <= 0 || tiles > 0x7fffffffLL) return KX_ERR_UNSUPPORTED;
-  p.num_tiles = static_cast<int>(tiles);
+  const int batch = pl.im2col ? 1 : g.N;
   p.splits = 1;
   p.kb_per_split = p.num_kb;
+  if (pl.splits > 1) {
+    const int kbps = (p.num_kb + pl.splits - 1) / pl.splits;
+    const int splits = (p.num_kb + kbps - 1) / kbps;
+    const size_t ws_bytes = sizeof(float) * static_cast<size_t>(splits) * batch *
+                            static_cast<size_t>(p.m) * p.n;
+    float* ws = static_cast<float*>(scratch_for(e.stream, ws_bytes, 1));
+    if (ws != nullptr) {
+      p.splits = splits;
+      p.kb_per_split = kbps;
+      p.ws = ws;
+    }
+  }
+  p.tiles_per_batch = p.num_mb * p.num_nb * p.splits;
+  const long long tiles = static_cast<long long>(p.tiles_per_batch) * batch;
+  if (tiles <= 0 || tiles > 0x7fffffffLL) return KX_ERR_UNSUPPORTED;
+  p.num_tiles = static_cast<int>(tiles);
   p.a_bcast = 0;
   p.b_bcast = 1;
 
@@ -234,29 +338,44 @@ int launch_conv_tc(const Exec& e, const ConvShape& g, const ConvShape& t, const 
       return KX_ERR_DEVICE;
     attr_set[di.device & 63] = true;
   }
-  // y through TMA stores: {Q, P, K, N} map, per-warp box {min(wbox,32),
-  // 32/min(wbox,32), 32 channels, 1}; needs 16-byte rows (Q % 4 == 0) and a
-  // box at least 16 bytes wide
+  // y through TMA stores (16-byte rows needed).  im2col: {P*Q, K, N} map, a
+  // warp's box {32 pixels, 32 channels, 1} when its rows lie in one image.
+  // Boxes: {Q, P, K, N} map, per-warp box {min(wbox,32), 32/min(wbox,32),
+  // 32 channels, 1}, at least 16 bytes wide.
   CUtensorMap md = ma;
   p.tma_store = 0;
-  if (g.Q % 4 == 0 && wbox >= 4 && !tma_store_disabled()) {
-    const int ww = wbox < 32 ? wbox : 32;
-    const uint64_t ydims[4] = {static_cast<uint64_t>(g.Q), static_cast<uint64_t>(g.P),
-                               static_cast<uint64_t>(g.K), static_cast<uint64_t>(g.N)};
-    const uint64_t ystr[3] = {static_cast<uint64_t>(g.Q) * 4, static_cast<uint64_t>(pq) * 4,
-                              static_cast<uint64_t>(pq) * g.K * 4};
-    const uint32_t ybox[4] = {static_cast<uint32_t>(ww), static_cast<uint32_t>(32 / ww), 32u, 1u};
-    if (encode_map(&md, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, y, ydims, ystr, ybox,
-                   CU_TENSOR_MAP_SWIZZLE_NONE))
-      p.tma_store = 1;
+  if (p.splits == 1 && !tma_store_disabled()) {
+    if (pl.im2col) {
+      if (pq % 4 == 0 && encode_map_3d(&md, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, y, pq, g.K, g.N,
+                                       pq, pq * g.K, 32, 32, CU_TENSOR_MAP_SWIZZLE_NONE))
+        p.tma_store = 1;
+    } else if (g.Q % 4 == 0 && wbox >= 4) {
+      const int ww = wbox < 32 ? wbox : 32;
+      const uint64_t ydims[4] = {static_cast<uint64_t>(g.Q), static_cast<uint64_t>(g.P),
+                                 static_cast<uint64_t>(g.K), static_cast<uint64_t>(g.N)};
+      const uint64_t ystr[3] = {static_cast<uint64_t>(g.Q) * 4, static_cast<uint64_t>(pq) * 4,
+                                static_cast<uint64_t>(pq) * g.K * 4};
+      const uint32_t ybox[4] = {static_cast<uint32_t>(ww), static_cast<uint32_t>(32 / ww), 32u,
+                                1u};
+      if (encode_map(&md, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, y, ydims, ystr, ybox,
+                     CU_TENSOR_MAP_SWIZZLE_NONE))
+        p.tma_store = 1;
+    }
   }
   const int grid = persistent_grid(e, p.num_tiles);
   p.pipe_stats = pipe_stats_begin();
   note_launch();
   kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, e.stream>>>(ma, mb, malo, mblo, md, p);
   pipe_stats_end(p.pipe_stats, "kx_conv_fwd_tc", e.stream, grid);
-  static char name[64];
-  if (name[0] == 0) snprintf(name, sizeof(name), "kx_conv_fwd_tc<bn%d,f32x3>", BN);
+  if (p.splits > 1) {
+    note_launch();
+    kx_splitk_reduce<<<splitk_reduce_grid(p.m, p.n, batch, di.num_sms), 256, 0, e.stream>>>(
+        p, batch);
+  }
+  static char names[2][64];
+  char* name = names[pl.im2col ? 1 : 0];
+  if (name[0] == 0)
+    snprintf(name, 64, "kx_conv_fwd_tc<bn%d,f32x3,%s>", BN, pl.im2col ? "im2col" : "box");
   set_last_kernel_name(name);
   return launch_status();
 }
@@ -294,7 +413,7 @@ int conv_fwd_implicit(const Exec& e, const ConvShape& g, const float* x, const f
   if (t.sw > 8 || t.sh > 8) return KX_ERR_UNSUPPORTED;
   const size_t stage_elems = static_cast<size_t>(t.N) * t.H * t.W * cp;
   const size_t wp_elems = static_cast<size_t>(g.K) * t.R * t.S * cp;
-  if (stage_elems > (1ull << 36) || static_cast<long long>(t.R) * t.S * cp > 0x7fffffffLL ||
+  if (stage_elems > (1ull << 36) || wp_elems >= (1ull << 31) ||
       static_cast<long long>(g.P) * g.Q * g.K > (1LL << 40))
     return KX_ERR_UNSUPPORTED;
   const size_t s_pad = round256(stage_elems), w_pad = round256(wp_elems);
@@ -307,7 +426,9 @@ int conv_fwd_implicit(const Exec& e, const ConvShape& g, const float* x, const f
   float* wp_lo = wp + w_pad;
   note_launch();
   if (folded) {
-    stage_folded_split<<<grid_for(stage_elems), 256, 0, e.stream>>>(x, xh, xl, g, kf);
+    dim3 grid((g.Q + kFoldQ - 1) / kFoldQ, g.P, g.N);
+    if (grid.y > 65535 || grid.z > 65535) return KX_ERR_UNSUPPORTED;
+    stage_folded_split<<<grid, 256, 0, e.stream>>>(x, xh, xl, g, kf);
   } else {
     const int hw = g.H * g.W;
     dim3 grid((hw + 31) / 32, cp / 32, g.N);
@@ -318,15 +439,9 @@ int conv_fwd_implicit(const Exec& e, const ConvShape& g, const float* x, const f
   pack_filter<<<grid_for(wp_elems), 256, 0, e.stream>>>(w, wp, wp_lo, g.K, g.C, g.R, g.S, cp,
                                                         folded ? 1 : 0, g.flip ? 1 : 0);
   if (launch_status() != KX_OK) return KX_ERR_DEVICE;
-  // 128-wide channel tiles when they fill the GPU and waste nothing
-  const int sms = persistent_grid(e, 1 << 30);
-  int wbox, hbox;
-  choose_box(g.P, g.Q, t.sw, t.sh, wbox, hbox);
-  const long long mtiles =
-      static_cast<long long>((g.Q + wbox - 1) / wbox) * ((g.P + hbox - 1) / hbox) * g.N;
-  if (g.K % 128 == 0 && mtiles * (g.K / 128) >= sms)
-    return launch_conv_tc<128>(e, g, t, xh, xl, cp, wp, wp_lo, y, alpha, beta);
-  return launch_conv_tc<64>(e, g, t, xh, xl, cp, wp, wp_lo, y, alpha, beta);
+  const ConvPlan pl = plan_conv(g, t, cp, persistent_grid(e, 1 << 30));
+  if (pl.bn == 128) return launch_conv_tc<128>(e, g, t, xh, xl, cp, wp, wp_lo, y, alpha, beta, pl);
+  return launch_conv_tc<64>(e, g, t, xh, xl, cp, wp, wp_lo, y, alpha, beta, pl);
 }
 
 }  // namespace kx

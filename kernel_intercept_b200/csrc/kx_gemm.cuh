@@ -95,12 +95,18 @@ struct GemmParams {
   // across a row); batch = image; D is NCHW (ld = P*Q).
   int cv_p, cv_q, cv_wbox, cv_hbox, cv_tiles_w, cv_s, cv_cb;
   int cv_pad_h, cv_pad_w, cv_str_h, cv_str_w, cv_dil_h, cv_dil_w;
+  // cv_im2col = 1: the A operand comes by im2col-mode TMA instead: M runs
+  // over all N*P*Q output pixels (batch 1), an A tile is 128 consecutive
+  // output pixels whatever row or image they fall in, and output row f is
+  // pixel f % cv_pq of image f / cv_pq (D offset image * strideD + pixel).
+  int cv_im2col, cv_pq;
   // Pipeline diagnostics (nullable): per CTA kPipeStats clock64 counters of
   // the time each role spends waiting (see PipeStat).
   unsigned long long* pipe_stats;
   // 1: the epilogue writes D through shared memory and TMA stores (map tmD:
-  // {m, n, batch} for GEMMs, {Q, P, K, N} for convolutions); 0: one st.global
-  // per element (unaligned D, split-K partials).
+  // {m, n, batch} for GEMMs, {Q, P, K, N} for box-tiled convolutions,
+  // {P*Q, K, N} for im2col convolutions); 0: one st.global per element
+  // (unaligned D, split-K partials).
   int tma_store;
 };
 
@@ -246,28 +252,51 @@ KX_DEV void tile_k_range(int tile, const GemmParams& p, int& kb0, int& nkb) {
 // epilogue.  Runs after the GEMM kernel on the same stream; does nothing when
 // that launch stopped early (yield or tile budget), in which case the
 // relaunch that completes the tiles is followed by another reduce.
+// Work unit = 1024 consecutive rows of one column of one batch entry, so the
+// index decode runs once per unit and every access is row-contiguous.
+constexpr int kReduceRows = 1024;
+
+// Grid of kx_splitk_reduce: one block per work unit, at most 8 per SM.
+inline int splitk_reduce_grid(int m, int n, int batch, int sms) {
+  const long long units = static_cast<long long>((m + kReduceRows - 1) / kReduceRows) * n * batch;
+  const long long cap = 8LL * sms;
+  return static_cast<int>(units < 1 ? 1 : (units > cap ? cap : units));
+}
+
 static __global__ void __launch_bounds__(256) kx_splitk_reduce(const GemmParams p, int batch) {
   if (p.work->status != 1) return;
   const float alpha = p.alpha_dev ? *p.alpha_dev : p.alpha;
   const float beta = p.beta_dev ? *p.beta_dev : p.beta;
   const long long mn = static_cast<long long>(p.m) * p.n;
-  const long long total = mn * batch;
-  for (long long e = blockIdx.x * 256LL + threadIdx.x; e < total;
-       e += static_cast<long long>(gridDim.x) * 256) {
-    const long long b = e / mn;
-    const long long r = e - b * mn;
-    const int col = static_cast<int>(r / p.m);
-    const int row = static_cast<int>(r - static_cast<long long>(col) * p.m);
-    const float* src = p.ws + b * p.splits * mn + r;
-    float acc = 0.f;
-    for (int s = 0; s < p.splits; ++s) acc += src[s * mn];
-    float o = alpha * acc;
-    if (beta != 0.f)
-      o += beta * load_scalar(p.C, p.c_type, b * p.strideC + static_cast<long long>(col) * p.ldc + row);
-    if (p.bias != nullptr) o += load_scalar(p.bias, p.bias_type, row);
-    if (p.relu) o = fmaxf(o, 0.f);
-    if (p.gelu) o = gelu_tanh(o);
-    store_scalar(p.D, p.d_type, b * p.strideD + static_cast<long long>(col) * p.ldd + row, o);
+  const int chunks = (p.m + kReduceRows - 1) / kReduceRows;
+  const long long units = static_cast<long long>(chunks) * p.n * batch;
+  for (long long u = blockIdx.x; u < units; u += gridDim.x) {
+    const long long bc = u / chunks;
+    const int chunk = static_cast<int>(u - bc * chunks);
+    const long long b = bc / p.n;
+    const int col = static_cast<int>(bc - b * p.n);
+    const float* src = p.ws + b * p.splits * mn + static_cast<long long>(col) * p.m;
+    const int r_end = min(p.m, (chunk + 1) * kReduceRows);
+    for (int row = chunk * kReduceRows + threadIdx.x; row < r_end; row += 256) {
+      float acc = 0.f;
+      for (int s = 0; s < p.splits; ++s) acc += src[s * mn + row];
+      float o = alpha * acc;
+      // im2col convolution: row = image * P*Q + pixel
+      long long cb = b * p.strideC, db = b * p.strideD;
+      int pix = row;
+      if (p.cv_im2col) {
+        const int img = row / p.cv_pq;
+        pix = row - img * p.cv_pq;
+        cb = static_cast<long long>(img) * p.strideC;
+        db = static_cast<long long>(img) * p.strideD;
+      }
+      if (beta != 0.f)
+        o += beta * load_scalar(p.C, p.c_type, cb + static_cast<long long>(col) * p.ldc + pix);
+      if (p.bias != nullptr) o += load_scalar(p.bias, p.bias_type, row);
+      if (p.relu) o = fmaxf(o, 0.f);
+      if (p.gelu) o = gelu_tanh(o);
+      store_scalar(p.D, p.d_type, db + static_cast<long long>(col) * p.ldd + pix, o);
+    }
   }
 }
 
@@ -283,6 +312,7 @@ __global__ void __launch_bounds__(256, 1)
                       const __grid_constant__ CUtensorMap tmD, const GemmParams p) {
   static_assert(!CONV || (Cfg::AR == Arith::F32x3 && !Cfg::A_MN),
                 "implicit convolution: 3xTF32 with a K-major A tile");
+  const long long t_start = clock64();  // CTA lifetime starts here
   constexpr int S = Cfg::STAGES;
   constexpr int R = Cfg::RING;
   // in-kernel 3xTF32 split (warps 2-3) unless the low parts come by TMA
@@ -340,7 +370,6 @@ __global__ void __launch_bounds__(256, 1)
   const long long t_ready = clock64();
 
   WaitCtl wc{&sb->abort_flag, p.err_word, p.timeout_ns};
-  const long long t_start = clock64();
   unsigned long long st_a = 0, st_b = 0, st_c = 0, st_d = 0, st_e = 0;  // per-role counters
   const bool stats = p.pipe_stats != nullptr;
 
@@ -393,6 +422,19 @@ __global__ void __launch_bounds__(256, 1)
               const int c0 = (kb - tap * p.cv_cb) * 32;
               const int rr = tap / p.cv_s;
               const int ss = tap - rr * p.cv_s;
+              if (p.cv_im2col) {
+                // first output pixel of the tile -> its filter-window corner
+                const int f0 = mb * Cfg::BM;
+                const int img = f0 / p.cv_pq;
+                const int rem = f0 - img * p.cv_pq;
+                const int oh = rem / p.cv_q;
+                const int ow = rem - oh * p.cv_q;
+                tma_load_4d_im2col(sa, map, fb, c0, ow * p.cv_str_w - p.cv_pad_w,
+                                   oh * p.cv_str_h - p.cv_pad_h, img,
+                                   static_cast<uint16_t>(ss * p.cv_dil_w),
+                                   static_cast<uint16_t>(rr * p.cv_dil_h));
+                return;
+              }
               const int th = mb / p.cv_tiles_w;
               const int tw = mb - th * p.cv_tiles_w;
               const int w0 = tw * p.cv_wbox * p.cv_str_w - p.cv_pad_w + ss * p.cv_dil_w;
@@ -575,19 +617,35 @@ __global__ void __launch_bounds__(256, 1)
       const int nseg = Cfg::PROMOTE ? (nkb + Cfg::SEG - 1) / Cfg::SEG : 1;
       int row = mb * Cfg::BM + q * 32 + static_cast<int>(lane);
       bool row_ok = row < p.m;
+      size_t d_base = static_cast<size_t>(b) * p.strideD + row;
+      size_t c_base = static_cast<size_t>(b) * p.strideC + row;
+      // im2col convolution: this warp's TMA store covers one image
+      bool warp_tma = use_tma_store;
+      int st_img = 0, st_pix = 0;
       if constexpr (CONV) {
-        // tile row i = output pixel (th*hbox + i / wbox, tw*wbox + i % wbox)
-        const int i = q * 32 + static_cast<int>(lane);
-        const int th = mb / p.cv_tiles_w;
-        const int tw = mb - th * p.cv_tiles_w;
-        const int op = th * p.cv_hbox + i / p.cv_wbox;
-        const int oq = tw * p.cv_wbox + (i - (i / p.cv_wbox) * p.cv_wbox);
-        row_ok = op < p.cv_p && oq < p.cv_q;
-        row = op * p.cv_q + oq;
+        if (p.cv_im2col) {
+          const int img = row / p.cv_pq;
+          const int pix = row - img * p.cv_pq;
+          d_base = static_cast<size_t>(img) * p.strideD + pix;
+          c_base = static_cast<size_t>(img) * p.strideC + pix;
+          const int f0 = mb * Cfg::BM + q * 32;
+          st_img = f0 / p.cv_pq;
+          st_pix = f0 - st_img * p.cv_pq;
+          warp_tma = use_tma_store && f0 < p.m && (f0 + 31) / p.cv_pq == st_img;
+        } else {
+          // tile row i = output pixel (th*hbox + i / wbox, tw*wbox + i % wbox)
+          const int i = q * 32 + static_cast<int>(lane);
+          const int th = mb / p.cv_tiles_w;
+          const int tw = mb - th * p.cv_tiles_w;
+          const int op = th * p.cv_hbox + i / p.cv_wbox;
+          const int oq = tw * p.cv_wbox + (i - (i / p.cv_wbox) * p.cv_wbox);
+          row_ok = op < p.cv_p && oq < p.cv_q;
+          row = op * p.cv_q + oq;
+          d_base = static_cast<size_t>(b) * p.strideD + row;
+          c_base = static_cast<size_t>(b) * p.strideC + row;
+        }
       }
       const float bias_v = (p.bias != nullptr && row_ok && !split) ? load_scalar(p.bias, p.bias_type, row) : 0.f;
-      const size_t d_base = static_cast<size_t>(b) * p.strideD + row;
-      const size_t c_base = static_cast<size_t>(b) * p.strideC + row;
       // split-K slice: raw fp32 partial, column-major with ld m
       float* ws_tile = split ? p.ws + (static_cast<size_t>(b) * p.splits + ks) *
                                           static_cast<size_t>(p.m) * p.n + row
@@ -667,12 +725,16 @@ __global__ void __launch_bounds__(256, 1)
         __syncwarp();
         if (lane == 0) {
           if constexpr (CONV) {
-            // warp q holds tile rows 32q .. 32q+31 = a {min(wbox,32), 32/min(wbox,32)} box
-            const int th = mb / p.cv_tiles_w;
-            const int tw = mb - th * p.cv_tiles_w;
-            const int i0 = q * 32;
-            tma_store_4d(&tmD, smem_addr(buf), tw * p.cv_wbox + i0 % p.cv_wbox,
-                         th * p.cv_hbox + i0 / p.cv_wbox, col0, b);
+            if (p.cv_im2col) {
+              tma_store_3d(&tmD, smem_addr(buf), st_pix, col0, st_img);
+            } else {
+              // warp q holds tile rows 32q .. 32q+31 = a {min(wbox,32), 32/min(wbox,32)} box
+              const int th = mb / p.cv_tiles_w;
+              const int tw = mb - th * p.cv_tiles_w;
+              const int i0 = q * 32;
+              tma_store_4d(&tmD, smem_addr(buf), tw * p.cv_wbox + i0 % p.cv_wbox,
+                           th * p.cv_hbox + i0 / p.cv_wbox, col0, b);
+            }
           } else {
             tma_store_3d(&tmD, smem_addr(buf), mb * Cfg::BM + q * 32, col0, b);
           }
@@ -709,7 +771,7 @@ __global__ void __launch_bounds__(256, 1)
         }
         if (!ok) break;
         const long long t_emit = stats ? clock64() : 0;
-        if (use_tma_store) {
+        if (warp_tma) {
 #pragma unroll
           for (int c = 0; c < Cfg::BN / 32; ++c) emit_tma(c * 32, acc[c]);
         } else {
@@ -733,7 +795,7 @@ __global__ void __launch_bounds__(256, 1)
           float f[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]);
-          if (use_tma_store)
+          if (warp_tma)
             emit_tma(c0, f);
           else
             emit(c0, f);

@@ -128,12 +128,9 @@ int launch_gemm_tc(const Exec& e, const TcProblem& pr, GemmParams p) {
   kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, e.stream>>>(ma, mb, malo, mblo, md, p);
   pipe_stats_end(p.pipe_stats, "kx_gemm_tc", e.stream, grid);
   if (p.splits > 1) {
-    const long long total = static_cast<long long>(pr.m) * pr.n * pr.batch;
-    long long rgrid = (total + 255) / 256;
-    const long long rcap = 8LL * device_info().num_sms;
-    if (rgrid > rcap) rgrid = rcap;
     note_launch();
-    kx_splitk_reduce<<<static_cast<int>(rgrid), 256, 0, e.stream>>>(p, pr.batch);
+    kx_splitk_reduce<<<splitk_reduce_grid(pr.m, pr.n, pr.batch, device_info().num_sms), 256, 0,
+                       e.stream>>>(p, pr.batch);
   }
   static char name[96];
   if (name[0] == 0)

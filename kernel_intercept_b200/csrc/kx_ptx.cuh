@@ -120,6 +120,20 @@ KX_DEV void tma_load_4d(uint32_t dst, const void* map, uint32_t bar, int c0, int
       : "memory");
 }
 
+// im2col-mode 4-D load {c, w, h, n}: the map's pixelsPerColumn consecutive
+// output positions starting at input coordinate (w, h) of image n, walked W,
+// then H, then N inside the map's bounding box, each shifted by the filter
+// tap offsets (off_w, off_h); channelsPerPixel channels from c per position.
+KX_DEV void tma_load_4d_im2col(uint32_t dst, const void* map, uint32_t bar, int c, int w, int h,
+                               int n, uint16_t off_w, uint16_t off_h) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.im2col.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6], {%7, %8};" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c), "r"(w), "r"(h), "r"(n), "r"(bar),
+      "h"(off_w), "h"(off_h)
+      : "memory");
+}
+
 // Make generic-proxy shared-memory writes visible to the async proxy
 // (tensor core operand reads).
 KX_DEV void fence_proxy_async_smem() {

@@ -47,6 +47,29 @@ EncodeTiledFn encode_fn() {
   return g_encode;
 }
 
+using EncodeIm2colFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                    const cuuint64_t*, const cuuint64_t*, const int*,
+                                    const int*, cuuint32_t, cuuint32_t, const cuuint32_t*,
+                                    CUtensorMapInterleave, CUtensorMapSwizzle,
+                                    CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+EncodeIm2colFn g_encode_im2col = nullptr;
+bool g_encode_im2col_looked_up = false;
+
+EncodeIm2colFn encode_im2col_fn() {
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_encode_im2col_looked_up) {
+    g_encode_im2col_looked_up = true;
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeIm2col", &fn, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess) {
+      g_encode_im2col = reinterpret_cast<EncodeIm2colFn>(fn);
+    }
+  }
+  return g_encode_im2col;
+}
+
 }  // namespace
 
 const DeviceInfo& device_info() {
@@ -168,6 +191,36 @@ bool encode_map(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* 
   CUresult r = fn(map, dt, static_cast<cuuint32_t>(rank), const_cast<void*>(base), d, s, b, es,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+bool encode_im2col_map(CUtensorMap* map, const void* base, const uint64_t* dims,
+                       const uint64_t* strides_bytes, const int* lower, const int* upper,
+                       uint32_t channels, uint32_t pixels, const uint32_t* elem_strides) {
+  EncodeIm2colFn fn = encode_im2col_fn();
+  if (fn == nullptr) return false;
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0) return false;
+  if (channels == 0 || channels * 4 > 128 || pixels == 0 || pixels > 1024) return false;
+  cuuint64_t d[4];
+  cuuint64_t s[3];
+  cuuint32_t es[4];
+  for (int i = 0; i < 4; ++i) {
+    if (dims[i] == 0 || dims[i] > (1ull << 32)) return false;
+    if (elem_strides[i] == 0 || elem_strides[i] > 8) return false;
+    d[i] = dims[i];
+    es[i] = elem_strides[i];
+  }
+  for (int i = 0; i < 3; ++i) {
+    if ((strides_bytes[i] & 15u) != 0 || strides_bytes[i] >= (1ull << 40)) return false;
+    s[i] = strides_bytes[i];
+  }
+  for (int i = 0; i < 2; ++i)
+    if (lower[i] < -128 || lower[i] > 127 || upper[i] < -128 || upper[i] > 127) return false;
+  std::memset(map, 0, sizeof(CUtensorMap));
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<void*>(base), d, s, lower,
+                  upper, channels, pixels, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 

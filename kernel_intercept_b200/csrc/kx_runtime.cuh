@@ -108,6 +108,16 @@ bool encode_map(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* 
                 CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B,
                 const uint32_t* elem_strides = nullptr);
 
+// im2col map of a 4-D NHWC tensor {C, W, H, N} (dims in elements, strides in
+// bytes) for cp.async.bulk.tensor ... .im2col: each load brings `pixels`
+// consecutive filter-window positions x `channels` channels.  lower / upper:
+// bounding-box corner offsets {w, h} (lower = -pad, upper = pad - dil*(taps-1)),
+// each within [-128, 127]; elem_strides {1, stride_w, stride_h, 1}.  128-byte
+// swizzle, zero OOB fill.  Returns false when the driver rejects the geometry.
+bool encode_im2col_map(CUtensorMap* map, const void* base, const uint64_t* dims,
+                       const uint64_t* strides_bytes, const int* lower, const int* upper,
+                       uint32_t channels, uint32_t pixels, const uint32_t* elem_strides);
+
 void set_last_kernel_name(const char* name);
 
 // Pipeline diagnostics of the tcgen05 kernels (KX_PIPE_STATS=1): a zeroed

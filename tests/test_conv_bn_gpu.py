@@ -1,5 +1,7 @@
 """GPU parity of the kx convolution and batch-norm entry points against the
 CPU oracle (fp32: normwise relative error <= 1e-5)."""
+import os
+
 import numpy as np
 import pytest
 
@@ -64,6 +66,10 @@ IMPLICIT_CASES = [
     (2, 64, 28, 28, 128, 3, 3, (1, 1), (2, 2), (1, 1), True),   # stride 2 (TMA element strides)
     (2, 32, 20, 22, 64, 3, 3, (2, 2), (1, 1), (2, 2), True),    # dilated taps
     (4, 3, 64, 64, 64, 3, 3, (1, 1), (1, 1), (1, 1), True),     # C = 3: taps folded into K
+    (3, 64, 14, 14, 128, 3, 3, (1, 1), (1, 1), (1, 1), True),   # 128-pixel tiles across images
+    (4, 32, 7, 7, 64, 3, 3, (1, 1), (1, 1), (1, 1), True),      # P*Q = 49: per-element stores
+    (2, 48, 21, 26, 96, 3, 5, (1, 2), (1, 2), (1, 1), True),    # R != S, pad_h != pad_w
+    (8, 256, 14, 14, 256, 3, 3, (1, 1), (1, 1), (1, 1), True),  # split K (4 slices)
 ]
 
 
@@ -83,8 +89,22 @@ def test_conv_fwd_implicit_gemm(cuda, case):
     dx, dw, dy = _dev(x), _dev(w), _dev(y0)
     kx.conv_fwd(kx.current_exec(), kd, 0.5, dx.data_ptr(), dw.data_ptr(), -0.25, dy.data_ptr())
     torch.cuda.synchronize()
-    assert kx.last_kernel_name().startswith("kx_conv_fwd_tc<")
+    name = kx.last_kernel_name()
+    assert name.startswith("kx_conv_fwd_tc<")
+    mode = os.environ.get("KX_CONV_IM2COL")
+    if mode is not None:
+        assert ("box>" if mode == "0" else "im2col>") in name
     assert o.normwise_rel_err(dy.cpu().numpy(), ref) <= TOL_F32
+
+
+@pytest.mark.parametrize("mode", ["0", "1"])
+@pytest.mark.parametrize("case", IMPLICIT_CASES)
+def test_conv_fwd_tile_modes(cuda, case, mode, monkeypatch):
+    """Both A-tile forms of the kernel on every case: 4-D TMA boxes of whole
+    output rows (KX_CONV_IM2COL=0) and im2col-mode loads of 128 consecutive
+    output pixels (KX_CONV_IM2COL=1)."""
+    monkeypatch.setenv("KX_CONV_IM2COL", mode)
+    test_conv_fwd_implicit_gemm(cuda, case)
 
 
 @pytest.mark.parametrize("case", CONV_CASES)
