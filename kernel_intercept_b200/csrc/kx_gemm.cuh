@@ -154,7 +154,10 @@ struct GemmCfg {
   static constexpr int STAGES_RAW = (192 * 1024) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
   static constexpr int RING = 4;  // depth of the tile-id broadcast ring
-  static constexpr int TMEM_COLS = (2 * BN) <= 32 ? 32 : (2 * BN) <= 64 ? 64 : (2 * BN) <= 128 ? 128 : (2 * BN) <= 256 ? 256 : 512;
+  // TMEM columns of one accumulator buffer.  3xTF32 keeps two BN-wide halves:
+  // [0, BN) = hi*hi + lo*hi and [BN, 2BN) = hi*lo (see the MMA issuer).
+  static constexpr int ACC_COLS = SPLIT ? 2 * BN : BN;
+  static constexpr int TMEM_COLS = (2 * ACC_COLS) <= 32 ? 32 : (2 * ACC_COLS) <= 64 ? 64 : (2 * ACC_COLS) <= 128 ? 128 : (2 * ACC_COLS) <= 256 ? 256 : 512;
   static constexpr int THREADS = 256;
   static constexpr int NUM_CONS = 1 + 4;  // ring consumers: MMA issuer + epilogue warps
   // 3xTF32: the tensor core's fp32 accumulation does not round to nearest, so
@@ -178,6 +181,8 @@ struct GemmCfg {
   static_assert(!PROMOTE || BN <= 128, "3xTF32 keeps a BN-wide fp32 accumulator per thread");
   static constexpr uint32_t FMT = (AR == Arith::BF16) ? 1u : (AR == Arith::F16) ? 0u : 2u;
   static constexpr uint32_t IDESC = make_idesc(FMT, A_MN, B_MN, BM, BN);
+  // 3xTF32: A_hi x [B_hi; B_lo] as one N = 2*BN product
+  static constexpr uint32_t IDESC2 = make_idesc(FMT, A_MN, B_MN, BM, SPLIT ? 2 * BN : BN);
   // epilogue staging (4 warps x 2 buffers of 32 x 32 fp32) after the stages,
   // then the barrier block
   static constexpr int EPI_OFF = STAGES * STAGE_BYTES;
@@ -251,53 +256,60 @@ KX_DEV void tile_k_range(int tile, const GemmParams& p, int& kb0, int& nkb) {
 // Sums the split-K partials of every output element and applies the
 // epilogue.  Runs after the GEMM kernel on the same stream; does nothing when
 // that launch stopped early (yield or tile budget), in which case the
-// relaunch that completes the tiles is followed by another reduce.
-// Work unit = 1024 consecutive rows of one column of one batch entry, so the
-// index decode runs once per unit and every access is row-contiguous.
-constexpr int kReduceRows = 1024;
-
-// Grid of kx_splitk_reduce: one block per work unit, at most 8 per SM.
-inline int splitk_reduce_grid(int m, int n, int batch, int sms) {
-  const long long units = static_cast<long long>((m + kReduceRows - 1) / kReduceRows) * n * batch;
-  const long long cap = 8LL * sms;
-  return static_cast<int>(units < 1 ? 1 : (units > cap ? cap : units));
+// relaunch that completes the tiles is followed by another reduce.  One
+// thread per output element (column-major: consecutive threads take
+// consecutive rows, so partial reads and output writes coalesce); I is the
+// index type, 32-bit whenever the batch of planes has fewer than 2^31
+// elements (integer division is the costliest part of the index decode).
+template <class I>
+KX_DEV void splitk_reduce_body(const GemmParams& p, int batch) {
+  const float alpha = p.alpha_dev ? *p.alpha_dev : p.alpha;
+  const float beta = p.beta_dev ? *p.beta_dev : p.beta;
+  const I m = static_cast<I>(p.m);
+  const I mn = m * static_cast<I>(p.n);
+  const I total = mn * static_cast<I>(batch);
+  for (I e = static_cast<I>(blockIdx.x) * 256 + threadIdx.x; e < total;
+       e += static_cast<I>(gridDim.x) * 256) {
+    const I b = e / mn;
+    const I r = e - b * mn;
+    const I col = r / m;
+    const I row = r - col * m;
+    const float* src = p.ws + static_cast<long long>(b) * p.splits * mn + r;
+    float acc = 0.f;
+    for (int s = 0; s < p.splits; ++s) acc += src[static_cast<long long>(s) * mn];
+    float o = alpha * acc;
+    // im2col convolution: row = image * P*Q + pixel
+    long long cb = static_cast<long long>(b) * p.strideC, db = static_cast<long long>(b) * p.strideD;
+    long long pix = row;
+    if (p.cv_im2col) {
+      const I img = row / static_cast<I>(p.cv_pq);
+      pix = row - img * static_cast<I>(p.cv_pq);
+      cb = static_cast<long long>(img) * p.strideC;
+      db = static_cast<long long>(img) * p.strideD;
+    }
+    if (beta != 0.f)
+      o += beta * load_scalar(p.C, p.c_type, cb + static_cast<long long>(col) * p.ldc + pix);
+    if (p.bias != nullptr) o += load_scalar(p.bias, p.bias_type, static_cast<size_t>(row));
+    if (p.relu) o = fmaxf(o, 0.f);
+    if (p.gelu) o = gelu_tanh(o);
+    store_scalar(p.D, p.d_type, db + static_cast<long long>(col) * p.ldd + pix, o);
+  }
 }
 
 static __global__ void __launch_bounds__(256) kx_splitk_reduce(const GemmParams p, int batch) {
   if (p.work->status != 1) return;
-  const float alpha = p.alpha_dev ? *p.alpha_dev : p.alpha;
-  const float beta = p.beta_dev ? *p.beta_dev : p.beta;
-  const long long mn = static_cast<long long>(p.m) * p.n;
-  const int chunks = (p.m + kReduceRows - 1) / kReduceRows;
-  const long long units = static_cast<long long>(chunks) * p.n * batch;
-  for (long long u = blockIdx.x; u < units; u += gridDim.x) {
-    const long long bc = u / chunks;
-    const int chunk = static_cast<int>(u - bc * chunks);
-    const long long b = bc / p.n;
-    const int col = static_cast<int>(bc - b * p.n);
-    const float* src = p.ws + b * p.splits * mn + static_cast<long long>(col) * p.m;
-    const int r_end = min(p.m, (chunk + 1) * kReduceRows);
-    for (int row = chunk * kReduceRows + threadIdx.x; row < r_end; row += 256) {
-      float acc = 0.f;
-      for (int s = 0; s < p.splits; ++s) acc += src[s * mn + row];
-      float o = alpha * acc;
-      // im2col convolution: row = image * P*Q + pixel
-      long long cb = b * p.strideC, db = b * p.strideD;
-      int pix = row;
-      if (p.cv_im2col) {
-        const int img = row / p.cv_pq;
-        pix = row - img * p.cv_pq;
-        cb = static_cast<long long>(img) * p.strideC;
-        db = static_cast<long long>(img) * p.strideD;
-      }
-      if (beta != 0.f)
-        o += beta * load_scalar(p.C, p.c_type, cb + static_cast<long long>(col) * p.ldc + pix);
-      if (p.bias != nullptr) o += load_scalar(p.bias, p.bias_type, row);
-      if (p.relu) o = fmaxf(o, 0.f);
-      if (p.gelu) o = gelu_tanh(o);
-      store_scalar(p.D, p.d_type, db + static_cast<long long>(col) * p.ldd + pix, o);
-    }
-  }
+  const long long total = static_cast<long long>(p.m) * p.n * batch;
+  if (total + 256LL * gridDim.x < (1LL << 31))
+    splitk_reduce_body<int>(p, batch);
+  else
+    splitk_reduce_body<long long>(p, batch);
+}
+
+// Grid of kx_splitk_reduce: one thread per element, at most 8 blocks per SM.
+inline int splitk_reduce_grid(int m, int n, int batch, int sms) {
+  const long long blocks = (static_cast<long long>(m) * n * batch + 255) / 256;
+  const long long cap = 8LL * sms;
+  return static_cast<int>(blocks < 1 ? 1 : (blocks > cap ? cap : blocks));
 }
 
 // CONV = true: implicit-GEMM convolution (see GemmParams::cv_*): the A tile
@@ -326,11 +338,15 @@ __global__ void __launch_bounds__(256, 1)
   const int warp = threadIdx.x >> 5;
   const uint32_t lane = threadIdx.x & 31;
 
+  // stage layout [A | B] (one operand set) or [A | A_lo | B | B_lo] (3xTF32:
+  // B_lo directly after B, so that B_hi and B_lo read as one 2*BN-row operand)
   auto stageA = [&](uint32_t s) { return smem + s * Cfg::STAGE_BYTES; };
-  auto stageB = [&](uint32_t s) { return smem + s * Cfg::STAGE_BYTES + Cfg::A_BYTES; };
-  auto stageAlo = [&](uint32_t s) { return smem + s * Cfg::STAGE_BYTES + Cfg::LOAD_BYTES; };
+  auto stageAlo = [&](uint32_t s) { return smem + s * Cfg::STAGE_BYTES + Cfg::A_BYTES; };
+  auto stageB = [&](uint32_t s) {
+    return smem + s * Cfg::STAGE_BYTES + (Cfg::SPLIT ? 2 : 1) * Cfg::A_BYTES;
+  };
   auto stageBlo = [&](uint32_t s) {
-    return smem + s * Cfg::STAGE_BYTES + Cfg::LOAD_BYTES + Cfg::A_BYTES;
+    return smem + s * Cfg::STAGE_BYTES + 2 * Cfg::A_BYTES + Cfg::B_BYTES;
   };
 
   if (threadIdx.x == 0) {
@@ -501,7 +517,7 @@ __global__ void __launch_bounds__(256, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t d_tmem = tmem + a * Cfg::BN;
+          const uint32_t d_tmem = tmem + a * Cfg::ACC_COLS;
           const int kend = (nkb - kb > Cfg::SEG) ? kb + Cfg::SEG : nkb;
           const int kfirst = kb;
           for (; kb < kend; ++kb, ++it) {
@@ -516,7 +532,6 @@ __global__ void __launch_bounds__(256, 1)
             const uint32_t a_hi = smem_addr(stageA(s));
             const uint32_t b_hi = smem_addr(stageB(s));
             const uint32_t a_lo = smem_addr(stageAlo(s));
-            const uint32_t b_lo = smem_addr(stageBlo(s));
 #pragma unroll
             for (int kk = 0; kk < Cfg::BK / Cfg::UMMA_K; ++kk) {
               const uint32_t aoff = Cfg::A_MN ? kk * Cfg::UMMA_K * 128 : kk * 32;
@@ -525,13 +540,13 @@ __global__ void __launch_bounds__(256, 1)
               const uint64_t bd = sdesc_sw128(b_hi + boff, Cfg::B_LBO, Cfg::B_SBO, Cfg::B_LAYOUT);
               const uint32_t acc = (kb > kfirst || kk > 0) ? 1u : 0u;
               if constexpr (Cfg::AR == Arith::F32x3) {
+                // hi*hi and hi*lo in one N = 2*BN MMA over [B_hi; B_lo]
+                // (columns [0, BN) and [BN, 2BN)), then lo*hi into [0, BN):
+                // A_hi is read from shared memory once per k-step, not twice
                 const uint64_t adl =
                     sdesc_sw128(a_lo + aoff, Cfg::A_LBO, Cfg::A_SBO, Cfg::A_LAYOUT);
-                const uint64_t bdl =
-                    sdesc_sw128(b_lo + boff, Cfg::B_LBO, Cfg::B_SBO, Cfg::B_LAYOUT);
-                umma_tf32(d_tmem, adl, bd, Cfg::IDESC, acc);
-                umma_tf32(d_tmem, ad, bdl, Cfg::IDESC, 1u);
-                umma_tf32(d_tmem, ad, bd, Cfg::IDESC, 1u);
+                umma_tf32(d_tmem, ad, bd, Cfg::IDESC2, acc);
+                umma_tf32(d_tmem, adl, bd, Cfg::IDESC, 1u);
               } else if constexpr (Cfg::AR == Arith::TF32) {
                 umma_tf32(d_tmem, ad, bd, Cfg::IDESC, acc);
               } else {
@@ -575,14 +590,22 @@ __global__ void __launch_bounds__(256, 1)
           ok = mbar_wait(smem_addr(&sb->full[s]), (it / S) & 1, wc);
           ok = __all_sync(0xffffffffu, ok);
           if (!ok) break;
-          // A and B (and their lo buffers) are contiguous: [A | B] and [Alo | Blo].
-          const float4* hi = reinterpret_cast<const float4*>(stageA(s));
-          float4* lo = reinterpret_cast<float4*>(stageAlo(s));
-          constexpr int NV = Cfg::LOAD_BYTES / 16;
+          // A -> A_lo and B -> B_lo (stage layout [A | A_lo | B | B_lo])
+          const float4* ha = reinterpret_cast<const float4*>(stageA(s));
+          float4* la = reinterpret_cast<float4*>(stageAlo(s));
+          const float4* hb = reinterpret_cast<const float4*>(stageB(s));
+          float4* lb = reinterpret_cast<float4*>(stageBlo(s));
+          constexpr int NA = Cfg::A_BYTES / 16;
+          constexpr int NB = Cfg::B_BYTES / 16;
 #pragma unroll 4
-          for (int v = ct; v < NV; v += 64) {
-            const float4 x = hi[v];
-            lo[v] = make_float4(tf32_lo(x.x), tf32_lo(x.y), tf32_lo(x.z), tf32_lo(x.w));
+          for (int v = ct; v < NA; v += 64) {
+            const float4 x = ha[v];
+            la[v] = make_float4(tf32_lo(x.x), tf32_lo(x.y), tf32_lo(x.z), tf32_lo(x.w));
+          }
+#pragma unroll 4
+          for (int v = ct; v < NB; v += 64) {
+            const float4 x = hb[v];
+            lb[v] = make_float4(tf32_lo(x.x), tf32_lo(x.y), tf32_lo(x.z), tf32_lo(x.w));
           }
           fence_proxy_async_smem();
           mbar_arrive(smem_addr(&sb->conv[s]));
@@ -759,10 +782,16 @@ __global__ void __launch_bounds__(256, 1)
 #pragma unroll
           for (int c = 0; c < Cfg::BN / 32; ++c) {
             uint32_t v[32];
-            tmem_ld_32x32b_x32(tmem + a * Cfg::BN + c * 32 + lane_off, v);
+            tmem_ld_32x32b_x32(tmem + a * Cfg::ACC_COLS + c * 32 + lane_off, v);
             tmem_ld_wait();
 #pragma unroll
             for (int j = 0; j < 32; ++j) acc[c][j] += __uint_as_float(v[j]);
+            if constexpr (Cfg::ACC_COLS == 2 * Cfg::BN) {
+              tmem_ld_32x32b_x32(tmem + a * Cfg::ACC_COLS + Cfg::BN + c * 32 + lane_off, v);
+              tmem_ld_wait();
+#pragma unroll
+              for (int j = 0; j < 32; ++j) acc[c][j] += __uint_as_float(v[j]);
+            }
           }
           tc_fence_before();
           __syncwarp();
@@ -790,7 +819,7 @@ __global__ void __launch_bounds__(256, 1)
 #pragma unroll 1
         for (int c0 = 0; c0 < Cfg::BN; c0 += 32) {
           uint32_t v[32];
-          tmem_ld_32x32b_x32(tmem + a * Cfg::BN + c0 + lane_off, v);
+          tmem_ld_32x32b_x32(tmem + a * Cfg::ACC_COLS + c0 + lane_off, v);
           tmem_ld_wait();
           float f[32];
 #pragma unroll
