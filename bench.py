@@ -430,6 +430,12 @@ def op_table(recs):
     return out
 
 
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the
+# dominant op class, from one ncu capture of a batch-32 VGG16 HP step: the mean
+# over its 13 convolution launches (profiles/vgg16_hp_step_launches.md).
+NCU_TRAFFIC_PER_LAUNCH = {"HP:CUDNN_CONV_FWD": 323066329}
+
+
 def roofline(recs, peaks, peak_src, tf32, sustained):
     """Dominant captured op class of a profiled phase: algorithmic FLOPs per
     launch (2mnk per GEMM, 2*N*K*C*R*S*P*Q per convolution) over the mean
@@ -447,7 +453,8 @@ def roofline(recs, peaks, peak_src, tf32, sustained):
     ceiling = tf32 / 3.0
     top = max(agg["kernels"].items(), key=lambda kv: kv[1])[0]
     return {"bound": "tensor", "achieved": round(achieved, 2), "peak": round(peak, 1),
-            "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "traffic": None,
+            "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+            "traffic": NCU_TRAFFIC_PER_LAUNCH.get(f"{client}:{op}"),
             "peak_source": f"{key} of {peak_src}",
             "tf32_cublas_tflops": round(tf32, 1),
             "fp32_3xtf32_ceiling": round(ceiling, 1),
