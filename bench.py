@@ -437,11 +437,14 @@ NCU_TRAFFIC_PER_LAUNCH = {"HP:CUDNN_CONV_FWD": 323066329}
 
 
 def roofline(recs, peaks, peak_src, tf32, sustained):
-    """Dominant captured op class of a profiled phase: algorithmic FLOPs per
-    launch (2mnk per GEMM, 2*N*K*C*R*S*P*Q per convolution) over the mean
+    """Dominant captured op class of the HP client in a profiled phase (the
+    client `value` measures; BE ops are throttled to the SMs HP leaves them,
+    so their rate measures the scheduler, not the kernel): algorithmic FLOPs
+    per launch (2mnk per GEMM, 2*N*K*C*R*S*P*Q per convolution) over the mean
     launch duration (CUDA events on the worker's dispatch stream)."""
     by_op = group_ops(recs)
-    dense = {k: v for k, v in by_op.items() if "BATCHNORM" not in k[1] and v["work"] > 0}
+    dense = {k: v for k, v in by_op.items()
+             if k[0] == "HP" and "BATCHNORM" not in k[1] and v["work"] > 0}
     if not dense:
         return None
     (client, op), agg = max(dense.items(), key=lambda kv: kv[1]["ms"])
