@@ -57,6 +57,8 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--be-keep-sms", type=int, default=-1,
                     help="SMs a BE op keeps while HP runs (default: the scheduler's)")
+    ap.add_argument("--gil-switch-ms", type=float, default=0.0,
+                    help="sys.setswitchinterval for the client threads (0: Python's default)")
     ap.add_argument("--hp-load", type=float, default=1.0 / 3.0,
                     help="HP duty cycle of the paced phase (request period = solo p50 / load)")
     return ap.parse_args()
@@ -209,6 +211,11 @@ class Clocks:
 def run_kx(args):
     import torch
     import torch.nn.functional as F
+
+    if args.gil_switch_ms > 0:
+        # HP and BE are Python threads of one process (as in the reference's
+        # drivers): the interval bounds how long one waits for the other's GIL
+        sys.setswitchinterval(args.gil_switch_ms / 1e3)
 
     from kernel_intercept_b200 import harness, kx
 
@@ -387,6 +394,10 @@ def run_kx(args):
                   "hp_p99_ms": round(harness.percentile(hp_p.latencies_ms, 0.99), 3),
                   "hp_p99_vs_solo": round(harness.percentile(hp_p.latencies_ms, 0.99) / s99, 4)
                   if s99 else None,
+                  "hp_issue_p50_ms": round(harness.percentile(hp_p.issue_ms, 0.5), 3),
+                  "hp_issue_p99_ms": round(harness.percentile(hp_p.issue_ms, 0.99), 3),
+                  "solo_issue_p99_ms": round(harness.percentile(hp_solo.issue_ms, 0.99), 3),
+                  "gil_switch_ms": round(sys.getswitchinterval() * 1e3, 3),
                   "be_iters_per_s": round(be_p.iters / (be_p.elapsed_ms / 1e3), 3)
                   if be_p.elapsed_ms else None,
                   "be_retention": round(be_p.iters / (be_p.elapsed_ms / 1e3) / be_solo_ips, 4)

@@ -165,12 +165,26 @@ struct ConvPlan {
   bool im2col; // A tiles by im2col-mode TMA (else wbox x hbox boxes)
   int splits;  // K slices (partials reduced by kx_splitk_reduce)
   int wbox, hbox;
+  bool pair;   // 2-CTA clusters: 256-row tiles, cta_group::2 MMAs
 };
 
 // KX_CONV_IM2COL: "0" = always box tiles, "1" = im2col whenever the map
 // can express the geometry, unset = by tile waste (see plan_conv).
 int im2col_mode() {
   const char* v = std::getenv("KX_CONV_IM2COL");
+  if (v == nullptr || v[0] == 0) return -1;
+  return v[0] == '0' ? 0 : 1;
+}
+
+// KX_CTA_PAIR: "1" = CTA pairs whenever possible; unset or "0" = one CTA per
+// tile.  Pairs stream 4 stages instead of 3 (the MMA waits for operands 6%
+// of its time instead of 27% on VGG16 conv3_2), but each SM still reads its
+// whole B operand half from its own and half from the peer's shared memory,
+// and on B200 the pair kernel measured 16% slower on conv3_2 and 21% slower
+// over the 13 VGG16 layers than the one-CTA kernel
+// with the merged hi*[hi; lo] product, so pairs are opt-in.
+int pair_mode() {
+  const char* v = std::getenv("KX_CTA_PAIR");
   if (v == nullptr || v[0] == 0) return -1;
   return v[0] == '0' ? 0 : 1;
 }
@@ -184,7 +198,7 @@ void im2col_corners(const ConvShape& t, int lower[2], int upper[2]) {
 }
 
 ConvPlan plan_conv(const ConvShape& g, const ConvShape& t, int cp, int sms) {
-  ConvPlan pl{64, false, 1, 0, 0};
+  ConvPlan pl{64, false, 1, 0, 0, false};
   choose_box(g.P, g.Q, t.sw, t.sh, pl.wbox, pl.hbox);
   const long long m = static_cast<long long>(g.N) * g.P * g.Q;
   int lo[2], up[2];
@@ -204,6 +218,11 @@ ConvPlan plan_conv(const ConvShape& g, const ConvShape& t, int cp, int sms) {
   const long long mt = pl.im2col ? (m + 127) / 128 : box_mt;
   // 128-wide channel tiles when they fill the GPU and waste nothing
   if (g.K % 128 == 0 && mt * (g.K / 128) >= sms) pl.bn = 128;
+  // CTA pairs: each CTA loads half of B, so 4 stages fit instead of 3
+  const long long pair_tiles = (mt + 1) / 2 * ((g.K + pl.bn - 1) / pl.bn);
+  const int pmode = pair_mode();
+  pl.pair = sms >= 2 && pmode == 1 && pair_tiles >= 1;
+  if (pl.pair) return pl;  // no split-K with pairs
   if (split_k_disabled()) return pl;
   // Split K when the tiles leave the last wave mostly empty: per slice count
   // s, waves x k-blocks per slice (a k-block ~0.55 us per CTA at BN 128),
@@ -229,12 +248,12 @@ ConvPlan plan_conv(const ConvShape& g, const ConvShape& t, int cp, int sms) {
   return pl;
 }
 
-template <int BN>
+template <int BN, bool PAIR>
 int launch_conv_tc(const Exec& e, const ConvShape& g, const ConvShape& t, const float* xh,
                    const float* xl, int cp, const float* wp, const float* wp_lo, float* y,
                    float alpha, float beta, const ConvPlan& pl) {
   // t: the geometry the kernel sees (g itself, or the folded 1x1 problem)
-  using Cfg = GemmCfg<BN, Arith::F32x3, false, false>;
+  using Cfg = GemmCfg<BN, Arith::F32x3, false, false, PAIR>;
   const long long kd = static_cast<long long>(t.R) * t.S * cp;
   const long long pq = static_cast<long long>(g.P) * g.Q;
   const int wbox = pl.wbox, hbox = pl.hbox;
@@ -261,9 +280,10 @@ int launch_conv_tc(const Exec& e, const ConvShape& g, const ConvShape& t, const 
                     CU_TENSOR_MAP_SWIZZLE_128B, es))
       return KX_ERR_UNSUPPORTED;
   }
-  if (!encode_map_3d(&mb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, wp, kd, g.K, 1, kd, 0, Cfg::BK, BN) ||
+  if (!encode_map_3d(&mb, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, wp, kd, g.K, 1, kd, 0, Cfg::BK,
+                     Cfg::B_ROWS) ||
       !encode_map_3d(&mblo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, wp_lo, kd, g.K, 1, kd, 0, Cfg::BK,
-                     BN))
+                     Cfg::B_ROWS))
     return KX_ERR_UNSUPPORTED;
   GemmParams p;
   std::memset(&p, 0, sizeof(p));
@@ -305,6 +325,9 @@ int launch_conv_tc(const Exec& e, const ConvShape& g, const ConvShape& t, const 
   p.cv_pq = static_cast<int>(pq);
   p.num_mb = pl.im2col ? (p.m + Cfg::BM - 1) / Cfg::BM
                        : p.cv_tiles_w * ((g.P + hbox - 1) / hbox);
+  // a pair tile covers two consecutive 128-row blocks (the second may lie
+  // past the end: its loads read zeros and its rows are not stored)
+  if (PAIR) p.num_mb = (p.num_mb + 1) / 2;
   p.num_nb = (g.K + BN - 1) / BN;
   p.num_kb = static_cast<int>(kd / Cfg::BK);
   const int batch = pl.im2col ? 1 : g.N;
@@ -362,10 +385,20 @@ int launch_conv_tc(const Exec& e, const ConvShape& g, const ConvShape& t, const 
         p.tma_store = 1;
     }
   }
-  const int grid = persistent_grid(e, p.num_tiles);
+  int grid = persistent_grid(e, p.num_tiles * (PAIR ? 2 : 1));
+  if (PAIR) {
+    grid = pair_grid(kern, Cfg::THREADS, Cfg::SMEM_BYTES, grid);
+    if (grid < 2) return KX_ERR_UNSUPPORTED;
+  }
   p.pipe_stats = pipe_stats_begin();
   note_launch();
-  kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, e.stream>>>(ma, mb, malo, mblo, md, p);
+  if (PAIR) {
+    if (launch_pair(kern, grid, Cfg::THREADS, Cfg::SMEM_BYTES, e.stream, ma, mb, malo, mblo, md,
+                    p) != cudaSuccess)
+      return KX_ERR_DEVICE;
+  } else {
+    kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, e.stream>>>(ma, mb, malo, mblo, md, p);
+  }
   pipe_stats_end(p.pipe_stats, "kx_conv_fwd_tc", e.stream, grid);
   if (p.splits > 1) {
     note_launch();
@@ -375,7 +408,8 @@ int launch_conv_tc(const Exec& e, const ConvShape& g, const ConvShape& t, const 
   static char names[2][64];
   char* name = names[pl.im2col ? 1 : 0];
   if (name[0] == 0)
-    snprintf(name, 64, "kx_conv_fwd_tc<bn%d,f32x3,%s>", BN, pl.im2col ? "im2col" : "box");
+    snprintf(name, 64, "kx_conv_fwd_tc<bn%d,f32x3,%s%s>", BN, pl.im2col ? "im2col" : "box",
+             PAIR ? ",pair" : "");
   set_last_kernel_name(name);
   return launch_status();
 }
@@ -440,8 +474,15 @@ int conv_fwd_implicit(const Exec& e, const ConvShape& g, const float* x, const f
                                                         folded ? 1 : 0, g.flip ? 1 : 0);
   if (launch_status() != KX_OK) return KX_ERR_DEVICE;
   const ConvPlan pl = plan_conv(g, t, cp, persistent_grid(e, 1 << 30));
-  if (pl.bn == 128) return launch_conv_tc<128>(e, g, t, xh, xl, cp, wp, wp_lo, y, alpha, beta, pl);
-  return launch_conv_tc<64>(e, g, t, xh, xl, cp, wp, wp_lo, y, alpha, beta, pl);
+  if (pl.pair) {
+    const int rc =
+        pl.bn == 128 ? launch_conv_tc<128, true>(e, g, t, xh, xl, cp, wp, wp_lo, y, alpha, beta, pl)
+                     : launch_conv_tc<64, true>(e, g, t, xh, xl, cp, wp, wp_lo, y, alpha, beta, pl);
+    if (rc != KX_ERR_UNSUPPORTED) return rc;
+  }
+  if (pl.bn == 128)
+    return launch_conv_tc<128, false>(e, g, t, xh, xl, cp, wp, wp_lo, y, alpha, beta, pl);
+  return launch_conv_tc<64, false>(e, g, t, xh, xl, cp, wp, wp_lo, y, alpha, beta, pl);
 }
 
 }  // namespace kx

@@ -35,6 +35,8 @@
 // that yields (host-mapped flag raised, or per-launch tile budget used up)
 // can be continued by relaunching the same call.
 #pragma once
+#include <mutex>
+#include <unordered_map>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
@@ -135,10 +137,16 @@ KX_DEV bool timed_wait(uint32_t bar, uint32_t parity, const WaitCtl& wc,
   return ok;
 }
 
-template <int BN_, Arith AR_, bool A_MN_, bool B_MN_>
+template <int BN_, Arith AR_, bool A_MN_, bool B_MN_, bool PAIR_ = false>
 struct GemmCfg {
-  static constexpr int BM = 128;
+  static constexpr int BM = 128;  // accumulator rows per CTA
   static constexpr int BN = BN_;
+  // PAIR: a 2-CTA cluster computes a 256 x BN tile with cta_group::2 MMAs
+  // issued by the leader; each CTA loads its 128 rows of A and BN/2 rows of B
+  // (3xTF32 with pre-split low parts only).
+  static constexpr bool PAIR = PAIR_;
+  static constexpr int MMA_M = PAIR ? 2 * BM : BM;
+  static constexpr int B_ROWS = PAIR ? BN / 2 : BN;  // rows of B in this CTA
   static constexpr Arith AR = AR_;
   static constexpr bool A_MN = A_MN_;
   static constexpr bool B_MN = B_MN_;
@@ -148,15 +156,17 @@ struct GemmCfg {
   static constexpr int CHUNK = 128 / ESIZE;    // M/N elements per 128-byte chunk (MN-major)
   static constexpr bool SPLIT = (AR == Arith::F32x3);
   static constexpr int A_BYTES = BM * 128;
-  static constexpr int B_BYTES = BN * 128;
+  static constexpr int B_BYTES = B_ROWS * 128;
   static constexpr int LOAD_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGE_BYTES = LOAD_BYTES * (SPLIT ? 2 : 1);
   static constexpr int STAGES_RAW = (192 * 1024) / STAGE_BYTES;
   static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
   static constexpr int RING = 4;  // depth of the tile-id broadcast ring
-  // TMEM columns of one accumulator buffer.  3xTF32 keeps two BN-wide halves:
-  // [0, BN) = hi*hi + lo*hi and [BN, 2BN) = hi*lo (see the MMA issuer).
-  static constexpr int ACC_COLS = SPLIT ? 2 * BN : BN;
+  // TMEM columns of one accumulator buffer.  3xTF32 on one CTA keeps two
+  // BN-wide halves: [0, BN) = hi*hi + lo*hi and [BN, 2BN) = hi*lo (see the
+  // MMA issuer); a pair issues the three products into one BN-wide buffer.
+  static constexpr bool MERGED = SPLIT && !PAIR;
+  static constexpr int ACC_COLS = MERGED ? 2 * BN : BN;
   static constexpr int TMEM_COLS = (2 * ACC_COLS) <= 32 ? 32 : (2 * ACC_COLS) <= 64 ? 64 : (2 * ACC_COLS) <= 128 ? 128 : (2 * ACC_COLS) <= 256 ? 256 : 512;
   static constexpr int THREADS = 256;
   static constexpr int NUM_CONS = 1 + 4;  // ring consumers: MMA issuer + epilogue warps
@@ -180,9 +190,9 @@ struct GemmCfg {
   static constexpr uint32_t B_LAYOUT = B_MN32 ? 1 : 2;
   static_assert(!PROMOTE || BN <= 128, "3xTF32 keeps a BN-wide fp32 accumulator per thread");
   static constexpr uint32_t FMT = (AR == Arith::BF16) ? 1u : (AR == Arith::F16) ? 0u : 2u;
-  static constexpr uint32_t IDESC = make_idesc(FMT, A_MN, B_MN, BM, BN);
-  // 3xTF32: A_hi x [B_hi; B_lo] as one N = 2*BN product
-  static constexpr uint32_t IDESC2 = make_idesc(FMT, A_MN, B_MN, BM, SPLIT ? 2 * BN : BN);
+  static constexpr uint32_t IDESC = make_idesc(FMT, A_MN, B_MN, MMA_M, BN);
+  // 3xTF32 on one CTA: A_hi x [B_hi; B_lo] as one N = 2*BN product
+  static constexpr uint32_t IDESC2 = make_idesc(FMT, A_MN, B_MN, MMA_M, MERGED ? 2 * BN : BN);
   // epilogue staging (4 warps x 2 buffers of 32 x 32 fp32) after the stages,
   // then the barrier block
   static constexpr int EPI_OFF = STAGES * STAGE_BYTES;
@@ -192,12 +202,14 @@ struct GemmCfg {
   static_assert(STAGES >= 2, "not enough shared memory for two stages");
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "bad BN");
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+  static_assert(!PAIR || (SPLIT && BN >= 64), "CTA pairs: 3xTF32, BN >= 64");
 };
 
 struct SmemBars {
   uint64_t full[8], conv[8], empty[8];
   uint64_t tfull[2], tempty[2];
   uint64_t ring_full[4], ring_empty[4];
+  uint64_t pair_full[8];  // leader: the follower's stage has landed
   uint64_t final_mma;
   int ring[4];
   uint32_t tmem_base;
@@ -312,6 +324,66 @@ inline int splitk_reduce_grid(int m, int n, int batch, int sms) {
   return static_cast<int>(blocks < 1 ? 1 : (blocks > cap ? cap : blocks));
 }
 
+// ---------------------------------------------------- CTA-pair launches --
+
+// Largest even grid <= want whose 2-CTA clusters can all be resident at once.
+// Tiles come from an atomic queue, so correctness does not depend on it; a
+// cluster that only starts after the others finished finds the queue empty.
+template <class K>
+int pair_grid(K kern, int threads, int smem, int want) {
+  static std::mutex mu;
+  static std::unordered_map<long long, int> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const long long key = (static_cast<long long>(reinterpret_cast<uintptr_t>(kern)) << 8) ^ dev;
+  int clusters = -1;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) clusters = it->second;
+  }
+  if (clusters < 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2, 1, 1);
+    cfg.blockDim = dim3(static_cast<unsigned>(threads), 1, 1);
+    cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg) != cudaSuccess) {
+      cudaGetLastError();
+      clusters = 0;
+    }
+    std::lock_guard<std::mutex> lk(mu);
+    cache[key] = clusters;
+  }
+  int g = want & ~1;
+  if (clusters > 0 && 2 * clusters < g) g = 2 * clusters;
+  return clusters > 0 ? g : 0;
+}
+
+template <class K, class... Args>
+cudaError_t launch_pair(K kern, int grid, int threads, int smem, cudaStream_t stream,
+                        const Args&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid), 1, 1);
+  cfg.blockDim = dim3(static_cast<unsigned>(threads), 1, 1);
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 // CONV = true: implicit-GEMM convolution (see GemmParams::cv_*): the A tile
 // of k-block (tap, channel block) is the 4-D box of the NHWC staging copy
 // shifted by the tap's offset, so TMA zero-fills the padding border.
@@ -327,8 +399,12 @@ __global__ void __launch_bounds__(256, 1)
   const long long t_start = clock64();  // CTA lifetime starts here
   constexpr int S = Cfg::STAGES;
   constexpr int R = Cfg::RING;
+  // CTA pair (Cfg::PAIR): rank 0 leads (tile ids, MMAs), rank 1 follows
+  constexpr bool PAIR = Cfg::PAIR;
+  const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
+  const bool leader = rank == 0;
   // in-kernel 3xTF32 split (warps 2-3) unless the low parts come by TMA
-  const bool convert = Cfg::SPLIT && !CONV && p.presplit == 0;
+  const bool convert = Cfg::SPLIT && !CONV && !PAIR && p.presplit == 0;
   const bool lo_by_tma = Cfg::SPLIT && !convert;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -355,13 +431,16 @@ __global__ void __launch_bounds__(256, 1)
       mbar_init(smem_addr(&sb->conv[s]), convert ? 64 : 1);
       mbar_init(smem_addr(&sb->empty[s]), 1);
     }
+    for (int s = 0; s < S; ++s) mbar_init(smem_addr(&sb->pair_full[s]), 1);
+    // pair: the leader's tempty / ring_empty also count the follower's
+    // epilogue warps (4) and its producer and forwarder threads (2)
     for (int a = 0; a < 2; ++a) {
       mbar_init(smem_addr(&sb->tfull[a]), 1);
-      mbar_init(smem_addr(&sb->tempty[a]), 4);
+      mbar_init(smem_addr(&sb->tempty[a]), PAIR ? 8 : 4);
     }
     for (int r = 0; r < R; ++r) {
       mbar_init(smem_addr(&sb->ring_full[r]), 1);
-      mbar_init(smem_addr(&sb->ring_empty[r]), Cfg::NUM_CONS + (convert ? 2 : 0));
+      mbar_init(smem_addr(&sb->ring_empty[r]), Cfg::NUM_CONS + (convert ? 2 : 0) + (PAIR ? 6 : 0));
     }
     mbar_init(smem_addr(&sb->final_mma), 1);
     sb->abort_flag = 0;
@@ -376,12 +455,22 @@ __global__ void __launch_bounds__(256, 1)
     }
   }
   if (warp == 1) {
-    tmem_alloc(smem_addr(&sb->tmem_base), Cfg::TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (PAIR) {
+      tmem_alloc_pair(smem_addr(&sb->tmem_base), Cfg::TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(smem_addr(&sb->tmem_base), Cfg::TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR)
+    cluster_sync();  // the peer's barriers are initialised before any remote arrival
+  else
+    __syncthreads();
   tc_fence_after();
+  // leader's barriers as seen from this CTA (pair only)
+  auto leader_bar = [&](const uint64_t* b) { return mapa_shared(smem_addr(b), 0u); };
   const uint32_t tmem = sb->tmem_base;
   const long long t_ready = clock64();
 
@@ -396,27 +485,41 @@ __global__ void __launch_bounds__(256, 1)
       int taken = 0;
       for (uint32_t slot = 0;; ++slot) {
         int tile;
-        // yield flag f: 0 = run; f > 0 = only CTAs below f keep taking tiles
-        // (the op still completes on them); f < 0 = every CTA stops.
-        const int f = p.yield_flag != nullptr ? *p.yield_flag : 0;
-        if (p.max_tiles > 0 && taken >= p.max_tiles) {
-          tile = -2;
-        } else if (f < 0 || (f > 0 && static_cast<int>(blockIdx.x) >= f)) {
-          tile = -2;
-        } else {
-          tile = static_cast<int>(atomicAdd(&p.work->next_tile, 1u));
-          if (tile >= p.num_tiles) tile = -1;
-        }
         const uint32_t r = slot % R;
-        if (!timed_wait(smem_addr(&sb->ring_empty[r]), ((slot / R) & 1) ^ 1, wc,
-                        stats ? &st_b : nullptr))
-          break;
-        sb->ring[r] = tile;
-        mbar_arrive(smem_addr(&sb->ring_full[r]));
+        if (leader) {
+          // yield flag f: 0 = run; f > 0 = only CTAs below f keep taking tiles
+          // (the op still completes on them); f < 0 = every CTA stops.
+          const int f = p.yield_flag != nullptr ? *p.yield_flag : 0;
+          if (p.max_tiles > 0 && taken >= p.max_tiles) {
+            tile = -2;
+          } else if (f < 0 || (f > 0 && static_cast<int>(blockIdx.x) >= f)) {
+            tile = -2;
+          } else {
+            tile = static_cast<int>(atomicAdd(&p.work->next_tile, 1u));
+            if (tile >= p.num_tiles) tile = -1;
+          }
+          const uint32_t eb = smem_addr(&sb->ring_empty[r]);
+          const uint32_t ep = ((slot / R) & 1) ^ 1;
+          if (!(PAIR ? mbar_wait_cluster(eb, ep, wc) : timed_wait(eb, ep, wc, stats ? &st_b : nullptr)))
+            break;
+          sb->ring[r] = tile;
+          mbar_arrive(smem_addr(&sb->ring_full[r]));
+          if constexpr (PAIR) {
+            // the same tile id into the follower's ring
+            st_shared_cluster_u32(mapa_shared(smem_addr(&sb->ring[r]), 1u),
+                                  static_cast<uint32_t>(tile));
+            mbar_arrive_cluster(mapa_shared(smem_addr(&sb->ring_full[r]), 1u));
+          }
+        } else {
+          if (!mbar_wait_cluster(smem_addr(&sb->ring_full[r]), (slot / R) & 1, wc)) break;
+          tile = sb->ring[r];
+          mbar_arrive_cluster(leader_bar(&sb->ring_empty[r]));
+        }
         if (tile < 0) break;
         ++taken;
         int b, ks, mb, nb, kb0, nkb;
         decode_tile(tile, p, b, ks, mb, nb);
+        if constexpr (PAIR) mb = 2 * mb + static_cast<int>(rank);  // this CTA's 128 rows
         tile_k_range(tile, p, kb0, nkb);
         const int ba = p.a_bcast ? 0 : b;
         const int bb = p.b_bcast ? 0 : b;
@@ -465,13 +568,15 @@ __global__ void __launch_bounds__(256, 1)
                             kb * Cfg::BK, ba);
             }
           };
+          // this CTA's rows of B: all BN, or half of them in a pair
+          const int n0 = nb * Cfg::BN + static_cast<int>(rank) * Cfg::B_ROWS;
           auto load_b = [&](uint32_t sbb, const CUtensorMap* map) {
             if (!Cfg::B_MN) {
-              tma_load_3d(sbb, map, fb, kb * Cfg::BK, nb * Cfg::BN, bb);
+              tma_load_3d(sbb, map, fb, kb * Cfg::BK, n0, bb);
             } else {
 #pragma unroll
-              for (int c = 0; c < Cfg::BN / Cfg::CHUNK; ++c)
-                tma_load_3d(sbb + c * Cfg::BK * 128, map, fb, nb * Cfg::BN + c * Cfg::CHUNK,
+              for (int c = 0; c < Cfg::B_ROWS / Cfg::CHUNK; ++c)
+                tma_load_3d(sbb + c * Cfg::BK * 128, map, fb, n0 + c * Cfg::CHUNK,
                             kb * Cfg::BK, bb);
             }
           };
@@ -494,7 +599,28 @@ __global__ void __launch_bounds__(256, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------- MMA issuer ---
-    if (lane == 0) {
+    if (lane == 0 && PAIR && !leader) {
+      // follower: forward each landed stage to the leader's pair_full[s]
+      uint32_t it = 0;
+      bool ok = true;
+      for (uint32_t slot = 0; ok; ++slot) {
+        const uint32_t r = slot % R;
+        if (!mbar_wait_cluster(smem_addr(&sb->ring_full[r]), (slot / R) & 1, wc)) break;
+        const int tile = sb->ring[r];
+        mbar_arrive_cluster(leader_bar(&sb->ring_empty[r]));
+        if (tile < 0) break;
+        int kb0, nkb;
+        tile_k_range(tile, p, kb0, nkb);
+        for (int kb = 0; kb < nkb; ++kb, ++it) {
+          const uint32_t s = it % S;
+          if (!timed_wait(smem_addr(&sb->full[s]), (it / S) & 1, wc, stats ? &st_a : nullptr)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_cluster(leader_bar(&sb->pair_full[s]));
+        }
+      }
+    } else if (lane == 0) {
       // `sc` counts accumulator segments across tiles; segment sc uses TMEM
       // buffer sc & 1 (one segment per tile unless PROMOTE splits K).
       uint32_t it = 0, sc = 0;
@@ -511,8 +637,11 @@ __global__ void __launch_bounds__(256, 1)
         tile_k_range(tile, p, kb0, nkb);
         for (int kb = 0; kb < nkb && ok; ++sc) {
           const uint32_t a = sc & 1;
-          if (!timed_wait(smem_addr(&sb->tempty[a]), ((sc >> 1) & 1) ^ 1, wc,
-                          stats ? &st_b : nullptr)) {
+          const bool tfree =
+              PAIR ? mbar_wait_cluster(smem_addr(&sb->tempty[a]), ((sc >> 1) & 1) ^ 1, wc)
+                   : timed_wait(smem_addr(&sb->tempty[a]), ((sc >> 1) & 1) ^ 1, wc,
+                                stats ? &st_b : nullptr);
+          if (!tfree) {
             ok = false;
             break;
           }
@@ -523,7 +652,8 @@ __global__ void __launch_bounds__(256, 1)
           for (; kb < kend; ++kb, ++it) {
             const uint32_t s = it % S;
             const uint32_t wb = convert ? smem_addr(&sb->conv[s]) : smem_addr(&sb->full[s]);
-            if (!timed_wait(wb, (it / S) & 1, wc, stats ? &st_a : nullptr)) {
+            if (!timed_wait(wb, (it / S) & 1, wc, stats ? &st_a : nullptr) ||
+                (PAIR && !mbar_wait_cluster(smem_addr(&sb->pair_full[s]), (it / S) & 1, wc))) {
               ok = false;
               break;
             }
@@ -539,7 +669,16 @@ __global__ void __launch_bounds__(256, 1)
               const uint64_t ad = sdesc_sw128(a_hi + aoff, Cfg::A_LBO, Cfg::A_SBO, Cfg::A_LAYOUT);
               const uint64_t bd = sdesc_sw128(b_hi + boff, Cfg::B_LBO, Cfg::B_SBO, Cfg::B_LAYOUT);
               const uint32_t acc = (kb > kfirst || kk > 0) ? 1u : 0u;
-              if constexpr (Cfg::AR == Arith::F32x3) {
+              if constexpr (PAIR) {
+                // 256 x BN over the pair: A rows and B rows from both CTAs
+                const uint64_t adl =
+                    sdesc_sw128(a_lo + aoff, Cfg::A_LBO, Cfg::A_SBO, Cfg::A_LAYOUT);
+                const uint64_t bdl = sdesc_sw128(smem_addr(stageBlo(s)) + boff, Cfg::B_LBO,
+                                                 Cfg::B_SBO, Cfg::B_LAYOUT);
+                umma_tf32_pair(d_tmem, ad, bd, Cfg::IDESC, acc);
+                umma_tf32_pair(d_tmem, ad, bdl, Cfg::IDESC, 1u);
+                umma_tf32_pair(d_tmem, adl, bd, Cfg::IDESC, 1u);
+              } else if constexpr (Cfg::AR == Arith::F32x3) {
                 // hi*hi and hi*lo in one N = 2*BN MMA over [B_hi; B_lo]
                 // (columns [0, BN) and [BN, 2BN)), then lo*hi into [0, BN):
                 // A_hi is read from shared memory once per k-step, not twice
@@ -553,15 +692,24 @@ __global__ void __launch_bounds__(256, 1)
                 umma_f16(d_tmem, ad, bd, Cfg::IDESC, acc);
               }
             }
-            tc_commit(smem_addr(&sb->empty[s]));
+            if constexpr (PAIR)
+              tc_commit_pair(smem_addr(&sb->empty[s]));  // frees the stage in both CTAs
+            else
+              tc_commit(smem_addr(&sb->empty[s]));
             if (stats) st_d += static_cast<unsigned long long>(clock64() - t_iss);
           }
           if (!ok) break;
-          tc_commit(smem_addr(&sb->tfull[a]));
+          if constexpr (PAIR)
+            tc_commit_pair(smem_addr(&sb->tfull[a]));
+          else
+            tc_commit(smem_addr(&sb->tfull[a]));
         }
       }
       // Wait (bounded) for every MMA this thread issued before TMEM is freed.
-      tc_commit(smem_addr(&sb->final_mma));
+      if constexpr (PAIR)
+        tc_commit_pair(smem_addr(&sb->final_mma));
+      else
+        tc_commit(smem_addr(&sb->final_mma));
       int dummy_abort = 0;
       WaitCtl drain{&dummy_abort, nullptr, p.timeout_ns};
       mbar_wait(smem_addr(&sb->final_mma), 0, drain);
@@ -627,15 +775,22 @@ __global__ void __launch_bounds__(256, 1)
     uint32_t sc = 0;
     for (uint32_t slot = 0;; ++slot) {
       const uint32_t r = slot % R;
-      bool ok = mbar_wait(smem_addr(&sb->ring_full[r]), (slot / R) & 1, wc);
+      bool ok = leader ? mbar_wait(smem_addr(&sb->ring_full[r]), (slot / R) & 1, wc)
+                       : mbar_wait_cluster(smem_addr(&sb->ring_full[r]), (slot / R) & 1, wc);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       const int tile = sb->ring[r];
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_addr(&sb->ring_empty[r]));
+      if (lane == 0) {
+        if (leader)
+          mbar_arrive(smem_addr(&sb->ring_empty[r]));
+        else
+          mbar_arrive_cluster(leader_bar(&sb->ring_empty[r]));
+      }
       if (tile < 0) break;
       int b, ks, mb, nb, kb0, nkb;
       decode_tile(tile, p, b, ks, mb, nb);
+      if constexpr (PAIR) mb = 2 * mb + static_cast<int>(rank);  // this CTA's 128 rows
       tile_k_range(tile, p, kb0, nkb);
       const int nseg = Cfg::PROMOTE ? (nkb + Cfg::SEG - 1) / Cfg::SEG : 1;
       int row = mb * Cfg::BM + q * 32 + static_cast<int>(lane);
@@ -795,7 +950,12 @@ __global__ void __launch_bounds__(256, 1)
           }
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(smem_addr(&sb->tempty[a]));
+          if (lane == 0) {
+            if (leader)
+              mbar_arrive(smem_addr(&sb->tempty[a]));
+            else
+              mbar_arrive_cluster(leader_bar(&sb->tempty[a]));
+          }
           if (stats) st_b += static_cast<unsigned long long>(clock64() - t_fold);
         }
         if (!ok) break;
@@ -832,7 +992,12 @@ __global__ void __launch_bounds__(256, 1)
         if (stats) st_c += static_cast<unsigned long long>(clock64() - t_emit);
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(smem_addr(&sb->tempty[a]));
+        if (lane == 0) {
+          if (leader)
+            mbar_arrive(smem_addr(&sb->tempty[a]));
+          else
+            mbar_arrive_cluster(leader_bar(&sb->tempty[a]));
+        }
         ++sc;
       }
     }
@@ -861,10 +1026,16 @@ __global__ void __launch_bounds__(256, 1)
     }
   }
   tc_fence_before();
-  __syncthreads();
+  if constexpr (PAIR)
+    cluster_sync();  // no remote arrival or MMA into this CTA is still pending
+  else
+    __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, Cfg::TMEM_COLS);
+    if constexpr (PAIR)
+      tmem_dealloc_pair(tmem, Cfg::TMEM_COLS);
+    else
+      tmem_dealloc(tmem, Cfg::TMEM_COLS);
   }
   if (threadIdx.x == 0) {
     const bool aborted = sb->abort_flag != 0;

@@ -217,6 +217,113 @@ KX_DEV void umma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t
       : "memory");
 }
 
+// ------------------------------------------------- CTA pairs (cluster 2) --
+//
+// Two CTAs of a 2-CTA cluster run one tcgen05.mma.cta_group::2 tile: each
+// holds half of A's rows and half of B's rows in its own shared memory at the
+// same offsets, and half of the accumulator rows in its own TMEM.  Rank 0 (the
+// leader) issues the MMAs; remote mbarrier arrivals synchronise the pair.
+
+KX_DEV uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// Address of the same shared-memory location in CTA `rank` of the cluster.
+KX_DEV uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+
+// Arrive on an mbarrier that may live in the peer CTA (address from mapa),
+// releasing this thread's prior writes at cluster scope.
+KX_DEV void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+
+KX_DEV void st_shared_cluster_u32(uint32_t cluster_addr, uint32_t v) {
+  asm volatile("st.shared::cluster.u32 [%0], %1;" ::"r"(cluster_addr), "r"(v) : "memory");
+}
+
+KX_DEV uint32_t mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred P1;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 P1, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, P1;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok;
+}
+
+// mbar_wait with cluster-scope acquire: for barriers the peer CTA arrives on
+// (its writes before the arrival are visible after the wait).
+KX_DEV bool mbar_wait_cluster(uint32_t bar, uint32_t parity, const WaitCtl& w) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  uint64_t t0 = 0;
+  uint32_t spins = 0;
+  while (true) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((++spins & 255u) == 0) {
+      if (*w.abort_flag) return false;
+      uint64_t now = globaltimer();
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > w.timeout_ns) {
+        *w.abort_flag = 1;
+        if (w.err_word) atomicCAS(w.err_word, 0, 3 /* KX_ERR_TIMEOUT */);
+        return false;
+      }
+    }
+  }
+}
+
+// Every thread of both CTAs: all prior shared-memory work of the pair is done
+// and visible (used after barrier init and before TMEM release / exit).
+KX_DEV void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" :::
+                   "memory");
+}
+
+KX_DEV void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
+               "r"(ncols)
+               : "memory");
+}
+
+KX_DEV void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+KX_DEV void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+// Leader only: arrive on `bar` (same offset) in both CTAs of the pair once
+// every tcgen05.mma this thread issued has completed.
+KX_DEV void tc_commit_pair(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(bar),
+      "h"(static_cast<uint16_t>(3))
+      : "memory");
+}
+
+KX_DEV void umma_tf32_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                           uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // 32 lanes x 32 consecutive 32-bit columns; thread t gets lane (base+t).
 KX_DEV void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
   asm volatile(

@@ -266,6 +266,9 @@ def vgg16_flops_forward(batch):
 class ClientResult:
     def __init__(self):
         self.latencies_ms: list[float] = []
+        # host wall time the client thread spent issuing each step (the step's
+        # Python and enqueue work, including waits for the GIL)
+        self.issue_ms: list[float] = []
         self.iters = 0
         self.elapsed_ms = 0.0
         self.error: BaseException | None = None
@@ -318,6 +321,7 @@ def run_clients(orion: Orion | None, hp_step, be_step, hp_steps: int, hp_warmup:
                     a.record(s)
                     hp_step()
                     b.record(s)
+                    hp_res.issue_ms.append((time.perf_counter() - t_issue) * 1e3)
                     if hp_period_ms > 0:
                         while (time.perf_counter() - t_issue) * 1e3 < hp_period_ms:
                             time.sleep(0.0002)

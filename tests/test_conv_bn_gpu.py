@@ -93,17 +93,24 @@ def test_conv_fwd_implicit_gemm(cuda, case):
     assert name.startswith("kx_conv_fwd_tc<")
     mode = os.environ.get("KX_CONV_IM2COL")
     if mode is not None:
-        assert ("box>" if mode == "0" else "im2col>") in name
+        assert ("box" if mode == "0" else "im2col") in name
+    pair = os.environ.get("KX_CTA_PAIR")
+    if pair is not None:
+        assert (",pair>" in name) == (pair == "1")
     assert o.normwise_rel_err(dy.cpu().numpy(), ref) <= TOL_F32
 
 
+@pytest.mark.parametrize("pair", ["0", "1"])
 @pytest.mark.parametrize("mode", ["0", "1"])
 @pytest.mark.parametrize("case", IMPLICIT_CASES)
-def test_conv_fwd_tile_modes(cuda, case, mode, monkeypatch):
-    """Both A-tile forms of the kernel on every case: 4-D TMA boxes of whole
-    output rows (KX_CONV_IM2COL=0) and im2col-mode loads of 128 consecutive
-    output pixels (KX_CONV_IM2COL=1)."""
+def test_conv_fwd_tile_modes(cuda, case, mode, pair, monkeypatch):
+    """Every A-tile form of the kernel on every case: 4-D TMA boxes of whole
+    output rows (KX_CONV_IM2COL=0) or im2col-mode loads of 128 consecutive
+    output pixels (KX_CONV_IM2COL=1), on one CTA per 128-row tile
+    (KX_CTA_PAIR=0) or on 2-CTA clusters with cta_group::2 MMAs over
+    256-row tiles (KX_CTA_PAIR=1)."""
     monkeypatch.setenv("KX_CONV_IM2COL", mode)
+    monkeypatch.setenv("KX_CTA_PAIR", pair)
     test_conv_fwd_implicit_gemm(cuda, case)
 
 
