@@ -360,7 +360,13 @@ def main(argv=None) -> int:
     ap.add_argument("--baseline", action="store_true")
     ap.add_argument("--list-models", action="store_true")
     ap.add_argument("--gpus", type=int, default=1, help="client groups, one per GPU")
+    ap.add_argument("--gil-switch-ms", type=float, default=0.5,
+                    help="sys.setswitchinterval of each group process: its HP and BE clients "
+                         "are Python threads, and at Python's default of 5 ms a BE thread "
+                         "can hold the GIL for 5 ms while HP waits to issue (0: default)")
     args = ap.parse_args(argv)
+    if args.gil_switch_ms > 0:
+        sys.setswitchinterval(args.gil_switch_ms / 1e3)
     if args.list_models:
         print("\n".join(list(MODEL_REGISTRY) + ["gpt"]))
         return 0
