@@ -297,12 +297,16 @@ def run_clients(orion: Orion | None, hp_step, be_step, hp_steps: int, hp_warmup:
     import torch
 
     hp_res, be_res = ClientResult(), ClientResult()
+    # CUDA's current device is per thread and a new thread starts on device 0:
+    # the client threads adopt the caller's device before creating streams
+    dev = torch.cuda.current_device()
     stop = threading.Event()
     ready = threading.Barrier(2 if (with_hp and with_be) else 1, action=on_start)
 
     def hp_thread():
         try:
-            s = torch.cuda.Stream()
+            torch.cuda.set_device(dev)
+            s = torch.cuda.Stream(device=dev)
             if orion is not None:
                 orion.orion_set_client_idx(0)
                 orion.orion_register_client_stream(0, ctypes.c_void_p(s.cuda_stream))
@@ -339,7 +343,8 @@ def run_clients(orion: Orion | None, hp_step, be_step, hp_steps: int, hp_warmup:
 
     def be_thread():
         try:
-            s = torch.cuda.Stream()
+            torch.cuda.set_device(dev)
+            s = torch.cuda.Stream(device=dev)
             if orion is not None:
                 orion.orion_set_client_idx(1)
                 orion.orion_register_client_stream(1, ctypes.c_void_p(s.cuda_stream))
