@@ -378,6 +378,14 @@ int get_async_mode_internal();
 void set_last_error(int client_idx, cudaError_t error);
 cudaError_t get_and_clear_last_error(int client_idx);
 
+/** Op log (addition of this build; see orion_op_log_start). */
+bool op_log_enabled();
+/** One intercepted dense call: client (resolved even with capture off), op
+ *  type, up to 8 shape / layout integers, and its route ("capture", "direct",
+ *  "real"). */
+void op_log_record(int client_idx, OperationType type, const long long* dims, int ndims,
+                   const char* route);
+
 }  // namespace orion
 
 extern "C" {
@@ -393,6 +401,18 @@ int orion_set_capture(int enabled);
 void orion_register_client_stream(int client_idx, void* stream);
 void orion_register_client_handle(int client_idx, void* handle);
 int orion_resolve_client_idx(void* stream, void* handle);
+
+/* Op log (addition of this build, no counterpart in the reference): records
+ * every dense library call the interposer intercepts (cuBLAS GEMMs, cuBLASLt
+ * matmul, cuDNN convolutions and batch norm), in the order the calling
+ * threads made them and whether it was captured, passed through, or made with
+ * capture off.  Comparing the log of a run through the real libraries with
+ * the log of the same program captured shows that capture keeps each
+ * client's op sequence (types, shapes, counts) unchanged.
+ * orion_op_log_end writes one tab-separated line per call (client, op type,
+ * route, shape integers) and returns the number of lines, or -1. */
+void orion_op_log_start(void);
+int orion_op_log_end(const char* path);
 }
 
 #endif  // ORION_GPU_CAPTURE_H

@@ -141,10 +141,21 @@ CublasGemmParams make_gemm(void* handle, int ta, int tb, int m, int n, int k, co
 
 // Runs / captures a decoded GEMM record.  `real` performs the call on the
 // real library when the op is not captured (or not supported).
+const char* route_name(Route r, bool supported) {
+  if (!supported || r == Route::kReal) return "real";
+  return r == Route::kDirect ? "direct" : "capture";
+}
+
 template <class RealFn>
 cublasStatus_t submit_gemm(OperationType type, CublasGemmParams p, bool supported, RealFn real) {
   int client = -1;
   const Route r = route_for(p.handle, p.stream, &client);
+  if (op_log_enabled()) {
+    const long long d[7] = {p.m, p.n, p.k, p.transa, p.transb, p.Atype,
+                            p.batchCount > 0 ? p.batchCount : 1};
+    op_log_record(client >= 0 ? client : resolve_client_idx(p.stream, p.handle), type, d, 7,
+                  route_name(r, supported));
+  }
   if (r == Route::kReal) return real();
   if (!supported) {
     drain_client(client);
@@ -495,6 +506,14 @@ extern "C" cublasStatus_t cublasLtMatmul(void* lightHandle, void* computeDesc, c
   if (orion::tl_is_scheduler_thread || orion::tl_in_scheduler_execution) return call_real();
   int client = -1;
   const Route r = route_for(lightHandle, stream, &client);
+  if (orion::op_log_enabled()) {
+    const LtDecoded dec = decode_lt(computeDesc, Adesc, Bdesc, Cdesc, Ddesc);
+    const long long d[8] = {dec.m, dec.n, dec.k, dec.transa, dec.transb, dec.Atype,
+                            dec.batch > 0 ? dec.batch : 1, dec.epilogue};
+    orion::op_log_record(client >= 0 ? client : orion::resolve_client_idx(stream, lightHandle),
+                         orion::OperationType::CUBLASLT_MATMUL, d, 8,
+                         route_name(r, dec.supported));
+  }
   if (r == Route::kReal) return call_real();
   CublasLtMatmulParams p;
   p.lightHandle = lightHandle;

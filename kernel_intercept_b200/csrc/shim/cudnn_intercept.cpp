@@ -133,10 +133,31 @@ bool conv_geometry(void* xDesc, void* wDesc, void* convDesc, void* yDesc, ConvGe
   return g.packed_nchw != 0;
 }
 
+// Shape integers of an intercepted call for the op log.
+int log_dims(const CudnnConvParams& p, long long* d) {
+  const ConvGeometry& g = p.geom;
+  const long long v[8] = {g.n, g.c, g.h, g.w, g.k, g.r, g.s, g.stride_h * 100 + g.pad_h};
+  for (int i = 0; i < 8; ++i) d[i] = v[i];
+  return 8;
+}
+int log_dims(const CudnnBatchNormParams& p, long long* d) {
+  const long long v[5] = {p.n, p.c, p.h, p.w, p.mode};
+  for (int i = 0; i < 5; ++i) d[i] = v[i];
+  return 5;
+}
+
 template <class Params, class RealFn>
 cudnnStatus_t submit_op(OperationType type, void* handle, Params p, bool supported, RealFn real) {
   int client = -1;
   const Route r = route_for(handle, p.stream, &client);
+  if (op_log_enabled()) {
+    long long d[8];
+    const int nd = log_dims(p, d);
+    op_log_record(client >= 0 ? client : resolve_client_idx(p.stream, handle), type, d, nd,
+                  (!supported || r == Route::kReal) ? "real"
+                  : r == Route::kDirect            ? "direct"
+                                                   : "capture");
+  }
   if (r == Route::kReal) return real();
   if (!supported) {
     static std::atomic<int> reported{0};
@@ -1045,7 +1066,9 @@ cudnnStatus_t cudnnBackendExecute(void* handle, void* executionPlan, void* varia
   const cudaStream_t stream = cudnn_stream(handle);
   int client = -1;
   const Route r = route_for(handle, stream, &client);
-  if (r == Route::kReal) return call_real();
+  // with the op log on, decode anyway: submit_op logs the call, then runs it
+  // on cuDNN (route "real")
+  if (r == Route::kReal && !orion::op_log_enabled()) return call_real();
   const PlanInfo info = plan_info(executionPlan);
   void *px = nullptr, *pw = nullptr, *py = nullptr;
   const bool ok = info.ok && variant_pointers(variantPack, info, &px, &pw, &py);

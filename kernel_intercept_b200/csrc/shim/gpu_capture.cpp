@@ -6,6 +6,8 @@
 // create/enqueue/wait 200-241, async mode 244, error latch 247-271, C API
 // 281-322); the queue, the bounded waits and the handle -> stream map are this
 // build's.
+#include <vector>
+#include <cstdio>
 #include <pthread.h>
 #include <time.h>
 
@@ -293,9 +295,60 @@ cudaError_t get_and_clear_last_error(int client_idx) {
   return static_cast<cudaError_t>(g_last_error[client_idx].exchange(cudaSuccess));
 }
 
+namespace {
+struct OpLogEntry {
+  int client;
+  OperationType type;
+  const char* route;
+  int ndims;
+  long long dims[8];
+};
+std::mutex g_oplog_mu;
+std::vector<OpLogEntry> g_oplog;
+std::atomic<bool> g_oplog_on{false};
+}  // namespace
+
+bool op_log_enabled() { return g_oplog_on.load(std::memory_order_relaxed); }
+
+void op_log_record(int client_idx, OperationType type, const long long* dims, int ndims,
+                   const char* route) {
+  if (!op_log_enabled()) return;
+  OpLogEntry e;
+  e.client = client_idx;
+  e.type = type;
+  e.route = route;
+  e.ndims = ndims < 0 ? 0 : (ndims > 8 ? 8 : ndims);
+  for (int i = 0; i < e.ndims; ++i) e.dims[i] = dims[i];
+  std::lock_guard<std::mutex> lk(g_oplog_mu);
+  g_oplog.push_back(e);
+}
+
 }  // namespace orion
 
 extern "C" {
+
+void orion_op_log_start(void) {
+  std::lock_guard<std::mutex> lk(orion::g_oplog_mu);
+  orion::g_oplog.clear();
+  orion::g_oplog_on.store(true);
+}
+
+int orion_op_log_end(const char* path) {
+  orion::g_oplog_on.store(false);
+  std::lock_guard<std::mutex> lk(orion::g_oplog_mu);
+  if (path == nullptr) return -1;
+  FILE* f = std::fopen(path, "w");
+  if (f == nullptr) return -1;
+  for (const auto& e : orion::g_oplog) {
+    std::fprintf(f, "%d\t%s\t%s", e.client, orion::op_type_name(e.type), e.route);
+    for (int i = 0; i < e.ndims; ++i) std::fprintf(f, "\t%lld", e.dims[i]);
+    std::fprintf(f, "\n");
+  }
+  std::fclose(f);
+  const int n = static_cast<int>(orion::g_oplog.size());
+  orion::g_oplog.clear();
+  return n;
+}
 
 int orion_init(int num_clients) { return orion::init_capture_layer(num_clients); }
 void orion_shutdown() { orion::shutdown_capture_layer(); }

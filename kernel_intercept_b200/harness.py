@@ -59,6 +59,7 @@ class Orion:
             "orion_load_profile": ([ctypes.c_char_p], I),
             "orion_start_profiling": ([ctypes.c_char_p], None),
             "orion_end_profiling": ([ctypes.c_char_p], None),
+            "orion_op_log_start": ([], None), "orion_op_log_end": ([ctypes.c_char_p], I),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)

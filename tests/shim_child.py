@@ -267,6 +267,100 @@ def scenario_hpbe(orion):
             "hp_p50_ms": harness.percentile(hp.latencies_ms, 0.5), "be_iters": be.iters}
 
 
+def read_op_log(path):
+    """Entries of an op log: (client, op type, route, shape integers)."""
+    out = []
+    with open(path) as f:
+        for line in f:
+            parts = line.rstrip("\n").split("\t")
+            out.append((int(parts[0]), parts[1], parts[2], tuple(int(v) for v in parts[3:])))
+    return out
+
+
+def scenario_oplog(orion):
+    """Op order and counts: one GPT training step (2 layers, batch 2 x 256)
+    issued by client 0 through the real libraries (capture off) and then
+    captured on the kx kernels must produce the same sequence of intercepted
+    calls (type, shape, transposes, dtype); the worker must execute the
+    captured ops in that order; and with an HP client (forward) and a BE
+    client (training steps) running at once, each client's sequence must be
+    its solo sequence (repeated per step)."""
+    import tempfile
+
+    import torch
+    import torch.nn.functional as F
+
+    from kernel_intercept_b200 import harness
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.manual_seed(0)
+    m = harness.make_gpt(layers=2, device="cuda")
+    opt = torch.optim.SGD(m.parameters(), lr=1e-3)
+    tok = torch.randint(0, 32000, (2, 256), device="cuda")
+    tgt = torch.randint(0, 32000, (2, 256), device="cuda")
+
+    def train_step():
+        logits = m(tok)
+        loss = F.cross_entropy(logits.view(-1, logits.shape[-1]), tgt.view(-1))
+        opt.zero_grad(set_to_none=True)
+        loss.backward()
+        opt.step()
+
+    def fwd_step():
+        with torch.no_grad():
+            m(tok)
+
+    tmp = tempfile.mkdtemp()
+    assert orion.orion_init_scheduler(2) == 0
+    orion.orion_set_capture(0)
+    train_step()  # warm-up: allocator, library handles
+    torch.cuda.synchronize()
+
+    def logged(path, fn):
+        orion.orion_op_log_start()
+        fn()
+        torch.cuda.synchronize()
+        n = orion.orion_op_log_end(path.encode())
+        return read_op_log(path) if n >= 0 else None
+
+    real = logged(os.path.join(tmp, "real.tsv"), lambda: run_on_client(orion, 0, train_step))
+    real_fwd = logged(os.path.join(tmp, "real_fwd.tsv"), lambda: run_on_client(orion, 0, fwd_step))
+    orion.orion_start_scheduler_thread()
+    orion.orion_set_capture(1)
+    prof = os.path.join(tmp, "prof.json")
+    orion.orion_start_profiling(b"oplog")
+    cap = logged(os.path.join(tmp, "cap.tsv"), lambda: run_on_client(orion, 0, train_step))
+    orion.orion_end_profiling(prof.encode())
+    with open(prof) as f:
+        recs = json.load(f).get("kernels", [])
+    both = logged(os.path.join(tmp, "both.tsv"), lambda: harness.run_clients(
+        orion, fwd_step, train_step, hp_steps=4, hp_warmup=0, be_warmup=0))
+    orion.orion_set_capture(0)
+    stats = {c: orion.stats(c) for c in (0, 1)}
+    orion.orion_stop_scheduler()
+
+    def key(e):
+        return (e[1], e[3])
+
+    res = {"stats": stats, "n_real": len(real), "n_cap": len(cap)}
+    res["same_sequence"] = [key(e) for e in real] == [key(e) for e in cap]
+    res["real_routes"] = sorted({e[2] for e in real})
+    res["cap_routes"] = sorted({e[2] for e in cap})
+    res["clients"] = sorted({e[0] for e in real + cap})
+    captured = [e[1] for e in cap if e[2] == "capture"]
+    res["dispatch_order_same"] = [r.get("op_type") for r in recs if r.get("client") == 0] == captured
+    hp = [key(e) for e in both if e[0] == 0]
+    be = [key(e) for e in both if e[0] == 1]
+    step_fwd = [key(e) for e in real_fwd]
+    step_train = [key(e) for e in real]
+    res["hp_steps_logged"] = len(hp) / max(1, len(step_fwd))
+    res["be_steps_logged"] = len(be) / max(1, len(step_train))
+    res["hp_matches_solo"] = len(hp) > 0 and hp == step_fwd * (len(hp) // max(1, len(step_fwd)))
+    res["be_matches_solo"] = (len(be) % max(1, len(step_train)) == 0 and
+                              be == step_train * (len(be) // max(1, len(step_train))))
+    res["op_types"] = sorted({e[1] for e in real})
+    return res
+
+
 def main():
     scenario = sys.argv[1]
     from kernel_intercept_b200 import harness

@@ -46,7 +46,7 @@ cudnnBatchNormalizationForwardTrainingEx cudnnBatchNormalizationBackwardEx cudnn
 cudnnBackendDestroyDescriptor cudnnBackendCreateDescriptor cudnnBackendSetAttribute
 cudnnBackendGetAttribute cudnnBackendFinalize cudaEventRecord cudaEventRecordWithFlags cudaStreamWaitEvent
 cudaEventSynchronize cudaEventQuery cudaStreamQuery orion_set_be_keep_sms orion_get_be_keep_sms
-orion_set_sm_budgets orion_get_client_stats
+orion_set_sm_budgets orion_get_client_stats orion_op_log_start orion_op_log_end
 """.split()
 
 

@@ -85,3 +85,23 @@ def test_hp_be_clients_contend():
         assert res["stats"][c]["errors"] == 0, res
     assert res["errors"]["hp"] <= F32_TOL and res["errors"]["be"] <= F32_TOL, res
     assert res["be_iters"] >= 1
+
+
+def test_capture_keeps_op_order_and_counts():
+    """The interposer's op log: a GPT training step through the real
+    libraries and the same step captured on the kx kernels issue the same
+    calls (type, shape, transposes, dtype) in the same order; the worker runs
+    the captured ops in that order; under HP + BE contention each client's
+    sequence is its solo sequence, step after step."""
+    res = run_child("oplog")
+    assert res["n_real"] > 50 and res["n_real"] == res["n_cap"], res
+    assert res["same_sequence"], res
+    assert res["real_routes"] == ["real"], res
+    assert res["cap_routes"] == ["capture"], res
+    assert res["clients"] == [0], res
+    assert res["dispatch_order_same"], res
+    assert res["hp_matches_solo"] and res["hp_steps_logged"] == 4, res
+    assert res["be_matches_solo"] and res["be_steps_logged"] >= 1, res
+    for c in ("0", "1"):
+        assert res["stats"][c]["errors"] == 0, res
+
