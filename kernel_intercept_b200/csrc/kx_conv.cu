@@ -246,6 +246,17 @@ extern "C" int kx_conv_bwd_data(const kx_exec* ex, const kx_conv_desc* d, const 
   ConvGeom g;
   if (!make_geom(d, g) || !w || !dy || !dx || !alpha || !beta) return KX_ERR_INVALID;
   Exec e = resolve_exec(ex);
+  // Stride 1: dx is the forward cross-correlation of dy with the filter
+  // transposed (K <-> C) and flipped (for cross-correlation; unflipped for
+  // true convolution), padded by dil*(taps-1) - pad: one implicit-GEMM launch.
+  const int pad_h = g.dh * (g.R - 1) - g.ph, pad_w = g.dw * (g.S - 1) - g.pw;
+  if (implicit_conv_enabled() && g.sh == 1 && g.sw == 1 && pad_h >= 0 && pad_w >= 0) {
+    ConvShape cs{g.N, g.K, g.P, g.Q, g.C, g.R, g.S, pad_h, pad_w, 1, 1, g.dh, g.dw, g.H, g.W,
+                 g.xcorr != 0};
+    cs.transposed = true;
+    const int rc = conv_fwd_implicit(e, cs, dy, w, dx, *alpha, *beta);
+    if (rc != KX_ERR_UNSUPPORTED) return rc;
+  }
   const int nb = images_per_chunk(g);
   const size_t col_elems = static_cast<size_t>(nb) * g.CRS * g.ldpq;
   const bool repack = !g.xcorr || (g.CRS & 3) != 0;

@@ -104,7 +104,7 @@ __global__ void __launch_bounds__(256) stage_folded_split(const float* __restric
 // or the folded order (folded = true: Wp[k][(c*R + r)*S + s], padded to cp).
 __global__ void pack_filter(const float* __restrict__ w, float* __restrict__ wp,
                             float* __restrict__ wp_lo, int K, int C, int R, int S, int cp,
-                            int folded, int flip) {
+                            int folded, int flip, int transposed) {
   // 32-bit index math: the caller keeps K * row below 2^31
   const int RS = R * S;
   const int row = folded ? cp : RS * cp;
@@ -133,7 +133,7 @@ __global__ void pack_filter(const float* __restrict__ w, float* __restrict__ wp,
         r = R - 1 - r;
         s = S - 1 - s;
       }
-      v = w[((k * C + c) * R + r) * S + s];
+      v = transposed ? w[((c * K + k) * R + r) * S + s] : w[((k * C + c) * R + r) * S + s];
     }
     wp[i] = v;
     wp_lo[i] = tf32_lo(v);
@@ -471,7 +471,8 @@ int conv_fwd_implicit(const Exec& e, const ConvShape& g, const float* x, const f
   }
   note_launch();
   pack_filter<<<grid_for(wp_elems), 256, 0, e.stream>>>(w, wp, wp_lo, g.K, g.C, g.R, g.S, cp,
-                                                        folded ? 1 : 0, g.flip ? 1 : 0);
+                                                        folded ? 1 : 0, g.flip ? 1 : 0,
+                                                        g.transposed ? 1 : 0);
   if (launch_status() != KX_OK) return KX_ERR_DEVICE;
   const ConvPlan pl = plan_conv(g, t, cp, persistent_grid(e, 1 << 30));
   if (pl.pair) {

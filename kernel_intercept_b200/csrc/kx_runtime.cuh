@@ -81,6 +81,9 @@ int persistent_grid(const Exec& e, int tiles);
 struct ConvShape {
   int N, C, H, W, K, R, S, ph, pw, sh, sw, dh, dw, P, Q;
   bool flip;  // CUDNN_CONVOLUTION (true convolution) rather than cross-correlation
+  // the filter is stored [C][K][R][S] (the transpose of this convolution's
+  // [K][C][R][S]): backward data run as a forward convolution of dy
+  bool transposed = false;
 };
 
 // Forward convolution on the implicit-GEMM tcgen05 kernel (3xTF32):

@@ -2,6 +2,7 @@
 
     python -m kernel_intercept_b200.opbench vgg  [--batch 32] [--check]
     python -m kernel_intercept_b200.opbench gemm [--check]
+    python -m kernel_intercept_b200.opbench vggbwd [--batch 32] [--check]
 
 One JSON line per operation.  Every time is the mean of R back-to-back calls
 on one stream measured with CUDA events after 3 warm-up calls (operands stay
@@ -13,6 +14,8 @@ wall time of one kx C-ABI call (enqueue only).  `--check` adds the normwise
 error max|kx - ref| / max|ref| against a float64 evaluation on the GPU.
 
 vgg : the 13 VGG16 3x3 convolutions (pad 1) at batch 32, forward.
+vggbwd: the same layers' backward data (dx) and backward filter (dw); the
+      library arm is aten::convolution_backward with one output each.
 gemm: the GEMM shapes of the benchmark's models in the transposes PyTorch
       issues (column-major, cuBLAS notation), fp32 through 3xTF32 and bf16.
 """
@@ -131,6 +134,60 @@ def run_vgg(batch, check):
           flush=True)
 
 
+def run_vgg_bwd(batch, check):
+    import torch
+
+    from . import kx
+    torch.backends.cudnn.allow_tf32 = False
+    torch.backends.cudnn.benchmark = True
+    torch.manual_seed(0)
+    ex = kx.current_exec()
+    tot = {"dgrad_kx": 0.0, "dgrad_lib": 0.0, "wgrad_kx": 0.0, "wgrad_lib": 0.0}
+    for li, (c, k, hw) in enumerate(VGG16_CONVS):
+        x = torch.randn(batch, c, hw, hw, device="cuda")
+        w = torch.randn(k, c, 3, 3, device="cuda") * (2.0 / (c * 9)) ** 0.5
+        dy = torch.randn(batch, k, hw, hw, device="cuda")
+        dx = torch.empty_like(x)
+        dw = torch.empty_like(w)
+        d = kx.ConvDesc(batch, c, hw, hw, k, 3, 3, 1, 1, 1, 1, 1, 1, 1)
+        fl = 2.0 * batch * k * c * 9 * hw * hw
+        rec = {"layer": li, "c": c, "k": k, "hw": hw, "batch": batch}
+
+        def lib(mask):
+            return torch.ops.aten.convolution_backward(dy, x, w, None, [1, 1], [1, 1], [1, 1],
+                                                       False, [0, 0], 1, mask)
+
+        for name, f_kx, mask in (
+                ("dgrad", lambda: kx.conv_bwd_data(ex, d, 1.0, w.data_ptr(), dy.data_ptr(), 0.0,
+                                                   dx.data_ptr()), [True, False, False]),
+                ("wgrad", lambda: kx.conv_bwd_filter(ex, d, 1.0, x.data_ptr(), dy.data_ptr(),
+                                                     0.0, dw.data_ptr()), [False, True, False])):
+            if li == 0 and name == "dgrad":
+                continue  # the first layer's input gradient is never needed
+            t_kx = _time(f_kx)
+            kname = kx.last_kernel_name()
+            t_lib = _time(lambda: lib(mask))
+            rec[f"{name}_kx_ms"] = round(t_kx, 4)
+            rec[f"{name}_kx_tflops"] = round(fl / (t_kx * 1e-3) / 1e12, 1)
+            rec[f"{name}_cudnn_ms"] = round(t_lib, 4)
+            rec[f"{name}_cudnn_tflops"] = round(fl / (t_lib * 1e-3) / 1e12, 1)
+            rec[f"{name}_kernel"] = kname
+            tot[f"{name}_kx"] += t_kx
+            tot[f"{name}_lib"] += t_lib
+            if check:
+                f_kx()
+                ref = torch.ops.aten.convolution_backward(
+                    dy.double(), x.double(), w.double(), None, [1, 1], [1, 1], [1, 1], False,
+                    [0, 0], 1, mask)
+                got = dx if name == "dgrad" else dw
+                rec[f"{name}_err_kx"] = float(f"{_err(got, ref[0 if name == 'dgrad' else 1]):.2e}")
+                del ref
+        print(json.dumps(rec), flush=True)
+        del x, w, dy, dx, dw
+        torch.cuda.empty_cache()
+    print(json.dumps({k: round(v, 3) for k, v in tot.items()}), flush=True)
+
+
 def run_gemm(check):
     import torch
 
@@ -193,12 +250,14 @@ def run_gemm(check):
 
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
-    ap.add_argument("what", choices=["vgg", "gemm"])
+    ap.add_argument("what", choices=["vgg", "vggbwd", "gemm"])
     ap.add_argument("--batch", type=int, default=32)
     ap.add_argument("--check", action="store_true")
     args = ap.parse_args(argv)
     if args.what == "vgg":
         run_vgg(args.batch, args.check)
+    elif args.what == "vggbwd":
+        run_vgg_bwd(args.batch, args.check)
     else:
         run_gemm(args.check)
     return 0

@@ -132,6 +132,26 @@ def test_conv_bwd_data(cuda, case):
     assert o.normwise_rel_err(ddx.cpu().numpy(), ref) <= TOL_F32
 
 
+# stride-1 cases: backward data runs as a forward implicit-GEMM convolution of
+# dy with the transposed, flipped filter
+DGRAD_IMPLICIT_CASES = [
+    (8, 32, 56, 56, 128, 3, 3, (1, 1), (1, 1), (1, 1), True),
+    (2, 32, 20, 22, 64, 3, 3, (2, 2), (1, 1), (2, 2), True),    # dilated
+    (2, 48, 21, 26, 96, 3, 5, (1, 2), (1, 1), (1, 1), True),    # R != S, pad_h != pad_w
+    (2, 16, 30, 30, 32, 5, 5, (2, 2), (1, 1), (1, 1), False),   # true convolution
+    (4, 3, 32, 32, 64, 3, 3, (1, 1), (1, 1), (1, 1), True),     # 3 input channels
+    (3, 64, 14, 14, 128, 3, 3, (1, 1), (1, 1), (1, 1), True),
+]
+
+
+@pytest.mark.parametrize("case", DGRAD_IMPLICIT_CASES)
+def test_conv_bwd_data_implicit(cuda, case):
+    """Backward data on the implicit-GEMM kernel (stride 1)."""
+    kx = _kx()
+    test_conv_bwd_data(cuda, case)
+    assert kx.last_kernel_name().startswith("kx_conv_fwd_tc<")
+
+
 @pytest.mark.parametrize("case", CONV_CASES)
 def test_conv_bwd_filter(cuda, case):
     kx = _kx()
