@@ -294,6 +294,13 @@ extern "C" int kx_conv_bwd_filter(const kx_exec* ex, const kx_conv_desc* d, cons
   ConvGeom g;
   if (!make_geom(d, g) || !x || !dy || !dw || !alpha || !beta) return KX_ERR_INVALID;
   Exec e = resolve_exec(ex);
+  if (implicit_conv_enabled()) {
+    // one implicit-GEMM launch over all images (split over the pixel sum)
+    const ConvShape cs{g.N, g.C, g.H, g.W, g.K, g.R, g.S, g.ph, g.pw, g.sh,
+                       g.sw, g.dh, g.dw, g.P, g.Q, g.xcorr == 0};
+    const int rc = conv_bwd_filter_implicit(e, cs, x, dy, dw, *alpha, *beta);
+    if (rc != KX_ERR_UNSUPPORTED) return rc;
+  }
   const int nb = images_per_chunk(g);
   const size_t col_elems = static_cast<size_t>(nb) * g.CRS * g.ldpq;
   const size_t acc_elems = g.xcorr ? 0 : static_cast<size_t>(g.K) * g.CRS;

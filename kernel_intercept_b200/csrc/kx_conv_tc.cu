@@ -422,6 +422,155 @@ int grid_for(size_t total) {
   return static_cast<int>(b < 1 ? 1 : (b > cap ? cap : b));
 }
 
+// ------------------------------------------------------- backward filter --
+
+// lo = x - trunc_tf32(x), elementwise (the 3xTF32 low part of dy)
+__global__ void __launch_bounds__(256) split_lo(const float* __restrict__ x,
+                                                float* __restrict__ lo, size_t n) {
+  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<size_t>(gridDim.x) * blockDim.x)
+    lo[i] = tf32_lo(x[i]);
+}
+
+// dw[k][c][r][s] = alpha * sum over K slices of D[k][(tap, c)] + beta * dw,
+// D column-major per slice (ld = K), tap = r*S + s, or (R-1-r)*S + (S-1-s)
+// for a true convolution (its forward pass applied the filter flipped).
+// Runs only when the GEMM launch completed all its tiles.
+__global__ void __launch_bounds__(256) wgrad_reduce(const float* __restrict__ ws,
+                                                    const WorkSlot* work, int splits, int K,
+                                                    int C, int R, int S, int cp, int flip,
+                                                    float alpha, float beta, float* dw) {
+  if (work->status != 1) return;
+  const int RS = R * S;
+  const long long total = static_cast<long long>(K) * C * RS;
+  const long long mn = static_cast<long long>(K) * RS * cp;
+  for (long long i = blockIdx.x * 256LL + threadIdx.x; i < total;
+       i += static_cast<long long>(gridDim.x) * 256) {
+    const int k = static_cast<int>(i / (static_cast<long long>(C) * RS));
+    const int rem = static_cast<int>(i - static_cast<long long>(k) * C * RS);
+    const int c = rem / RS;
+    const int rs = rem - c * RS;
+    const int r = rs / S;
+    const int s = rs - r * S;
+    const int tap = flip ? (R - 1 - r) * S + (S - 1 - s) : rs;
+    const long long col = static_cast<long long>(tap) * cp + c;
+    float acc = 0.f;
+    for (int sl = 0; sl < splits; ++sl) acc += ws[sl * mn + col * K + k];
+    float o = alpha * acc;
+    if (beta != 0.f) o += beta * dw[i];
+    dw[i] = o;
+  }
+}
+
+template <int BN>
+int launch_wgrad(const Exec& e, const ConvShape& g, const float* xh, const float* xl, int cp,
+                 const float* dy, const float* dy_lo, float* dw, float alpha, float beta) {
+  using Cfg = GemmCfg<BN, Arith::F32x3, false, true>;
+  const long long pq = static_cast<long long>(g.P) * g.Q;
+  // A: dy as {P*Q, K, N}, 32 pixels x 128 output channels per box
+  CUtensorMap ma, malo, mb, mblo;
+  if (!encode_map_3d(&ma, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, dy, pq, g.K, g.N, pq, pq * g.K,
+                     Cfg::BK, Cfg::BM) ||
+      !encode_map_3d(&malo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, dy_lo, pq, g.K, g.N, pq,
+                     pq * g.K, Cfg::BK, Cfg::BM))
+    return KX_ERR_UNSUPPORTED;
+  // B: im2col of the NHWC staging, 32 pixels x 32 channels, M/N-major tf32
+  const uint64_t dims[4] = {static_cast<uint64_t>(cp), static_cast<uint64_t>(g.W),
+                            static_cast<uint64_t>(g.H), static_cast<uint64_t>(g.N)};
+  const uint64_t strides[3] = {static_cast<uint64_t>(cp) * 4,
+                               static_cast<uint64_t>(cp) * g.W * 4,
+                               static_cast<uint64_t>(cp) * g.W * g.H * 4};
+  const uint32_t es[4] = {1u, static_cast<uint32_t>(g.sw), static_cast<uint32_t>(g.sh), 1u};
+  int lo[2], up[2];
+  im2col_corners(g, lo, up);
+  if (!encode_im2col_map(&mb, xh, dims, strides, lo, up, 32, 32, es,
+                         CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B) ||
+      !encode_im2col_map(&mblo, xl, dims, strides, lo, up, 32, 32, es,
+                         CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B))
+    return KX_ERR_UNSUPPORTED;
+  GemmParams p;
+  std::memset(&p, 0, sizeof(p));
+  const int pb = static_cast<int>((pq + 31) / 32);
+  const long long num_kb = static_cast<long long>(g.N) * pb;
+  if (num_kb > 0x7fffffffLL / 32) return KX_ERR_UNSUPPORTED;
+  p.m = g.K;
+  p.n = g.R * g.S * cp;
+  p.k = static_cast<int>(num_kb * 32);
+  p.alpha = 1.f;
+  p.beta = 0.f;
+  p.d_type = DT_F32;
+  p.c_type = DT_F32;
+  p.work = work_slot_for(e.stream);
+  if (p.work == nullptr) return KX_ERR_NOMEM;
+  p.yield_flag = e.yield_flag;
+  p.done_flag = e.done_flag;
+  p.max_tiles = e.max_tiles;
+  p.timeout_ns = e.timeout_ns;
+  p.err_word = e.err_word ? e.err_word : &p.work->err;
+  p.presplit = 1;
+  p.cv_wgrad = 1;
+  p.cv_pb = pb;
+  p.cv_nb_per_tap = cp / BN;
+  p.cv_p = g.P;
+  p.cv_q = g.Q;
+  p.cv_s = g.S;
+  p.cv_pad_h = g.ph;
+  p.cv_pad_w = g.pw;
+  p.cv_str_h = g.sh;
+  p.cv_str_w = g.sw;
+  p.cv_dil_h = g.dh;
+  p.cv_dil_w = g.dw;
+  p.num_mb = (g.K + Cfg::BM - 1) / Cfg::BM;
+  p.num_nb = g.R * g.S * (cp / BN);
+  p.num_kb = static_cast<int>(num_kb);
+  // K slices: enough work units for 2 waves, at least 8 k-blocks each
+  const long long tiles = static_cast<long long>(p.num_mb) * p.num_nb;
+  const int sms = persistent_grid(e, 1 << 30);
+  long long want = (2LL * sms + tiles - 1) / tiles;
+  const long long by_k = num_kb / 8;
+  if (want > by_k) want = by_k;
+  if (want > 64) want = 64;
+  if (want < 1) want = 1;
+  const int kbps = static_cast<int>((num_kb + want - 1) / want);
+  p.splits = static_cast<int>((num_kb + kbps - 1) / kbps);
+  p.kb_per_split = kbps;
+  const size_t plane = static_cast<size_t>(p.m) * p.n;
+  float* ws = static_cast<float*>(scratch_for(e.stream, sizeof(float) * plane * p.splits, 1));
+  if (ws == nullptr) return KX_ERR_NOMEM;
+  p.ws = ws;
+  // one slice: the plain epilogue writes the raw sums (alpha 1, beta 0) to ws
+  p.D = ws;
+  p.ldd = p.m;
+  p.C = ws;
+  p.ldc = p.m;
+  p.tiles_per_batch = p.num_mb * p.num_nb * p.splits;
+  if (static_cast<long long>(p.tiles_per_batch) > 0x7fffffffLL) return KX_ERR_UNSUPPORTED;
+  p.num_tiles = p.tiles_per_batch;
+  p.tma_store = 0;
+  auto kern = kx_gemm_tc_kernel<Cfg, true>;
+  static bool attr_set[64] = {false};
+  const DeviceInfo& di = device_info();
+  if (!attr_set[di.device & 63]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             Cfg::SMEM_BYTES) != cudaSuccess)
+      return KX_ERR_DEVICE;
+    attr_set[di.device & 63] = true;
+  }
+  CUtensorMap md = ma;  // unused (no TMA stores)
+  const int grid = persistent_grid(e, p.num_tiles);
+  p.pipe_stats = pipe_stats_begin();
+  note_launch();
+  kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, e.stream>>>(ma, mb, malo, mblo, md, p);
+  pipe_stats_end(p.pipe_stats, "kx_conv_wgrad_tc", e.stream, grid);
+  note_launch();
+  wgrad_reduce<<<grid_for(static_cast<size_t>(g.K) * g.C * g.R * g.S), 256, 0, e.stream>>>(
+      ws, p.work, p.splits, g.K, g.C, g.R, g.S, cp, g.flip ? 1 : 0, alpha, beta, dw);
+  static char name[64];
+  if (name[0] == 0) snprintf(name, sizeof(name), "kx_conv_wgrad_tc<bn%d,f32x3>", BN);
+  set_last_kernel_name(name);
+  return launch_status();
+}
+
 }  // namespace
 
 int conv_fwd_implicit(const Exec& e, const ConvShape& g, const float* x, const float* w, float* y,
@@ -486,4 +635,38 @@ int conv_fwd_implicit(const Exec& e, const ConvShape& g, const float* x, const f
   return launch_conv_tc<64, false>(e, g, t, xh, xl, cp, wp, wp_lo, y, alpha, beta, pl);
 }
 
+int conv_bwd_filter_implicit(const Exec& e, const ConvShape& g, const float* x, const float* dy,
+                             float* dw, float alpha, float beta) {
+  if (e.fp32_mode != KX_FP32_3XTF32) return KX_ERR_UNSUPPORTED;
+  const long long pq = static_cast<long long>(g.P) * g.Q;
+  const int cp = (g.C + 31) / 32 * 32;
+  // 16-byte dy rows for the TMA map; channel blocks of 64 or 128
+  if (pq % 4 != 0 || cp % 64 != 0 || g.sw > 8 || g.sh > 8) return KX_ERR_UNSUPPORTED;
+  int lo[2], up[2];
+  im2col_corners(g, lo, up);
+  for (int i = 0; i < 2; ++i)
+    if (lo[i] < -128 || up[i] < -128 || up[i] > 127) return KX_ERR_UNSUPPORTED;
+  if (g.dw * (g.S - 1) >= 65536 || g.dh * (g.R - 1) >= 65536) return KX_ERR_UNSUPPORTED;
+  const size_t stage_elems = static_cast<size_t>(g.N) * g.H * g.W * cp;
+  const size_t dy_elems = static_cast<size_t>(g.N) * g.K * pq;
+  if (stage_elems > (1ull << 36) || dy_elems > (1ull << 36)) return KX_ERR_UNSUPPORTED;
+  const size_t s_pad = round256(stage_elems), d_pad = round256(dy_elems);
+  float* base = static_cast<float*>(scratch_for(e.stream, (2 * s_pad + d_pad) * sizeof(float)));
+  if (base == nullptr) return KX_ERR_NOMEM;
+  float* xh = base;
+  float* xl = base + s_pad;
+  float* dy_lo = base + 2 * s_pad;
+  const int hw = g.H * g.W;
+  dim3 grid((hw + 31) / 32, cp / 32, g.N);
+  if (grid.y > 65535 || grid.z > 65535) return KX_ERR_UNSUPPORTED;
+  note_launch();
+  stage_nhwc_split<<<grid, 256, 0, e.stream>>>(x, xh, xl, g.C, hw, cp);
+  note_launch();
+  split_lo<<<grid_for(dy_elems), 256, 0, e.stream>>>(dy, dy_lo, dy_elems);
+  if (launch_status() != KX_OK) return KX_ERR_DEVICE;
+  if (cp % 128 == 0) return launch_wgrad<128>(e, g, xh, xl, cp, dy, dy_lo, dw, alpha, beta);
+  return launch_wgrad<64>(e, g, xh, xl, cp, dy, dy_lo, dw, alpha, beta);
+}
+
 }  // namespace kx
+

@@ -102,6 +102,15 @@ struct GemmParams {
   // output pixels whatever row or image they fall in, and output row f is
   // pixel f % cv_pq of image f / cv_pq (D offset image * strideD + pixel).
   int cv_im2col, cv_pq;
+  // cv_wgrad = 1: backward filter (kernel instantiated with CONV = true and an
+  // MN-major B).  M = output channels, N = (filter tap, input channel) as
+  // cv_nb_per_tap channel blocks of BN per tap, K = output pixels of every
+  // image in blocks of 32 (cv_pb blocks per image; pixels past P*Q read zero
+  // from dy).  A = dy as a {P*Q, K, N} map; B = 32 pixels x 32 channels
+  // im2col-mode loads of the NHWC staging of x at the tile's tap.  Partials
+  // always go to ws (or to D = ws when splits == 1); a reduce kernel writes
+  // dw.
+  int cv_wgrad, cv_pb, cv_nb_per_tap;
   // Pipeline diagnostics (nullable): per CTA kPipeStats clock64 counters of
   // the time each role spends waiting (see PipeStat).
   unsigned long long* pipe_stats;
@@ -535,8 +544,20 @@ __global__ void __launch_bounds__(256, 1)
           // 3xTF32 with pre-split operands: the low parts arrive by TMA beside
           // the high parts.
           mbar_arrive_expect_tx(fb, Cfg::LOAD_BYTES * (lo_by_tma ? 2 : 1));
+          // backward filter: k-block -> (image, 32-pixel block of P*Q)
+          int wg_img = 0, wg_f0 = 0;
+          if constexpr (CONV) {
+            if (p.cv_wgrad) {
+              wg_img = kb / p.cv_pb;
+              wg_f0 = (kb - wg_img * p.cv_pb) * 32;
+            }
+          }
           auto load_a = [&](uint32_t sa, const CUtensorMap* map) {
             if constexpr (CONV) {
+              if (p.cv_wgrad) {  // dy rows k = mb*128.., 32 pixels
+                tma_load_3d(sa, map, fb, wg_f0, mb * Cfg::BM, wg_img);
+                return;
+              }
               const int tap = kb / p.cv_cb;
               const int c0 = (kb - tap * p.cv_cb) * 32;
               const int rr = tap / p.cv_s;
@@ -571,6 +592,22 @@ __global__ void __launch_bounds__(256, 1)
           // this CTA's rows of B: all BN, or half of them in a pair
           const int n0 = nb * Cfg::BN + static_cast<int>(rank) * Cfg::B_ROWS;
           auto load_b = [&](uint32_t sbb, const CUtensorMap* map) {
+            if constexpr (CONV && Cfg::B_MN) {
+              // backward filter: BN/32 im2col loads of 32 pixels x 32 channels
+              const int tap = nb / p.cv_nb_per_tap;
+              const int cb = nb - tap * p.cv_nb_per_tap;
+              const int rr = tap / p.cv_s;
+              const int ss = tap - rr * p.cv_s;
+              const int oh = wg_f0 / p.cv_q;
+              const int ow = wg_f0 - oh * p.cv_q;
+#pragma unroll
+              for (int c = 0; c < Cfg::B_ROWS / 32; ++c)
+                tma_load_4d_im2col(sbb + c * Cfg::BK * 128, map, fb, cb * Cfg::BN + c * 32,
+                                   ow * p.cv_str_w - p.cv_pad_w, oh * p.cv_str_h - p.cv_pad_h,
+                                   wg_img, static_cast<uint16_t>(ss * p.cv_dil_w),
+                                   static_cast<uint16_t>(rr * p.cv_dil_h));
+              return;
+            }
             if (!Cfg::B_MN) {
               tma_load_3d(sbb, map, fb, kb * Cfg::BK, n0, bb);
             } else {
@@ -801,7 +838,9 @@ __global__ void __launch_bounds__(256, 1)
       bool warp_tma = use_tma_store;
       int st_img = 0, st_pix = 0;
       if constexpr (CONV) {
-        if (p.cv_im2col) {
+        if (p.cv_wgrad) {
+          // plain GEMM rows (output channels) into ws / D
+        } else if (p.cv_im2col) {
           const int img = row / p.cv_pq;
           const int pix = row - img * p.cv_pq;
           d_base = static_cast<size_t>(img) * p.strideD + pix;

@@ -196,7 +196,8 @@ bool encode_map(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* 
 
 bool encode_im2col_map(CUtensorMap* map, const void* base, const uint64_t* dims,
                        const uint64_t* strides_bytes, const int* lower, const int* upper,
-                       uint32_t channels, uint32_t pixels, const uint32_t* elem_strides) {
+                       uint32_t channels, uint32_t pixels, const uint32_t* elem_strides,
+                       CUtensorMapSwizzle swz) {
   EncodeIm2colFn fn = encode_im2col_fn();
   if (fn == nullptr) return false;
   if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0) return false;
@@ -218,8 +219,8 @@ bool encode_im2col_map(CUtensorMap* map, const void* base, const uint64_t* dims,
     if (lower[i] < -128 || lower[i] > 127 || upper[i] < -128 || upper[i] > 127) return false;
   std::memset(map, 0, sizeof(CUtensorMap));
   CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<void*>(base), d, s, lower,
-                  upper, channels, pixels, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  upper, channels, pixels, es, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }

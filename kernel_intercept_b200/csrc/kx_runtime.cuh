@@ -93,6 +93,13 @@ struct ConvShape {
 int conv_fwd_implicit(const Exec& e, const ConvShape& g, const float* x, const float* w, float* y,
                       float alpha, float beta);
 
+// Backward filter on the implicit-GEMM tcgen05 kernel (3xTF32):
+// dw = alpha * dL/dw + beta * dw.  KX_ERR_UNSUPPORTED outside its reach
+// (P*Q not a multiple of 4, fewer than 64 padded channels, ...): the caller
+// then lowers through im2col.  Defined in kx_conv_tc.cu.
+int conv_bwd_filter_implicit(const Exec& e, const ConvShape& g, const float* x, const float* dy,
+                             float* dw, float alpha, float beta);
+
 
 // cuTensorMapEncodeTiled through cudaGetDriverEntryPoint (no libcuda link).
 // 3-D map {inner, outer, batch} with 128-byte swizzle.  Returns false when the
@@ -119,7 +126,8 @@ bool encode_map(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* 
 // swizzle, zero OOB fill.  Returns false when the driver rejects the geometry.
 bool encode_im2col_map(CUtensorMap* map, const void* base, const uint64_t* dims,
                        const uint64_t* strides_bytes, const int* lower, const int* upper,
-                       uint32_t channels, uint32_t pixels, const uint32_t* elem_strides);
+                       uint32_t channels, uint32_t pixels, const uint32_t* elem_strides,
+                       CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B);
 
 void set_last_kernel_name(const char* name);
 

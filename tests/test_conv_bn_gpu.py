@@ -170,6 +170,24 @@ def test_conv_bwd_filter(cuda, case):
     assert o.normwise_rel_err(ddw.cpu().numpy(), ref) <= TOL_F32
 
 
+# backward filter on the implicit-GEMM kernel (>= 64 channels, P*Q % 4 == 0):
+# dy as the A operand, im2col-mode loads of x as B, split over the pixel sum
+WGRAD_IMPLICIT_CASES = [
+    (8, 64, 56, 56, 128, 3, 3, (1, 1), (1, 1), (1, 1), True),
+    (2, 128, 20, 22, 64, 3, 3, (2, 2), (1, 1), (2, 2), True),   # dilated
+    (2, 128, 20, 28, 96, 3, 5, (1, 2), (1, 2), (1, 1), True),   # R != S, stride 2 in W
+    (2, 64, 16, 16, 32, 5, 5, (2, 2), (1, 1), (1, 1), False),   # true convolution
+    (3, 512, 14, 14, 128, 3, 3, (1, 1), (1, 1), (1, 1), True),  # P*Q = 196: partial block
+]
+
+
+@pytest.mark.parametrize("case", WGRAD_IMPLICIT_CASES)
+def test_conv_bwd_filter_implicit(cuda, case):
+    kx = _kx()
+    test_conv_bwd_filter(cuda, case)
+    assert kx.last_kernel_name().startswith("kx_conv_wgrad_tc<")
+
+
 def test_conv_invalid(cuda):
     kx = _kx()
     bad = kx.ConvDesc(1, 1, 2, 2, 1, 5, 5, 0, 0, 1, 1, 1, 1, 1)  # filter larger than input
