@@ -11,6 +11,8 @@ memory (small enough for a multi-pass profiler capture):
 
   conv3_2     VGG16 conv3_2 forward, batch 32, 256 -> 256 channels, 56x56, 3x3
               pad 1 (x and y 103 MB each)
+  dgrad3_2    the same layer's backward data (dx from dy and w)
+  wgrad3_2    the same layer's backward filter (dw from x and dy)
   vgg16_convs the 13 VGG16 convolution layers, batch 32, forward, in order
   gemm_f32    4096^3 fp32 SGEMM (3xTF32 with pre-split operands)
   gemm_bf16   2048 x 4096 x 2048 bf16 GemmEx (a LLaMA-7B query projection)
@@ -24,7 +26,8 @@ import argparse
 import os
 import sys
 
-CASES = ("conv3_2", "vgg16_convs", "gemm_f32", "gemm_bf16", "bn_train", "hp_step")
+CASES = ("conv3_2", "dgrad3_2", "wgrad3_2", "vgg16_convs", "gemm_f32", "gemm_bf16", "bn_train",
+         "hp_step")
 
 # VGG16 convolution stack: (in channels, out channels, spatial size)
 VGG16_CONVS = [(3, 64, 224), (64, 64, 224), (64, 128, 112), (128, 128, 112),
@@ -52,6 +55,20 @@ def _direct(case, reps):
             d = kx.ConvDesc(n, c, hw, hw, k, 3, 3, 1, 1, 1, 1, 1, 1, 1)
             calls.append(lambda d=d, x=x, w=w, y=y: kx.conv_fwd(
                 ex, d, 1.0, x.data_ptr(), w.data_ptr(), 0.0, y.data_ptr()))
+    elif case in ("dgrad3_2", "wgrad3_2"):
+        n, c, k, hw = 32, 256, 256, 56
+        x = torch.randn(n, c, hw, hw, device=dev)
+        w = torch.randn(k, c, 3, 3, device=dev) * (2.0 / (c * 9)) ** 0.5
+        dy = torch.randn(n, k, hw, hw, device=dev)
+        dx = torch.empty_like(x)
+        dw = torch.empty_like(w)
+        d = kx.ConvDesc(n, c, hw, hw, k, 3, 3, 1, 1, 1, 1, 1, 1, 1)
+        if case == "dgrad3_2":
+            calls.append(lambda: kx.conv_bwd_data(ex, d, 1.0, w.data_ptr(), dy.data_ptr(), 0.0,
+                                                  dx.data_ptr()))
+        else:
+            calls.append(lambda: kx.conv_bwd_filter(ex, d, 1.0, x.data_ptr(), dy.data_ptr(), 0.0,
+                                                    dw.data_ptr()))
     elif case == "gemm_f32":
         s = 4096
         a = torch.randn(s, s, device=dev)

@@ -178,6 +178,7 @@ WGRAD_IMPLICIT_CASES = [
     (2, 128, 20, 28, 96, 3, 5, (1, 2), (1, 2), (1, 1), True),   # R != S, stride 2 in W
     (2, 64, 16, 16, 32, 5, 5, (2, 2), (1, 1), (1, 1), False),   # true convolution
     (3, 512, 14, 14, 128, 3, 3, (1, 1), (1, 1), (1, 1), True),  # P*Q = 196: partial block
+    (4, 3, 32, 32, 64, 3, 3, (1, 1), (1, 1), (1, 1), True),     # C = 3: taps folded
 ]
 
 
