@@ -532,6 +532,48 @@ __global__ void __launch_bounds__(256, 1)
         tile_k_range(tile, p, kb0, nkb);
         const int ba = p.a_bcast ? 0 : b;
         const int bb = p.b_bcast ? 0 : b;
+        // this CTA's rows of B: all BN, or half of them in a pair
+        const int n0 = nb * Cfg::BN + static_cast<int>(rank) * Cfg::B_ROWS;
+        // Per-tile coordinate state (the single producer thread's issue loop
+        // is on the critical path: no divisions per k-block).
+        //  conv (forward): the tile's filter-window origin (w0, h0, image) and
+        //    a (tap row rr, tap column ss, channel block cb) cursor over K;
+        //  backward filter: the B operand's tap / channel block (fixed per
+        //    tile) and an (image, pixel f0, output row oh, column ow) cursor.
+        int cv_w0 = 0, cv_h0 = 0, cv_img = b, rr = 0, ss = 0, cb = 0;
+        int wg_img = 0, wg_f0 = 0, wg_oh = 0, wg_ow = 0, wg_c0 = 0, wg_offw = 0, wg_offh = 0;
+        if constexpr (CONV) {
+          if (p.cv_wgrad) {
+            wg_img = kb0 / p.cv_pb;
+            wg_f0 = (kb0 - wg_img * p.cv_pb) * 32;
+            wg_oh = wg_f0 / p.cv_q;
+            wg_ow = wg_f0 - wg_oh * p.cv_q;
+            const int tap = nb / p.cv_nb_per_tap;
+            const int tr = tap / p.cv_s;
+            wg_c0 = (nb - tap * p.cv_nb_per_tap) * Cfg::BN;
+            wg_offw = (tap - tr * p.cv_s) * p.cv_dil_w;
+            wg_offh = tr * p.cv_dil_h;
+          } else {
+            if (p.cv_im2col) {
+              const int f0 = mb * Cfg::BM;
+              cv_img = f0 / p.cv_pq;
+              const int rem = f0 - cv_img * p.cv_pq;
+              const int oh = rem / p.cv_q;
+              const int ow = rem - oh * p.cv_q;
+              cv_w0 = ow * p.cv_str_w - p.cv_pad_w;
+              cv_h0 = oh * p.cv_str_h - p.cv_pad_h;
+            } else {
+              const int th = mb / p.cv_tiles_w;
+              const int tw = mb - th * p.cv_tiles_w;
+              cv_w0 = tw * p.cv_wbox * p.cv_str_w - p.cv_pad_w;
+              cv_h0 = th * p.cv_hbox * p.cv_str_h - p.cv_pad_h;
+            }
+            const int tap = kb0 / p.cv_cb;
+            cb = kb0 - tap * p.cv_cb;
+            rr = tap / p.cv_s;
+            ss = tap - rr * p.cv_s;
+          }
+        }
         bool ok = true;
         for (int kb = kb0; kb < kb0 + nkb; ++kb, ++it) {
           const uint32_t s = it % S;
@@ -544,42 +586,18 @@ __global__ void __launch_bounds__(256, 1)
           // 3xTF32 with pre-split operands: the low parts arrive by TMA beside
           // the high parts.
           mbar_arrive_expect_tx(fb, Cfg::LOAD_BYTES * (lo_by_tma ? 2 : 1));
-          // backward filter: k-block -> (image, 32-pixel block of P*Q)
-          int wg_img = 0, wg_f0 = 0;
-          if constexpr (CONV) {
-            if (p.cv_wgrad) {
-              wg_img = kb / p.cv_pb;
-              wg_f0 = (kb - wg_img * p.cv_pb) * 32;
-            }
-          }
           auto load_a = [&](uint32_t sa, const CUtensorMap* map) {
             if constexpr (CONV) {
               if (p.cv_wgrad) {  // dy rows k = mb*128.., 32 pixels
                 tma_load_3d(sa, map, fb, wg_f0, mb * Cfg::BM, wg_img);
-                return;
-              }
-              const int tap = kb / p.cv_cb;
-              const int c0 = (kb - tap * p.cv_cb) * 32;
-              const int rr = tap / p.cv_s;
-              const int ss = tap - rr * p.cv_s;
-              if (p.cv_im2col) {
-                // first output pixel of the tile -> its filter-window corner
-                const int f0 = mb * Cfg::BM;
-                const int img = f0 / p.cv_pq;
-                const int rem = f0 - img * p.cv_pq;
-                const int oh = rem / p.cv_q;
-                const int ow = rem - oh * p.cv_q;
-                tma_load_4d_im2col(sa, map, fb, c0, ow * p.cv_str_w - p.cv_pad_w,
-                                   oh * p.cv_str_h - p.cv_pad_h, img,
+              } else if (p.cv_im2col) {
+                tma_load_4d_im2col(sa, map, fb, cb * 32, cv_w0, cv_h0, cv_img,
                                    static_cast<uint16_t>(ss * p.cv_dil_w),
                                    static_cast<uint16_t>(rr * p.cv_dil_h));
-                return;
+              } else {
+                tma_load_4d(sa, map, fb, cb * 32, cv_w0 + ss * p.cv_dil_w,
+                            cv_h0 + rr * p.cv_dil_h, cv_img);
               }
-              const int th = mb / p.cv_tiles_w;
-              const int tw = mb - th * p.cv_tiles_w;
-              const int w0 = tw * p.cv_wbox * p.cv_str_w - p.cv_pad_w + ss * p.cv_dil_w;
-              const int h0 = th * p.cv_hbox * p.cv_str_h - p.cv_pad_h + rr * p.cv_dil_h;
-              tma_load_4d(sa, map, fb, c0, w0, h0, b);
             } else if (!Cfg::A_MN) {
               tma_load_3d(sa, map, fb, kb * Cfg::BK, mb * Cfg::BM, ba);
             } else {
@@ -589,26 +607,17 @@ __global__ void __launch_bounds__(256, 1)
                             kb * Cfg::BK, ba);
             }
           };
-          // this CTA's rows of B: all BN, or half of them in a pair
-          const int n0 = nb * Cfg::BN + static_cast<int>(rank) * Cfg::B_ROWS;
           auto load_b = [&](uint32_t sbb, const CUtensorMap* map) {
             if constexpr (CONV && Cfg::B_MN) {
               // backward filter: BN/32 im2col loads of 32 pixels x 32 channels
-              const int tap = nb / p.cv_nb_per_tap;
-              const int cb = nb - tap * p.cv_nb_per_tap;
-              const int rr = tap / p.cv_s;
-              const int ss = tap - rr * p.cv_s;
-              const int oh = wg_f0 / p.cv_q;
-              const int ow = wg_f0 - oh * p.cv_q;
+              const int wx = wg_ow * p.cv_str_w - p.cv_pad_w;
+              const int hy = wg_oh * p.cv_str_h - p.cv_pad_h;
 #pragma unroll
               for (int c = 0; c < Cfg::B_ROWS / 32; ++c)
-                tma_load_4d_im2col(sbb + c * Cfg::BK * 128, map, fb, cb * Cfg::BN + c * 32,
-                                   ow * p.cv_str_w - p.cv_pad_w, oh * p.cv_str_h - p.cv_pad_h,
-                                   wg_img, static_cast<uint16_t>(ss * p.cv_dil_w),
-                                   static_cast<uint16_t>(rr * p.cv_dil_h));
-              return;
-            }
-            if (!Cfg::B_MN) {
+                tma_load_4d_im2col(sbb + c * Cfg::BK * 128, map, fb, wg_c0 + c * 32, wx, hy,
+                                   wg_img, static_cast<uint16_t>(wg_offw),
+                                   static_cast<uint16_t>(wg_offh));
+            } else if (!Cfg::B_MN) {
               tma_load_3d(sbb, map, fb, kb * Cfg::BK, n0, bb);
             } else {
 #pragma unroll
@@ -622,6 +631,30 @@ __global__ void __launch_bounds__(256, 1)
           if (lo_by_tma) {
             load_a(smem_addr(stageAlo(s)), &tmAlo);
             load_b(smem_addr(stageBlo(s)), &tmBlo);
+          }
+          // advance the coordinate cursors to the next k-block
+          if constexpr (CONV) {
+            if (p.cv_wgrad) {
+              wg_f0 += 32;
+              if (wg_f0 >= p.cv_pb * 32) {
+                wg_f0 = 0;
+                wg_oh = 0;
+                wg_ow = 0;
+                ++wg_img;
+              } else {
+                wg_ow += 32;
+                while (wg_ow >= p.cv_q) {
+                  wg_ow -= p.cv_q;
+                  ++wg_oh;
+                }
+              }
+            } else if (++cb == p.cv_cb) {
+              cb = 0;
+              if (++ss == p.cv_s) {
+                ss = 0;
+                ++rr;
+              }
+            }
           }
         }
         if (!ok) break;
