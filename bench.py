@@ -60,6 +60,9 @@ def parse():
     ap.add_argument("--gil-switch-ms", type=float, default=0.5,
                     help="sys.setswitchinterval of the process (HP and BE are Python threads; "
                          "0: Python's default of 5 ms)")
+    ap.add_argument("--gc-freeze", type=int, default=0,
+                    help="1: freeze the warm-up's objects and pause Python's cyclic garbage "
+                         "collector while the clients run (collections stop every thread)")
     ap.add_argument("--hp-load", type=float, default=1.0 / 3.0,
                     help="HP duty cycle of the paced phase (request period = solo p50 / load)")
     return ap.parse_args()
@@ -275,6 +278,11 @@ def run_kx(args):
         orion.orion_set_be_keep_sms(args.be_keep_sms)
     orion.orion_start_scheduler_thread()
     orion.orion_set_capture(1)
+    if args.gc_freeze:
+        import gc
+        gc.collect()
+        gc.freeze()
+        gc.disable()
 
     def barrier():
         torch.cuda.synchronize()
@@ -386,7 +394,8 @@ def run_kx(args):
                    "hp_batch": HP_BATCH, "be_batch": BE_BATCH, "be_seq": BE_SEQ,
                    "parallelism": f"placement x{world} (one HP+BE group per GPU, no collective)",
                    "l2": "inputs larger than L2 (VGG16 first-block activations 411 MB)",
-                   "gil_switch_ms": round(sys.getswitchinterval() * 1e3, 3)},
+                   "gil_switch_ms": round(sys.getswitchinterval() * 1e3, 3),
+                   "gc_frozen": bool(args.gc_freeze)},
         "hp": {"p50_ms": round(p50, 3), "p99_ms": round(p99, 3), "solo_p50_ms": round(s50, 3),
                "solo_p99_ms": round(s99, 3), "p99_vs_solo": round(p99 / s99, 4) if s99 else None,
                "steps": args.steps, "solo_steps": lat_steps},
