@@ -111,6 +111,10 @@ struct GemmParams {
   // always go to ws (or to D = ws when splits == 1); a reduce kernel writes
   // dw.
   int cv_wgrad, cv_pb, cv_nb_per_tap;
+  // 1: the M/N-major A (B) tile arrives as one 4-D TMA box {CHUNK, BK,
+  // chunks, 1} of a map whose third dimension steps CHUNK elements through
+  // M (N), instead of one load per 128-byte chunk (M, N multiples of CHUNK).
+  int a_single, b_single;
   // Pipeline diagnostics (nullable): per CTA kPipeStats clock64 counters of
   // the time each role spends waiting (see PipeStat).
   unsigned long long* pipe_stats;
@@ -600,6 +604,8 @@ __global__ void __launch_bounds__(256, 1)
               }
             } else if (!Cfg::A_MN) {
               tma_load_3d(sa, map, fb, kb * Cfg::BK, mb * Cfg::BM, ba);
+            } else if (p.a_single) {
+              tma_load_4d(sa, map, fb, 0, kb * Cfg::BK, mb * (Cfg::BM / Cfg::CHUNK), ba);
             } else {
 #pragma unroll
               for (int c = 0; c < Cfg::BM / Cfg::CHUNK; ++c)
@@ -619,6 +625,8 @@ __global__ void __launch_bounds__(256, 1)
                                    static_cast<uint16_t>(wg_offh));
             } else if (!Cfg::B_MN) {
               tma_load_3d(sbb, map, fb, kb * Cfg::BK, n0, bb);
+            } else if (p.b_single) {
+              tma_load_4d(sbb, map, fb, 0, kb * Cfg::BK, n0 / Cfg::CHUNK, bb);
             } else {
 #pragma unroll
               for (int c = 0; c < Cfg::B_ROWS / Cfg::CHUNK; ++c)

@@ -54,10 +54,42 @@ int launch_gemm_tc(const Exec& e, const TcProblem& pr, GemmParams p) {
                : encode_map_3d(m, dt, Cfg::ESIZE, base, pr.k, pr.n, pr.batch, pr.ldb, pr.strideB,
                                Cfg::BK, BN);
   };
-  if (!map_a(&ma, pr.A) || !map_b(&mb, pr.B)) return KX_ERR_UNSUPPORTED;
-  if (Cfg::SPLIT && p.presplit) {
-    if (pr.Alo == nullptr || pr.Blo == nullptr) return KX_ERR_INVALID;
-    if (!map_a(&malo, pr.Alo) || !map_b(&mblo, pr.Blo)) return KX_ERR_UNSUPPORTED;
+  // M/N-major tile in one TMA box: {CHUNK, K, rows / CHUNK, batch} with the
+  // third dimension stepping CHUNK elements.  Only when the rows are a
+  // multiple of CHUNK (the box's inner dimension is a whole chunk, so a
+  // partial last chunk would read past the matrix).
+  auto map_single = [&](CUtensorMap* m, const void* base, long long rows, long long ld,
+                        long long stride, int box_chunks, CUtensorMapSwizzle swz) {
+    const bool batched = pr.batch > 1 && stride != 0;
+    const uint64_t dims[4] = {static_cast<uint64_t>(Cfg::CHUNK), static_cast<uint64_t>(pr.k),
+                              static_cast<uint64_t>(rows / Cfg::CHUNK),
+                              static_cast<uint64_t>(batched ? pr.batch : 1)};
+    const uint64_t strides[3] = {static_cast<uint64_t>(ld) * Cfg::ESIZE,
+                                 static_cast<uint64_t>(Cfg::CHUNK) * Cfg::ESIZE,
+                                 static_cast<uint64_t>(batched ? stride : rows * ld) * Cfg::ESIZE};
+    const uint32_t box[4] = {static_cast<uint32_t>(Cfg::CHUNK), static_cast<uint32_t>(Cfg::BK),
+                             static_cast<uint32_t>(box_chunks), 1u};
+    return encode_map(m, dt, 4, base, dims, strides, box, swz);
+  };
+  p.a_single = 0;
+  p.b_single = 0;
+  const bool lo_maps = Cfg::SPLIT && p.presplit;
+  if (lo_maps && (pr.Alo == nullptr || pr.Blo == nullptr)) return KX_ERR_INVALID;
+  if (AMN && pr.m % Cfg::CHUNK == 0 && !single_box_disabled() &&
+      map_single(&ma, pr.A, pr.m, pr.lda, pr.strideA, Cfg::BM / Cfg::CHUNK, swzA) &&
+      (!lo_maps ||
+       map_single(&malo, pr.Alo, pr.m, pr.lda, pr.strideA, Cfg::BM / Cfg::CHUNK, swzA)))
+    p.a_single = 1;
+  if (BMN && pr.n % Cfg::CHUNK == 0 && !single_box_disabled() &&
+      map_single(&mb, pr.B, pr.n, pr.ldb, pr.strideB, Cfg::B_ROWS / Cfg::CHUNK, swzB) &&
+      (!lo_maps ||
+       map_single(&mblo, pr.Blo, pr.n, pr.ldb, pr.strideB, Cfg::B_ROWS / Cfg::CHUNK, swzB)))
+    p.b_single = 1;
+  if ((!p.a_single && !map_a(&ma, pr.A)) || (!p.b_single && !map_b(&mb, pr.B)))
+    return KX_ERR_UNSUPPORTED;
+  if (lo_maps) {
+    if ((!p.a_single && !map_a(&malo, pr.Alo)) || (!p.b_single && !map_b(&mblo, pr.Blo)))
+      return KX_ERR_UNSUPPORTED;
   } else {
     malo = ma;
     mblo = mb;

@@ -248,6 +248,14 @@ bool encode_map_3d(CUtensorMap* map, CUtensorMapDataType dt, int esize, const vo
 
 void set_last_kernel_name(const char* name) { tl_kernel_name = name; }
 
+bool single_box_disabled() {
+  static const bool off = [] {
+    const char* v = std::getenv("KX_SINGLE_BOX");
+    return v != nullptr && v[0] == '0';
+  }();
+  return off;
+}
+
 unsigned long long* pipe_stats_begin() {
   static const bool on = [] {
     const char* s = std::getenv("KX_PIPE_STATS");

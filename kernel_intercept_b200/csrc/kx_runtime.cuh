@@ -131,6 +131,9 @@ bool encode_im2col_map(CUtensorMap* map, const void* base, const uint64_t* dims,
 
 void set_last_kernel_name(const char* name);
 
+// KX_SINGLE_BOX=0: M/N-major GEMM tiles as one TMA load per 128-byte chunk.
+bool single_box_disabled();
+
 // Pipeline diagnostics of the tcgen05 kernels (KX_PIPE_STATS=1): a zeroed
 // device buffer for GemmParams::pipe_stats (nullptr when off), and a report of
 // the per-role wait fractions to stderr after the launch (synchronises).
