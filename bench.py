@@ -338,8 +338,11 @@ def run_kx(args):
     s50_now = harness.percentile(hp_solo.latencies_ms, 0.5)
     period = s50_now / max(args.hp_load, 1e-3)
     paced_steps = lat_steps
+    for c in (0, 1):
+        orion.waits(c, reset=True)
     hp_p, be_p = harness.run_clients(orion, hp_step, be_step, paced_steps, args.warmup,
                                      hp_period_ms=period)
+    paced_waits = {("hp", "be")[c]: orion.waits(c) for c in (0, 1)}
     # phase 5: e2e (host buffers in every HP step), contended
     hp_e2e = None
     if not args.no_e2e:
@@ -410,7 +413,10 @@ def run_kx(args):
                   "be_iters_per_s": round(be_p.iters / (be_p.elapsed_ms / 1e3), 3)
                   if be_p.elapsed_ms else None,
                   "be_retention": round(be_p.iters / (be_p.elapsed_ms / 1e3) / be_solo_ips, 4)
-                  if be_p.elapsed_ms and be_solo_ips else None},
+                  if be_p.elapsed_ms and be_solo_ips else None,
+                  "client_waits": {k: {kk: round(vv, 3) if isinstance(vv, float) else vv
+                                       for kk, vv in w.items()}
+                                   for k, w in paced_waits.items()}},
         "be": {"iters_per_s": round(be_c_ips, 3), "solo_iters_per_s": round(be_solo_ips, 3),
                "retention": round(be_c_ips / be_solo_ips, 4) if be_solo_ips else None,
                "tokens_per_s": round(be_c_ips * BE_BATCH * BE_SEQ, 1)},

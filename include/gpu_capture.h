@@ -57,6 +57,7 @@ struct KernelLaunchParams {
     int api;
     const void* ex_config;   // cudaLaunchConfig_t* (api 1)
     void** extra;            // cuLaunchKernel extra (api 2)
+    std::shared_ptr<void> ex_owned;  // keeps *ex_config and its attributes alive (api 1)
 
     KernelLaunchParams()
         : func(nullptr), sharedMem(0), stream(nullptr), original_args(nullptr), num_args(0),
@@ -378,6 +379,10 @@ int get_async_mode_internal();
 void set_last_error(int client_idx, cudaError_t error);
 cudaError_t get_and_clear_last_error(int client_idx);
 
+/** Time client threads spent blocked in wait_operation (see
+ *  orion_get_client_waits). */
+void get_wait_stats(int client_idx, unsigned long long* out4, bool reset);
+
 /** Op log (addition of this build; see orion_op_log_start). */
 bool op_log_enabled();
 /** One intercepted dense call: client (resolved even with capture off), op
@@ -413,6 +418,13 @@ int orion_resolve_client_idx(void* stream, void* handle);
  * route, shape integers) and returns the number of lines, or -1. */
 void orion_op_log_start(void);
 int orion_op_log_end(const char* path);
+
+/* Client-thread blocking (addition of this build): how often and how long a
+ * client's threads waited for its worker inside intercepted calls (those that
+ * must complete before returning: copies from pageable memory, allocations,
+ * launches whose arguments could not be copied, ...).  out4 = {waits,
+ * total ns, longest ns, OperationType of the longest}; reset != 0 clears. */
+int orion_get_client_waits(int client_idx, unsigned long long* out4, int reset);
 }
 
 #endif  // ORION_GPU_CAPTURE_H

@@ -237,13 +237,10 @@ cudaError_t cudaLaunchKernelExC(const cudaLaunchConfig_t* config, const void* fu
   kp.stream = config->stream;
   kp.original_args = args;
   kp.ex_config = &owned->cfg;
+  kp.ex_owned = owned;  // the config and its attributes live as long as the record
   const bool copied = deep_copy_args(kp, args, func, false);
   op->params = std::move(kp);
-  // keep the config alive with the record: must wait when not copied anyway;
-  // when copied, wait too if attributes are present (they live in `owned`)
-  const bool must_wait = !copied || true;
-  cudaError_t r = run_captured(op, must_wait);
-  return r;
+  return run_captured(op, !copied);
 }
 
 CUresult cuLaunchKernel(CUfunction f, unsigned int gridDimX, unsigned int gridDimY,

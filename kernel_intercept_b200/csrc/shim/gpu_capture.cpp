@@ -268,8 +268,37 @@ void enqueue_operation(OperationPtr op) {
   g_capture_state.client_queues[op->client_idx]->push(std::move(op));
 }
 
+namespace {
+// How long client threads block in wait_operation, per client.
+struct WaitStats {
+  std::atomic<unsigned long long> count{0}, total_ns{0}, max_ns{0}, max_type{0};
+};
+WaitStats g_wait_stats[MAX_CLIENTS];
+}  // namespace
+
 void wait_operation(OperationPtr op) {
-  if (op) op->wait_completion();
+  if (!op) return;
+  if (op->completed.load(std::memory_order_acquire)) return;
+  const int64_t t0 = now_ns();
+  op->wait_completion();
+  const unsigned long long dt = static_cast<unsigned long long>(now_ns() - t0);
+  if (op->client_idx < 0 || op->client_idx >= MAX_CLIENTS) return;
+  WaitStats& w = g_wait_stats[op->client_idx];
+  w.count.fetch_add(1, std::memory_order_relaxed);
+  w.total_ns.fetch_add(dt, std::memory_order_relaxed);
+  unsigned long long prev = w.max_ns.load(std::memory_order_relaxed);
+  while (dt > prev && !w.max_ns.compare_exchange_weak(prev, dt)) {
+  }
+  if (dt >= prev) w.max_type.store(static_cast<unsigned long long>(op->type));
+}
+
+void get_wait_stats(int client_idx, unsigned long long* out4, bool reset) {
+  if (client_idx < 0 || client_idx >= MAX_CLIENTS) return;
+  WaitStats& w = g_wait_stats[client_idx];
+  out4[0] = reset ? w.count.exchange(0) : w.count.load();
+  out4[1] = reset ? w.total_ns.exchange(0) : w.total_ns.load();
+  out4[2] = reset ? w.max_ns.exchange(0) : w.max_ns.load();
+  out4[3] = reset ? w.max_type.exchange(0) : w.max_type.load();
 }
 
 OperationPtr submit_operation(int client_idx, OperationType type) {
@@ -326,6 +355,12 @@ void op_log_record(int client_idx, OperationType type, const long long* dims, in
 }  // namespace orion
 
 extern "C" {
+
+int orion_get_client_waits(int client_idx, unsigned long long* out4, int reset) {
+  if (out4 == nullptr || client_idx < 0 || client_idx >= orion::MAX_CLIENTS) return -1;
+  orion::get_wait_stats(client_idx, out4, reset != 0);
+  return 0;
+}
 
 void orion_op_log_start(void) {
   std::lock_guard<std::mutex> lk(orion::g_oplog_mu);

@@ -60,6 +60,7 @@ class Orion:
             "orion_start_profiling": ([ctypes.c_char_p], None),
             "orion_end_profiling": ([ctypes.c_char_p], None),
             "orion_op_log_start": ([], None), "orion_op_log_end": ([ctypes.c_char_p], I),
+            "orion_get_client_waits": ([I, ctypes.POINTER(ctypes.c_ulonglong), I], I),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)
@@ -68,6 +69,12 @@ class Orion:
 
     def __getattr__(self, name):
         return getattr(self.lib, name)
+
+    def waits(self, client: int, reset: bool = False) -> dict:
+        out = (ctypes.c_ulonglong * 4)()
+        self.lib.orion_get_client_waits(client, out, 1 if reset else 0)
+        return {"waits": int(out[0]), "total_ms": out[1] / 1e6, "max_ms": out[2] / 1e6,
+                "max_op": int(out[3])}
 
     def stats(self, client: int) -> dict:
         out = (ctypes.c_ulonglong * 6)()
