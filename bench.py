@@ -63,6 +63,10 @@ def parse():
     ap.add_argument("--gc-freeze", type=int, default=0,
                     help="1: freeze the warm-up's objects and pause Python's cyclic garbage "
                          "collector while the clients run (collections stop every thread)")
+    ap.add_argument("--trace", default="",
+                    help="write a Chrome trace of the interposer's activity in the paced phase "
+                         "(client issues and waits, worker execution, HP flag) to this path; "
+                         "a .gz path is compressed")
     ap.add_argument("--hp-load", type=float, default=1.0 / 3.0,
                     help="HP duty cycle of the paced phase (request period = solo p50 / load)")
     return ap.parse_args()
@@ -340,8 +344,12 @@ def run_kx(args):
     paced_steps = lat_steps
     for c in (0, 1):
         orion.waits(c, reset=True)
+    if args.trace:
+        orion.orion_trace_start()
     hp_p, be_p = harness.run_clients(orion, hp_step, be_step, paced_steps, args.warmup,
                                      hp_period_ms=period)
+    if args.trace:
+        harness.write_trace(orion, args.trace)
     paced_waits = {("hp", "be")[c]: orion.waits(c) for c in (0, 1)}
     # phase 5: e2e (host buffers in every HP step), contended
     hp_e2e = None

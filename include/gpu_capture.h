@@ -275,6 +275,8 @@ struct OperationRecord {
     cudaError_t result{cudaSuccess};
     void* result_ptr{nullptr};
     int64_t enqueue_ns{0};
+    int64_t start_ns{0};  // worker began executing it
+    int64_t end_ns{0};    // worker finished executing it
 
     OperationRecord()
         : type(OperationType::UNKNOWN), op_id(0), client_idx(-1), params(MallocParams{}) {}
@@ -381,7 +383,16 @@ cudaError_t get_and_clear_last_error(int client_idx);
 
 /** Time client threads spent blocked in wait_operation (see
  *  orion_get_client_waits). */
-void get_wait_stats(int client_idx, unsigned long long* out4, bool reset);
+void get_wait_stats(int client_idx, unsigned long long* out8, bool reset);
+
+/** Capture trace (addition of this build; see orion_trace_start). */
+bool trace_enabled();
+/** The worker executed `op` (start_ns .. end_ns set). */
+void trace_executed(const OperationRecord& op);
+/** A client thread waited for `op` from t0 to t1 (CLOCK_MONOTONIC ns). */
+void trace_client_wait(const OperationRecord& op, int64_t t0, int64_t t1);
+/** A scheduler event without duration (e.g. the HP flag changing). */
+void trace_marker(const char* name, int value);
 
 /** Op log (addition of this build; see orion_op_log_start). */
 bool op_log_enabled();
@@ -422,9 +433,22 @@ int orion_op_log_end(const char* path);
 /* Client-thread blocking (addition of this build): how often and how long a
  * client's threads waited for its worker inside intercepted calls (those that
  * must complete before returning: copies from pageable memory, allocations,
- * launches whose arguments could not be copied, ...).  out4 = {waits,
- * total ns, longest ns, OperationType of the longest}; reset != 0 clears. */
-int orion_get_client_waits(int client_idx, unsigned long long* out4, int reset);
+ * launches whose arguments could not be copied, ...).  out8 = {waits,
+ * total ns, longest ns, and for the longest: OperationType, ns queued before
+ * the worker took it, ns the worker spent executing it, bytes (allocation or
+ * copy size, else 0), 0}; reset != 0 clears. */
+int orion_get_client_waits(int client_idx, unsigned long long* out8, int reset);
+
+/* Capture trace (addition of this build): a Chrome trace (JSON, chrome://tracing
+ * or Perfetto) of the interposer's own activity between orion_trace_start and
+ * orion_trace_end: per client, one track for the client thread (each captured
+ * call as an instant at the moment it was issued, and the calls that blocked
+ * as spans), one for its worker (each op's execution span with op id, time
+ * queued and size as args), and a scheduler track with the HP-flag changes.
+ * Timestamps are CLOCK_MONOTONIC microseconds.  At most 4 M events are kept;
+ * orion_trace_end writes the file and returns the number of events, or -1. */
+void orion_trace_start(void);
+int orion_trace_end(const char* path);
 }
 
 #endif  // ORION_GPU_CAPTURE_H

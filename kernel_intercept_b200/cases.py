@@ -11,6 +11,8 @@ memory (small enough for a multi-pass profiler capture):
 
   conv3_2     VGG16 conv3_2 forward, batch 32, 256 -> 256 channels, 56x56, 3x3
               pad 1 (x and y 103 MB each)
+  conv1_2     VGG16 conv1_2 forward, batch 32, 64 -> 64 channels, 224x224
+              (x and y 411 MB each; the 64-column tile shape)
   dgrad3_2    the same layer's backward data (dx from dy and w)
   wgrad3_2    the same layer's backward filter (dw from x and dy)
   vgg16_convs the 13 VGG16 convolution layers, batch 32, forward, in order
@@ -26,7 +28,7 @@ import argparse
 import os
 import sys
 
-CASES = ("conv3_2", "dgrad3_2", "wgrad3_2", "vgg16_convs", "gemm_f32", "gemm_bf16", "bn_train",
+CASES = ("conv3_2", "conv1_2", "dgrad3_2", "wgrad3_2", "vgg16_convs", "gemm_f32", "gemm_bf16", "bn_train",
          "hp_step")
 
 # VGG16 convolution stack: (in channels, out channels, spatial size)
@@ -45,8 +47,8 @@ def _direct(case, reps):
     ex = kx.current_exec()
     dev = "cuda"
     calls = []
-    if case in ("conv3_2", "vgg16_convs"):
-        layers = [(256, 256, 56)] if case == "conv3_2" else VGG16_CONVS
+    if case in ("conv3_2", "conv1_2", "vgg16_convs"):
+        layers = {"conv3_2": [(256, 256, 56)], "conv1_2": [(64, 64, 224)]}.get(case, VGG16_CONVS)
         n = 32
         for c, k, hw in layers:
             x = torch.randn(n, c, hw, hw, device=dev)

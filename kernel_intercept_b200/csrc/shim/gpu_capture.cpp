@@ -271,8 +271,16 @@ void enqueue_operation(OperationPtr op) {
 namespace {
 // How long client threads block in wait_operation, per client.
 struct WaitStats {
-  std::atomic<unsigned long long> count{0}, total_ns{0}, max_ns{0}, max_type{0};
+  std::atomic<unsigned long long> count{0}, total_ns{0}, max_ns{0};
+  std::mutex mu;  // guards the description of the longest wait
+  unsigned long long max_desc[5] = {0, 0, 0, 0, 0};
 };
+
+unsigned long long op_bytes(const OperationRecord& op) {
+  if (auto* m = std::get_if<MallocParams>(&op.params)) return m->size;
+  if (auto* c = std::get_if<MemcpyParams>(&op.params)) return c->count;
+  return 0;
+}
 WaitStats g_wait_stats[MAX_CLIENTS];
 }  // namespace
 
@@ -281,7 +289,9 @@ void wait_operation(OperationPtr op) {
   if (op->completed.load(std::memory_order_acquire)) return;
   const int64_t t0 = now_ns();
   op->wait_completion();
-  const unsigned long long dt = static_cast<unsigned long long>(now_ns() - t0);
+  const int64_t t1 = now_ns();
+  if (trace_enabled()) trace_client_wait(*op, t0, t1);
+  const unsigned long long dt = static_cast<unsigned long long>(t1 - t0);
   if (op->client_idx < 0 || op->client_idx >= MAX_CLIENTS) return;
   WaitStats& w = g_wait_stats[op->client_idx];
   w.count.fetch_add(1, std::memory_order_relaxed);
@@ -289,16 +299,30 @@ void wait_operation(OperationPtr op) {
   unsigned long long prev = w.max_ns.load(std::memory_order_relaxed);
   while (dt > prev && !w.max_ns.compare_exchange_weak(prev, dt)) {
   }
-  if (dt >= prev) w.max_type.store(static_cast<unsigned long long>(op->type));
+  if (dt > prev) {
+    auto span = [](int64_t a, int64_t b) {
+      return b > a && a > 0 ? static_cast<unsigned long long>(b - a) : 0ULL;
+    };
+    std::lock_guard<std::mutex> lk(w.mu);
+    w.max_desc[0] = static_cast<unsigned long long>(op->type);
+    w.max_desc[1] = span(op->enqueue_ns, op->start_ns);
+    w.max_desc[2] = span(op->start_ns, op->end_ns);
+    w.max_desc[3] = op_bytes(*op);
+    w.max_desc[4] = 0;
+  }
 }
 
-void get_wait_stats(int client_idx, unsigned long long* out4, bool reset) {
+void get_wait_stats(int client_idx, unsigned long long* out8, bool reset) {
   if (client_idx < 0 || client_idx >= MAX_CLIENTS) return;
   WaitStats& w = g_wait_stats[client_idx];
-  out4[0] = reset ? w.count.exchange(0) : w.count.load();
-  out4[1] = reset ? w.total_ns.exchange(0) : w.total_ns.load();
-  out4[2] = reset ? w.max_ns.exchange(0) : w.max_ns.load();
-  out4[3] = reset ? w.max_type.exchange(0) : w.max_type.load();
+  out8[0] = reset ? w.count.exchange(0) : w.count.load();
+  out8[1] = reset ? w.total_ns.exchange(0) : w.total_ns.load();
+  out8[2] = reset ? w.max_ns.exchange(0) : w.max_ns.load();
+  std::lock_guard<std::mutex> lk(w.mu);
+  for (int i = 0; i < 5; ++i) {
+    out8[3 + i] = w.max_desc[i];
+    if (reset) w.max_desc[i] = 0;
+  }
 }
 
 OperationPtr submit_operation(int client_idx, OperationType type) {
@@ -339,6 +363,48 @@ std::atomic<bool> g_oplog_on{false};
 
 bool op_log_enabled() { return g_oplog_on.load(std::memory_order_relaxed); }
 
+namespace {
+// kind 0: worker execution span; 1: client wait span; 2: scheduler marker
+struct TraceEvent {
+  int kind;
+  int client;
+  OperationType type;
+  uint64_t op_id;
+  int64_t enq, t0, t1;
+  unsigned long long bytes;
+  const char* name;
+  int value;
+};
+constexpr size_t kTraceMax = size_t(4) << 20;
+std::mutex g_trace_mu;
+std::vector<TraceEvent> g_trace;
+std::atomic<bool> g_trace_on{false};
+
+void trace_push(const TraceEvent& e) {
+  std::lock_guard<std::mutex> lk(g_trace_mu);
+  if (g_trace.size() < kTraceMax) g_trace.push_back(e);
+}
+}  // namespace
+
+bool trace_enabled() { return g_trace_on.load(std::memory_order_relaxed); }
+
+void trace_executed(const OperationRecord& op) {
+  if (!trace_enabled()) return;
+  trace_push({0, op.client_idx, op.type, op.op_id, op.enqueue_ns, op.start_ns, op.end_ns,
+              op_bytes(op), nullptr, 0});
+}
+
+void trace_client_wait(const OperationRecord& op, int64_t t0, int64_t t1) {
+  trace_push({1, op.client_idx, op.type, op.op_id, op.enqueue_ns, t0, t1, op_bytes(op), nullptr,
+              0});
+}
+
+void trace_marker(const char* name, int value) {
+  if (!trace_enabled()) return;
+  const int64_t t = now_ns();
+  trace_push({2, -1, OperationType::UNKNOWN, 0, t, t, t, 0, name, value});
+}
+
 void op_log_record(int client_idx, OperationType type, const long long* dims, int ndims,
                    const char* route) {
   if (!op_log_enabled()) return;
@@ -356,9 +422,9 @@ void op_log_record(int client_idx, OperationType type, const long long* dims, in
 
 extern "C" {
 
-int orion_get_client_waits(int client_idx, unsigned long long* out4, int reset) {
-  if (out4 == nullptr || client_idx < 0 || client_idx >= orion::MAX_CLIENTS) return -1;
-  orion::get_wait_stats(client_idx, out4, reset != 0);
+int orion_get_client_waits(int client_idx, unsigned long long* out8, int reset) {
+  if (out8 == nullptr || client_idx < 0 || client_idx >= orion::MAX_CLIENTS) return -1;
+  orion::get_wait_stats(client_idx, out8, reset != 0);
   return 0;
 }
 
@@ -366,6 +432,70 @@ void orion_op_log_start(void) {
   std::lock_guard<std::mutex> lk(orion::g_oplog_mu);
   orion::g_oplog.clear();
   orion::g_oplog_on.store(true);
+}
+
+void orion_trace_start(void) {
+  std::lock_guard<std::mutex> lk(orion::g_trace_mu);
+  orion::g_trace.clear();
+  orion::g_trace.reserve(size_t(1) << 16);
+  orion::g_trace_on.store(true);
+}
+
+int orion_trace_end(const char* path) {
+  orion::g_trace_on.store(false);
+  std::lock_guard<std::mutex> lk(orion::g_trace_mu);
+  if (path == nullptr) return -1;
+  FILE* f = std::fopen(path, "w");
+  if (f == nullptr) return -1;
+  auto track_name = [](int client, bool worker) {
+    static thread_local char buf[32];
+    if (client == 0) std::snprintf(buf, sizeof(buf), "HP-%s", worker ? "Worker" : "Client");
+    else std::snprintf(buf, sizeof(buf), "BE%d-%s", client, worker ? "Worker" : "Client");
+    return buf;
+  };
+  std::fprintf(f, "{\"displayTimeUnit\": \"ms\", \"traceEvents\": [\n");
+  std::fprintf(f, "{\"ph\": \"M\", \"pid\": 1, \"tid\": 0, \"name\": \"process_name\", "
+                  "\"args\": {\"name\": \"orion capture\"}}");
+  const int nclients = orion::g_capture_state.num_clients;
+  for (int c = 0; c < nclients; ++c)
+    for (int w = 0; w < 2; ++w)
+      std::fprintf(f, ",\n{\"ph\": \"M\", \"pid\": 1, \"tid\": %d, \"name\": \"thread_name\", "
+                      "\"args\": {\"name\": \"%s\"}}",
+                   (w ? 100 : 1) + c, track_name(c, w != 0));
+  std::fprintf(f, ",\n{\"ph\": \"M\", \"pid\": 1, \"tid\": 200, \"name\": \"thread_name\", "
+                  "\"args\": {\"name\": \"Scheduler\"}}");
+  for (const auto& e : orion::g_trace) {
+    const double us0 = e.t0 / 1e3, dur = (e.t1 - e.t0) / 1e3;
+    if (e.kind == 2) {
+      std::fprintf(f, ",\n{\"ph\": \"i\", \"s\": \"t\", \"pid\": 1, \"tid\": 200, "
+                      "\"ts\": %.3f, \"name\": \"%s\", \"args\": {\"value\": %d}}",
+                   us0, e.name, e.value);
+      continue;
+    }
+    const char* tn = orion::op_type_name(e.type);
+    if (e.kind == 0) {
+      // the issue instant on the client track, then the execution span
+      std::fprintf(f, ",\n{\"ph\": \"i\", \"s\": \"t\", \"pid\": 1, \"tid\": %d, "
+                      "\"ts\": %.3f, \"name\": \"%s\", \"args\": {\"op_id\": %llu}}",
+                   1 + e.client, e.enq / 1e3, tn, static_cast<unsigned long long>(e.op_id));
+      std::fprintf(f, ",\n{\"ph\": \"X\", \"pid\": 1, \"tid\": %d, \"ts\": %.3f, "
+                      "\"dur\": %.3f, \"name\": \"%s\", \"args\": {\"op_id\": %llu, "
+                      "\"queued_us\": %.3f, \"bytes\": %llu}}",
+                   100 + e.client, us0, dur, tn, static_cast<unsigned long long>(e.op_id),
+                   (e.t0 - e.enq) / 1e3, e.bytes);
+    } else {
+      std::fprintf(f, ",\n{\"ph\": \"X\", \"pid\": 1, \"tid\": %d, \"ts\": %.3f, "
+                      "\"dur\": %.3f, \"name\": \"wait %s\", \"args\": {\"op_id\": %llu, "
+                      "\"bytes\": %llu}}",
+                   1 + e.client, us0, dur, tn, static_cast<unsigned long long>(e.op_id), e.bytes);
+    }
+  }
+  std::fprintf(f, "\n]}\n");
+  std::fclose(f);
+  const int n = static_cast<int>(orion::g_trace.size());
+  orion::g_trace.clear();
+  orion::g_trace.shrink_to_fit();
+  return n;
 }
 
 int orion_op_log_end(const char* path) {

@@ -349,6 +349,7 @@ bool Scheduler::orion_should_schedule(OperationPtr op, int client_idx) {
 }
 
 void Scheduler::publish_hp_flag(int value) {
+  trace_marker(value != 0 ? "hp_flag_raise" : "hp_flag_clear", value);
   hp_flag_host_[0] = value;
   std::atomic_thread_fence(std::memory_order_seq_cst);
   // the copy reads the pinned host value when it executes, so the latest
@@ -488,7 +489,10 @@ void Scheduler::run_worker(int client_idx) {
     }
     op = q->try_pop();
     if (!op) continue;
+    op->start_ns = mono_ns();
     cudaError_t err = execute_operation(op, fallback);
+    op->end_ns = mono_ns();
+    if (trace_enabled()) trace_executed(*op);
     if (err != cudaSuccess) set_last_error(client_idx, err);
     if (client_idx == 0 && !isolated_ && is_kernel_op(op->type) && !is_dense_op(op->type)) {
       // HP kernels the interposer only re-issues count as HP activity too

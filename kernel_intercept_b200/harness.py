@@ -61,6 +61,7 @@ class Orion:
             "orion_end_profiling": ([ctypes.c_char_p], None),
             "orion_op_log_start": ([], None), "orion_op_log_end": ([ctypes.c_char_p], I),
             "orion_get_client_waits": ([I, ctypes.POINTER(ctypes.c_ulonglong), I], I),
+            "orion_trace_start": ([], None), "orion_trace_end": ([ctypes.c_char_p], I),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)
@@ -71,10 +72,11 @@ class Orion:
         return getattr(self.lib, name)
 
     def waits(self, client: int, reset: bool = False) -> dict:
-        out = (ctypes.c_ulonglong * 4)()
+        out = (ctypes.c_ulonglong * 8)()
         self.lib.orion_get_client_waits(client, out, 1 if reset else 0)
         return {"waits": int(out[0]), "total_ms": out[1] / 1e6, "max_ms": out[2] / 1e6,
-                "max_op": int(out[3])}
+                "max_op": int(out[3]), "max_queued_ms": out[4] / 1e6,
+                "max_exec_ms": out[5] / 1e6, "max_bytes": int(out[6])}
 
     def stats(self, client: int) -> dict:
         out = (ctypes.c_ulonglong * 6)()
@@ -282,6 +284,25 @@ class ClientResult:
         self.error: BaseException | None = None
 
 
+def write_trace(orion: Orion, path: str) -> int:
+    """Ends the interposer's capture trace and writes it to path (gzip when the
+    path ends in .gz).  Returns the number of events."""
+    import gzip
+    import shutil
+    import tempfile
+    if not path.endswith(".gz"):
+        return orion.orion_trace_end(path.encode())
+    fd, tmp = tempfile.mkstemp(suffix=".json")
+    os.close(fd)
+    try:
+        n = orion.orion_trace_end(tmp.encode())
+        with open(tmp, "rb") as src, gzip.open(path, "wb") as dst:
+            shutil.copyfileobj(src, dst)
+    finally:
+        os.unlink(tmp)
+    return n
+
+
 def percentile(xs, q):
     if not xs:
         return float("nan")
@@ -321,12 +342,17 @@ def run_clients(orion: Orion | None, hp_step, be_step, hp_steps: int, hp_warmup:
             with torch.cuda.stream(s):
                 for _ in range(hp_warmup):
                     hp_step()
-                s.synchronize()
-                ready.wait()
+                # torch creates a CUDA event at its first record, and creating
+                # one can block the thread for milliseconds (the driver grows its
+                # event pool): create all timing events before the timed loop
                 evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                        for _ in range(hp_steps)]
                 first = torch.cuda.Event(enable_timing=True)
                 last = torch.cuda.Event(enable_timing=True)
+                for ev in [first, last] + [e for pair in evs for e in pair]:
+                    ev.record(s)
+                s.synchronize()
+                ready.wait()
                 first.record(s)
                 for a, b in evs:
                     t_issue = time.perf_counter()

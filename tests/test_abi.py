@@ -47,7 +47,7 @@ cudnnBackendDestroyDescriptor cudnnBackendCreateDescriptor cudnnBackendSetAttrib
 cudnnBackendGetAttribute cudnnBackendFinalize cudaEventRecord cudaEventRecordWithFlags cudaStreamWaitEvent
 cudaEventSynchronize cudaEventQuery cudaStreamQuery orion_set_be_keep_sms orion_get_be_keep_sms
 orion_set_sm_budgets orion_get_client_stats orion_op_log_start orion_op_log_end
-orion_get_client_waits
+orion_get_client_waits orion_trace_start orion_trace_end
 """.split()
 
 
@@ -135,6 +135,17 @@ L.orion_set_be_keep_sms(24); assert L.orion_get_be_keep_sms() == 24
 out = (ctypes.c_ulonglong * 6)()
 assert L.orion_get_client_stats(1, out) == 0 and list(out) == [0] * 6
 assert L.orion_get_client_stats(99, out) != 0
+w = (ctypes.c_ulonglong * 8)()
+assert L.orion_get_client_waits(0, w, 1) == 0 and list(w) == [0] * 8
+assert L.orion_get_client_waits(99, w, 0) != 0
+# capture trace: an empty trace is valid Chrome-trace JSON naming every track
+import json, os, tempfile
+path = os.path.join(tempfile.mkdtemp(), "t.json")
+L.orion_trace_start()
+assert L.orion_trace_end(path.encode()) == 0
+ev = json.load(open(path))["traceEvents"]
+names = {e["args"]["name"] for e in ev if e["ph"] == "M"}
+assert {"HP-Client", "HP-Worker", "BE1-Client", "BE1-Worker", "Scheduler"} <= names, names
 L.orion_shutdown()
 print("ok")
 """
