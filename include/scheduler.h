@@ -142,6 +142,10 @@ public:
 
     /** Resolves the CUDA events recorded around profiled ops into g_profiler. */
     void flush_profile();
+    /** Creates n timing events for profiled ops up front: creating a CUDA event
+     *  can block the calling thread for milliseconds while other clients'
+     *  work is in flight, so workers take events from this pool. */
+    void reserve_profile_events(int n);
 
     std::atomic<bool> running_{false};
 
@@ -193,6 +197,8 @@ private:
     };
     std::mutex prof_mu_;
     std::vector<PendingProfile> pending_prof_;
+    std::vector<cudaEvent_t> prof_events_;  // free timing events (guarded by prof_mu_)
+    cudaEvent_t take_profile_event();
 };
 
 extern Scheduler g_scheduler;

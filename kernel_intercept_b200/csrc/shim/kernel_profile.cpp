@@ -266,6 +266,8 @@ int orion_load_profile(const char* filepath) {
 }
 
 void orion_start_profiling(const char* model_name) {
+  // timing events for the profiled ops, made here rather than by the workers
+  if (orion::g_scheduler.running_.load()) orion::g_scheduler.reserve_profile_events(16384);
   orion::g_profiler.start_session(model_name ? model_name : "unnamed");
 }
 

@@ -411,8 +411,8 @@ cudaError_t Scheduler::execute_operation(OperationPtr op, cudaStream_t fallback)
   cudaEvent_t ev_start = nullptr, ev_end = nullptr;
   const bool profiling = g_profiler.active();
   if (profiling) {
-    ORION_REAL(cudart, cudaEventCreate)(&ev_start);
-    ORION_REAL(cudart, cudaEventCreate)(&ev_end);
+    ev_start = take_profile_event();
+    ev_end = take_profile_event();
     ORION_REAL(cudart, cudaEventRecord)(ev_start, pol.stream);
   }
   tl_in_scheduler_execution = true;
@@ -545,6 +545,11 @@ void Scheduler::reset() {
     ORION_REAL(cudart, cudaEventDestroy)(hp_last_event_);
     hp_last_event_ = nullptr;
   }
+  {
+    std::lock_guard<std::mutex> lk(prof_mu_);
+    for (cudaEvent_t e : prof_events_) ORION_REAL(cudart, cudaEventDestroy)(e);
+    prof_events_.clear();
+  }
   if (flag_stream_) {
     ORION_REAL(cudart, cudaStreamSynchronize)(flag_stream_);
     ORION_REAL(cudart, cudaStreamDestroy)(flag_stream_);
@@ -587,9 +592,41 @@ void Scheduler::flush_profile() {
     ORION_REAL(cudart, cudaEventElapsedTime)(&ms, pp.start, pp.end);
     pp.rec.duration_ms = ms;
     g_profiler.record(pp.rec);
-    ORION_REAL(cudart, cudaEventDestroy)(pp.start);
-    ORION_REAL(cudart, cudaEventDestroy)(pp.end);
   }
+  std::lock_guard<std::mutex> lk(prof_mu_);
+  for (auto& pp : pend) {
+    prof_events_.push_back(pp.start);
+    prof_events_.push_back(pp.end);
+  }
+}
+
+cudaEvent_t Scheduler::take_profile_event() {
+  {
+    std::lock_guard<std::mutex> lk(prof_mu_);
+    if (!prof_events_.empty()) {
+      cudaEvent_t e = prof_events_.back();
+      prof_events_.pop_back();
+      return e;
+    }
+  }
+  cudaEvent_t e = nullptr;
+  ORION_REAL(cudart, cudaEventCreate)(&e);
+  return e;
+}
+
+void Scheduler::reserve_profile_events(int n) {
+  std::vector<cudaEvent_t> made;
+  {
+    std::lock_guard<std::mutex> lk(prof_mu_);
+    n -= static_cast<int>(prof_events_.size());
+  }
+  for (int i = 0; i < n; ++i) {
+    cudaEvent_t e = nullptr;
+    if (ORION_REAL(cudart, cudaEventCreate)(&e) != cudaSuccess) break;
+    made.push_back(e);
+  }
+  std::lock_guard<std::mutex> lk(prof_mu_);
+  prof_events_.insert(prof_events_.end(), made.begin(), made.end());
 }
 
 bool start_scheduler(int num_clients, const SchedulerConfig& config) {
