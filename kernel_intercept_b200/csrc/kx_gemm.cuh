@@ -138,7 +138,8 @@ enum PipeStat : int {
   PS_EPI_FOLD,        // epilogue (warp 4): folding segments from TMEM
   PS_EPI_EMIT,        // epilogue (warp 4): output stores
   PS_EPI_STWAIT,      // epilogue (warp 4): proxy fences before its TMA stores
-  kPipeStats = 12
+  PS_PROD_ISSUE,      // producer: coordinates and TMA issue of a k-block's loads
+  kPipeStats = 13
 };
 
 KX_DEV bool timed_wait(uint32_t bar, uint32_t parity, const WaitCtl& wc,
@@ -586,6 +587,7 @@ __global__ void __launch_bounds__(256, 1)
             ok = false;
             break;
           }
+          const long long t_iss = stats ? clock64() : 0;
           const uint32_t fb = smem_addr(&sb->full[s]);
           // 3xTF32 with pre-split operands: the low parts arrive by TMA beside
           // the high parts.
@@ -664,6 +666,7 @@ __global__ void __launch_bounds__(256, 1)
               }
             }
           }
+          if (stats) st_c += static_cast<unsigned long long>(clock64() - t_iss);
         }
         if (!ok) break;
       }
@@ -1091,6 +1094,7 @@ __global__ void __launch_bounds__(256, 1)
     if (warp == 0) {
       ps[PS_PROD_EMPTY] = st_a;
       ps[PS_PROD_RING] = st_b;
+      ps[PS_PROD_ISSUE] = st_c;
     } else if (warp == 1) {
       ps[PS_MMA_DATA] = st_a;
       ps[PS_MMA_TMEM] = st_b;
