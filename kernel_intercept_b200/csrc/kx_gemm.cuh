@@ -146,7 +146,9 @@ enum PipeStat : int {
   PS_EPI_EMIT,        // epilogue (warp 4): output stores
   PS_EPI_STWAIT,      // epilogue (warp 4): proxy fences before its TMA stores
   PS_PROD_ISSUE,      // producer: coordinates and TMA issue of a k-block's loads
-  kPipeStats = 13
+  PS_MMA_LOOP,        // MMA issuer: its whole tile loop
+  PS_MMA_KLOOP,       // MMA issuer: inside its k-block loops (waits, issue, bookkeeping)
+  kPipeStats = 15
 };
 
 KX_DEV bool timed_wait(uint32_t bar, uint32_t parity, const WaitCtl& wc,
@@ -509,7 +511,7 @@ __global__ void __launch_bounds__(256, 1)
   const long long t_ready = clock64();
 
   WaitCtl wc{&sb->abort_flag, p.err_word, p.timeout_ns};
-  unsigned long long st_a = 0, st_b = 0, st_c = 0, st_d = 0, st_e = 0;  // per-role counters
+  unsigned long long st_a = 0, st_b = 0, st_c = 0, st_d = 0, st_e = 0, st_f = 0;  // per role
   const bool stats = p.pipe_stats != nullptr;
 
   if (warp == 0) {
@@ -786,6 +788,7 @@ __global__ void __launch_bounds__(256, 1)
       // buffer sc & 1 (one segment per tile unless PROMOTE splits K).
       uint32_t it = 0, sc = 0;
       uint32_t ia = 0, ib = 0;  // tap reuse: A boxes and B k-blocks consumed
+      const long long t_loop = stats ? clock64() : 0;
       bool ok = true;
       for (uint32_t slot = 0; ok; ++slot) {
         const uint32_t r = slot % R;
@@ -874,6 +877,7 @@ __global__ void __launch_bounds__(256, 1)
           const uint32_t d_tmem = tmem + a * Cfg::ACC_COLS;
           const int kend = (nkb - kb > Cfg::SEG) ? kb + Cfg::SEG : nkb;
           const int kfirst = kb;
+          const long long t_k = stats ? clock64() : 0;
           for (; kb < kend; ++kb, ++it) {
             const uint32_t s = it % S;
             const uint32_t wb = convert ? smem_addr(&sb->conv[s]) : smem_addr(&sb->full[s]);
@@ -923,6 +927,7 @@ __global__ void __launch_bounds__(256, 1)
               tc_commit(smem_addr(&sb->empty[s]));
             if (stats) st_d += static_cast<unsigned long long>(clock64() - t_iss);
           }
+          if (stats) st_f += static_cast<unsigned long long>(clock64() - t_k);
           if (!ok) break;
           if constexpr (PAIR)
             tc_commit_pair(smem_addr(&sb->tfull[a]));
@@ -930,6 +935,7 @@ __global__ void __launch_bounds__(256, 1)
             tc_commit(smem_addr(&sb->tfull[a]));
         }
       }
+      if (stats) st_e = static_cast<unsigned long long>(clock64() - t_loop);
       // Wait (bounded) for every MMA this thread issued before TMEM is freed.
       if constexpr (PAIR)
         tc_commit_pair(smem_addr(&sb->final_mma));
@@ -1244,6 +1250,8 @@ __global__ void __launch_bounds__(256, 1)
       ps[PS_MMA_TMEM] = st_b;
       ps[PS_MMA_RING] = st_c;
       ps[PS_MMA_ISSUE] = st_d;
+      ps[PS_MMA_LOOP] = st_e;
+      ps[PS_MMA_KLOOP] = st_f;
     } else if (warp == 4) {
       ps[PS_EPI_TFULL] = st_a;
       ps[PS_EPI_FOLD] = st_b;

@@ -284,11 +284,14 @@ void pipe_stats_end(unsigned long long* buf, const char* kernel, cudaStream_t st
   std::fprintf(stderr,
                "[kx pipe] %s grid %d cycles/CTA %.0f | share: prologue %.3f prod-empty %.3f "
                "prod-ring %.3f prod-issue %.3f mma-data %.3f mma-tmem %.3f mma-ring %.3f "
-               "mma-issue %.3f epi-tfull %.3f epi-fold %.3f epi-emit %.3f (proxy fences %.3f)\n",
+               "mma-issue %.3f mma-loop %.3f mma-kloop %.3f epi-tfull %.3f epi-fold %.3f "
+               "epi-emit %.3f (proxy fences %.3f)\n",
                kernel, grid, tot / grid, sum[PS_PROLOGUE] / tot, sum[PS_PROD_EMPTY] / tot,
                sum[PS_PROD_RING] / tot, sum[PS_PROD_ISSUE] / tot, sum[PS_MMA_DATA] / tot,
                sum[PS_MMA_TMEM] / tot,
-               sum[PS_MMA_RING] / tot, sum[PS_MMA_ISSUE] / tot, sum[PS_EPI_TFULL] / tot,
+               sum[PS_MMA_RING] / tot, sum[PS_MMA_ISSUE] / tot, sum[PS_MMA_LOOP] / tot,
+               sum[PS_MMA_KLOOP] / tot,
+               sum[PS_EPI_TFULL] / tot,
                sum[PS_EPI_FOLD] / tot, sum[PS_EPI_EMIT] / tot, sum[PS_EPI_STWAIT] / tot);
 }
 
