@@ -267,6 +267,53 @@ def scenario_hpbe(orion):
             "hp_p50_ms": harness.percentile(hp.latencies_ms, 0.5), "be_iters": be.iters}
 
 
+def scenario_trace(orion):
+    """Capture trace of an HP + BE run: per-client issue instants, worker
+    execution spans, blocking waits and HP-flag markers, as Chrome-trace JSON;
+    plus the per-client wait counters."""
+    import tempfile
+
+    import torch
+
+    from kernel_intercept_b200 import harness
+    torch.backends.cuda.matmul.allow_tf32 = False
+    g = torch.Generator(device="cuda").manual_seed(5)
+    a = torch.randn(256, 1024, device="cuda", generator=g)
+    b = torch.randn(1024, 1024, device="cuda", generator=g)
+    A = torch.randn(2048, 2048, device="cuda", generator=g)
+    assert orion.orion_init_scheduler(2) == 0
+    orion.orion_set_capture(0)
+    torch.cuda.synchronize()
+    orion.orion_start_scheduler_thread()
+    orion.orion_set_capture(1)
+    for c in (0, 1):
+        orion.waits(c, reset=True)
+    orion.orion_trace_start()
+    hp, be = harness.run_clients(orion, lambda: a @ b, lambda: A @ A, hp_steps=20, hp_warmup=2)
+    path = os.path.join(tempfile.mkdtemp(), "trace.json.gz")
+    n = harness.write_trace(orion, path)
+    waits = {c: orion.waits(c) for c in (0, 1)}
+    orion.orion_set_capture(0)
+    orion.orion_stop_scheduler()
+    torch.cuda.synchronize()
+    import gzip
+    ev = json.load(gzip.open(path))["traceEvents"]
+    names = sorted({e["args"]["name"] for e in ev if e["ph"] == "M" and "name" in e["args"]})
+    spans = [e for e in ev if e["ph"] == "X" and e["tid"] >= 100 and e["tid"] < 200]
+    issues = {(e["tid"], e["args"]["op_id"]): e["ts"] for e in ev if e["ph"] == "i" and e["tid"] < 100}
+    hp_gemms = [e for e in spans if e["tid"] == 100 and "GEMM" in e["name"] or
+                e["tid"] == 100 and "MATMUL" in e["name"]]
+    be_gemms = [e for e in spans if e["tid"] == 101 and ("GEMM" in e["name"] or "MATMUL" in e["name"])]
+    matched = all((e["tid"] - 99, e["args"]["op_id"]) in issues and
+                  issues[(e["tid"] - 99, e["args"]["op_id"])] <= e["ts"] + 1e-3 for e in spans)
+    return {"events": n, "json_events": len(ev), "names": names, "hp_gemms": len(hp_gemms),
+            "be_gemms": len(be_gemms), "spans_matched": matched,
+            "nonneg": all(e["dur"] >= 0 and e["args"]["queued_us"] >= 0 for e in spans),
+            "flag_markers": sorted({e["name"] for e in ev if e.get("tid") == 200 and e["ph"] == "i"}),
+            "hp_waits": [e["name"] for e in ev if e["ph"] == "X" and e["tid"] == 1],
+            "waits": waits, "hp_iters": hp.iters, "be_iters": be.iters}
+
+
 def read_op_log(path):
     """Entries of an op log: (client, op type, route, shape integers)."""
     out = []

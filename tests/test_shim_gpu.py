@@ -105,3 +105,19 @@ def test_capture_keeps_op_order_and_counts():
     for c in ("0", "1"):
         assert res["stats"][c]["errors"] == 0, res
 
+
+
+def test_capture_trace():
+    """orion_trace_start / orion_trace_end: a Chrome trace of an HP + BE run
+    holds every captured op as an issue instant on its client's track and an
+    execution span on its worker's track (same op id, issued before it ran),
+    the HP client's blocking waits, and the HP flag being raised."""
+    res = run_child("trace")
+    assert res["events"] > 0 and res["json_events"] > res["events"], res
+    for t in ("HP-Client", "HP-Worker", "BE1-Client", "BE1-Worker", "Scheduler"):
+        assert t in res["names"], res
+    assert res["hp_gemms"] >= 22 and res["be_gemms"] >= 1, res
+    assert res["spans_matched"] and res["nonneg"], res
+    assert "hp_flag_raise" in res["flag_markers"], res
+    assert any(w.startswith("wait ") for w in res["hp_waits"]), res
+    assert res["waits"]["0"]["waits"] >= 1, res
