@@ -19,8 +19,9 @@ end-to-end repeat.  The timed region is the K HP steps of the contended phase,
 bracketed by a barrier and a device synchronize, timed with CUDA events on
 the HP stream (max over ranks).  `value` = HP images/s under contention
 (whole job: sum over ranks).
-`e2e` repeats the contended phase with the HP input copied from pinned host
-memory and the logits copied back inside every step.  `roofline` is the
+`e2e` repeats the contended phase (over max(K, 200) HP steps, like the
+latency phases) with the HP input copied from pinned host memory and the
+logits copied back inside every step.  `roofline` is the
 dominant captured kernel class (HP convolutions) from CUDA events recorded
 around each captured op during the timed region.  `cpu_baseline` is the CPU
 oracle's VGG16 forward on a bounded sample, timed on this host.
@@ -351,10 +352,13 @@ def run_kx(args):
     if args.trace:
         harness.write_trace(orion, args.trace)
     paced_waits = {("hp", "be")[c]: orion.waits(c) for c in (0, 1)}
-    # phase 5: e2e (host buffers in every HP step), contended
+    # phase 5: e2e (host buffers in every HP step), contended, over as many
+    # steps as the latency phases so that one host-side stall on one rank does
+    # not stand for the whole run
     hp_e2e = None
+    e2e_steps = lat_steps
     if not args.no_e2e:
-        hp_e2e, _ = harness.run_clients(orion, hp_step_e2e, be_step, args.steps, args.warmup)
+        hp_e2e, _ = harness.run_clients(orion, hp_step_e2e, be_step, e2e_steps, args.warmup)
     stats = {c: orion.stats(c) for c in (0, 1)}
     orion.orion_set_capture(0)
     orion.orion_stop_scheduler()
@@ -368,10 +372,14 @@ def run_kx(args):
     hp_ms = hp_c.elapsed_ms
     imgs = HP_BATCH * args.steps
     e2e_ms = hp_e2e.elapsed_ms if hp_e2e else 0.0
+    per_rank = [[hp_ms, e2e_ms]]
     if pg is not None:
         t = torch.tensor([hp_ms, e2e_ms], device=dev)
-        pg.all_reduce(t, op=pg.ReduceOp.MAX)
-        hp_ms, e2e_ms = float(t[0]), float(t[1])
+        parts = [torch.zeros_like(t) for _ in range(world)]
+        pg.all_gather(parts, t)
+        per_rank = [[float(v) for v in x.tolist()] for x in parts]
+        hp_ms = max(r[0] for r in per_rank)
+        e2e_ms = max(r[1] for r in per_rank)
     value = world * imgs / (hp_ms / 1e3)
     p50 = harness.percentile(hp_c.latencies_ms, 0.5)
     p99 = harness.percentile(hp_c.latencies_ms, 0.99)
@@ -432,11 +440,16 @@ def run_kx(args):
         "cpu_baseline": cpu, "clocks": clk, "gpu_launches": int(launches),
         "captured": stats,
     }
+    if world > 1:
+        line["ms_per_step_per_rank"] = [round(r[0] / args.steps, 3) for r in per_rank]
     if e2e_ms:
         h2d = HP_BATCH * 3 * 224 * 224 * 4
         d2h = HP_BATCH * 1000 * 4
-        line["e2e"] = {"value": round(world * imgs / (e2e_ms / 1e3), 3), "unit": "images/s",
+        line["e2e"] = {"value": round(world * HP_BATCH * e2e_steps / (e2e_ms / 1e3), 3),
+                       "unit": "images/s", "steps": e2e_steps,
                        "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+        if world > 1:
+            line["e2e"]["ms_per_step_per_rank"] = [round(r[1] / e2e_steps, 3) for r in per_rank]
     print(json.dumps(line), flush=True)
     return 0
 
