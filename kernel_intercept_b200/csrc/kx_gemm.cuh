@@ -236,7 +236,8 @@ struct GemmCfg {
   static_assert(STAGES >= 2, "not enough shared memory for two stages");
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 256, "bad BN");
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
-  static_assert(!PAIR || (SPLIT && BN >= 64), "CTA pairs: 3xTF32, BN >= 64");
+  static_assert(!PAIR || (BN >= 64 && (SPLIT || (!A_MN && !B_MN && ESIZE == 2))),
+                "CTA pairs: 3xTF32, or 16-bit operands with K-major A and B; BN >= 64");
   static_assert(!TAPR || (SPLIT && !PAIR && !A_MN && !B_MN && SB >= 2),
                 "tap reuse: 3xTF32 K-major operands on one CTA");
 };
@@ -898,7 +899,10 @@ __global__ void __launch_bounds__(256, 1)
               const uint64_t ad = sdesc_sw128(a_hi + aoff, Cfg::A_LBO, Cfg::A_SBO, Cfg::A_LAYOUT);
               const uint64_t bd = sdesc_sw128(b_hi + boff, Cfg::B_LBO, Cfg::B_SBO, Cfg::B_LAYOUT);
               const uint32_t acc = (kb > kfirst || kk > 0) ? 1u : 0u;
-              if constexpr (PAIR) {
+              if constexpr (PAIR && !Cfg::SPLIT) {
+                // 16-bit operands: one 256 x BN MMA over the pair's A and B rows
+                umma_f16_pair(d_tmem, ad, bd, Cfg::IDESC, acc);
+              } else if constexpr (PAIR) {
                 // 256 x BN over the pair: A rows and B rows from both CTAs
                 const uint64_t adl =
                     sdesc_sw128(a_lo + aoff, Cfg::A_LBO, Cfg::A_SBO, Cfg::A_LAYOUT);

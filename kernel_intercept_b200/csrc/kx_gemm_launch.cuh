@@ -32,9 +32,20 @@ constexpr const char* arith_name() {
   return AR == Arith::F32x3 ? "f32x3" : AR == Arith::TF32 ? "tf32" : AR == Arith::BF16 ? "bf16" : "f16";
 }
 
-template <int BN, Arith AR, bool AMN, bool BMN>
+// KX_GEMM_PAIR=1: 16-bit GEMMs with K-major operands run on 2-CTA clusters
+// (256-row tiles, cta_group::2 MMAs; each SM loads half of the B tile).  Off
+// by default: on B200 8192^3 bf16 ran at 766 TFLOP/s with pairs against 1328
+// without, 2048 x 4096 x 2048 at 594 against 756 (the follower forwards every
+// landed stage to the leader, one more cross-CTA wait per k-block on the MMA
+// issuer's path).
+inline bool gemm_pair_mode() {
+  const char* s = std::getenv("KX_GEMM_PAIR");
+  return s != nullptr && s[0] == '1';
+}
+
+template <int BN, Arith AR, bool AMN, bool BMN, bool PAIR = false>
 int launch_gemm_tc(const Exec& e, const TcProblem& pr, GemmParams p) {
-  using Cfg = GemmCfg<BN, AR, AMN, BMN>;
+  using Cfg = GemmCfg<BN, AR, AMN, BMN, PAIR>;
   constexpr CUtensorMapDataType dt = map_dtype<AR>();
   CUtensorMap ma, mb, malo, mblo;
   // M/N-major tf32 operands need the 32-byte-atom variant of the 128-byte swizzle
@@ -52,7 +63,7 @@ int launch_gemm_tc(const Exec& e, const TcProblem& pr, GemmParams p) {
     return BMN ? encode_map_3d(m, dt, Cfg::ESIZE, base, pr.n, pr.k, pr.batch, pr.ldb, pr.strideB,
                                Cfg::CHUNK, Cfg::BK, swzB)
                : encode_map_3d(m, dt, Cfg::ESIZE, base, pr.k, pr.n, pr.batch, pr.ldb, pr.strideB,
-                               Cfg::BK, BN);
+                               Cfg::BK, Cfg::B_ROWS);
   };
   // M/N-major tile in one TMA box: {CHUNK, K, rows / CHUNK, batch} with the
   // third dimension stepping CHUNK elements.  Only when the rows are a
@@ -96,6 +107,9 @@ int launch_gemm_tc(const Exec& e, const TcProblem& pr, GemmParams p) {
   }
 
   p.num_mb = (pr.m + Cfg::BM - 1) / Cfg::BM;
+  // a pair tile covers two consecutive 128-row blocks (the second may lie
+  // past the end: its loads read zeros and its rows are not stored)
+  if (PAIR) p.num_mb = (p.num_mb + 1) / 2;
   p.num_nb = (pr.n + BN - 1) / BN;
   p.num_kb = (pr.k + Cfg::BK - 1) / Cfg::BK;
   p.tiles_per_batch = p.num_mb * p.num_nb;
@@ -120,7 +134,7 @@ int launch_gemm_tc(const Exec& e, const TcProblem& pr, GemmParams p) {
   const int cap = persistent_grid(e, 1 << 30);
   p.splits = 1;
   p.kb_per_split = p.num_kb;
-  if (tiles * 2 <= cap && p.num_kb >= 2 * MIN_KB && !split_k_disabled()) {
+  if (!PAIR && tiles * 2 <= cap && p.num_kb >= 2 * MIN_KB && !split_k_disabled()) {
     long long want = cap / tiles;
     const long long by_k = p.num_kb / MIN_KB;
     if (want > by_k) want = by_k;
@@ -154,10 +168,20 @@ int launch_gemm_tc(const Exec& e, const TcProblem& pr, GemmParams p) {
                                  32, CU_TENSOR_MAP_SWIZZLE_NONE))
       p.tma_store = 1;
   }
-  const int grid = persistent_grid(e, p.num_tiles);
+  int grid = persistent_grid(e, p.num_tiles * (PAIR ? 2 : 1));
+  if (PAIR) {
+    grid = pair_grid(kern, Cfg::THREADS, Cfg::SMEM_BYTES, grid);
+    if (grid < 2) return KX_ERR_UNSUPPORTED;
+  }
   p.pipe_stats = pipe_stats_begin();
   note_launch();
-  kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, e.stream>>>(ma, mb, malo, mblo, md, p);
+  if (PAIR) {
+    if (launch_pair(kern, grid, Cfg::THREADS, Cfg::SMEM_BYTES, e.stream, ma, mb, malo, mblo, md,
+                    p) != cudaSuccess)
+      return KX_ERR_DEVICE;
+  } else {
+    kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, e.stream>>>(ma, mb, malo, mblo, md, p);
+  }
   pipe_stats_end(p.pipe_stats, "kx_gemm_tc", e.stream, grid);
   if (p.splits > 1) {
     note_launch();
@@ -166,8 +190,8 @@ int launch_gemm_tc(const Exec& e, const TcProblem& pr, GemmParams p) {
   }
   static char name[96];
   if (name[0] == 0)
-    snprintf(name, sizeof(name), "kx_gemm_tc<bn%d,%s,A%s,B%s>", BN, arith_name<AR>(),
-             AMN ? "mn" : "k", BMN ? "mn" : "k");
+    snprintf(name, sizeof(name), "kx_gemm_tc<bn%d,%s,A%s,B%s%s>", BN, arith_name<AR>(),
+             AMN ? "mn" : "k", BMN ? "mn" : "k", PAIR ? ",pair" : "");
   set_last_kernel_name(name);
   return launch_status();
 }
@@ -182,6 +206,14 @@ int dispatch_gemm_tc(int bn, bool amn, bool bmn, const Exec& e, const TcProblem&
     if (!amn && bmn) return launch_gemm_tc<BNV, AR, false, true>(e, pr, p);     \
     if (amn && !bmn) return launch_gemm_tc<BNV, AR, true, false>(e, pr, p);     \
     return launch_gemm_tc<BNV, AR, true, true>(e, pr, p);                       \
+  }
+  if constexpr (AR == Arith::BF16 || AR == Arith::F16) {
+    if (!amn && !bmn && gemm_pair_mode()) {
+      const int rc = bn == 256   ? launch_gemm_tc<256, AR, false, false, true>(e, pr, p)
+                     : bn == 128 ? launch_gemm_tc<128, AR, false, false, true>(e, pr, p)
+                                 : launch_gemm_tc<64, AR, false, false, true>(e, pr, p);
+      if (rc != KX_ERR_UNSUPPORTED) return rc;
+    }
   }
   if constexpr (AR != Arith::F32x3) {
     KX_CASE(256)

@@ -258,8 +258,23 @@ def test_gemm_ex_bf16(cuda, ta, tb, m, n, k):
         assert _kx().last_kernel_name().startswith("kx_gemm_tc<")
 
 
-def test_gemm_strided_batched_ex_bf16_attention(cuda):
-    # LLaMA attention scores: batch 64, 1024 x 1024 x 128 (q k^T), bf16
+@pytest.mark.parametrize("m,n,k", [(512, 384, 256), (300, 200, 72), (2048, 1024, 2048),
+                                   (2048, 4096, 512), (1000, 520, 136)])
+def test_gemm_ex_bf16_cta_pair(cuda, m, n, k, monkeypatch):
+    """16-bit GEMM with K-major A and B on 2-CTA clusters (KX_GEMM_PAIR=1):
+    256-row tiles of cta_group::2 MMAs, each CTA loading half of the B tile;
+    odd numbers of 128-row blocks leave the second half of the last pair
+    tile past the end of M."""
+    monkeypatch.setenv("KX_GEMM_PAIR", "1")
+    test_gemm_ex_bf16(cuda, 1, 0, m, n, k)
+    assert ",pair>" in _kx().last_kernel_name(), _kx().last_kernel_name()
+
+
+@pytest.mark.parametrize("pair", ["0", "1"])
+def test_gemm_strided_batched_ex_bf16_attention(cuda, pair, monkeypatch):
+    # LLaMA attention scores: batch 64, 1024 x 1024 x 128 (q k^T), bf16; one
+    # CTA per tile or 2-CTA clusters
+    monkeypatch.setenv("KX_GEMM_PAIR", pair)
     kx = _kx()
     import torch
     rng = np.random.default_rng(21)
