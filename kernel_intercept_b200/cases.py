@@ -18,6 +18,8 @@ memory (small enough for a multi-pass profiler capture):
   vgg16_convs the 13 VGG16 convolution layers, batch 32, forward, in order
   gemm_f32    4096^3 fp32 SGEMM (3xTF32 with pre-split operands)
   gemm_bf16   2048 x 4096 x 2048 bf16 GemmEx (a LLaMA-7B query projection)
+  gemm_fc6    VGG16 fc6 at batch 32: 4096 x 32 x 25088 fp32 SGEMM (TN), weights
+              411 MB
   bn_train    batch-norm training forward, spatial, 32 x 256 x 56 x 56
   hp_step     one batch-32 VGG16 inference step (the HP client of the
               benchmark) through the LD_PRELOAD interposer and the scheduler
@@ -28,8 +30,8 @@ import argparse
 import os
 import sys
 
-CASES = ("conv3_2", "conv1_2", "dgrad3_2", "wgrad3_2", "vgg16_convs", "gemm_f32", "gemm_bf16", "bn_train",
-         "hp_step")
+CASES = ("conv3_2", "conv1_2", "dgrad3_2", "wgrad3_2", "vgg16_convs", "gemm_f32", "gemm_bf16",
+         "gemm_fc6", "bn_train", "hp_step")
 
 # VGG16 convolution stack: (in channels, out channels, spatial size)
 VGG16_CONVS = [(3, 64, 224), (64, 64, 224), (64, 128, 112), (128, 128, 112),
@@ -71,6 +73,13 @@ def _direct(case, reps):
         else:
             calls.append(lambda: kx.conv_bwd_filter(ex, d, 1.0, x.data_ptr(), dy.data_ptr(), 0.0,
                                                     dw.data_ptr()))
+    elif case == "gemm_fc6":
+        m, n_, k = 4096, 32, 25088
+        w = torch.randn(m, k, device=dev) * 0.01
+        xin = torch.randn(n_, k, device=dev)
+        c_ = torch.empty(n_, m, device=dev)
+        calls.append(lambda: kx.sgemm(ex, 1, 0, m, n_, k, 1.0, w.data_ptr(), k, xin.data_ptr(), k,
+                                      0.0, c_.data_ptr(), m))
     elif case == "gemm_f32":
         s = 4096
         a = torch.randn(s, s, device=dev)

@@ -465,7 +465,7 @@ __global__ void __launch_bounds__(256, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(smem_addr(&sb->full[s]), 1);
-      mbar_init(smem_addr(&sb->conv[s]), convert ? 64 : 1);
+      mbar_init(smem_addr(&sb->conv[s]), convert ? 2 : 1);  // one arrival per converter warp
       mbar_init(smem_addr(&sb->empty[s]), 1);
     }
     for (int s = 0; s < S; ++s) mbar_init(smem_addr(&sb->pair_full[s]), 1);
@@ -980,18 +980,21 @@ __global__ void __launch_bounds__(256, 1)
           float4* lb = reinterpret_cast<float4*>(stageBlo(s));
           constexpr int NA = Cfg::A_BYTES / 16;
           constexpr int NB = Cfg::B_BYTES / 16;
-#pragma unroll 4
+#pragma unroll 8
           for (int v = ct; v < NA; v += 64) {
             const float4 x = ha[v];
             la[v] = make_float4(tf32_lo(x.x), tf32_lo(x.y), tf32_lo(x.z), tf32_lo(x.w));
           }
-#pragma unroll 4
+#pragma unroll 8
           for (int v = ct; v < NB; v += 64) {
             const float4 x = hb[v];
             lb[v] = make_float4(tf32_lo(x.x), tf32_lo(x.y), tf32_lo(x.z), tf32_lo(x.w));
           }
+          // every thread orders its own writes before the async proxy reads;
+          // then one arrival per warp
           fence_proxy_async_smem();
-          mbar_arrive(smem_addr(&sb->conv[s]));
+          __syncwarp();
+          if (lane == 0) mbar_arrive(smem_addr(&sb->conv[s]));
         }
         if (!ok) break;
       }
