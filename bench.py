@@ -480,7 +480,7 @@ def op_table(recs):
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the
 # dominant op class, from one ncu capture of a batch-32 VGG16 HP step: the mean
 # over its 13 convolution launches (profiles/vgg16_hp_step_launches.md).
-NCU_TRAFFIC_PER_LAUNCH = {"HP:CUDNN_CONV_FWD": 324301174}
+NCU_TRAFFIC_PER_LAUNCH = {"HP:CUDNN_CONV_FWD": 324059668}
 
 
 def roofline(recs, peaks, peak_src, tf32, sustained):
