@@ -387,6 +387,18 @@ def run_kx(args):
     s99 = harness.percentile(hp_solo.latencies_ms, 0.99)
     be_solo_ips = be_solo.iters / (be_solo.elapsed_ms / 1e3) if be_solo.elapsed_ms else 0.0
     be_c_ips = be_c.iters / (be_c.elapsed_ms / 1e3) if be_c.elapsed_ms else 0.0
+    # HP latency against its own solo run, per rank: the line's hp / paced
+    # blocks are rank 0's; at N > 1 the worst rank's ratios are added
+    pp99 = harness.percentile(hp_p.latencies_ms, 0.99)
+    be_p_ips = be_p.iters / (be_p.elapsed_ms / 1e3) if be_p.elapsed_ms else 0.0
+    ratios = [p99 / s99 if s99 else 0.0, pp99 / s99 if s99 else 0.0,
+              be_p_ips / be_solo_ips if be_solo_ips else 0.0]
+    rank_ratios = [ratios]
+    if pg is not None:
+        t = torch.tensor(ratios, device=dev, dtype=torch.float64)
+        parts = [torch.zeros_like(t) for _ in range(world)]
+        pg.all_gather(parts, t)
+        rank_ratios = [[float(v) for v in x.tolist()] for x in parts]
 
     cpu = None
     if rank == 0:
@@ -442,6 +454,10 @@ def run_kx(args):
     }
     if world > 1:
         line["ms_per_step_per_rank"] = [round(r[0] / args.steps, 3) for r in per_rank]
+        line["worst_rank"] = {
+            "hp_p99_vs_solo": round(max(r[0] for r in rank_ratios), 4),
+            "paced_hp_p99_vs_solo": round(max(r[1] for r in rank_ratios), 4),
+            "paced_be_retention": round(min(r[2] for r in rank_ratios), 4)}
     if e2e_ms:
         h2d = HP_BATCH * 3 * 224 * 224 * 4
         d2h = HP_BATCH * 1000 * 4
