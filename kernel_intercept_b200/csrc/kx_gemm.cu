@@ -262,6 +262,10 @@ int choose_bn(int m, int n, int batch, int sms, int max_bn) {
   };
   if (max_bn >= 256 && tiles(256) >= sms && waste(256) <= 0.125) return 256;
   if (tiles(128) >= sms && waste(128) <= 0.125) return 128;
+  // N <= 32 (a classifier at batch 32): a 32-wide tile halves the B side of
+  // the in-kernel 3xTF32 split and the MMA width that would only multiply
+  // zero rows (fp32 only; max_bn 128 marks it)
+  if (max_bn == 128 && n <= 32) return 32;
   return 64;
 }
 

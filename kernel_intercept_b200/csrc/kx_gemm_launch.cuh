@@ -220,6 +220,9 @@ int dispatch_gemm_tc(int bn, bool amn, bool bmn, const Exec& e, const TcProblem&
   }
   KX_CASE(128)
   KX_CASE(64)
+  if constexpr (AR == Arith::F32x3) {
+    KX_CASE(32)
+  }
 #undef KX_CASE
   return KX_ERR_UNSUPPORTED;
 }
