@@ -200,13 +200,17 @@ int kx_bn_fwd_training(const kx_exec* ex, int mode, const float* alpha, const fl
                        float* save_mean, float* save_inv_var);
 
 /* Allocation-free kx_bn_fwd_training (no counterpart in the reference: an
- * addition for callers that cannot allocate device memory).  Same arguments
- * and results; its statistics scratch is one file-scope device array of
- * 4 MiB per device, so it calls no cudaMalloc / cudaFree.  Returns
- * KX_ERR_INVALID when the call needs more scratch than that: 16 bytes per
- * channel-split partial plus 8 bytes per channel (modes 1, 2), 8 bytes per
- * activation c*h*w (mode 0).  All calls share the array: calls that overlap
- * on the GPU race and must be serialised by the caller. */
+ * addition for callers that cannot allocate device memory, such as code that
+ * runs while a CUDA graph is being captured or under an allocator that owns
+ * every device byte).  Same arguments and results; its statistics scratch is
+ * one file-scope device array of 4 MiB per device, so it calls no
+ * cudaMalloc / cudaFree.  Returns KX_ERR_INVALID when the call needs more
+ * scratch than that (16 bytes per channel-split partial plus 8 bytes per
+ * channel in modes 1 and 2; 8 bytes per activation c*h*w in mode 0), or when
+ * ex->stream belongs to another device than the current one.  The first call
+ * on a device looks up the array's device address; make it before any stream
+ * capture.  All calls share the array: calls that overlap on the GPU race and
+ * must be serialised by the caller. */
 int kx_bn_fwd_training_noalloc(const kx_exec* ex, int mode, const float* alpha,
                                const float* beta, int n, int c, int h, int w, const float* x,
                                float* y, const float* scale, const float* bias,
@@ -251,6 +255,11 @@ const char* kx_version(void);
 /* Number of kernels this library has launched in this process (all devices,
  * all threads; the count is taken on the host just before each launch). */
 unsigned long long kx_launch_count(void);
+
+/* Number of device-memory allocations and frees (cudaMalloc / cudaFree) this
+ * library has made in this process, all devices.  Scratch buffers grow on
+ * demand; a call that leaves this count unchanged allocated nothing. */
+unsigned long long kx_device_alloc_count(void);
 
 #ifdef __cplusplus
 }

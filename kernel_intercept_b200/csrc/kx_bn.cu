@@ -34,7 +34,7 @@ __device__ double block_sum(double v, double* sh) {
 // the work items s, s+S, ... of channel c, where K = x[0, c, 0] is a shift
 // that keeps the second moment free of cancellation.
 __global__ void __launch_bounds__(kThreads) bn_stats_spatial(const float* __restrict__ x, int N,
-                                                              int C, int HW, int S,
+                                                              int C, int HW, int S, bool vec,
                                                               double* __restrict__ part) {
   __shared__ double sh[kThreads / 32];
   const int c = blockIdx.x, s = blockIdx.y;
@@ -42,7 +42,6 @@ __global__ void __launch_bounds__(kThreads) bn_stats_spatial(const float* __rest
   const int chunks = (HW + kChunk - 1) / kChunk;
   const long long items = static_cast<long long>(N) * chunks;
   float s1 = 0.f, s2 = 0.f;
-  const bool vec = (HW & 3) == 0;
   for (long long it = s; it < items; it += S) {
     const int n = static_cast<int>(it / chunks), ch = static_cast<int>(it % chunks);
     const float* row = x + (static_cast<size_t>(n) * C + c) * HW;
@@ -106,9 +105,9 @@ __global__ void bn_finalize_spatial(const float* __restrict__ x, int N, int C, i
 // y = alpha*(a_c*x + b_c) + beta*y over rows (n, c) of HW elements.
 __global__ void __launch_bounds__(kThreads) bn_apply_spatial(const float* __restrict__ x, float* y,
                                                               int C, int HW, long long rows,
+                                                              bool vec,
                                                               const float2* __restrict__ coef,
                                                               float alpha, float beta) {
-  const bool vec = (HW & 3) == 0;
   for (long long row = blockIdx.y; row < rows; row += gridDim.y) {
     const float2 ab = coef[row % C];
     const float a = alpha * ab.x, b = alpha * ab.y;
@@ -192,14 +191,13 @@ __global__ void bn_apply_per_activation(const float* __restrict__ x, float* y, i
 // Partials of sum(dy) and sum(dy * (x - mean)) per channel (spatial mode).
 __global__ void __launch_bounds__(kThreads) bn_bwd_reduce_spatial(
     const float* __restrict__ x, const float* __restrict__ dy, int N, int C, int HW, int S,
-    const float* __restrict__ mean_c, double* __restrict__ part) {
+    bool vec, const float* __restrict__ mean_c, double* __restrict__ part) {
   __shared__ double sh[kThreads / 32];
   const int c = blockIdx.x, s = blockIdx.y;
   const float mu = mean_c[c];
   const int chunks = (HW + kChunk - 1) / kChunk;
   const long long items = static_cast<long long>(N) * chunks;
   float sd = 0.f, sdx = 0.f;
-  const bool vec = (HW & 3) == 0;
   for (long long it = s; it < items; it += S) {
     const int n = static_cast<int>(it / chunks), ch = static_cast<int>(it % chunks);
     const size_t off = (static_cast<size_t>(n) * C + c) * HW;
@@ -257,8 +255,7 @@ __global__ void bn_bwd_finalize(int G, double cnt, int S, const double* __restri
 
 __global__ void __launch_bounds__(kThreads) bn_bwd_apply_spatial(
     const float* __restrict__ x, const float* __restrict__ dy, float* dx, int C, int HW,
-    long long rows, const float4* __restrict__ coef, float alpha, float beta) {
-  const bool vec = (HW & 3) == 0;
+    long long rows, bool vec, const float4* __restrict__ coef, float alpha, float beta) {
   for (long long row = blockIdx.y; row < rows; row += gridDim.y) {
     const float4 k = coef[row % C];
     const float k1 = alpha * k.x, k2 = alpha * k.y, k3 = alpha * k.z;
@@ -342,7 +339,21 @@ dim3 apply_grid(long long rows, int HW) {
   return dim3(gx, static_cast<unsigned>(gy));
 }
 
-bool bad_dims(int n, int c, int h, int w) { return n <= 0 || c <= 0 || h <= 0 || w <= 0; }
+// 128-bit loads and stores need every (n, c) row to start on a 16-byte
+// boundary: HW a multiple of 4 floats and each tensor's base 16-byte aligned
+// (cuDNN accepts any 4-byte aligned pointer, e.g. a view with a storage offset).
+bool vec_ok(int HW, const void* a, const void* b = nullptr, const void* c = nullptr) {
+  const uintptr_t bits = reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) |
+                         reinterpret_cast<uintptr_t>(c);
+  return (HW & 3) == 0 && (bits & 15u) == 0;
+}
+
+// Sizes are ints in the ABI; c*h*w (one sample, the per-activation feature
+// count) must also fit one, since the kernels index features with it.
+bool bad_dims(int n, int c, int h, int w) {
+  if (n <= 0 || c <= 0 || h <= 0 || w <= 0) return true;
+  return static_cast<long long>(c) * h * w > 0x7fffffffLL;
+}
 
 }  // namespace
 }  // namespace kx
@@ -381,7 +392,8 @@ extern "C" int kx_bn_fwd_training(const kx_exec* ex, int mode, const float* alph
   double* part = reinterpret_cast<double*>(base);
   float2* coef = reinterpret_cast<float2*>(base + ((part_bytes + 255) & ~static_cast<size_t>(255)));
   note_launch();
-  bn_stats_spatial<<<dim3(c, S), kThreads, 0, e.stream>>>(x, n, c, HW, S, part);
+  bn_stats_spatial<<<dim3(c, S), kThreads, 0, e.stream>>>(x, n, c, HW, S, vec_ok(HW, x),
+                                                           part);
   note_launch();
   bn_finalize_spatial<<<(c + 127) / 128, 128, 0, e.stream>>>(x, n, c, HW, S, part, scale, bias,
                                                              exp_avg_factor, running_mean,
@@ -389,8 +401,8 @@ extern "C" int kx_bn_fwd_training(const kx_exec* ex, int mode, const float* alph
                                                              save_inv_var, coef);
   const long long rows = static_cast<long long>(n) * c;
   note_launch();
-  bn_apply_spatial<<<apply_grid(rows, HW), kThreads, 0, e.stream>>>(x, y, c, HW, rows, coef,
-                                                                   *alpha, *beta);
+  bn_apply_spatial<<<apply_grid(rows, HW), kThreads, 0, e.stream>>>(
+      x, y, c, HW, rows, vec_ok(HW, x, y), coef, *alpha, *beta);
   set_last_kernel_name("kx_bn_apply_spatial");
   return launch_status();
 }
@@ -419,8 +431,8 @@ extern "C" int kx_bn_fwd_inference(const kx_exec* ex, int mode, const float* alp
   } else {
     const long long rows = static_cast<long long>(n) * c;
     note_launch();
-    bn_apply_spatial<<<apply_grid(rows, HW), kThreads, 0, e.stream>>>(x, y, c, HW, rows, coef,
-                                                                     *alpha, *beta);
+    bn_apply_spatial<<<apply_grid(rows, HW), kThreads, 0, e.stream>>>(
+        x, y, c, HW, rows, vec_ok(HW, x, y), coef, *alpha, *beta);
   }
   set_last_kernel_name("kx_bn_fwd_inference");
   return launch_status();
@@ -465,7 +477,8 @@ extern "C" int kx_bn_bwd(const kx_exec* ex, int mode, const float* alpha_data,
           nullptr);
     } else {
       note_launch();
-      bn_stats_spatial<<<dim3(c, S), kThreads, 0, e.stream>>>(x, n, c, HW, S, part);
+      bn_stats_spatial<<<dim3(c, S), kThreads, 0, e.stream>>>(x, n, c, HW, S, vec_ok(HW, x),
+                                                           part);
       note_launch();
       bn_finalize_spatial<<<(c + 127) / 128, 128, 0, e.stream>>>(
           x, n, c, HW, S, part, scale, scale, 0.0, nullptr, nullptr, eps, mean_g, inv_g, fcoef);
@@ -480,7 +493,8 @@ extern "C" int kx_bn_bwd(const kx_exec* ex, int mode, const float* alpha_data,
         *beta_param);
   } else {
     note_launch();
-    bn_bwd_reduce_spatial<<<dim3(c, S), kThreads, 0, e.stream>>>(x, dy, n, c, HW, S, mu, part);
+    bn_bwd_reduce_spatial<<<dim3(c, S), kThreads, 0, e.stream>>>(
+        x, dy, n, c, HW, S, vec_ok(HW, x, dy), mu, part);
     note_launch();
     bn_bwd_finalize<<<(c + 127) / 128, 128, 0, e.stream>>>(
         c, static_cast<double>(n) * HW, S, part, mu, iv, scale, dscale, dbias, *alpha_param,
@@ -488,7 +502,7 @@ extern "C" int kx_bn_bwd(const kx_exec* ex, int mode, const float* alpha_data,
     const long long rows = static_cast<long long>(n) * c;
     note_launch();
     bn_bwd_apply_spatial<<<apply_grid(rows, HW), kThreads, 0, e.stream>>>(
-        x, dy, dx, c, HW, rows, coef, *alpha_data, *beta_data);
+        x, dy, dx, c, HW, rows, vec_ok(HW, x, dy, dx), coef, *alpha_data, *beta_data);
   }
   set_last_kernel_name("kx_bn_bwd");
   return launch_status();
@@ -515,21 +529,32 @@ __device__ __align__(256) unsigned char g_bn_noalloc_scratch[kNoAllocScratchByte
 std::mutex g_noalloc_mu;
 void* g_noalloc_ptr[64] = {nullptr};
 
-// Device address of the array for the current device, looked up once per
-// device (with that device current).
-void* noalloc_scratch() {
+// Device address of the array on the device that runs `stream`, looked up
+// once per device with that device current.  The stream must belong to the
+// current device (the launches below go to the current device's copy of the
+// array); any other stream is rejected with KX_ERR_INVALID.
+int noalloc_scratch(cudaStream_t stream, void** out) {
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return KX_ERR_DEVICE;
+  if (stream != nullptr) {
+    int sdev = -1;
+    if (cudaStreamGetDevice(stream, &sdev) != cudaSuccess) {
+      cudaGetLastError();
+      return KX_ERR_INVALID;
+    }
+    if (sdev != dev) return KX_ERR_INVALID;
+  }
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
   if (g_noalloc_ptr[dev] == nullptr) {
     void* p = nullptr;
     if (cudaGetSymbolAddress(&p, g_bn_noalloc_scratch) != cudaSuccess) {
       cudaGetLastError();
-      return nullptr;
+      return KX_ERR_DEVICE;
     }
     g_noalloc_ptr[dev] = p;
   }
-  return g_noalloc_ptr[dev];
+  *out = g_noalloc_ptr[dev];
+  return KX_OK;
 }
 
 }  // namespace
@@ -544,16 +569,20 @@ extern "C" int kx_bn_fwd_training_noalloc(const kx_exec* ex, int mode, const flo
   if (bad_dims(n, c, h, w) || !x || !y || !scale || !bias || !alpha || !beta) return KX_ERR_INVALID;
   if (mode != 0 && mode != 1 && mode != 2) return KX_ERR_UNSUPPORTED;
   Exec e = resolve_exec(ex);
-  const int HW = h * w;
+  // sizes in 64 bits (bad_dims has bounded c*h*w by INT_MAX, so HW fits an int)
+  const long long hw64 = static_cast<long long>(h) * w;
+  const int HW = static_cast<int>(hw64);
   // scratch this call needs; more than the array holds is rejected
-  const int S = mode == 0 ? 0 : split_for(static_cast<long long>(n) * HW, c);
+  const int S = mode == 0 ? 0 : split_for(static_cast<long long>(n) * hw64, c);
   const size_t part_bytes = sizeof(double) * 2 * static_cast<size_t>(c) * S;
   const size_t coef_off = (part_bytes + 255) & ~static_cast<size_t>(255);
-  const size_t need = mode == 0 ? sizeof(float2) * static_cast<size_t>(c) * HW
+  const size_t need = mode == 0 ? sizeof(float2) * static_cast<size_t>(c) * hw64
                                 : coef_off + sizeof(float2) * static_cast<size_t>(c);
   if (need > kNoAllocScratchBytes) return KX_ERR_INVALID;
-  char* base = static_cast<char*>(noalloc_scratch());
-  if (base == nullptr) return KX_ERR_DEVICE;
+  void* vbase = nullptr;
+  const int st = noalloc_scratch(e.stream, &vbase);
+  if (st != KX_OK) return st;
+  char* base = static_cast<char*>(vbase);
   if (mode == 0) {
     const int G = c * HW;
     float2* coef = reinterpret_cast<float2*>(base);
@@ -572,7 +601,8 @@ extern "C" int kx_bn_fwd_training_noalloc(const kx_exec* ex, int mode, const flo
   double* part = reinterpret_cast<double*>(base);
   float2* coef = reinterpret_cast<float2*>(base + coef_off);
   note_launch();
-  bn_stats_spatial<<<dim3(c, S), kThreads, 0, e.stream>>>(x, n, c, HW, S, part);
+  bn_stats_spatial<<<dim3(c, S), kThreads, 0, e.stream>>>(x, n, c, HW, S, vec_ok(HW, x),
+                                                           part);
   note_launch();
   bn_finalize_spatial<<<(c + 127) / 128, 128, 0, e.stream>>>(x, n, c, HW, S, part, scale, bias,
                                                              exp_avg_factor, running_mean,
@@ -580,8 +610,8 @@ extern "C" int kx_bn_fwd_training_noalloc(const kx_exec* ex, int mode, const flo
                                                              save_inv_var, coef);
   const long long rows = static_cast<long long>(n) * c;
   note_launch();
-  bn_apply_spatial<<<apply_grid(rows, HW), kThreads, 0, e.stream>>>(x, y, c, HW, rows, coef,
-                                                                   *alpha, *beta);
+  bn_apply_spatial<<<apply_grid(rows, HW), kThreads, 0, e.stream>>>(
+      x, y, c, HW, rows, vec_ok(HW, x, y), coef, *alpha, *beta);
   set_last_kernel_name("kx_bn_apply_spatial");
   return launch_status();
 }

@@ -8,6 +8,10 @@
 
 namespace kx {
 
+static std::atomic<unsigned long long> g_device_allocs{0};
+
+void note_device_alloc() { g_device_allocs.fetch_add(1, std::memory_order_relaxed); }
+
 namespace {
 
 std::mutex g_mu;
@@ -94,6 +98,7 @@ WorkSlot* work_slot_for(cudaStream_t stream) {
   SlotPool& pool = g_pools[dev];
   if (pool.base == nullptr) {
     void* p = nullptr;
+    note_device_alloc();
     if (cudaMalloc(&p, sizeof(WorkSlot) * kSlotsPerDevice) != cudaSuccess) return nullptr;
     if (cudaMemset(p, 0, sizeof(WorkSlot) * kSlotsPerDevice) != cudaSuccess) return nullptr;
     if (cudaDeviceSynchronize() != cudaSuccess) return nullptr;
@@ -126,12 +131,14 @@ void* scratch_for(cudaStream_t stream, size_t bytes, int slot) {
   Scratch& s = g_scratch[dev][slot][stream];
   if (s.bytes >= bytes) return s.ptr;
   if (s.ptr != nullptr) {
+    note_device_alloc();
     cudaFree(s.ptr);
     s.ptr = nullptr;
     s.bytes = 0;
   }
   size_t want = bytes + bytes / 8;  // headroom against repeated small growth
   want = (want + 255) & ~static_cast<size_t>(255);
+  note_device_alloc();
   if (cudaMalloc(&s.ptr, want) != cudaSuccess) {
     cudaGetLastError();
     s.ptr = nullptr;
@@ -264,6 +271,7 @@ unsigned long long* pipe_stats_begin() {
   if (!on) return nullptr;
   static unsigned long long* buf = nullptr;
   const size_t bytes = sizeof(unsigned long long) * kPipeStats * 1024;
+  if (buf == nullptr) note_device_alloc();
   if (buf == nullptr && cudaMalloc(&buf, bytes) != cudaSuccess) {
     buf = nullptr;
     return nullptr;
@@ -303,6 +311,10 @@ void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
 extern "C" unsigned long long kx_launch_count(void) {
   return kx::g_launches.load(std::memory_order_relaxed);
+}
+
+extern "C" unsigned long long kx_device_alloc_count(void) {
+  return kx::g_device_allocs.load(std::memory_order_relaxed);
 }
 
 extern "C" int kx_num_sms(void) { return kx::device_info().num_sms; }

@@ -144,6 +144,11 @@ void pipe_stats_end(unsigned long long* buf, const char* kernel, cudaStream_t st
 // kx_launch_count).  Every `<<<...>>>` site calls it just before launching.
 void note_launch();
 
+// Counts one device-memory allocation or free by this library (cudaMalloc /
+// cudaFree of scratch, work slots and diagnostics), read back by
+// kx_device_alloc_count.  Every cudaMalloc / cudaFree site calls it.
+void note_device_alloc();
+
 // Status mapping helper.
 inline int launch_status() {
   cudaError_t e = cudaGetLastError();

@@ -309,8 +309,64 @@ cublasStatus_t cublasGemmStridedBatchedEx(void* handle, int transa, int transb, 
   return submit_gemm(OperationType::CUBLAS_GEMM_STRIDED_BATCHED_EX, p, ok, call_real);
 }
 
-// fp16 scalars (__half) with fp16 compute are outside the fp32-accumulate
-// contract of kx: counted and passed to the real library.
+}  // extern "C"
+
+namespace {
+
+// cublasHgemm / cublasHgemmStridedBatched: fp16 A, B, C with __half
+// alpha / beta.  kx runs them on the kind::f16 tensor-core kernel with fp32
+// accumulation and one rounding of the result to fp16 (cuBLAS's
+// CUBLAS_COMPUTE_16F may accumulate in fp16; fp32 accumulation is at least as
+// accurate).  Host-mode scalars are converted to fp32 on the calling thread;
+// __half scalars in device memory (CUBLAS_POINTER_MODE_DEVICE) are not
+// decoded and such calls run on the real library (counted as passthrough).
+float half_bits_to_float(const void* p) {
+  uint16_t h = 0;
+  std::memcpy(&h, p, sizeof(h));
+  const uint32_t sign = static_cast<uint32_t>(h & 0x8000u) << 16;
+  uint32_t exp = (h >> 10) & 0x1fu;
+  uint32_t man = h & 0x3ffu;
+  uint32_t bits;
+  if (exp == 0x1fu) {
+    bits = sign | 0x7f800000u | (man << 13);          // inf / nan
+  } else if (exp != 0) {
+    bits = sign | ((exp + 112u) << 23) | (man << 13);  // normal: rebias 15 -> 127
+  } else if (man == 0) {
+    bits = sign;                                        // signed zero
+  } else {                                              // subnormal: normalise
+    int e = -1;
+    do {
+      man <<= 1;
+      ++e;
+    } while ((man & 0x400u) == 0);
+    bits = sign | (static_cast<uint32_t>(112 - e) << 23) | ((man & 0x3ffu) << 13);
+  }
+  float f;
+  std::memcpy(&f, &bits, sizeof(f));
+  return f;
+}
+
+CublasGemmParams make_hgemm(void* handle, int ta, int tb, int m, int n, int k, const void* alpha,
+                            const void* A, int lda, const void* B, int ldb, const void* beta,
+                            void* C, int ldc, bool* supported) {
+  CublasGemmParams p = make_gemm(handle, ta, tb, m, n, k, nullptr, A, lda, B, ldb, nullptr, C,
+                                 ldc);
+  p.Atype = p.Btype = p.Ctype = KX_R_16F;
+  *supported = !p.scalars_on_device && alpha != nullptr && beta != nullptr;
+  if (*supported) {
+    p.alpha_value = half_bits_to_float(alpha);
+    p.beta_value = half_bits_to_float(beta);
+    p.alpha = &p.alpha_value;
+    p.beta = &p.beta_value;
+    p.use_stored_scalars = true;
+  }
+  return p;
+}
+
+}  // namespace
+
+extern "C" {
+
 cublasStatus_t cublasHgemm(void* handle, int transa, int transb, int m, int n, int k,
                            const void* alpha, const void* A, int lda, const void* B, int ldb,
                            const void* beta, void* C, int ldc) {
@@ -322,9 +378,10 @@ cublasStatus_t cublasHgemm(void* handle, int transa, int transb, int m, int n, i
     return real(handle, transa, transb, m, n, k, alpha, A, lda, B, ldb, beta, C, ldc);
   };
   if (orion::tl_is_scheduler_thread || orion::tl_in_scheduler_execution) return call_real();
-  CublasGemmParams p = make_gemm(handle, transa, transb, m, n, k, nullptr, A, lda, B, ldb,
-                                 nullptr, C, ldc);
-  return submit_gemm(OperationType::CUBLAS_GEMM_EX, p, false, call_real);
+  bool ok = false;
+  CublasGemmParams p = make_hgemm(handle, transa, transb, m, n, k, alpha, A, lda, B, ldb, beta,
+                                  C, ldc, &ok);
+  return submit_gemm(OperationType::CUBLAS_GEMM_EX, p, ok, call_real);
 }
 
 cublasStatus_t cublasHgemmStridedBatched(void* handle, int transa, int transb, int m, int n, int k,
@@ -342,9 +399,15 @@ cublasStatus_t cublasHgemmStridedBatched(void* handle, int transa, int transb, i
                 ldc, strideC, batchCount);
   };
   if (orion::tl_is_scheduler_thread || orion::tl_in_scheduler_execution) return call_real();
-  CublasGemmParams p = make_gemm(handle, transa, transb, m, n, k, nullptr, A, lda, B, ldb,
-                                 nullptr, C, ldc);
-  return submit_gemm(OperationType::CUBLAS_GEMM_STRIDED_BATCHED_EX, p, false, call_real);
+  bool ok = false;
+  CublasGemmParams p = make_hgemm(handle, transa, transb, m, n, k, alpha, A, lda, B, ldb, beta,
+                                  C, ldc, &ok);
+  p.strideA = strideA;
+  p.strideB = strideB;
+  p.strideC = strideC;
+  p.batchCount = batchCount;
+  p.is_strided = true;
+  return submit_gemm(OperationType::CUBLAS_GEMM_STRIDED_BATCHED_EX, p, ok, call_real);
 }
 
 cublasStatus_t cublasSgemmEx(void* handle, int transa, int transb, int m, int n, int k,

@@ -111,6 +111,8 @@ def lib() -> ctypes.CDLL:
             L.kx_version.restype = ctypes.c_char_p
             L.kx_launch_count.argtypes = []
             L.kx_launch_count.restype = ctypes.c_ulonglong
+            L.kx_device_alloc_count.argtypes = []
+            L.kx_device_alloc_count.restype = ctypes.c_ulonglong
             _lib = L
     return _lib
 

@@ -23,8 +23,15 @@ legacy entry points the shim wraps, so convolution fixtures are produced by
 ``torch.nn.functional.conv2d`` and its autograd (cuDNN, TF32 disabled) on the
 same B200; they pin the oracle to cuDNN's results, not to the shim.
 
-Each fixture is a small ``.npz`` with the seeded inputs, the call's arguments
-and the library's output.
+Batch-norm fixtures come from cuDNN's batch norm (``aten::cudnn_batch_norm``
+and its backward, the calls behind PyTorch's ``batch_norm`` on CUDA) at
+VGG-like shapes (N = 64, C in {64, 512}, H = W in {14, 56}).  Their inputs are
+too large to store, so the fixture holds the seed they are regenerated from
+(``bn_inputs``), the per-channel outputs in full and two images x three
+channels of y and dx.
+
+Each fixture is a small ``.npz`` with the seeded inputs (or their seed), the
+call's arguments and the library's output.
 """
 from __future__ import annotations
 
@@ -38,6 +45,8 @@ import numpy as np
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(os.path.dirname(HERE))
 REF_SHIM = os.path.join(ROOT, "oracle", "_ref", "libgpu_scheduler.so")
+# where fixtures are written (default: next to this script)
+OUT = os.environ.get("KX_GOLDEN_DIR", HERE)
 
 
 def _parent() -> int:
@@ -164,6 +173,57 @@ def _child_gemm() -> int:
     os._exit(0)
 
 
+def bn_inputs(shape, seed):
+    """Inputs of a batch-norm fixture, regenerated from its seed:
+    x, scale, bias, running mean, running var, dy (float32)."""
+    n, c, h, w = shape
+    rng = np.random.default_rng(seed)
+    x = (rng.standard_normal(shape, dtype=np.float32) * 3 + 2).astype(np.float32)
+    scale = (rng.random(c) + 0.5).astype(np.float32)
+    bias = rng.standard_normal(c).astype(np.float32)
+    rm = rng.standard_normal(c).astype(np.float32)
+    rv = (rng.random(c) + 0.5).astype(np.float32)
+    dy = rng.standard_normal(shape, dtype=np.float32)
+    return x, scale, bias, rm, rv, dy
+
+
+BN_SHAPES = [(64, 64, 56, 56), (64, 64, 14, 14), (64, 512, 56, 56), (64, 512, 14, 14)]
+BN_FACTOR, BN_EPS = 0.1, 1e-5
+
+
+def bn_sample(shape):
+    """Images and channels of y / dx stored in a batch-norm fixture."""
+    n, c = shape[0], shape[1]
+    return np.array([0, n - 1]), np.array([0, c // 2, c - 1])
+
+
+def _child_bn() -> list:
+    import torch
+    written = []
+    for i, shape in enumerate(BN_SHAPES):
+        seed = 500 + i
+        x, scale, bias, rm, rv, dy = bn_inputs(shape, seed)
+        t = lambda a: torch.from_numpy(a).cuda()  # noqa: E731
+        rmt, rvt = t(rm), t(rv)
+        y, smean, sinv, reserve = torch.ops.aten.cudnn_batch_norm(
+            t(x), t(scale), t(bias), rmt, rvt, True, BN_FACTOR, BN_EPS)
+        dx, dscale, dbias = torch.ops.aten.cudnn_batch_norm_backward(
+            t(x), t(dy), t(scale), rmt, rvt, smean, sinv, BN_EPS, reserve)
+        torch.cuda.synchronize()
+        ni, ci = bn_sample(shape)
+        sl = lambda a: a.cpu().numpy()[ni][:, ci]  # noqa: E731
+        os.makedirs(OUT, exist_ok=True)
+        path = os.path.join(OUT, f"bn_spatial_{i}.npz")
+        np.savez_compressed(path, kind="bn_spatial", dims=np.array(shape), seed=seed,
+                            scalars=np.array([BN_FACTOR, BN_EPS]), y=sl(y), dx=sl(dx),
+                            running_mean=rmt.cpu().numpy(), running_var=rvt.cpu().numpy(),
+                            save_mean=smean.cpu().numpy(), save_inv_std=sinv.cpu().numpy(),
+                            dscale=dscale.cpu().numpy(), dbias=dbias.cpu().numpy())
+        written.append(path)
+        del x, dy, y, dx, reserve
+    return written
+
+
 def _child_conv() -> int:
     import torch
 
@@ -188,6 +248,7 @@ def _child_conv() -> int:
             path = os.path.join(HERE, f"{kind}_{i}.npz")
             np.savez_compressed(path, kind=kind, dims=dims, out=out.cpu().numpy(), **extra)
             written.append(path)
+    written += _child_bn()
     for p in written:
         print(os.path.relpath(p, ROOT), os.path.getsize(p))
     return 0
@@ -199,4 +260,8 @@ if __name__ == "__main__":
         sys.exit(_child_gemm())
     if mode == "conv":
         sys.exit(_child_conv())
+    if mode == "bn":  # batch-norm fixtures alone (no preload needed)
+        for p in _child_bn():
+            print(p, os.path.getsize(p))
+        sys.exit(0)
     sys.exit(_parent())

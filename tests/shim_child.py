@@ -314,6 +314,213 @@ def scenario_trace(orion):
             "waits": waits, "hp_iters": hp.iters, "be_iters": be.iters}
 
 
+def scenario_hgemm(orion):
+    """cublasHgemm, cublasHgemmStridedBatched and cublasSgemmEx called
+    directly (PyTorch issues none of them): captured on client 0 they run on
+    the kx kernels; the same calls with capture off run on the real cuBLAS.
+    Both are compared with a float64 product of the same operands."""
+    import torch
+    g = ctypes.CDLL(None)  # global scope: the preloaded interposer comes first
+    P, I, LL = ctypes.c_void_p, ctypes.c_int, ctypes.c_longlong
+    g.cublasHgemm.argtypes = [P, I, I, I, I, I, P, P, I, P, I, P, P, I]
+    g.cublasHgemmStridedBatched.argtypes = [P, I, I, I, I, I, P, P, I, LL, P, I, LL, P, P, I,
+                                            LL, I]
+    g.cublasSgemmEx.argtypes = [P, I, I, I, I, I, P, P, I, I, P, I, I, P, P, I, I]
+    for f in (g.cublasHgemm, g.cublasHgemmStridedBatched, g.cublasSgemmEx):
+        f.restype = I
+    gen = torch.Generator(device="cuda").manual_seed(7)
+
+    def r(*shape, dtype):
+        return torch.randn(*shape, device="cuda", generator=gen).to(dtype)
+
+    def half(v):
+        return ctypes.byref(ctypes.c_uint16(
+            int(torch.tensor([v], dtype=torch.float16).view(torch.int16).item()) & 0xFFFF))
+
+    def f32(v):
+        return ctypes.byref(ctypes.c_float(v))
+
+    h, bf = torch.float16, torch.bfloat16
+    # column-major views: y^T (m x n) = W (m x k, stored k-major: transa = T) . x^T
+    m, n, k = 384, 256, 320
+    A, B = r(m, k, dtype=h), r(n, k, dtype=h)
+    C0 = r(n, m, dtype=h)
+    batch, sA, sB, sC = 3, m * k, n * k, n * m
+    Ab, Bb, Cb0 = r(batch, m, k, dtype=h), r(batch, n, k, dtype=h), r(batch, n, m, dtype=h)
+    Abf, Bbf = r(m, k, dtype=bf), r(n, k, dtype=bf)
+
+    def ref64(a, b, alpha=1.0, beta=0.0, c=None):
+        out = alpha * (b.double() @ a.double().t())
+        if c is not None and beta != 0.0:
+            out = out + beta * c.double()
+        return out
+
+    refs = {"hgemm": ref64(A, B, 1.5, 0.5, C0),
+            "hgemm_strided_batched": torch.stack([ref64(Ab[i], Bb[i], 0.75, -1.0, Cb0[i])
+                                                  for i in range(batch)]),
+            "sgemmex_bf16_f32": ref64(Abf, Bbf),
+            "sgemmex_f16_f16": ref64(A, B, 2.0, 0.0)}
+
+    def run():
+        handle = ctypes.c_void_p(torch.cuda.current_blas_handle())
+        out = {}
+        C = C0.clone()
+        st = g.cublasHgemm(handle, 1, 0, m, n, k, half(1.5), A.data_ptr(), k, B.data_ptr(), k,
+                           half(0.5), C.data_ptr(), m)
+        out["hgemm"] = (st, C)
+        Cb = Cb0.clone()
+        st = g.cublasHgemmStridedBatched(handle, 1, 0, m, n, k, half(0.75), Ab.data_ptr(), k, sA,
+                                         Bb.data_ptr(), k, sB, half(-1.0), Cb.data_ptr(), m, sC,
+                                         batch)
+        out["hgemm_strided_batched"] = (st, Cb)
+        D = torch.zeros(n, m, device="cuda")
+        st = g.cublasSgemmEx(handle, 1, 0, m, n, k, f32(1.0), Abf.data_ptr(), 14, k,
+                             Bbf.data_ptr(), 14, k, f32(0.0), D.data_ptr(), 0, m)
+        out["sgemmex_bf16_f32"] = (st, D)
+        E = torch.zeros(n, m, device="cuda", dtype=h)
+        st = g.cublasSgemmEx(handle, 1, 0, m, n, k, f32(2.0), A.data_ptr(), 2, k, B.data_ptr(),
+                             2, k, f32(0.0), E.data_ptr(), 2, m)
+        out["sgemmex_f16_f16"] = (st, E)
+        torch.cuda.current_stream().synchronize()
+        return out
+
+    assert orion.orion_init_scheduler(1) == 0
+    orion.orion_set_capture(0)
+    real = run_on_client(orion, 0, run)
+    torch.cuda.synchronize()
+    orion.orion_start_scheduler_thread()
+    orion.orion_set_capture(1)
+    cap = run_on_client(orion, 0, run)
+    orion.orion_set_capture(0)
+    stats = orion.stats(0)
+    orion.orion_stop_scheduler()
+    res = {"stats": stats, "status": {}, "errors": {}, "real_errors": {}}
+    for name, ref in refs.items():
+        res["status"][name] = [real[name][0], cap[name][0]]
+        res["errors"][name] = rel(cap[name][1], ref)
+        res["real_errors"][name] = rel(real[name][1], ref)
+    return res
+
+
+def scenario_vgg16(orion):
+    """End-to-end: the VGG16 forward of the HP client (fp32, batch 32 x
+    3x224x224) captured on the kx kernels vs the same forward through the
+    real cuDNN / cuBLAS (TF32 off), both against a float64 forward of two of
+    the images (samples are independent in eval mode)."""
+    import copy
+
+    import torch
+
+    from kernel_intercept_b200 import harness
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cudnn.allow_tf32 = False
+    torch.manual_seed(0)
+    m = harness.make_vgg16("cuda").eval()
+    x = torch.randn(32, 3, 224, 224, device="cuda")
+    pick = [0, 31]
+    assert orion.orion_init_scheduler(1) == 0
+    orion.orion_set_capture(0)
+    with torch.no_grad():
+        ref = m(x)
+        ref64 = copy.deepcopy(m).double()(x[pick].double())
+    torch.cuda.synchronize()
+    orion.orion_start_scheduler_thread()
+    orion.orion_set_capture(1)
+
+    def fwd():
+        with torch.no_grad():
+            return m(x)
+
+    out = run_on_client(orion, 0, fwd)
+    orion.orion_set_capture(0)
+    stats = orion.stats(0)
+    orion.orion_stop_scheduler()
+    return {"errors": {"kx_vs_f64": rel(out[pick], ref64), "lib_vs_f64": rel(ref[pick], ref64),
+                       "kx_vs_lib": rel(out, ref)}, "stats": stats}
+
+
+def scenario_llama(orion):
+    """End-to-end: the LLaMA-style decoder forward of the bf16 HP client
+    (12 layers, d_model 2048, batch 4 x seq 1024) captured on the kx kernels
+    vs the same forward through the real cuBLAS (bf16 in / out, fp32
+    accumulation), both against an fp32 copy of the model (TF32 off) on one
+    of the sequences."""
+    import copy
+
+    import torch
+
+    from kernel_intercept_b200 import harness
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.manual_seed(0)
+    m = harness.make_llama(device="cuda", dtype=torch.bfloat16).eval()
+    tok = torch.randint(0, 32000, (4, 1024), device="cuda")
+    assert orion.orion_init_scheduler(1) == 0
+    orion.orion_set_capture(0)
+    with torch.no_grad():
+        ref = m(tok)
+        m32 = copy.deepcopy(m).float()
+        ref32 = m32(tok[:1])
+        del m32
+    torch.cuda.synchronize()
+    orion.orion_start_scheduler_thread()
+    orion.orion_set_capture(1)
+
+    def fwd():
+        with torch.no_grad():
+            return m(tok)
+
+    out = run_on_client(orion, 0, fwd)
+    orion.orion_set_capture(0)
+    stats = orion.stats(0)
+    orion.orion_stop_scheduler()
+    return {"errors": {"kx_vs_f32": rel(out[:1], ref32), "lib_vs_f32": rel(ref[:1], ref32),
+                       "kx_vs_lib": rel(out, ref)}, "stats": stats}
+
+
+def scenario_gpt_train(orion):
+    """End-to-end: one BE training step of the GPT decoder (fp32, batch 16 x
+    256, cross-entropy against random targets): loss and gradients captured
+    on the kx kernels vs the real libraries (TF32 off), both against a
+    float64 copy of the model."""
+    import copy
+
+    import torch
+    import torch.nn.functional as F
+
+    from kernel_intercept_b200 import harness
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.manual_seed(0)
+    m = harness.make_gpt(device="cuda")
+    tok = torch.randint(0, 32000, (16, 256), device="cuda")
+    tgt = torch.randint(0, 32000, (16, 256), device="cuda")
+    names = ["lm.weight", "blocks.0.heads.0.query.weight", "blocks.5.l1.weight", "tok.weight"]
+
+    def step(model):
+        model.zero_grad(set_to_none=True)
+        logits = model(tok)
+        loss = F.cross_entropy(logits.view(-1, logits.shape[-1]), tgt.view(-1))
+        loss.backward()
+        params = dict(model.named_parameters())
+        return loss.detach().clone(), {n: params[n].grad.detach().clone() for n in names}
+
+    assert orion.orion_init_scheduler(1) == 0
+    orion.orion_set_capture(0)
+    loss_ref, g_ref = step(m)
+    loss64, g64 = step(copy.deepcopy(m).double())
+    torch.cuda.synchronize()
+    orion.orion_start_scheduler_thread()
+    orion.orion_set_capture(1)
+    loss_kx, g_kx = run_on_client(orion, 0, lambda: step(m))
+    orion.orion_set_capture(0)
+    stats = orion.stats(0)
+    orion.orion_stop_scheduler()
+    errs = {"loss": {"kx_vs_f64": rel(loss_kx, loss64), "lib_vs_f64": rel(loss_ref, loss64)}}
+    for n in names:
+        errs[n] = {"kx_vs_f64": rel(g_kx[n], g64[n]), "lib_vs_f64": rel(g_ref[n], g64[n]),
+                   "kx_vs_lib": rel(g_kx[n], g_ref[n])}
+    return {"errors": errs, "stats": stats, "loss": float(loss_kx)}
+
+
 def read_op_log(path):
     """Entries of an op log: (client, op type, route, shape integers)."""
     out = []

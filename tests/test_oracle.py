@@ -6,6 +6,7 @@ batch_norm) and, when present, against the golden fixtures captured from the
 reference shim on a B200 (tests/golden/*.npz, made by tests/golden/make_golden.py).
 """
 import glob
+import sys
 import os
 
 import numpy as np
@@ -176,6 +177,29 @@ def test_batchnorm_matches_torch(mode):
 
 # ------------------------------------------------------ golden fixtures ---
 
+def _check_bn_golden(z, path):
+    """cuDNN spatial batch norm (training forward + backward) at a VGG-like
+    shape: inputs regenerated from the fixture's seed, the oracle's outputs
+    against cuDNN's per-channel results and sampled y / dx."""
+    sys.path.insert(0, GOLDEN)
+    import make_golden as mg
+    shape = tuple(int(v) for v in z["dims"])
+    factor, eps = (float(v) for v in z["scalars"])
+    x, scale, bias, rm, rv, dy = mg.bn_inputs(shape, int(z["seed"]))
+    c = shape[1]
+    y = np.zeros(shape, np.float32)
+    sm, si = np.zeros(c, np.float32), np.zeros(c, np.float32)
+    o.bn_fwd_training(1, 1.0, 0.0, x, y, scale, bias, factor, rm, rv, eps, sm, si)
+    dx = np.zeros(shape, np.float32)
+    ds, db = np.zeros(c, np.float32), np.zeros(c, np.float32)
+    o.bn_bwd(1, 1.0, 0.0, 1.0, 0.0, x, dy, dx, scale, ds, db, eps, sm, si)
+    ni, ci = mg.bn_sample(shape)
+    for name, got in (("y", y[ni][:, ci]), ("dx", dx[ni][:, ci]), ("running_mean", rm),
+                      ("running_var", rv), ("save_mean", sm), ("save_inv_std", si),
+                      ("dscale", ds), ("dbias", db)):
+        assert o.normwise_rel_err(got, z[name]) < 1e-5, (path, name)
+
+
 def _golden_files():
     return sorted(glob.glob(os.path.join(GOLDEN, "*.npz")))
 
@@ -220,6 +244,8 @@ def test_oracle_pinned_to_reference_goldens():
             else:
                 got = o.conv_bwd_filter(d, 1.0, z["x"], z["dy"])
             assert o.normwise_rel_err(got, z["out"]) < 1e-5, path
+        elif kind == "bn_spatial":
+            _check_bn_golden(z, path)
         else:
             continue
         checked += 1

@@ -71,12 +71,64 @@ def test_batchnorm_through_interposer():
         assert err <= F32_TOL, (name, err)
 
 
+def test_fp16_and_sgemmex_through_interposer():
+    """cublasHgemm / cublasHgemmStridedBatched (fp16, kx accumulates in fp32)
+    and cublasSgemmEx run on kx when captured, none of them on the real
+    cuBLAS; results within the 16-bit tolerance of a float64 product, as the
+    real library's are."""
+    res = run_child("hgemm")
+    st = res["stats"]
+    assert st["errors"] == 0 and st["passthrough_ops"] == 0, st
+    assert st["kx_ops"] == 4, st
+    for name, (st_real, st_cap) in res["status"].items():
+        assert st_real == 0 and st_cap == 0, (name, st_real, st_cap)
+    for name, err in res["errors"].items():
+        assert err <= BF16_TOL, (name, err, res["real_errors"][name])
+
+
 def test_gpt_forward_through_interposer():
     res = run_child("gpt")
     st = res["stats"]
     assert st["errors"] == 0, st
     assert st["kx_ops"] > 200, st  # 144 per-head GEMMs + 96 batched + Lt per forward
     assert res["errors"]["logits"] <= F32_TOL, res
+
+
+def test_vgg16_forward_through_interposer():
+    """The HP model of the VGG16 configuration, batch 32, end to end: every
+    convolution and classifier GEMM on kx, within 1e-5 of a float64 forward
+    (cuDNN's own fp32 forward is reported beside it)."""
+    res = run_child("vgg16", timeout=600)
+    st = res["stats"]
+    assert st["errors"] == 0 and st["passthrough_ops"] == 0, st
+    assert st["kx_ops"] >= 16, st  # 13 convolutions + 3 classifier GEMMs
+    e = res["errors"]
+    assert e["kx_vs_f64"] <= F32_TOL, e
+    assert e["kx_vs_lib"] <= e["lib_vs_f64"] + F32_TOL, e
+
+
+def test_llama_bf16_forward_through_interposer():
+    """The HP model of the LLaMA configuration (bf16, batch 4 x 1024) end to
+    end on kx: no further from an fp32 copy of the model than cuBLAS's own
+    bf16 forward is, within the bf16 tolerance."""
+    res = run_child("llama", timeout=600)
+    st = res["stats"]
+    assert st["errors"] == 0 and st["passthrough_ops"] == 0, st
+    assert st["kx_ops"] >= 12 * 9 + 1, st  # per layer 7 projections + 2 attention bmm; head
+    e = res["errors"]
+    assert e["kx_vs_f32"] <= max(BF16_TOL, 1.25 * e["lib_vs_f32"]), e
+    assert e["kx_vs_lib"] <= BF16_TOL + e["lib_vs_f32"], e
+
+
+def test_gpt_training_step_through_interposer():
+    """One BE training step of the GPT configuration (batch 16 x 256): loss
+    and weight gradients on kx no further from a float64 step than the real
+    libraries' fp32 step is, plus 1e-5."""
+    res = run_child("gpt_train", timeout=600)
+    st = res["stats"]
+    assert st["errors"] == 0 and st["passthrough_ops"] == 0, st
+    for name, e in res["errors"].items():
+        assert e["kx_vs_f64"] <= e["lib_vs_f64"] + F32_TOL, (name, e)
 
 
 def test_hp_be_clients_contend():
