@@ -1,34 +1,41 @@
 #!/usr/bin/env python
 """Benchmark: HP/BE co-scheduling on the kx kernels through the drop-in
-interposer: HP VGG16 inference against BE GPT training.
+interposer, on one of the five benchmark configurations (--config, default 4;
+kernel_intercept_b200/configs.py defines them).
 
-Workload (one "step" = one HP request):
-  HP  = VGG16 inference, fp32, batch 32 x 3x224x224 N(0,1), Kaiming-normal init
-  BE  = training steps of a GPT (6 layers, d_model 512, 8 heads,
-        FFN 2048, vocab 32000), batch 16 x seq 256, AdamW lr 1e-4,
-        cross-entropy against uniform random targets
-Both run as PyTorch models in one process under
-LD_PRELOAD=kernel_intercept_b200/libgpu_scheduler.so; client 0 (HP) and client
-1 (BE) are registered threads, every captured GEMM / convolution runs on the
-kx sm_100a kernels (bench.py re-executes itself with the preload when needed).
+Default workload (--config 4, the per-GPU group of the placement sweep), one
+"step" = one HP request:
+  HP  = LLaMA-style decoder inference, bf16, batch 4 x 1024 tokens (12 layers,
+        d_model 2048, 16 heads, SwiGLU 5504, vocab 32000)
+  BE1 = VGG16 training, fp32, batch 64, SGD momentum 0.9, random labels
+  BE2 = GPT training, fp32 (6 layers, d512), batch 16 x 256, AdamW
+All clients are PyTorch models in one process under
+LD_PRELOAD=kernel_intercept_b200/libgpu_scheduler.so (bench.py re-executes
+itself with the preload when needed); client 0 is HP, 1.. are BE; every
+captured GEMM / convolution runs on the kx sm_100a kernels.
 
-Phases (same models and inputs): HP alone, BE alone, HP + BE together (HP
-back to back: the timed region), HP paced at a duty cycle of --hp-load
-against BE (the Orion setting: HP p99 vs solo and BE retention), and the
-end-to-end repeat.  The timed region is the K HP steps of the contended phase,
-bracketed by a barrier and a device synchronize, timed with CUDA events on
-the HP stream (max over ranks).  `value` = HP images/s under contention
-(whole job: sum over ranks).
-`e2e` repeats the contended phase (over max(K, 200) HP steps, like the
-latency phases) with the HP input copied from pinned host memory and the
-logits copied back inside every step.  `roofline` is the
-dominant captured kernel class (HP convolutions) from CUDA events recorded
-around each captured op during the timed region.  `cpu_baseline` is the CPU
-oracle's VGG16 forward on a bounded sample, timed on this host.
+Phases per rank (same models and inputs):
+  library arm  capture off: PyTorch calls cuBLAS / cuDNN itself (TF32 off),
+               the clients on their own streams with no scheduler (HP alone,
+               BE alone, HP + BE back to back, HP paced);
+  kx arm       capture on, the HP/BE scheduler: HP alone, BE alone, HP + BE
+               back to back (the timed region: K HP steps bracketed by a
+               barrier and a device synchronize, CUDA events on the HP stream,
+               max over ranks), HP paced at --hp-load duty against BE (HP p99
+               vs solo and BE retention), and the end-to-end repeat with host
+               buffers.
+`value` = HP tokens/s (images/s for config 1) under contention, whole job.
+`e2e` = the same with the HP input copied from pinned host memory and the
+result (next-token logits; logits for VGG16) copied back in every step.
+`roofline` = the HP client's dominant captured op class from CUDA events the
+worker records around each captured op during the timed region.
+`cpu_baseline` = the HP model's plain PyTorch CPU forward on this host (all
+cores, rank 0 at N = 1).
 
---impl reference prints the same line for the reference's CPU path of the
-captured ops (the oracle restatement of cuBLAS / cuDNN semantics, all host
-threads), on a bounded sample per step.
+--config 3 runs the GEMM contention microbench instead (see run_microbench).
+--impl reference prints the same line for the configuration's CPU-runnable
+form: the HP model's PyTorch CPU forward (no interception), a bounded sample
+per step, all host threads, rank 0 only.
 """
 from __future__ import annotations
 
@@ -43,8 +50,6 @@ import time
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-HP_BATCH = 32
-BE_BATCH, BE_SEQ = 16, 256
 METRIC = "HP p99 latency vs solo + BE iters/s; captured GEMM/conv % of B200 peak"
 
 
@@ -53,11 +58,19 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", type=int, default=4, choices=[0, 1, 2, 3, 4])
     ap.add_argument("--impl", default="kx", choices=["kx", "reference"])
     ap.add_argument("--be-seconds", type=float, default=4.0)
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-library", action="store_true",
+                    help="skip the library arm (capture off, cuBLAS / cuDNN)")
+    ap.add_argument("--lat-steps", type=int, default=200,
+                    help="HP steps of the latency phases (solo, paced, e2e)")
     ap.add_argument("--be-keep-sms", type=int, default=-1,
                     help="SMs a BE op keeps while HP runs (default: the scheduler's)")
+    ap.add_argument("--kernel-info", default="",
+                    help="directory of per-client kernel_info CSV tables (client<i>.csv) "
+                         "for the Orion admission gate")
     ap.add_argument("--gil-switch-ms", type=float, default=0.5,
                     help="sys.setswitchinterval of the process (HP and BE are Python threads; "
                          "0: Python's default of 5 ms)")
@@ -66,8 +79,7 @@ def parse():
                          "collector while the clients run (collections stop every thread)")
     ap.add_argument("--trace", default="",
                     help="write a Chrome trace of the interposer's activity in the paced phase "
-                         "(client issues and waits, worker execution, HP flag) to this path; "
-                         "a .gz path is compressed")
+                         "to this path; a .gz path is compressed")
     ap.add_argument("--hp-load", type=float, default=1.0 / 3.0,
                     help="HP duty cycle of the paced phase (request period = solo p50 / load)")
     return ap.parse_args()
@@ -88,84 +100,60 @@ def measured_peaks():
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
 
 
-# --------------------------------------------------------- CPU baseline ----
+def rnd(v, n=3):
+    return None if v is None else round(float(v), n)
 
-def oracle_vgg16_images_per_s(sample_images=1, threads=None):
-    """VGG16 forward of `sample_images` images through the oracle (conv and FC
-    restatements; ReLU / max-pool in numpy).  Returns (images/s, cores)."""
-    import numpy as np
 
-    from oracle import oracle as o
-    if threads:
-        o.set_num_threads(threads)
-    cores = o.num_threads()
-    rng = np.random.default_rng(0)
-    cfg = [64, 64, "M", 128, 128, "M", 256, 256, 256, "M", 512, 512, 512, "M", 512, 512, 512, "M"]
-    x = rng.standard_normal((sample_images, 3, 224, 224)).astype(np.float32)
-    c_in = 3
-    weights = []
-    for v in cfg:
-        if v == "M":
-            continue
-        std = (2.0 / (v * 9)) ** 0.5
-        weights.append((rng.standard_normal((v, c_in, 3, 3)).astype(np.float32) * std,
-                        np.zeros(v, np.float32)))
-        c_in = v
-    fcs = [(25088, 4096), (4096, 4096), (4096, 1000)]
-    fcw = [(rng.standard_normal((o_, i_)).astype(np.float32) * 0.01, np.zeros(o_, np.float32))
-           for i_, o_ in fcs]
-    t0 = time.perf_counter()
-    h = x
-    wi = 0
-    for v in cfg:
-        if v == "M":
-            n, c, hh, ww = h.shape
-            h = h.reshape(n, c, hh // 2, 2, ww // 2, 2).max(axis=(3, 5))
-            continue
-        w, b = weights[wi]
-        wi += 1
-        n, c, hh, ww = h.shape
-        d = o.conv_desc(n, c, hh, ww, w.shape[0], 3, 3, pad=(1, 1))
-        h = o.conv_fwd(d, 1.0, h, w) + b[None, :, None, None]
-        h = np.maximum(h, 0.0, dtype=np.float32)
-    h = h.reshape(h.shape[0], -1)
-    for i, (w, b) in enumerate(fcw):
-        n = h.shape[0]
-        out = np.zeros((n, w.shape[0]), np.float32)
-        # y^T (out x n) = W (out x in) . h^T: cuBLAS view transa = T, transb = N
-        o.gemm_ex(1, 0, w.shape[0], n, w.shape[1], 1.0, np.ascontiguousarray(w), o.R_32F,
-                  w.shape[1], np.ascontiguousarray(h), o.R_32F, w.shape[1], 0.0, None, o.R_32F,
-                  w.shape[0], D=out, Dtype=o.R_32F, ldd=w.shape[0], epilogue=4, bias=b)
-        h = np.maximum(out, 0.0) if i < 2 else out
-    dt = time.perf_counter() - t0
-    return sample_images / dt, cores
-
+# ------------------------------------------------------- reference arm ----
 
 def run_reference(args):
+    """The configuration's CPU-runnable form: the HP model as plain PyTorch on
+    the host cores (no interception), one image / one sequence per step."""
     rank, world, _ = dist_info()
     if rank != 0:
         return 0  # rank 0 alone runs the CPU path
-    cores = os.cpu_count() or 1
-    vals = []
-    for _ in range(max(0, args.warmup)):
-        pass  # the oracle has no warm-up state; warm-up steps are not timed
-    t0 = time.perf_counter()
-    for _ in range(args.steps):
-        v, used = oracle_vgg16_images_per_s(1, threads=cores)
-        vals.append(v)
-    total = time.perf_counter() - t0
-    value = args.steps / total
+    import torch
+
+    from kernel_intercept_b200 import configs, harness
+    cfg = args.config
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)  # torchrun sets OMP_NUM_THREADS=1
+    torch.manual_seed(0)
+    if cfg == 0:
+        m = harness.make_gpt(device="cpu").eval()
+        x = torch.randint(0, 32000, (1, configs.GPT_SEQ))
+        units, unit = configs.GPT_SEQ, "tokens/s"
+        what = f"1 x {configs.GPT_SEQ} tokens of the batch-8 GPT forward, fp32"
+    elif cfg in (1, 3):
+        m = harness.make_vgg16("cpu").eval()
+        x = torch.randn(1, 3, 224, 224)
+        units, unit = 1, "images/s"
+        what = "1 image of the batch-32 VGG16 forward, fp32"
+    else:
+        m = harness.make_llama(device="cpu").eval()
+        x = torch.randint(0, 32000, (1, configs.LLAMA_SEQ))
+        units, unit = configs.LLAMA_SEQ, "tokens/s"
+        what = (f"1 x {configs.LLAMA_SEQ} tokens of the batch-4 LLaMA-style decoder forward, "
+                "fp32 weights on the CPU")
+    with torch.no_grad():
+        for _ in range(max(0, args.warmup)):
+            m(x)
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            m(x)
+        total = time.perf_counter() - t0
+    value = units * args.steps / total
+    used = torch.get_num_threads()
     line = {
-        "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "images/s",
+        "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": unit,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(total / args.steps * 1e3, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f64-accumulate",
-        "data": "synthetic", "config": {"workload": "VGG16 inference fp32 (the HP model), CPU "
-                                        "path of the captured ops, 1-image sample per step",
-                                        "batch": 1},
-        "cpu_baseline": {"value": round(value, 4), "unit": "images/s", "cores": used,
-                         "kind": "port", "sample": "1 image of the batch-32 VGG16 forward per step"},
-        "e2e": {"value": round(value, 4), "unit": "images/s", "h2d_bytes_per_step": 0,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": configs.DESCRIPTIONS[cfg] + "; CPU-runnable form: the HP "
+                   "model's PyTorch CPU forward, no interception", "config": cfg},
+        "cpu_baseline": {"value": round(value, 4), "unit": unit, "cores": used, "kind": "port",
+                         "sample": what + f", {used} threads"},
+        "e2e": {"value": round(value, 4), "unit": unit, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -214,71 +202,171 @@ class Clocks:
         mx = max(float(r[1]) for r in rows if r[1].replace(".", "").isdigit())
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in rows for i in range(4) if r[3 + i] == "Active"})
-        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": reasons}
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": reasons,
+                "samples": len(rows)}
 
 
-def run_kx(args):
+class Ranks:
+    """Barrier and gathers over the process group (no-ops at N = 1)."""
+
+    def __init__(self, world, dev):
+        self.world, self.dev, self.pg = world, dev, None
+        if world > 1:
+            import datetime
+
+            import torch.distributed as dist
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                    device_id=dev)
+            self.pg = dist
+
+    def barrier(self):
+        import torch
+        torch.cuda.synchronize()
+        if self.pg is not None:
+            self.pg.barrier()
+
+    def gather(self, values):
+        """Per-rank lists of floats (every rank gets all of them)."""
+        if self.pg is None:
+            return [list(values)]
+        import torch
+        t = torch.tensor(values, device=self.dev, dtype=torch.float64)
+        parts = [torch.zeros_like(t) for _ in range(self.world)]
+        self.pg.all_gather(parts, t)
+        return [[float(v) for v in x.tolist()] for x in parts]
+
+    def close(self):
+        if self.pg is not None:
+            self.pg.barrier()
+            self.pg.destroy_process_group()
+
+
+def rate(res, units):
+    return res.iters * units / (res.elapsed_ms / 1e3) if res.elapsed_ms else 0.0
+
+
+def latency_block(harness, solo, cont, paced, hp_units, period):
+    s99 = harness.percentile(solo.latencies_ms, 0.99)
+    p99 = harness.percentile(cont.latencies_ms, 0.99)
+    out = {"solo_p50_ms": rnd(harness.percentile(solo.latencies_ms, 0.5)),
+           "solo_p99_ms": rnd(s99),
+           "p50_ms": rnd(harness.percentile(cont.latencies_ms, 0.5)), "p99_ms": rnd(p99),
+           "p99_vs_solo": rnd(p99 / s99, 4) if s99 else None,
+           "units_per_s": rnd(rate(cont, hp_units), 1)}
+    if paced is not None:
+        pp99 = harness.percentile(paced.latencies_ms, 0.99)
+        out["paced"] = {"period_ms": rnd(period), "steps": paced.iters,
+                        "p50_ms": rnd(harness.percentile(paced.latencies_ms, 0.5)),
+                        "p99_ms": rnd(pp99), "p99_vs_solo": rnd(pp99 / s99, 4) if s99 else None,
+                        "issue_p50_ms": rnd(harness.percentile(paced.issue_ms, 0.5)),
+                        "issue_p99_ms": rnd(harness.percentile(paced.issue_ms, 0.99))}
+    return out
+
+
+def be_block(bes, solo, cont, paced):
+    """Per BE client: solo / contended / paced rates and retention."""
+    out = []
+    for i, c in enumerate(bes):
+        s = rate(solo[i], 1)
+        row = {"client": i + 1, "workload": c.name, "unit": c.unit,
+               "solo_iters_per_s": rnd(s), "iters_per_s": rnd(rate(cont[i], 1)),
+               "retention": rnd(rate(cont[i], 1) / s, 4) if s else None,
+               f"{c.unit}_per_s": rnd(rate(cont[i], c.units), 1)}
+        if paced is not None:
+            row["paced_iters_per_s"] = rnd(rate(paced[i], 1))
+            row["paced_retention"] = rnd(rate(paced[i], 1) / s, 4) if s else None
+            row[f"paced_{c.unit}_per_s"] = rnd(rate(paced[i], c.units), 1)
+        out.append(row)
+    return out
+
+
+def run_phases(harness, orion, hp, bes, args, lat_steps, hp_steps, e2e, profiled=None,
+               clocks=None, kxlib=None, ranks=None):
+    """Solo, BE-alone, contended (timed), paced and (optionally) e2e phases.
+    Returns a dict of ClientResults and the timed region's extras."""
+    res = {}
+    prof = profiled or (lambda tag, run: (run(None), []))
+    ranks.barrier()
+    (res["hp_solo"], _), res["solo_recs"] = prof("hp_solo", lambda on_start: harness.run_clients(
+        orion, hp.step, [], lat_steps, args.warmup, with_be=False, on_start=on_start))
+    ranks.barrier()
+    _, res["be_solo"] = harness.run_clients(orion, hp.step, [c.step for c in bes], 0, 0,
+                                            with_hp=False, be_seconds=args.be_seconds)
+    ranks.barrier()
+    launches0 = kxlib.kx_launch_count() if kxlib is not None else 0
+    if clocks is not None:
+        clocks.start()
+    (res["hp_cont"], res["be_cont"]), res["cont_recs"] = prof(
+        "contended", lambda on_start: harness.run_clients(
+            orion, hp.step, [c.step for c in bes], hp_steps, args.warmup, on_start=on_start))
+    res["clocks"] = clocks.stop() if clocks is not None else None
+    res["launches"] = (kxlib.kx_launch_count() - launches0) if kxlib is not None else 0
+    ranks.barrier()
+    s50 = harness.percentile(res["hp_solo"].latencies_ms, 0.5)
+    res["period"] = s50 / max(args.hp_load, 1e-3)
+    if orion is not None and args.trace and e2e:
+        orion.orion_trace_start()
+    res["hp_paced"], res["be_paced"] = harness.run_clients(
+        orion, hp.step, [c.step for c in bes], lat_steps, args.warmup, hp_period_ms=res["period"])
+    if orion is not None and args.trace and e2e:
+        harness.write_trace(orion, args.trace)
+    res["hp_e2e"] = None
+    if e2e and hp.e2e_step is not None:
+        ranks.barrier()
+        res["hp_e2e"], _ = harness.run_clients(orion, hp.e2e_step, [c.step for c in bes],
+                                               lat_steps, args.warmup)
+    return res
+
+
+def run_group(args):
     import torch
-    import torch.nn.functional as F
 
     if args.gil_switch_ms > 0:
         # HP and BE are Python threads of one process (as in the reference's
         # drivers): the interval bounds how long one waits for the other's GIL
         sys.setswitchinterval(args.gil_switch_ms / 1e3)
 
-    from kernel_intercept_b200 import harness, kx
+    from kernel_intercept_b200 import configs, harness, kx
 
     rank, world, local = dist_info()
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    pg = None
-    if world > 1:
-        import datetime
-
-        import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=dev)
-        pg = dist
-
+    ranks = Ranks(world, dev)
     orion = harness.Orion()
     torch.backends.cuda.matmul.allow_tf32 = False
     torch.backends.cudnn.allow_tf32 = False
     torch.backends.cudnn.benchmark = False
-    torch.manual_seed(0)
-
-    # ---- models and resident inputs
-    vgg = harness.make_vgg16(dev).eval()
-    gpt = harness.make_gpt(device=dev)
-    opt = torch.optim.AdamW(gpt.parameters(), lr=1e-4)
-    img = torch.randn(HP_BATCH, 3, 224, 224, device=dev)
-    img_host = img.cpu().pin_memory()
-    out_host = torch.empty(HP_BATCH, 1000).pin_memory()
-    tok = torch.randint(0, 32000, (BE_BATCH, BE_SEQ), device=dev)
-    tgt = torch.randint(0, 32000, (BE_BATCH, BE_SEQ), device=dev)
-
-    def hp_step():
-        with torch.no_grad():
-            vgg(img)
-
-    def hp_step_e2e():
-        with torch.no_grad():
-            img.copy_(img_host, non_blocking=True)
-            out = vgg(img)
-            out_host.copy_(out, non_blocking=True)
-
-    def be_step():
-        logits = gpt(tok)
-        loss = F.cross_entropy(logits.view(-1, logits.shape[-1]), tgt.view(-1))
-        opt.zero_grad(set_to_none=True)
-        loss.backward()
-        opt.step()
+    hp, bes = configs.build(args.config, dev)
+    n_clients = 1 + len(bes)
 
     # native warm-up with capture off (allocator, cuDNN plans), like the reference drivers
-    assert orion.orion_init_scheduler(2) == 0, "orion_init_scheduler failed"
+    assert orion.orion_init_scheduler(n_clients) == 0, "orion_init_scheduler failed"
     orion.orion_set_capture(0)
-    hp_step()
-    be_step()
+    for c in [hp] + bes:
+        c.step()
+    if hp.e2e_step is not None:
+        hp.e2e_step()
     torch.cuda.synchronize()
+    lat_steps = max(args.steps, args.lat_steps)
+
+    # ---- library arm: capture off, PyTorch calls cuBLAS / cuDNN itself
+    lib = None
+    if not args.no_library:
+        lr = run_phases(harness, None, hp, bes, args, max(50, lat_steps // 2), args.steps,
+                        e2e=False, ranks=ranks)
+        lib = {"hp": latency_block(harness, lr["hp_solo"], lr["hp_cont"], lr["hp_paced"],
+                                   hp.units, lr["period"]),
+               "be": be_block(bes, lr["be_solo"], lr["be_cont"], lr["be_paced"]),
+               "ms_per_step": rnd(lr["hp_cont"].elapsed_ms / args.steps),
+               "note": "capture off: cuBLAS / cuDNN (TF32 off) called by PyTorch, clients on "
+                       "their own streams, no scheduler"}
+
+    # ---- kx arm
+    if args.kernel_info:
+        for c in range(n_clients):
+            path = os.path.join(args.kernel_info, f"client{c}.csv")
+            if os.path.exists(path):
+                orion.orion_load_kernel_info(c, path.encode())
     if args.be_keep_sms >= 0:
         orion.orion_set_be_keep_sms(args.be_keep_sms)
     orion.orion_start_scheduler_thread()
@@ -288,18 +376,11 @@ def run_kx(args):
         gc.collect()
         gc.freeze()
         gc.disable()
-
-    def barrier():
-        torch.cuda.synchronize()
-        if pg is not None:
-            pg.barrier()
-
     kxlib = kx.lib()
 
     def profiled(tag, run):
         """Runs run(on_start); the profiling session opens in on_start (after
-        both clients' warm-up, so warm-up launches are not in the records) and
-        closes when run returns.  Returns (run's result, records)."""
+        every client's warm-up) and closes when run returns."""
         path = tempfile.mktemp(prefix="kx_prof_", suffix=".json")
         opened = []
 
@@ -308,7 +389,7 @@ def run_kx(args):
             opened.append(True)
 
         try:
-            res = run(on_start)
+            out = run(on_start)
         finally:
             if opened:
                 orion.orion_end_profiling(path.encode())
@@ -317,163 +398,214 @@ def run_kx(args):
             with open(path) as f:
                 recs = json.load(f).get("kernels", [])
             os.unlink(path)
-        return res, recs
+        return out, recs
 
-    # phase 1: HP alone (per-op timing for the solo roofline)
-    barrier()
-    # latency phases run at least 200 HP steps so that p99 is a percentile
-    lat_steps = max(args.steps, 200)
-    (hp_solo, _), solo_recs = profiled("hp_solo", lambda on_start: harness.run_clients(
-        orion, hp_step, be_step, lat_steps, args.warmup, with_be=False, on_start=on_start))
-    # phase 2: BE alone
-    _, be_solo = harness.run_clients(orion, hp_step, be_step, 0, 0, with_hp=False,
-                                     be_seconds=args.be_seconds)
-    # phase 3 (timed): HP + BE, per-op timing, clocks, launch count
-    clocks = Clocks(local)
-    barrier()
-    launches0 = kxlib.kx_launch_count()
-    clocks.start()
-    (hp_c, be_c), cont_recs = profiled("contended", lambda on_start: harness.run_clients(
-        orion, hp_step, be_step, args.steps, args.warmup, on_start=on_start))
-    clk = clocks.stop()
-    launches = kxlib.kx_launch_count() - launches0
-    barrier()
-    # phase 4: paced HP (requests every solo_p50 / hp_load ms) against BE, the
-    # Orion setting in which HP latency vs solo and BE retention are judged
-    s50_now = harness.percentile(hp_solo.latencies_ms, 0.5)
-    period = s50_now / max(args.hp_load, 1e-3)
-    paced_steps = lat_steps
-    for c in (0, 1):
+    for c in range(n_clients):
         orion.waits(c, reset=True)
-    if args.trace:
-        orion.orion_trace_start()
-    hp_p, be_p = harness.run_clients(orion, hp_step, be_step, paced_steps, args.warmup,
-                                     hp_period_ms=period)
-    if args.trace:
-        harness.write_trace(orion, args.trace)
-    paced_waits = {("hp", "be")[c]: orion.waits(c) for c in (0, 1)}
-    # phase 5: e2e (host buffers in every HP step), contended, over as many
-    # steps as the latency phases so that one host-side stall on one rank does
-    # not stand for the whole run
-    hp_e2e = None
-    e2e_steps = lat_steps
-    if not args.no_e2e:
-        hp_e2e, _ = harness.run_clients(orion, hp_step_e2e, be_step, e2e_steps, args.warmup)
-    stats = {c: orion.stats(c) for c in (0, 1)}
+    kr = run_phases(harness, orion, hp, bes, args, lat_steps, args.steps, e2e=not args.no_e2e,
+                    profiled=profiled, clocks=Clocks(local), kxlib=kxlib, ranks=ranks)
+    waits = {c: orion.waits(c) for c in range(n_clients)}
+    stats = {c: orion.stats(c) for c in range(n_clients)}
     orion.orion_set_capture(0)
     orion.orion_stop_scheduler()
 
     peaks, peak_src = measured_peaks()
     tf32 = measure_tf32_peak(dev)  # capture is off: this runs cuBLAS itself
-    roof = roofline(cont_recs, peaks, peak_src, tf32, sustained=True)
-    roof_solo = roofline(solo_recs, peaks, peak_src, tf32, sustained=False)
+    roof = roofline(kr["cont_recs"], peaks, peak_src, tf32, sustained=True, cfg=args.config)
+    roof_solo = roofline(kr["solo_recs"], peaks, peak_src, tf32, sustained=False,
+                         cfg=args.config)
 
     # ---- aggregate over ranks
-    hp_ms = hp_c.elapsed_ms
-    imgs = HP_BATCH * args.steps
-    e2e_ms = hp_e2e.elapsed_ms if hp_e2e else 0.0
-    per_rank = [[hp_ms, e2e_ms]]
-    if pg is not None:
-        t = torch.tensor([hp_ms, e2e_ms], device=dev)
-        parts = [torch.zeros_like(t) for _ in range(world)]
-        pg.all_gather(parts, t)
-        per_rank = [[float(v) for v in x.tolist()] for x in parts]
-        hp_ms = max(r[0] for r in per_rank)
-        e2e_ms = max(r[1] for r in per_rank)
-    value = world * imgs / (hp_ms / 1e3)
-    p50 = harness.percentile(hp_c.latencies_ms, 0.5)
-    p99 = harness.percentile(hp_c.latencies_ms, 0.99)
-    s50 = harness.percentile(hp_solo.latencies_ms, 0.5)
-    s99 = harness.percentile(hp_solo.latencies_ms, 0.99)
-    be_solo_ips = be_solo.iters / (be_solo.elapsed_ms / 1e3) if be_solo.elapsed_ms else 0.0
-    be_c_ips = be_c.iters / (be_c.elapsed_ms / 1e3) if be_c.elapsed_ms else 0.0
-    # HP latency against its own solo run, per rank: the line's hp / paced
-    # blocks are rank 0's; at N > 1 the worst rank's ratios are added
-    pp99 = harness.percentile(hp_p.latencies_ms, 0.99)
-    be_p_ips = be_p.iters / (be_p.elapsed_ms / 1e3) if be_p.elapsed_ms else 0.0
-    ratios = [p99 / s99 if s99 else 0.0, pp99 / s99 if s99 else 0.0,
-              be_p_ips / be_solo_ips if be_solo_ips else 0.0]
-    rank_ratios = [ratios]
-    if pg is not None:
-        t = torch.tensor(ratios, device=dev, dtype=torch.float64)
-        parts = [torch.zeros_like(t) for _ in range(world)]
-        pg.all_gather(parts, t)
-        rank_ratios = [[float(v) for v in x.tolist()] for x in parts]
+    hp_ms = kr["hp_cont"].elapsed_ms
+    e2e_ms = kr["hp_e2e"].elapsed_ms if kr["hp_e2e"] else 0.0
+    hp_block = latency_block(harness, kr["hp_solo"], kr["hp_cont"], kr["hp_paced"], hp.units,
+                             kr["period"])
+    be = be_block(bes, kr["be_solo"], kr["be_cont"], kr["be_paced"])
+    mine = [hp_ms, e2e_ms, hp_block["p99_vs_solo"] or 0.0,
+            hp_block["paced"]["p99_vs_solo"] or 0.0,
+            min((b["paced_retention"] or 0.0) for b in be) if be else 0.0,
+            min((b["retention"] or 0.0) for b in be) if be else 0.0]
+    per_rank = ranks.gather(mine)
+    hp_ms = max(r[0] for r in per_rank)
+    e2e_ms = max(r[1] for r in per_rank)
+    value = world * hp.units * args.steps / (hp_ms / 1e3)
 
     cpu = None
-    if rank == 0:
-        v, cores = oracle_vgg16_images_per_s(1, threads=os.cpu_count())
-        cpu = {"value": round(v, 4), "unit": "images/s", "cores": cores, "kind": "port",
-               "sample": "1 image of the batch-32 VGG16 forward (oracle conv + GEMM "
-                         "restatement, float64 accumulation)"}
-        tv, tcores = torch_cpu_vgg16_images_per_s(2)
-        cpu["torch_cpu_forward"] = {"value": round(tv, 4), "unit": "images/s",
-                                    "cores": tcores, "sample": "2 images, torch fp32 CPU"}
-    if pg is not None:
-        pg.barrier()
-        pg.destroy_process_group()
+    if rank == 0 and world == 1:
+        v, unit, used, what, dt = configs.cpu_forward_rate(
+            args.config if args.config != 3 else 1, os.cpu_count(), sample=1)
+        cpu = {"value": round(v, 4), "unit": f"{unit}/s", "cores": used, "kind": "port",
+               "sample": f"{what}: the HP model's PyTorch CPU forward ({dt}), no interception"}
+    ranks.close()
     if rank != 0:
         return 0
+    be_totals = {}
+    for b, c in zip(be, bes):
+        be_totals[f"{c.unit}_per_s"] = be_totals.get(f"{c.unit}_per_s", 0.0) + \
+            b[f"{c.unit}_per_s"] * world
+        be_totals[f"paced_{c.unit}_per_s"] = be_totals.get(f"paced_{c.unit}_per_s", 0.0) + \
+            b[f"paced_{c.unit}_per_s"] * world
     line = {
-        "metric": METRIC, "value": round(value, 3), "unit": "images/s", "n_gpus": world,
+        "metric": METRIC, "value": round(value, 3), "unit": f"{hp.unit}/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(hp_ms / args.steps, 3),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": hp.dtype,
         "data": "synthetic",
-        "config": {"workload": "HP VGG16 inference fp32 b32 3x224x224 + BE GPT (6L, d512, "
-                               "8 heads, vocab 32000) training fp32 b16 s256 AdamW, through "
-                               "the LD_PRELOAD interposer",
-                   "hp_batch": HP_BATCH, "be_batch": BE_BATCH, "be_seq": BE_SEQ,
-                   "parallelism": f"placement x{world} (one HP+BE group per GPU, no collective)",
-                   "l2": "inputs larger than L2 (VGG16 first-block activations 411 MB)",
+        "config": {"workload": configs.DESCRIPTIONS[args.config] + ", through the LD_PRELOAD "
+                               "interposer", "config": args.config,
+                   "hp": hp.name, "be": [c.name for c in bes],
+                   "parallelism": f"placement x{world} (one client group per GPU, no collective)",
+                   "l2": "inputs larger than L2 between HP steps (activations of one step "
+                         "exceed 126 MB)",
                    "gil_switch_ms": round(sys.getswitchinterval() * 1e3, 3),
                    "gc_frozen": bool(args.gc_freeze)},
-        "hp": {"p50_ms": round(p50, 3), "p99_ms": round(p99, 3), "solo_p50_ms": round(s50, 3),
-               "solo_p99_ms": round(s99, 3), "p99_vs_solo": round(p99 / s99, 4) if s99 else None,
-               "steps": args.steps, "solo_steps": lat_steps},
-        "paced": {"hp_load": round(args.hp_load, 3), "period_ms": round(period, 3),
-                  "hp_steps": paced_steps,
-                  "hp_p50_ms": round(harness.percentile(hp_p.latencies_ms, 0.5), 3),
-                  "hp_p99_ms": round(harness.percentile(hp_p.latencies_ms, 0.99), 3),
-                  "hp_p99_vs_solo": round(harness.percentile(hp_p.latencies_ms, 0.99) / s99, 4)
-                  if s99 else None,
-                  "hp_issue_p50_ms": round(harness.percentile(hp_p.issue_ms, 0.5), 3),
-                  "hp_issue_p99_ms": round(harness.percentile(hp_p.issue_ms, 0.99), 3),
-                  "be_iters_per_s": round(be_p.iters / (be_p.elapsed_ms / 1e3), 3)
-                  if be_p.elapsed_ms else None,
-                  "be_retention": round(be_p.iters / (be_p.elapsed_ms / 1e3) / be_solo_ips, 4)
-                  if be_p.elapsed_ms and be_solo_ips else None,
-                  "client_waits": {k: {kk: round(vv, 3) if isinstance(vv, float) else vv
-                                       for kk, vv in w.items()}
-                                   for k, w in paced_waits.items()}},
-        "be": {"iters_per_s": round(be_c_ips, 3), "solo_iters_per_s": round(be_solo_ips, 3),
-               "retention": round(be_c_ips / be_solo_ips, 4) if be_solo_ips else None,
-               "tokens_per_s": round(be_c_ips * BE_BATCH * BE_SEQ, 1)},
-        "roofline": roof, "roofline_hp_solo": roof_solo, "ops": op_table(cont_recs),
-        "cpu_baseline": cpu, "clocks": clk, "gpu_launches": int(launches),
+        "hp": hp_block,
+        "be": be, "be_total": {k: round(v, 1) for k, v in be_totals.items()},
+        "roofline": roof, "roofline_hp_solo": roof_solo, "ops": op_table(kr["cont_recs"]),
+        "cpu_baseline": cpu, "clocks": kr["clocks"], "gpu_launches": int(kr["launches"]),
         "captured": stats,
+        "client_waits": {str(c): {k: rnd(v) if isinstance(v, float) else v for k, v in w.items()}
+                         for c, w in waits.items()},
+        "library": lib,
     }
+    if lib is not None:
+        line["library"]["vs_kx"] = {
+            "hp_ms_per_step_lib_over_kx": rnd(lib["ms_per_step"] / (hp_ms / args.steps), 4)}
     if world > 1:
         line["ms_per_step_per_rank"] = [round(r[0] / args.steps, 3) for r in per_rank]
-        line["worst_rank"] = {
-            "hp_p99_vs_solo": round(max(r[0] for r in rank_ratios), 4),
-            "paced_hp_p99_vs_solo": round(max(r[1] for r in rank_ratios), 4),
-            "paced_be_retention": round(min(r[2] for r in rank_ratios), 4)}
+        line["worst_rank"] = {"hp_p99_vs_solo": rnd(max(r[2] for r in per_rank), 4),
+                              "paced_hp_p99_vs_solo": rnd(max(r[3] for r in per_rank), 4),
+                              "paced_be_retention": rnd(min(r[4] for r in per_rank), 4),
+                              "be_retention": rnd(min(r[5] for r in per_rank), 4)}
     if e2e_ms:
-        h2d = HP_BATCH * 3 * 224 * 224 * 4
-        d2h = HP_BATCH * 1000 * 4
-        line["e2e"] = {"value": round(world * HP_BATCH * e2e_steps / (e2e_ms / 1e3), 3),
-                       "unit": "images/s", "steps": e2e_steps,
-                       "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+        steps = kr["hp_e2e"].iters
+        line["e2e"] = {"value": round(world * hp.units * steps / (e2e_ms / 1e3), 3),
+                       "unit": f"{hp.unit}/s", "steps": steps,
+                       "h2d_bytes_per_step": hp.h2d_bytes, "d2h_bytes_per_step": hp.d2h_bytes}
         if world > 1:
-            line["e2e"]["ms_per_step_per_rank"] = [round(r[1] / e2e_steps, 3) for r in per_rank]
+            line["e2e"]["ms_per_step_per_rank"] = [round(r[1] / steps, 3) for r in per_rank]
     print(json.dumps(line), flush=True)
     return 0
 
 
+# ----------------------------------------------------- GEMM microbench ----
+
+def run_microbench(args):
+    """Configuration 3: HP GEMMs M x N=K (M in 64/128/256, N=K in
+    1024/4096; one every 200 us, cycling through the shapes) against
+    back-to-back 8192^3 BE GEMMs, in fp32 and in bf16, with the BE SM quota
+    at 16, 32, 64 and all SMs.  Quotas below the SM count are disjoint
+    budgets (HP gets the rest); at all SMs BE is not throttled.  Reports HP op
+    latency p50 / p99 (CUDA events per op on the HP stream) and BE TFLOP/s per
+    quota, solo and contended."""
+    import torch
+
+    if args.gil_switch_ms > 0:
+        sys.setswitchinterval(args.gil_switch_ms / 1e3)
+    from kernel_intercept_b200 import harness, kx
+    rank, world, local = dist_info()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    ranks = Ranks(world, dev)
+    orion = harness.Orion()
+    torch.backends.cuda.matmul.allow_tf32 = False
+    g = torch.Generator(device=dev).manual_seed(0)
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    quotas = [16, 32, 64, sms]
+    hp_ops = max(400, args.lat_steps * 5)
+    out = {}
+    assert orion.orion_init_scheduler(2) == 0
+    orion.orion_set_capture(0)
+    orion.orion_start_scheduler_thread()
+    kxlib = kx.lib()
+    launches = 0
+    clocks = Clocks(local)
+    clk = None
+    for dtype_name, dtype in (("f32", torch.float32), ("bf16", torch.bfloat16)):
+        shapes = [(m, nk) for m in (64, 128, 256) for nk in (1024, 4096)]
+        hp_in = [(torch.randn(m, nk, device=dev, generator=g).to(dtype),
+                  torch.randn(nk, nk, device=dev, generator=g).to(dtype)) for m, nk in shapes]
+        A = torch.randn(8192, 8192, device=dev, generator=g).to(dtype)
+        B = torch.randn(8192, 8192, device=dev, generator=g).to(dtype)
+        C = torch.empty(8192, 8192, device=dev, dtype=dtype)
+        i_hp = [0]
+
+        def hp_step():
+            a, b = hp_in[i_hp[0] % len(hp_in)]
+            i_hp[0] += 1
+            torch.matmul(a, b)
+
+        def be_step():
+            torch.matmul(A, B, out=C)
+
+        for step in (hp_step, be_step):  # library warm-up, capture off
+            step()
+        torch.cuda.synchronize()
+        orion.orion_set_capture(1)
+        rows = []
+        solo, _ = harness.run_clients(orion, hp_step, be_step, hp_ops, args.warmup,
+                                      with_be=False, hp_period_ms=0.2)
+        for q in quotas:
+            if q < sms:
+                orion.orion_set_sm_budgets(sms - q, q)
+            else:
+                orion.orion_set_sm_budgets(0, 0)
+                orion.orion_set_be_keep_sms(sms)
+            ranks.barrier()
+            _, be_solo = harness.run_clients(orion, hp_step, be_step, 0, 0, with_hp=False,
+                                             be_seconds=min(args.be_seconds, 1.5))
+            l0 = kxlib.kx_launch_count()
+            if dtype_name == "bf16" and q == sms:
+                clocks.start()
+            hp_c, be_c = harness.run_clients(orion, hp_step, be_step, hp_ops, args.warmup,
+                                             hp_period_ms=0.2)
+            if dtype_name == "bf16" and q == sms:
+                clk = clocks.stop()
+            launches += kxlib.kx_launch_count() - l0
+            tf = 2 * 8192 ** 3 / 1e12
+            s99 = harness.percentile(solo.latencies_ms, 0.99)
+            rows.append({
+                "be_quota_sms": q,
+                "hp_op_p50_us": rnd(harness.percentile(hp_c.latencies_ms, 0.5) * 1e3, 1),
+                "hp_op_p99_us": rnd(harness.percentile(hp_c.latencies_ms, 0.99) * 1e3, 1),
+                "hp_op_p99_vs_solo": rnd(harness.percentile(hp_c.latencies_ms, 0.99) / s99, 4),
+                "be_tflops": rnd(be_c.iters * tf / (be_c.elapsed_ms / 1e3), 1),
+                "be_solo_tflops": rnd(be_solo.iters * tf / (be_solo.elapsed_ms / 1e3), 1),
+                "be_retention": rnd((be_c.iters / be_c.elapsed_ms) /
+                                    (be_solo.iters / be_solo.elapsed_ms), 4),
+                "hp_ops": hp_c.iters})
+        orion.orion_set_sm_budgets(0, 0)
+        orion.orion_set_be_keep_sms(8)
+        orion.orion_set_capture(0)
+        out[dtype_name] = {"hp_solo_op_p50_us": rnd(harness.percentile(solo.latencies_ms, 0.5) * 1e3, 1),
+                           "hp_solo_op_p99_us": rnd(harness.percentile(solo.latencies_ms, 0.99) * 1e3, 1),
+                           "quotas": rows}
+        del A, B, C, hp_in
+        torch.cuda.empty_cache()
+    stats = orion.stats(0), orion.stats(1)
+    orion.orion_stop_scheduler()
+    ranks.close()
+    if rank != 0:
+        return 0
+    top = out["bf16"]["quotas"][-1]
+    line = {
+        "metric": METRIC, "value": top["be_tflops"], "unit": "TFLOP/s", "n_gpus": world,
+        "steps": hp_ops, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16+f32", "data": "synthetic",
+        "config": {"workload": "GEMM contention microbench (value: bf16 BE TFLOP/s with HP "
+                               "GEMMs every 200 us, BE unthrottled)", "config": 3},
+        "sweep": out, "clocks": clk, "gpu_launches": int(launches),
+        "captured": {"hp": stats[0], "be": stats[1]},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ------------------------------------------------------------- helpers -----
+
 def group_ops(recs):
     by_op = {}
     for r in recs:
-        key = ("HP" if r.get("client") == 0 else "BE", r.get("op_type", "?"))
+        key = ("HP" if r.get("client") == 0 else f"BE{r.get('client')}", r.get("op_type", "?"))
         agg = by_op.setdefault(key, {"n": 0, "ms": 0.0, "work": 0.0, "kernels": {}})
         agg["n"] += 1
         agg["ms"] += float(r["duration_ms"])
@@ -486,25 +618,25 @@ def group_ops(recs):
 def op_table(recs):
     out = {}
     for (client, op), v in sorted(group_ops(recs).items()):
-        rate = v["work"] / (v["ms"] * 1e-3) / 1e12 if v["ms"] > 0 else None
+        r = v["work"] / (v["ms"] * 1e-3) / 1e12 if v["ms"] > 0 else None
         out[f"{client}:{op}"] = {"launches": v["n"], "ms": round(v["ms"], 3),
-                                 "rate": round(rate, 2) if rate is not None else None,
+                                 "rate": round(r, 2) if r is not None else None,
                                  "rate_unit": "TB/s" if "BATCHNORM" in op else "TFLOP/s"}
     return out
 
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the
-# dominant op class, from one ncu capture of a batch-32 VGG16 HP step: the mean
-# over its 13 convolution launches (profiles/vgg16_hp_step_launches.md).
-NCU_TRAFFIC_PER_LAUNCH = {"HP:CUDNN_CONV_FWD": 324059668}
+# dominant HP op class, from one ncu capture (files under profiles/): the mean
+# over the captured launches of that class.
+NCU_TRAFFIC_PER_LAUNCH = {(1, "HP:CUDNN_CONV_FWD"): 324059668}
 
 
-def roofline(recs, peaks, peak_src, tf32, sustained):
+def roofline(recs, peaks, peak_src, tf32, sustained, cfg):
     """Dominant captured op class of the HP client in a profiled phase (the
-    client `value` measures; BE ops are throttled to the SMs HP leaves them,
-    so their rate measures the scheduler, not the kernel): algorithmic FLOPs
-    per launch (2mnk per GEMM, 2*N*K*C*R*S*P*Q per convolution) over the mean
-    launch duration (CUDA events on the worker's dispatch stream)."""
+    client `value` measures; BE ops run on the SMs HP leaves them, so their
+    rate measures the scheduler, not the kernel): algorithmic FLOPs per launch
+    (2mnk per GEMM, 2*N*K*C*R*S*P*Q per convolution) over the mean launch
+    duration (CUDA events on the worker's dispatch stream)."""
     by_op = group_ops(recs)
     dense = {k: v for k, v in by_op.items()
              if k[0] == "HP" and "BATCHNORM" not in k[1] and v["work"] > 0}
@@ -515,20 +647,20 @@ def roofline(recs, peaks, peak_src, tf32, sustained):
     achieved = agg["work"] / agg["n"] / (avg_ms * 1e-3) / 1e12
     key = "bf16_tflops_sustained" if sustained else "bf16_tflops"
     peak = float(peaks.get(key, peaks.get("bf16_tflops")))
-    # fp32 runs as 3xTF32 (three TF32 products per MAC): its ceiling is the TF32 rate / 3
-    ceiling = tf32 / 3.0
     top = max(agg["kernels"].items(), key=lambda kv: kv[1])[0]
-    return {"bound": "tensor", "achieved": round(achieved, 2), "peak": round(peak, 1),
-            "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
-            "traffic": NCU_TRAFFIC_PER_LAUNCH.get(f"{client}:{op}"),
-            "peak_source": f"{key} of {peak_src}",
-            "tf32_cublas_tflops": round(tf32, 1),
-            "fp32_3xtf32_ceiling": round(ceiling, 1),
-            "frac_of_3xtf32_ceiling": round(achieved / ceiling, 4),
-            "ffma_ceiling": round(peaks.get("sm_max_mhz", 1965.0) * 148 * 256 / 1e6, 1),
-            "op": f"{client}:{op}", "kernel": top, "launches": agg["n"],
-            "avg_ms": round(avg_ms, 4), "share_of_captured_ms":
-            round(agg["ms"] / sum(v["ms"] for v in by_op.values()), 4)}
+    out = {"bound": "tensor", "achieved": round(achieved, 2), "peak": round(peak, 1),
+           "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+           "traffic": NCU_TRAFFIC_PER_LAUNCH.get((cfg, f"{client}:{op}")),
+           "peak_source": f"{key} of {peak_src}",
+           "op": f"{client}:{op}", "kernel": top, "launches": agg["n"],
+           "avg_ms": round(avg_ms, 4), "share_of_captured_ms":
+           round(agg["ms"] / sum(v["ms"] for v in by_op.values()), 4)}
+    if "bf16" not in top and "f16" not in top:
+        # fp32 runs as 3xTF32 (three TF32 products per MAC): its ceiling is the TF32 rate / 3
+        ceiling = tf32 / 3.0
+        out.update({"tf32_cublas_tflops": round(tf32, 1), "fp32_3xtf32_ceiling": round(ceiling, 1),
+                    "frac_of_3xtf32_ceiling": round(achieved / ceiling, 4)})
+    return out
 
 
 def measure_tf32_peak(dev):
@@ -555,22 +687,6 @@ def measure_tf32_peak(dev):
     return 2 * 8192 ** 3 / (best * 1e-3) / 1e12
 
 
-def torch_cpu_vgg16_images_per_s(sample_images=2):
-    """The reference's CPU-runnable form: the same VGG16 as plain PyTorch on
-    the host cores (no interception), fp32."""
-    import torch
-
-    from kernel_intercept_b200 import harness
-    m = harness.make_vgg16("cpu").eval()
-    x = torch.randn(sample_images, 3, 224, 224)
-    with torch.no_grad():
-        m(x[:1])
-        t0 = time.perf_counter()
-        m(x)
-        dt = time.perf_counter() - t0
-    return sample_images / dt, torch.get_num_threads()
-
-
 def main():
     args = parse()
     if args.impl == "reference":
@@ -579,7 +695,9 @@ def main():
     if not harness.preloaded():
         env = harness.preload_env({"ORION_LOG_LEVEL": os.environ.get("ORION_LOG_LEVEL", "WARN")})
         os.execve(sys.executable, [sys.executable] + sys.argv, env)
-    return run_kx(args)
+    if args.config == 3:
+        return run_microbench(args)
+    return run_group(args)
 
 
 if __name__ == "__main__":

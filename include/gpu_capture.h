@@ -272,6 +272,16 @@ struct OperationRecord {
 
     std::atomic<bool> completed{false};
     std::atomic<bool> started{false};
+    /** Life cycle: kQueued -> kClaimed (the worker took it and will run it)
+     *  or kQueued -> kCancelled (the client gave up waiting first; the
+     *  worker then skips it).  Exactly one of the two transitions wins. */
+    enum : int { kQueued = 0, kClaimed = 1, kCancelled = 2 };
+    std::atomic<int> state{kQueued};
+    /** True when running the record later touches nothing the issuing
+     *  thread owns (its arguments were copied into the record): the client
+     *  may stop waiting for it even after the worker claimed it. */
+    bool detachable{false};
+    /** Written by the worker only, before `completed` is released. */
     cudaError_t result{cudaSuccess};
     void* result_ptr{nullptr};
     int64_t enqueue_ns{0};
@@ -286,8 +296,24 @@ struct OperationRecord {
     OperationRecord(OperationRecord&&) = delete;
     OperationRecord& operator=(OperationRecord&&) = delete;
 
-    /** Waits for the worker; gives up after wait_timeout_ns() with cudaErrorTimeout. */
-    void wait_completion();
+    /** Waits for the worker and returns the op's result.  After
+     *  wait_timeout_ns() a record the worker has not claimed is cancelled
+     *  (it never runs) and cudaErrorTimeout is returned; a detachable
+     *  record is abandoned the same way; any other claimed record is
+     *  running on the worker and is waited for to the end, because it still
+     *  reads or writes memory of the issuing thread. */
+    cudaError_t wait_completion();
+
+    /** Worker side: claims a queued record; false when it was cancelled. */
+    bool claim() {
+        int expect = kQueued;
+        return state.compare_exchange_strong(expect, kClaimed, std::memory_order_acq_rel);
+    }
+    /** Client side: cancels a record the worker has not claimed. */
+    bool cancel() {
+        int expect = kQueued;
+        return state.compare_exchange_strong(expect, kCancelled, std::memory_order_acq_rel);
+    }
 
     void mark_completed(cudaError_t res) {
         result = res;
@@ -308,8 +334,9 @@ public:
     ClientQueue();
     ~ClientQueue();
 
-    /** Enqueue; spins (yielding) while the ring is full. */
-    void push(OperationPtr op);
+    /** Enqueue; spins (yielding) while the ring is full, for at most
+     *  wait_timeout_ns(); false when the ring stayed full that long. */
+    bool push(OperationPtr op);
     /** Non-blocking enqueue; false when full. */
     bool try_push(OperationPtr op);
     /** Dequeue or nullptr when empty. */
@@ -355,8 +382,13 @@ int get_current_client_idx();
 void set_current_client_idx(int idx);
 
 OperationPtr create_operation(int client_idx, OperationType type);
-void enqueue_operation(OperationPtr op);
-void wait_operation(OperationPtr op);
+/** Queues the record for its client's worker.  False when the queue stayed
+ *  full for wait_timeout_ns(): the record is then completed with
+ *  cudaErrorTimeout, never runs, and the client's error latch is set. */
+bool enqueue_operation(OperationPtr op);
+/** Bounded wait for the worker (see OperationRecord::wait_completion);
+ *  returns the op's result, cudaErrorTimeout when the client gave up. */
+cudaError_t wait_operation(OperationPtr op);
 
 /** create + enqueue in one step (the record must be filled before the
  *  worker can see it: callers fill params on the returned record only when

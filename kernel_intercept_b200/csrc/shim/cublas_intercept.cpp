@@ -184,10 +184,9 @@ cublasStatus_t submit_gemm(OperationType type, CublasGemmParams p, bool supporte
     stored.alpha = &stored.alpha_value;
     stored.beta = &stored.beta_value;
   }
-  enqueue_operation(op);
+  if (!enqueue_operation(op)) return kStatusExecFailed;
   if (get_async_mode_internal() == 1) return kStatusOk;
-  wait_operation(op);
-  return op->result == cudaSuccess ? kStatusOk : kStatusExecFailed;
+  return wait_operation(op) == cudaSuccess ? kStatusOk : kStatusExecFailed;
 }
 
 }  // namespace
@@ -611,8 +610,7 @@ extern "C" cublasStatus_t cublasLtMatmul(void* lightHandle, void* computeDesc, c
   auto op = orion::create_operation(client, orion::OperationType::CUBLASLT_MATMUL);
   if (!op) return call_real();
   op->params = p;
-  orion::enqueue_operation(op);
+  if (!orion::enqueue_operation(op)) return kStatusExecFailed;
   if (orion::get_async_mode_internal() == 1) return kStatusOk;
-  orion::wait_operation(op);
-  return op->result == cudaSuccess ? kStatusOk : kStatusExecFailed;
+  return orion::wait_operation(op) == cudaSuccess ? kStatusOk : kStatusExecFailed;
 }

@@ -118,11 +118,16 @@ struct OwnedConfig {
   std::vector<cudaLaunchAttribute> attrs;
 };
 
+// Queues a captured runtime call.  must_wait: the record refers to memory of
+// the calling thread (launch arguments on its stack, an out-pointer, a host
+// buffer), so the call returns only once the worker ran it; otherwise, in
+// async mode, at once.  A record whose arguments were copied is detachable: a
+// timed-out client may stop waiting for it even while it runs.
 cudaError_t run_captured(OperationPtr op, bool must_wait) {
-  enqueue_operation(op);
+  op->detachable = !must_wait;
+  if (!enqueue_operation(op)) return cudaErrorTimeout;
   if (!must_wait && get_async_mode_internal() == 1) return cudaSuccess;
-  wait_operation(op);
-  return op->result;
+  return wait_operation(op);
 }
 
 }  // namespace

@@ -179,10 +179,9 @@ cudnnStatus_t submit_op(OperationType type, void* handle, Params p, bool support
   auto op = create_operation(client, type);
   if (!op) return real();
   op->params = p;  // filled before the worker can see it
-  enqueue_operation(op);
+  if (!enqueue_operation(op)) return kExecFailed;
   if (get_async_mode_internal() == 1) return kOk;
-  wait_operation(op);
-  return op->result == cudaSuccess ? kOk : kExecFailed;
+  return wait_operation(op) == cudaSuccess ? kOk : kExecFailed;
 }
 
 float scalar(const void* p, float dflt) { return p ? *static_cast<const float*>(p) : dflt; }

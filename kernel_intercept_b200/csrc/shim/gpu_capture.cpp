@@ -54,21 +54,33 @@ int64_t wait_timeout_ns() {
   return t;
 }
 
-void OperationRecord::wait_completion() {
-  if (completed.load(std::memory_order_acquire)) return;
-  const int64_t deadline = now_ns() + wait_timeout_ns();
+cudaError_t OperationRecord::wait_completion() {
+  if (completed.load(std::memory_order_acquire)) return result;
+  int64_t deadline = now_ns() + wait_timeout_ns();
   uint32_t spins = 0;
   while (!completed.load(std::memory_order_acquire)) {
     if (++spins > 2048) {
       std::this_thread::yield();
       if ((spins & 1023) == 0 && now_ns() > deadline) {
-        LOG_ERROR("op %lu (%s) not completed within %lld ms; giving up", (unsigned long)op_id,
+        if (cancel()) {
+          LOG_ERROR("op %lu (%s) not started within %lld ms; cancelled", (unsigned long)op_id,
+                    op_type_name(type), (long long)(wait_timeout_ns() / 1000000));
+          return cudaErrorTimeout;
+        }
+        if (detachable) {
+          LOG_ERROR("op %lu (%s) not completed within %lld ms; no longer waited for",
+                    (unsigned long)op_id, op_type_name(type),
+                    (long long)(wait_timeout_ns() / 1000000));
+          return cudaErrorTimeout;
+        }
+        // running on the worker with the caller's memory: wait it out
+        LOG_ERROR("op %lu (%s) still running after %lld ms; waiting for it", (unsigned long)op_id,
                   op_type_name(type), (long long)(wait_timeout_ns() / 1000000));
-        result = cudaErrorTimeout;
-        return;
+        deadline = now_ns() + wait_timeout_ns();
       }
     }
   }
+  return result;
 }
 
 // ---------------------------------------------------------------- queue ----
@@ -99,8 +111,14 @@ bool ClientQueue::try_push(OperationPtr op) {
   }
 }
 
-void ClientQueue::push(OperationPtr op) {
-  while (!try_push(op)) std::this_thread::yield();
+bool ClientQueue::push(OperationPtr op) {
+  if (try_push(op)) return true;
+  const int64_t deadline = now_ns() + wait_timeout_ns();
+  while (!try_push(op)) {
+    if (now_ns() > deadline) return false;
+    std::this_thread::yield();
+  }
+  return true;
 }
 
 OperationPtr ClientQueue::try_pop() {
@@ -263,9 +281,16 @@ OperationPtr create_operation(int client_idx, OperationType type) {
   return op;
 }
 
-void enqueue_operation(OperationPtr op) {
-  if (!op) return;
-  g_capture_state.client_queues[op->client_idx]->push(std::move(op));
+bool enqueue_operation(OperationPtr op) {
+  if (!op) return false;
+  if (g_capture_state.client_queues[op->client_idx]->push(op)) return true;
+  LOG_ERROR("client %d: queue full for %lld ms; op %lu (%s) dropped", op->client_idx,
+            (long long)(wait_timeout_ns() / 1000000), (unsigned long)op->op_id,
+            op_type_name(op->type));
+  op->state.store(OperationRecord::kCancelled, std::memory_order_release);
+  op->mark_completed(cudaErrorTimeout);
+  set_last_error(op->client_idx, cudaErrorTimeout);
+  return false;
 }
 
 namespace {
@@ -284,15 +309,15 @@ unsigned long long op_bytes(const OperationRecord& op) {
 WaitStats g_wait_stats[MAX_CLIENTS];
 }  // namespace
 
-void wait_operation(OperationPtr op) {
-  if (!op) return;
-  if (op->completed.load(std::memory_order_acquire)) return;
+cudaError_t wait_operation(OperationPtr op) {
+  if (!op) return cudaErrorInvalidValue;
+  if (op->completed.load(std::memory_order_acquire)) return op->result;
   const int64_t t0 = now_ns();
-  op->wait_completion();
+  const cudaError_t res = op->wait_completion();
   const int64_t t1 = now_ns();
   if (trace_enabled()) trace_client_wait(*op, t0, t1);
   const unsigned long long dt = static_cast<unsigned long long>(t1 - t0);
-  if (op->client_idx < 0 || op->client_idx >= MAX_CLIENTS) return;
+  if (op->client_idx < 0 || op->client_idx >= MAX_CLIENTS) return res;
   WaitStats& w = g_wait_stats[op->client_idx];
   w.count.fetch_add(1, std::memory_order_relaxed);
   w.total_ns.fetch_add(dt, std::memory_order_relaxed);
@@ -310,6 +335,7 @@ void wait_operation(OperationPtr op) {
     w.max_desc[3] = op_bytes(*op);
     w.max_desc[4] = 0;
   }
+  return res;
 }
 
 void get_wait_stats(int client_idx, unsigned long long* out8, bool reset) {

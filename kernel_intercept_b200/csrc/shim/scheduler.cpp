@@ -489,6 +489,11 @@ void Scheduler::run_worker(int client_idx) {
     }
     op = q->try_pop();
     if (!op) continue;
+    if (!op->claim()) {
+      // the client gave up waiting before the op started: it must not run
+      op->mark_completed(cudaErrorTimeout);
+      continue;
+    }
     op->start_ns = mono_ns();
     cudaError_t err = execute_operation(op, fallback);
     op->end_ns = mono_ns();
@@ -509,6 +514,10 @@ void Scheduler::run_worker(int client_idx) {
   }
   // drain what is left so no client waits forever
   while (OperationPtr op = q->try_pop()) {
+    if (!op->claim()) {
+      op->mark_completed(cudaErrorTimeout);
+      continue;
+    }
     cudaError_t err = execute_operation(op, fallback);
     op->mark_completed(err);
   }

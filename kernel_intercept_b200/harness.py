@@ -318,19 +318,26 @@ def run_clients(orion: Orion | None, hp_step, be_step, hp_steps: int, hp_warmup:
                 be_seconds: float | None = None, hp_period_ms: float = 0.0,
                 on_start=None):
     """Runs the HP loop (hp_warmup + hp_steps timed iterations, CUDA events per
-    iteration in the HP client's stream order) and, concurrently, the BE loop
-    until HP finishes (or for be_seconds when HP is off).  Client identity:
-    HP = 0, BE = 1, registered on each thread as the reference drivers do.
-    on_start, when given, runs once after both clients finished their warm-up
-    and before either issues a measured step."""
+    iteration in the HP client's stream order) and, concurrently, the BE
+    loop(s) until HP finishes (or for be_seconds when HP is off).  Client
+    identity: HP = 0, BE = 1, 2, ... registered on each thread as the
+    reference drivers do.  be_step is one step function or a list of them
+    (one BE client each); the BE result is returned in the same form.
+    on_start, when given, runs once after every client finished its warm-up
+    and before any issues a measured step."""
     import torch
 
-    hp_res, be_res = ClientResult(), ClientResult()
+    be_steps = list(be_step) if isinstance(be_step, (list, tuple)) else [be_step]
+    if not with_be:
+        be_steps = []
+    hp_res = ClientResult()
+    be_res = [ClientResult() for _ in be_steps]
     # CUDA's current device is per thread and a new thread starts on device 0:
     # the client threads adopt the caller's device before creating streams
     dev = torch.cuda.current_device()
     stop = threading.Event()
-    ready = threading.Barrier(2 if (with_hp and with_be) else 1, action=on_start)
+    parties = (1 if with_hp else 0) + len(be_steps)
+    ready = threading.Barrier(max(1, parties), action=on_start)
 
     def hp_thread():
         try:
@@ -370,21 +377,23 @@ def run_clients(orion: Orion | None, hp_step, be_step, hp_steps: int, hp_warmup:
                 hp_res.iters = hp_steps
         except BaseException as e:  # noqa: BLE001 - reported by the caller
             hp_res.error = e
+            ready.abort()
         finally:
             stop.set()
             if orion is not None:
                 orion.orion_set_client_idx(-1)
 
-    def be_thread():
+    def be_thread(i):
+        res, step, client = be_res[i], be_steps[i], i + 1
         try:
             torch.cuda.set_device(dev)
             s = torch.cuda.Stream(device=dev)
             if orion is not None:
-                orion.orion_set_client_idx(1)
-                orion.orion_register_client_stream(1, ctypes.c_void_p(s.cuda_stream))
+                orion.orion_set_client_idx(client)
+                orion.orion_register_client_stream(client, ctypes.c_void_p(s.cuda_stream))
             with torch.cuda.stream(s):
                 for _ in range(be_warmup):
-                    be_step()
+                    step()
                 s.synchronize()
                 ready.wait()
                 start = torch.cuda.Event(enable_timing=True)
@@ -393,7 +402,7 @@ def run_clients(orion: Orion | None, hp_step, be_step, hp_steps: int, hp_warmup:
                 t0 = time.perf_counter()
                 n = 0
                 while True:
-                    be_step()
+                    step()
                     n += 1
                     if with_hp and stop.is_set():
                         break
@@ -401,10 +410,11 @@ def run_clients(orion: Orion | None, hp_step, be_step, hp_steps: int, hp_warmup:
                         break
                 end.record(s)
                 s.synchronize()
-                be_res.iters = n
-                be_res.elapsed_ms = start.elapsed_time(end)
+                res.iters = n
+                res.elapsed_ms = start.elapsed_time(end)
         except BaseException as e:  # noqa: BLE001
-            be_res.error = e
+            res.error = e
+            ready.abort()
         finally:
             if orion is not None:
                 orion.orion_set_client_idx(-1)
@@ -412,13 +422,18 @@ def run_clients(orion: Orion | None, hp_step, be_step, hp_steps: int, hp_warmup:
     threads = []
     if with_hp:
         threads.append(threading.Thread(target=hp_thread, name="HP-Client"))
-    if with_be:
-        threads.append(threading.Thread(target=be_thread, name="BE1-Client"))
+    for i in range(len(be_steps)):
+        threads.append(threading.Thread(target=be_thread, args=(i,), name=f"BE{i + 1}-Client"))
     for t in threads:
         t.start()
     for t in threads:
         t.join()
-    for r in (hp_res, be_res):
+    for r in [hp_res] + be_res:
+        if r.error is not None and not isinstance(r.error, threading.BrokenBarrierError):
+            raise r.error
+    for r in [hp_res] + be_res:
         if r.error is not None:
             raise r.error
-    return hp_res, be_res
+    if isinstance(be_step, (list, tuple)):
+        return hp_res, be_res
+    return hp_res, (be_res[0] if be_res else ClientResult())

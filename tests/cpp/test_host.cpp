@@ -5,6 +5,7 @@
 // ops are completed by the test itself, 236-276) with real assertions.
 // Built and run by tests/test_host_cpp.py against libgpu_scheduler.so.
 #include <atomic>
+#include <chrono>
 #include <cstdio>
 #include <cstdlib>
 #include <fstream>
@@ -87,8 +88,9 @@ static void test_submit_and_complete() {
   auto got = q->try_pop();
   CHECK(got.get() == op.get());
   CHECK(q->empty());
+  CHECK(got->claim());
   std::thread worker([got] { got->mark_completed(cudaSuccess); });
-  op->wait_completion();
+  CHECK(op->wait_completion() == cudaSuccess);
   worker.join();
   CHECK(op->completed.load());
   CHECK(op->result == cudaSuccess);
@@ -98,13 +100,82 @@ static void test_submit_and_complete() {
   CHECK(b->op_id > a->op_id);
 }
 
+static int64_t ms_since(std::chrono::steady_clock::time_point t0) {
+  return std::chrono::duration_cast<std::chrono::milliseconds>(
+             std::chrono::steady_clock::now() - t0).count();
+}
+
 static void test_bounded_wait() {
-  // ORION_WAIT_TIMEOUT_MS=200 is set by the driver: an op nobody completes
-  // returns cudaErrorTimeout instead of blocking.
+  // ORION_WAIT_TIMEOUT_MS=200 is set by the driver: an op nobody starts is
+  // cancelled after the deadline and reports cudaErrorTimeout.
   auto op = create_operation(0, OperationType::KERNEL_LAUNCH);
-  op->wait_completion();
+  CHECK(op->wait_completion() == cudaErrorTimeout);
   CHECK(!op->completed.load());
-  CHECK(op->result == cudaErrorTimeout);
+  CHECK(op->state.load() == OperationRecord::kCancelled);
+  // a stalled worker that reaches the record later must skip it
+  CHECK(!op->claim());
+}
+
+static void test_timeout_paths_with_stalled_worker() {
+  // 1) queued, the worker stalls: the client cancels it, the worker skips it
+  auto& q = g_capture_state.client_queues[0];
+  while (!q->empty()) q->try_pop();
+  auto op = create_operation(0, OperationType::CUBLAS_SGEMM);
+  CHECK(enqueue_operation(op));
+  auto t0 = std::chrono::steady_clock::now();
+  CHECK(wait_operation(op) == cudaErrorTimeout);
+  CHECK(ms_since(t0) >= 150);
+  auto popped = q->try_pop();
+  CHECK(popped.get() == op.get());
+  CHECK(!popped->claim());  // never executed
+  // 2) claimed by a slow worker, ordinary record (reads the caller's memory):
+  //    the client waits past the deadline until the worker finishes
+  auto slow = create_operation(0, OperationType::MALLOC);
+  CHECK(slow->claim());
+  std::thread w1([slow] {
+    std::this_thread::sleep_for(std::chrono::milliseconds(450));
+    slow->mark_completed(cudaSuccess);
+  });
+  t0 = std::chrono::steady_clock::now();
+  CHECK(slow->wait_completion() == cudaSuccess);
+  CHECK(ms_since(t0) >= 400);
+  w1.join();
+  // 3) claimed, detachable (arguments copied into the record): the client
+  //    stops waiting at the deadline; the worker finishes later on its own
+  auto det = create_operation(0, OperationType::KERNEL_LAUNCH);
+  det->detachable = true;
+  CHECK(det->claim());
+  std::thread w2([det] {
+    std::this_thread::sleep_for(std::chrono::milliseconds(500));
+    det->mark_completed(cudaSuccess);
+  });
+  t0 = std::chrono::steady_clock::now();
+  CHECK(det->wait_completion() == cudaErrorTimeout);
+  CHECK(ms_since(t0) < 450);
+  w2.join();
+  CHECK(det->completed.load());
+}
+
+static void test_bounded_push() {
+  // a full ring: push gives up after the deadline instead of spinning forever
+  ClientQueue q;
+  for (size_t i = 0; i < ClientQueue::kCapacity; ++i)
+    CHECK(q.try_push(std::make_shared<OperationRecord>()));
+  auto t0 = std::chrono::steady_clock::now();
+  CHECK(!q.push(std::make_shared<OperationRecord>()));
+  CHECK(ms_since(t0) >= 150);
+  // enqueue_operation on a full client queue: the record completes with a
+  // timeout, is marked cancelled and the client's error latch is set
+  auto& cq = g_capture_state.client_queues[2];
+  while (!cq->empty()) cq->try_pop();
+  for (size_t i = 0; i < ClientQueue::kCapacity; ++i)
+    CHECK(cq->try_push(create_operation(2, OperationType::MEMSET)));
+  auto op = create_operation(2, OperationType::CUBLAS_SGEMM);
+  CHECK(!enqueue_operation(op));
+  CHECK(op->completed.load() && op->result == cudaErrorTimeout);
+  CHECK(!op->claim());
+  CHECK(get_and_clear_last_error(2) == cudaErrorTimeout);
+  while (!cq->empty()) cq->try_pop();
 }
 
 static void test_queue_fifo_concurrent() {
@@ -303,6 +374,8 @@ int main(int argc, char** argv) {
   test_stream_handle_maps();
   test_submit_and_complete();
   test_bounded_wait();
+  test_timeout_paths_with_stalled_worker();
+  test_bounded_push();
   test_queue_fifo_concurrent();
   test_kernel_info_and_decision(dir);
   test_profile_tables(dir);
