@@ -68,9 +68,11 @@ def parse():
                     help="HP steps of the latency phases (solo, paced, e2e)")
     ap.add_argument("--be-keep-sms", type=int, default=-1,
                     help="SMs a BE op keeps while HP runs (default: the scheduler's)")
-    ap.add_argument("--kernel-info", default="",
-                    help="directory of per-client kernel_info CSV tables (client<i>.csv) "
-                         "for the Orion admission gate")
+    ap.add_argument("--kernel-info", default="auto",
+                    help="per-client kernel tables for the Orion admission gate: 'auto' "
+                         "measures them in-process before the timed phases (one step of each "
+                         "client alone, kernel_intercept_b200.profile_tables), a directory "
+                         "loads client<i>.csv from it, 'none' leaves the gate without tables")
     ap.add_argument("--gil-switch-ms", type=float, default=0.5,
                     help="sys.setswitchinterval of the process (HP and BE are Python threads; "
                          "0: Python's default of 5 ms)")
@@ -362,15 +364,23 @@ def run_group(args):
                        "their own streams, no scheduler"}
 
     # ---- kx arm
-    if args.kernel_info:
-        for c in range(n_clients):
-            path = os.path.join(args.kernel_info, f"client{c}.csv")
-            if os.path.exists(path):
-                orion.orion_load_kernel_info(c, path.encode())
     if args.be_keep_sms >= 0:
         orion.orion_set_be_keep_sms(args.be_keep_sms)
     orion.orion_start_scheduler_thread()
     orion.orion_set_capture(1)
+    tables = None
+    if args.kernel_info != "none":
+        from kernel_intercept_b200 import profile_tables
+        if args.kernel_info == "auto":
+            for i, c in enumerate([hp] + bes):  # captured warm-up step per client
+                profile_tables._run_on_client(orion, i, c.step)
+            paths = profile_tables.generate(orion, [c.step for c in [hp] + bes],
+                                            tempfile.mkdtemp(prefix="kx_tables_"))
+        else:
+            paths = [os.path.join(args.kernel_info, f"client{c}.csv") for c in range(n_clients)]
+        rows = profile_tables.load(orion, paths)
+        tables = {"source": args.kernel_info, "rows": rows,
+                  "hp_kernels_ms": rnd(sum(r[4] for r in profile_tables.read_csv(paths[0])) / 1e6)}
     if args.gc_freeze:
         import gc
         gc.collect()
@@ -465,7 +475,7 @@ def run_group(args):
         "captured": stats,
         "client_waits": {str(c): {k: rnd(v) if isinstance(v, float) else v for k, v in w.items()}
                          for c, w in waits.items()},
-        "library": lib,
+        "library": lib, "kernel_tables": tables,
     }
     if lib is not None:
         line["library"]["vs_kx"] = {

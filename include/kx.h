@@ -249,6 +249,11 @@ int kx_num_sms(void);
  * thread selected (for profile tables); never NULL. */
 const char* kx_last_kernel_name(void);
 
+/* Grid (persistent CTAs, i.e. SMs occupied) of the last persistent GEMM /
+ * convolution launch this thread made: min(work tiles, SM quota, SM count).
+ * For profile tables; 0 before the first such launch. */
+int kx_last_grid(void);
+
 /* Version string of the library. */
 const char* kx_version(void);
 

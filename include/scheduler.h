@@ -134,6 +134,8 @@ public:
     int hp_quota() const;
     int be_quota() const;
     void set_be_keep_sms(int sms) { be_keep_sms_.store(sms); }
+    /** Profiling sessions also time the kernels the interposer re-issues. */
+    void set_profile_launches(bool on) { profile_launches_.store(on); }
     int be_keep_sms() const { return be_keep_sms_.load(); }
     volatile int* hp_flag_host() const { return hp_flag_host_; }
     int* hp_flag_device() const { return hp_flag_dev_; }
@@ -197,6 +199,7 @@ private:
     };
     std::mutex prof_mu_;
     std::vector<PendingProfile> pending_prof_;
+    std::atomic<bool> profile_launches_{false};
     std::vector<cudaEvent_t> prof_events_;  // free timing events (guarded by prof_mu_)
     cudaEvent_t take_profile_event();
 };
@@ -227,6 +230,10 @@ int orion_start_scheduler_thread();
 // Additions of this build.
 /** SMs BE kernels keep while HP work is in flight (DEFAULT mode). */
 void orion_set_be_keep_sms(int sms);
+/** Addition: 1 = profiling sessions (orion_start_profiling) also record every
+ *  kernel the interposer re-issues (name, SMs its grid fills, device time),
+ *  for per-client kernel tables; 0 (default) = captured dense ops only. */
+void orion_set_profile_launches(int on);
 int orion_get_be_keep_sms();
 /** Fixed HP / BE SM budgets (ISOLATED mode); 0,0 returns to DEFAULT. */
 int orion_set_sm_budgets(int hp_sms, int be_sms);

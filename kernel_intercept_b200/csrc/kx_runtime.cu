@@ -28,6 +28,7 @@ SlotPool g_pools[64];
 constexpr int kSlotsPerDevice = 4096;
 
 thread_local const char* tl_kernel_name = "none";
+thread_local int tl_last_grid = 0;
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                    const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
@@ -167,7 +168,8 @@ int persistent_grid(const Exec& e, int tiles) {
   int sms = device_info().num_sms;
   int cap = (e.sm_quota > 0 && e.sm_quota < sms) ? e.sm_quota : sms;
   if (tiles < cap) cap = tiles;
-  return cap < 1 ? 1 : cap;
+  tl_last_grid = cap < 1 ? 1 : cap;
+  return tl_last_grid;
 }
 
 bool encode_map(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* base,
@@ -320,6 +322,8 @@ extern "C" unsigned long long kx_device_alloc_count(void) {
 extern "C" int kx_num_sms(void) { return kx::device_info().num_sms; }
 
 extern "C" const char* kx_last_kernel_name(void) { return kx::tl_kernel_name; }
+
+extern "C" int kx_last_grid(void) { return kx::tl_last_grid; }
 
 extern "C" const char* kx_version(void) { return "kx 0.1 sm_100a"; }
 

@@ -217,7 +217,12 @@ void KernelProfiler::end_session(const std::string& output_path) {
   f << "{\n  \"model_name\": \"" << model_name_ << "\",\n  \"kernels\": [\n";
   for (size_t i = 0; i < recorded_profiles_.size(); ++i) {
     const KernelProfile& p = recorded_profiles_[i];
-    f << "    {\"kernel_id\": \"" << p.kernel_id << "\", \"duration_ms\": " << p.duration_ms
+    std::string id;  // JSON string escaping of the kernel name
+    for (char ch : p.kernel_id) {
+      if (ch == '"' || ch == '\\') id.push_back('\\');
+      if (static_cast<unsigned char>(ch) >= 0x20) id.push_back(ch);
+    }
+    f << "    {\"kernel_id\": \"" << id << "\", \"duration_ms\": " << p.duration_ms
       << ", \"sm_needed\": " << p.sm_needed << ", \"profile_type\": \""
       << profile_type_str(p.profile_type) << "\", \"grid_size\": " << p.grid_size
       << ", \"block_size\": " << p.block_size << ", \"client\": " << p.client_idx

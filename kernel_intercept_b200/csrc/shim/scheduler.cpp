@@ -22,6 +22,8 @@
 //    as in the reference (src/scheduler.cpp:84-153).
 #include "scheduler.h"
 
+#include <cuda.h>
+
 #include <time.h>
 
 #include <algorithm>
@@ -385,12 +387,79 @@ void Scheduler::hp_activity_poll() {
   publish_hp_flag(0);
 }
 
+// Name and SM need of a kernel the interposer re-issues (profile tables):
+// the function's name from the runtime / driver, and the SMs its grid fills
+// at the occupancy the function reaches with its block and shared memory
+// (total blocks / resident blocks per SM, at most every SM).
+static void describe_launch(const KernelLaunchParams& p, int num_sms, std::string* name,
+                            int* sm_needed, int* blocks, int* threads) {
+  const long long b = static_cast<long long>(p.gridDim.x) * p.gridDim.y * p.gridDim.z;
+  const int t = static_cast<int>(p.blockDim.x * p.blockDim.y * p.blockDim.z);
+  int per_sm = 0;
+  const char* nm = nullptr;
+  size_t smem = p.sharedMem;
+  if (p.api == 1 && p.ex_config != nullptr)
+    smem = static_cast<const cudaLaunchConfig_t*>(p.ex_config)->dynamicSmemBytes;
+  if (p.api == 2) {
+    using NameFn = CUresult (*)(const char**, CUfunction);
+    using OccFn = CUresult (*)(int*, CUfunction, int, size_t);
+    auto fn = reinterpret_cast<CUfunction>(const_cast<void*>(p.func));
+    if (auto get = ORION_REAL_T(cudadrv, NameFn, "cuFuncGetName")) get(&nm, fn);
+    if (auto occ = ORION_REAL_T(cudadrv, OccFn, "cuOccupancyMaxActiveBlocksPerMultiprocessor"))
+      occ(&per_sm, fn, t, smem);
+  } else {
+    using NameFn = cudaError_t (*)(const char**, const void*);
+    using OccFn = cudaError_t (*)(int*, const void*, int, size_t);
+    if (auto get = ORION_REAL_T(cudart, NameFn, "cudaFuncGetName"))
+      if (get(&nm, p.func) != cudaSuccess) nm = nullptr;
+    if (auto occ = ORION_REAL_T(cudart, OccFn, "cudaOccupancyMaxActiveBlocksPerMultiprocessor"))
+      if (occ(&per_sm, p.func, t, smem) != cudaSuccess) per_sm = 0;
+    ORION_REAL(cudart, cudaGetLastError)();
+  }
+  *name = nm != nullptr ? nm : "kernel";
+  if (per_sm < 1) per_sm = 1;
+  const long long need = (b + per_sm - 1) / per_sm;
+  *sm_needed = static_cast<int>(need < num_sms ? (need < 1 ? 1 : need) : num_sms);
+  *blocks = static_cast<int>(b < 0x7fffffffLL ? b : 0x7fffffffLL);
+  *threads = t;
+}
+
+static bool is_launch_op(OperationType t) {
+  return t == OperationType::KERNEL_LAUNCH || t == OperationType::KERNEL_LAUNCH_EX ||
+         t == OperationType::KERNEL_LAUNCH_DRV;
+}
+
 cudaError_t Scheduler::execute_operation(OperationPtr op, cudaStream_t fallback) {
   op->started.store(true);
   const int c = op->client_idx;
   ClientStats& st = stats(c);
   st.ops.fetch_add(1);
-  if (!is_dense_op(op->type)) return dispatch_runtime(*op, fallback);
+  if (!is_dense_op(op->type)) {
+    if (!(g_profiler.active() && profile_launches_.load() && is_launch_op(op->type)))
+      return dispatch_runtime(*op, fallback);
+    // profiled re-issued kernel: timed on its stream like the dense ops
+    auto& kp = std::get<KernelLaunchParams>(op->params);
+    cudaStream_t s = kp.stream ? kp.stream : fallback;
+    if (op->type == OperationType::KERNEL_LAUNCH_EX && kp.ex_config != nullptr) {
+      cudaStream_t cs = static_cast<const cudaLaunchConfig_t*>(kp.ex_config)->stream;
+      s = cs ? cs : fallback;
+    }
+    PendingProfile pp;
+    pp.start = take_profile_event();
+    pp.end = take_profile_event();
+    ORION_REAL(cudart, cudaEventRecord)(pp.start, s);
+    const cudaError_t err = dispatch_runtime(*op, fallback);
+    ORION_REAL(cudart, cudaEventRecord)(pp.end, s);
+    describe_launch(kp, config_.num_sms, &pp.rec.kernel_id, &pp.rec.sm_needed, &pp.rec.grid_size,
+                    &pp.rec.block_size);
+    pp.rec.profile_type = ProfileType::UNKNOWN;
+    pp.rec.client_idx = c;
+    pp.rec.op_type = op_type_name(op->type);
+    pp.rec.work = 0.0;
+    std::lock_guard<std::mutex> lk(prof_mu_);
+    pending_prof_.push_back(pp);
+    return err;
+  }
 
   ExecPolicy pol;
   pol.stream = op_stream(*op);
@@ -442,6 +511,13 @@ cudaError_t Scheduler::execute_operation(OperationPtr op, cudaStream_t fallback)
     pp.end = ev_end;
     pp.rec.kernel_id = kx_last_kernel_name();
     pp.rec.sm_needed = pol.sm_quota > 0 ? pol.sm_quota : config_.num_sms;
+    if (op->type != OperationType::CUDNN_BATCHNORM_FWD &&
+        op->type != OperationType::CUDNN_BATCHNORM_BWD &&
+        op->type != OperationType::CUDNN_BATCHNORM_INF) {
+      // GEMMs and convolutions: the persistent grid min(work tiles, quota)
+      const int g = kx_last_grid();
+      if (g > 0 && g < pp.rec.sm_needed) pp.rec.sm_needed = g;
+    }
     pp.rec.grid_size = pp.rec.sm_needed;
     pp.rec.block_size = 256;
     pp.rec.profile_type = (op->type == OperationType::CUDNN_BATCHNORM_FWD ||
@@ -700,6 +776,8 @@ void orion_sync_client_stream(int client_idx) { orion::g_scheduler.sync_client_s
 void orion_reset_state() { orion::g_orion_state.reset(); }
 
 int orion_autotune_green_ctx() { return orion::g_scheduler.autotune_green_ctx(); }
+
+void orion_set_profile_launches(int on) { orion::g_scheduler.set_profile_launches(on != 0); }
 
 void orion_set_be_keep_sms(int sms) { orion::g_scheduler.set_be_keep_sms(sms < 0 ? 0 : sms); }
 

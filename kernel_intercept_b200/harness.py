@@ -54,6 +54,7 @@ class Orion:
             "orion_resolve_client_idx": ([P, P], I), "orion_set_async_mode": ([I], None),
             "orion_get_async_mode": ([], I), "orion_init": ([I], I), "orion_shutdown": ([], None),
             "orion_set_be_keep_sms": ([I], None), "orion_get_be_keep_sms": ([], I),
+            "orion_set_profile_launches": ([I], None),
             "orion_set_sm_budgets": ([I, I], I),
             "orion_get_client_stats": ([I, ctypes.POINTER(ctypes.c_ulonglong)], I),
             "orion_load_profile": ([ctypes.c_char_p], I),

@@ -88,6 +88,7 @@ _SIGNATURES = {
     "kx_wait_flag": [_P, _P, ctypes.c_ulonglong, _P],
     "kx_num_sms": [],
     "kx_last_kernel_name": [],
+    "kx_last_grid": [],
     "kx_version": [],
 }
 

@@ -521,6 +521,62 @@ def scenario_gpt_train(orion):
     return {"errors": errs, "stats": stats, "loss": float(loss_kx)}
 
 
+def scenario_tables(orion):
+    """Per-client kernel tables measured through the interposer's profiler
+    (kernel_intercept_b200.profile_tables): one row per kernel op the worker
+    executes in a step, in order; then, with the tables loaded, an HP + BE
+    run in which the Orion admission gate holds BE ops back."""
+    import tempfile
+
+    import torch
+
+    from kernel_intercept_b200 import harness, profile_tables
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.manual_seed(0)
+    m = harness.make_gpt(layers=2, device="cuda").eval()
+    tok = torch.randint(0, 32000, (2, 256), device="cuda")
+    g = torch.Generator(device="cuda").manual_seed(9)
+    A = torch.randn(4096, 4096, device="cuda", generator=g)
+
+    def hp_step():
+        with torch.no_grad():
+            m(tok)
+
+    def be_step():
+        A @ A
+
+    assert orion.orion_init_scheduler(2) == 0
+    orion.orion_set_capture(0)
+    hp_step()
+    be_step()
+    torch.cuda.synchronize()
+    orion.orion_start_scheduler_thread()
+    orion.orion_set_capture(1)
+    for i, f in enumerate((hp_step, be_step)):
+        profile_tables._run_on_client(orion, i, f)
+    st0 = [orion.stats(c) for c in (0, 1)]
+    d = tempfile.mkdtemp()
+    paths = profile_tables.generate(orion, [hp_step, be_step], d)
+    st1 = [orion.stats(c) for c in (0, 1)]
+    rows = [profile_tables.read_csv(p) for p in paths]
+    loaded = profile_tables.load(orion, paths)
+    blocked0 = orion.stats(1)["be_blocked"]
+    harness.run_clients(orion, hp_step, be_step, hp_steps=20, hp_warmup=1)
+    stats = {c: orion.stats(c) for c in (0, 1)}
+    orion.orion_set_capture(0)
+    orion.orion_stop_scheduler()
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    return {"rows": [len(r) for r in rows], "loaded": loaded,
+            "step_ops": [b["ops"] - a["ops"] for a, b in zip(st0, st1)],
+            "step_kx_ops": [b["kx_ops"] - a["kx_ops"] for a, b in zip(st0, st1)],
+            "hp_profiles": sorted({r[1] for r in rows[0]}),
+            "sm_ok": all(1 <= r[3] <= sms for rs in rows for r in rs),
+            "dur_ok": all(r[4] > 0 for rs in rows for r in rs),
+            "names_ok": all(r[0] for rs in rows for r in rs),
+            "hp_gemm_rows": sum(1 for r in rows[0] if r[1] == 1),
+            "be_blocked": stats[1]["be_blocked"] - blocked0, "stats": stats}
+
+
 def read_op_log(path):
     """Entries of an op log: (client, op type, route, shape integers)."""
     out = []

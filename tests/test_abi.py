@@ -47,7 +47,7 @@ cudnnBackendDestroyDescriptor cudnnBackendCreateDescriptor cudnnBackendSetAttrib
 cudnnBackendGetAttribute cudnnBackendFinalize cudaEventRecord cudaEventRecordWithFlags cudaStreamWaitEvent
 cudaEventSynchronize cudaEventQuery cudaStreamQuery orion_set_be_keep_sms orion_get_be_keep_sms
 orion_set_sm_budgets orion_get_client_stats orion_op_log_start orion_op_log_end
-orion_get_client_waits orion_trace_start orion_trace_end
+orion_get_client_waits orion_trace_start orion_trace_end orion_set_profile_launches
 """.split()
 
 
