@@ -2,6 +2,8 @@
 #include "kx_runtime.cuh"
 
 #include <atomic>
+#include <chrono>
+#include <cstdint>
 #include <cstdio>
 #include <cstring>
 #include <vector>
@@ -118,8 +120,60 @@ namespace {
 struct Scratch {
   void* ptr = nullptr;
   size_t bytes = 0;
+  int64_t last_use_ns = 0;
 };
 std::unordered_map<cudaStream_t, Scratch> g_scratch[64][3];
+size_t g_scratch_total[64] = {0};
+
+int64_t now_ns() {
+  return std::chrono::duration_cast<std::chrono::nanoseconds>(
+             std::chrono::steady_clock::now().time_since_epoch())
+      .count();
+}
+
+// Budget for the scratch buffers of one device: KX_SCRATCH_BUDGET_MB, else a
+// quarter of the device's memory (at most 24 GiB).
+size_t scratch_budget(int dev) {
+  static size_t budget[64] = {0};
+  if (budget[dev] == 0) {
+    size_t b = 0;
+    if (const char* s = std::getenv("KX_SCRATCH_BUDGET_MB")) b = std::strtoull(s, nullptr, 10) << 20;
+    if (b == 0) {
+      size_t free_b = 0, total_b = 0;
+      cudaMemGetInfo(&free_b, &total_b);
+      b = total_b / 4;
+      if (b > (24ull << 30)) b = 24ull << 30;
+      if (b < (1ull << 30)) b = 1ull << 30;
+    }
+    budget[dev] = b;
+  }
+  return budget[dev];
+}
+
+// Frees the buffers of streams other than `keep` that no op has asked for in
+// the last `idle_ns`, oldest first, until `need` more bytes fit the budget
+// (need = SIZE_MAX: every such buffer).  A buffer idle that long belongs to a
+// stream whose ops were enqueued long ago; cudaFree waits for the device, so
+// none of them is still running.  Caller holds g_mu.
+void evict_idle(int dev, cudaStream_t keep, size_t need, int64_t idle_ns) {
+  const int64_t now = now_ns();
+  const size_t budget = scratch_budget(dev);
+  while (need == SIZE_MAX || g_scratch_total[dev] + need > budget) {
+    Scratch* oldest = nullptr;
+    for (int slot = 0; slot < 3; ++slot)
+      for (auto& kv : g_scratch[dev][slot]) {
+        Scratch& s = kv.second;
+        if (kv.first == keep || s.ptr == nullptr || now - s.last_use_ns < idle_ns) continue;
+        if (oldest == nullptr || s.last_use_ns < oldest->last_use_ns) oldest = &s;
+      }
+    if (oldest == nullptr) return;
+    note_device_alloc();
+    cudaFree(oldest->ptr);
+    g_scratch_total[dev] -= oldest->bytes;
+    oldest->ptr = nullptr;
+    oldest->bytes = 0;
+  }
+}
 }  // namespace
 
 void* scratch_for(cudaStream_t stream, size_t bytes, int slot) {
@@ -130,22 +184,34 @@ void* scratch_for(cudaStream_t stream, size_t bytes, int slot) {
   if (bytes == 0) bytes = 256;
   std::lock_guard<std::mutex> lk(g_mu);
   Scratch& s = g_scratch[dev][slot][stream];
+  s.last_use_ns = now_ns();
   if (s.bytes >= bytes) return s.ptr;
   if (s.ptr != nullptr) {
     note_device_alloc();
     cudaFree(s.ptr);
+    g_scratch_total[dev] -= s.bytes;
     s.ptr = nullptr;
     s.bytes = 0;
   }
   size_t want = bytes + bytes / 8;  // headroom against repeated small growth
   want = (want + 255) & ~static_cast<size_t>(255);
+  // streams come and go (a client may run each phase on a new stream): keep
+  // the buffers of streams idle for a second within the budget
+  evict_idle(dev, stream, want, 1000000000LL);
   note_device_alloc();
   if (cudaMalloc(&s.ptr, want) != cudaSuccess) {
     cudaGetLastError();
-    s.ptr = nullptr;
-    return nullptr;
+    // out of memory: give back every other stream's idle buffer and retry
+    evict_idle(dev, stream, SIZE_MAX, 100000000LL);
+    note_device_alloc();
+    if (cudaMalloc(&s.ptr, want) != cudaSuccess) {
+      cudaGetLastError();
+      s.ptr = nullptr;
+      return nullptr;
+    }
   }
   s.bytes = want;
+  g_scratch_total[dev] += want;
   return s.ptr;
 }
 

@@ -34,7 +34,12 @@ WorkSlot* work_slot_for(cudaStream_t stream);
 // Scratch device memory reserved for `stream` on the current device, at least
 // `bytes` long.  Growing it frees the previous buffer (cudaFree waits for the
 // device), so ops on one stream may reuse it back to back; ops on different
-// streams get different buffers.  Returns nullptr on allocation failure.
+// streams get different buffers.  The buffers of one device stay within a
+// budget (KX_SCRATCH_BUDGET_MB, default a quarter of device memory, at most
+// 24 GiB): a growing buffer first frees the buffers of streams that have not
+// asked for theirs in the last second, oldest first; on an allocation
+// failure every other stream's buffer idle for 100 ms is freed and the
+// allocation retried.  Returns nullptr on allocation failure.
 // Slot 0 serves the operator entry points (im2col buffers, batch-norm
 // statistics); slot 1 is the GEMM's own split-K workspace and slot 2 holds
 // the 3xTF32 low parts of its operands, so a GEMM issued by an operator never

@@ -746,7 +746,34 @@ int orion_start_scheduler(int num_clients) {
   return orion::start_scheduler(num_clients) ? 0 : -1;
 }
 
-void orion_stop_scheduler() { orion::stop_scheduler(); }
+// ORION_STATS_FILE=<path>: orion_stop_scheduler writes the per-client
+// counters (orion_get_client_stats) there as JSON, so runs of drivers that do
+// not read them (the reference's own scripts) can still be checked.
+static void write_stats_file() {
+  const char* path = std::getenv("ORION_STATS_FILE");
+  if (path == nullptr || path[0] == '\0') return;
+  FILE* f = std::fopen(path, "w");
+  if (f == nullptr) return;
+  const int n = orion::g_capture_state.num_clients;
+  std::fprintf(f, "{\"clients\": [");
+  for (int c = 0; c < n; ++c) {
+    orion::ClientStats& s = orion::g_scheduler.stats(c);
+    std::fprintf(f,
+                 "%s{\"client\": %d, \"ops\": %llu, \"kx_ops\": %llu, \"passthrough_ops\": %llu, "
+                 "\"be_blocked\": %llu, \"yields\": %llu, \"errors\": %llu}",
+                 c ? ", " : "", c, (unsigned long long)s.ops.load(),
+                 (unsigned long long)s.kx_ops.load(), (unsigned long long)s.passthrough_ops.load(),
+                 (unsigned long long)s.be_blocked.load(), (unsigned long long)s.yields.load(),
+                 (unsigned long long)s.errors.load());
+  }
+  std::fprintf(f, "]}\n");
+  std::fclose(f);
+}
+
+void orion_stop_scheduler() {
+  orion::stop_scheduler();
+  write_stats_file();
+}
 
 int orion_load_kernel_info(int client_idx, const char* file_path) {
   if (file_path == nullptr) return -1;

@@ -314,6 +314,24 @@ def percentile(xs, q):
     return s[f] + (s[c] - s[f]) * (k - f)
 
 
+_client_streams: dict = {}
+_streams_lock = threading.Lock()
+
+
+def client_stream(dev: int, client: int):
+    """The stream client `client` issues its work on, on device `dev`: one per
+    client for the life of the process, so every phase of a run reuses it
+    (per-stream state such as the kx scratch buffers is then made once).  The
+    HP client's stream has the device's highest priority, so the hardware
+    schedules its blocks ahead of BE blocks waiting for the same SMs."""
+    import torch
+    with _streams_lock:
+        key = (dev, client)
+        if key not in _client_streams:
+            _client_streams[key] = torch.cuda.Stream(device=dev, priority=-1 if client == 0 else 0)
+        return _client_streams[key]
+
+
 def run_clients(orion: Orion | None, hp_step, be_step, hp_steps: int, hp_warmup: int,
                 be_warmup: int = 1, with_be: bool = True, with_hp: bool = True,
                 be_seconds: float | None = None, hp_period_ms: float = 0.0,
@@ -343,7 +361,7 @@ def run_clients(orion: Orion | None, hp_step, be_step, hp_steps: int, hp_warmup:
     def hp_thread():
         try:
             torch.cuda.set_device(dev)
-            s = torch.cuda.Stream(device=dev)
+            s = client_stream(dev, 0)
             if orion is not None:
                 orion.orion_set_client_idx(0)
                 orion.orion_register_client_stream(0, ctypes.c_void_p(s.cuda_stream))
@@ -388,7 +406,7 @@ def run_clients(orion: Orion | None, hp_step, be_step, hp_steps: int, hp_warmup:
         res, step, client = be_res[i], be_steps[i], i + 1
         try:
             torch.cuda.set_device(dev)
-            s = torch.cuda.Stream(device=dev)
+            s = client_stream(dev, client)
             if orion is not None:
                 orion.orion_set_client_idx(client)
                 orion.orion_register_client_stream(client, ctypes.c_void_p(s.cuda_stream))

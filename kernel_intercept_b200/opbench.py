@@ -46,6 +46,11 @@ GEMMS = [
     ("big_f32", 1, 0, 8192, 8192, 8192, 1, "f32"),
     ("llama_wq_bf16", 1, 0, 2048, 4096, 2048, 1, "bf16"),
     ("llama_up_bf16", 1, 0, 5504, 4096, 2048, 1, "bf16"),
+    ("llama_down_bf16", 1, 0, 2048, 4096, 5504, 1, "bf16"),
+    ("llama_lm_head_bf16", 1, 0, 32000, 4096, 2048, 1, "bf16"),
+    ("llama_scores_bf16", 1, 0, 1024, 1024, 128, 64, "bf16"),
+    ("llama_context_bf16", 0, 0, 128, 1024, 1024, 64, "bf16"),
+    ("gpt_l1_wgrad_bf16", 0, 1, 512, 2048, 4096, 1, "bf16"),
     ("big_bf16", 1, 0, 8192, 8192, 8192, 1, "bf16"),
 ]
 
@@ -188,7 +193,7 @@ def run_vgg_bwd(batch, check):
     print(json.dumps({k: round(v, 3) for k, v in tot.items()}), flush=True)
 
 
-def run_gemm(check):
+def run_gemm(check, only=""):
     import torch
 
     from . import kx
@@ -196,6 +201,8 @@ def run_gemm(check):
     torch.manual_seed(0)
     ex = kx.current_exec()
     for name, ta, tb, m, n, k, batch, dt in GEMMS:
+        if only and only not in name:
+            continue
         tdt = torch.float32 if dt == "f32" else torch.bfloat16
         # row-major storage of the column-major operands (cuBLAS view)
         a_shape = (m, k) if ta else (k, m)
@@ -253,13 +260,14 @@ def main(argv=None):
     ap.add_argument("what", choices=["vgg", "vggbwd", "gemm"])
     ap.add_argument("--batch", type=int, default=32)
     ap.add_argument("--check", action="store_true")
+    ap.add_argument("--only", default="", help="gemm: run the shapes whose name contains this")
     args = ap.parse_args(argv)
     if args.what == "vgg":
         run_vgg(args.batch, args.check)
     elif args.what == "vggbwd":
         run_vgg_bwd(args.batch, args.check)
     else:
-        run_gemm(args.check)
+        run_gemm(args.check, args.only)
     return 0
 
 

@@ -88,13 +88,15 @@ def read_csv(path: str) -> list[tuple]:
 def _run_on_client(orion, client: int, fn) -> None:
     """Runs fn() on a thread registered as `client`, on its own stream."""
     import torch
+
+    from .harness import client_stream
     err = []
     dev = torch.cuda.current_device()
 
     def body():
         try:
             torch.cuda.set_device(dev)
-            s = torch.cuda.Stream(device=dev)
+            s = client_stream(dev, client)
             orion.orion_set_client_idx(client)
             orion.orion_register_client_stream(client, ctypes.c_void_p(s.cuda_stream))
             with torch.cuda.stream(s):
