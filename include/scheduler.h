@@ -162,6 +162,8 @@ private:
     bool create_streams();
     void destroy_streams();
     int peek_sm_requirement(int client_idx, int offset = 0);
+    /** Table duration (ns) of the client's next kernel; 0 without a table. */
+    float peek_duration(int client_idx);
     double estimate_client_time_ns(int client_idx, unsigned int allocated_sms) const;
     void hp_activity_begin();
     void hp_activity_poll();
@@ -184,6 +186,9 @@ private:
     // HP idle hysteresis: the flag drops only after HP has been idle this long
     int64_t hp_idle_since_ns_{0};
     int64_t hp_hold_ns_{1000000};
+    // Longest table duration of a BE kernel that may share SMs with an active
+    // HP client (KX_BE_MAX_US, default 50 us); longer ones wait for HP to idle.
+    float be_max_ns_{50000.0f};
     cudaStream_t flag_stream_{nullptr};
     void publish_hp_flag(int value);
     std::atomic<int> be_keep_sms_{0};

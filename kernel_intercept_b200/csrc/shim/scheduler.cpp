@@ -231,6 +231,7 @@ bool Scheduler::init(int num_clients, const SchedulerConfig& config) {
   if (const char* s = std::getenv("KX_BE_KEEP_SMS")) keep = std::atoi(s);
   be_keep_sms_.store(std::max(0, std::min(keep, sms)));
   if (const char* s = std::getenv("KX_HP_HOLD_US")) hp_hold_ns_ = std::max(0LL, std::atoll(s)) * 1000;
+  if (const char* s = std::getenv("KX_BE_MAX_US")) be_max_ns_ = std::max(0.0f, std::strtof(s, nullptr)) * 1000.f;
   ORION_REAL(cudart, cudaEventCreateWithFlags)(&hp_last_event_, cudaEventDisableTiming);
   g_orion_state.init(num_clients, sms);
   g_orion_state.sm_threshold = config_.sm_threshold;
@@ -340,14 +341,40 @@ int Scheduler::peek_sm_requirement(int client_idx, int offset) {
   return rows[idx].sm_used;
 }
 
+float Scheduler::peek_duration(int client_idx) {
+  std::lock_guard<std::mutex> lk(g_orion_state.mutex);
+  if (client_idx < 0 || client_idx >= static_cast<int>(g_orion_state.op_info_vector.size()))
+    return 0.f;
+  auto& rows = g_orion_state.op_info_vector[client_idx];
+  if (rows.empty()) return 0.f;
+  const int n = static_cast<int>(rows.size());
+  const int idx = ((g_orion_state.seen[client_idx]) % n + n) % n;
+  return rows[idx].duration;
+}
+
+// Admission of a BE kernel op (the reference's rule, src/scheduler.cpp:997-1034:
+// run when HP's next kernel and this one fit in the SMs together, or when HP
+// has nothing queued), with two changes for kernels that cannot yield:
+//  * HP counts as active while its flag is raised, not only while its queue
+//    holds ops: a request's ops reach the queue one at a time, and a BE
+//    kernel admitted into such a gap holds the SMs HP's next kernel needs;
+//  * a BE kernel that does not fit beside HP's next one may still run when its
+//    table duration is at most be_max_ns_ (it delays HP by that much at most).
+// Captured dense BE ops are always admitted: they run as persistent kx kernels
+// that leave the SMs above the HP flag at their next tile boundary.
 bool Scheduler::orion_should_schedule(OperationPtr op, int client_idx) {
   if (is_memory_op(op->type) || !is_kernel_op(op->type)) return true;
   if (isolated_) return true;  // disjoint budgets: no interference to arbitrate
+  if (is_dense_op(op->type)) return true;
+  auto& q = g_capture_state.client_queues[0];
+  const bool hp_active =
+      (q && !q->empty()) || (hp_flag_host_ != nullptr && hp_flag_host_[0] != 0);
+  if (!hp_active) return true;
   const int hp = peek_sm_requirement(0);
   const int be = peek_sm_requirement(client_idx);
   if (hp + be <= config_.num_sms) return true;
-  auto& q = g_capture_state.client_queues[0];
-  return q && q->empty();
+  const float dur = peek_duration(client_idx);
+  return dur > 0.f && dur <= be_max_ns_;
 }
 
 void Scheduler::publish_hp_flag(int value) {
@@ -364,8 +391,11 @@ void Scheduler::publish_hp_flag(int value) {
 void Scheduler::hp_activity_begin() {
   if (isolated_ || hp_flag_host_ == nullptr) return;
   hp_idle_since_ns_ = 0;
+  // be_keep_sms is what all BE clients together keep: each BE op's CTAs
+  // below its share stay, the others retire at their next tile boundary
   const int keep = be_keep_sms_.load();
-  const int v = keep > 0 ? keep : -1;
+  const int n_be = num_clients_ > 1 ? num_clients_ - 1 : 1;
+  const int v = keep > 0 ? std::max(1, keep / n_be) : -1;
   if (hp_flag_host_[0] != v) publish_hp_flag(v);
 }
 
@@ -575,8 +605,11 @@ void Scheduler::run_worker(int client_idx) {
     op->end_ns = mono_ns();
     if (trace_enabled()) trace_executed(*op);
     if (err != cudaSuccess) set_last_error(client_idx, err);
-    if (client_idx == 0 && !isolated_ && is_kernel_op(op->type) && !is_dense_op(op->type)) {
-      // HP kernels the interposer only re-issues count as HP activity too
+    if (client_idx == 0 && !isolated_ && is_kernel_op(op->type) && !is_dense_op(op->type) &&
+        q->empty()) {
+      // HP kernels the interposer only re-issues count as HP activity too;
+      // the event goes after the last HP op queued so far (a later op records
+      // its own), one record per burst instead of one per kernel
       cudaStream_t s = op_stream(*op);
       std::lock_guard<std::mutex> lk(hp_mu_);
       ORION_REAL(cudart, cudaEventRecord)(hp_last_event_, s ? s : fallback);

@@ -359,14 +359,17 @@ KXO_API void kxo_conv_bwd_filter(const kxo_conv* d, float alpha, const float* x,
  * (count/(count-1)), as cuDNN documents; save_inv_var = 1/sqrt(var + eps)
  * with the biased batch variance.
  */
+/* mode 0 = CUDNN_BATCHNORM_PER_ACTIVATION (one group per c,h,w); 1 =
+ * CUDNN_BATCHNORM_SPATIAL and 2 = CUDNN_BATCHNORM_SPATIAL_PERSISTENT (the
+ * same numbers: one group per channel over n,h,w). */
 static void bn_geometry(int mode, int n, int c, int h, int w, int* groups, size_t* count) {
-    if (mode == 1) { *groups = c; *count = (size_t)n * h * w; }
+    if (mode != 0) { *groups = c; *count = (size_t)n * h * w; }
     else { *groups = c * h * w; *count = (size_t)n; }
 }
 
 static size_t bn_index(int mode, int c, int h, int w, int g, size_t t) {
     /* t-th element of statistics group g, NCHW contiguous */
-    if (mode == 1) {
+    if (mode != 0) {
         size_t hw = (size_t)h * w;
         size_t nn = t / hw, sp = t % hw;
         return (nn * c + g) * hw + sp;

@@ -236,9 +236,10 @@ static void test_kernel_info_and_decision(const std::string& dir) {
   write_file(be.c_str(),
              "Name,Profile,Memory_footprint,SM_usage,Duration\n"
              "conv_fwd,1,0,60,90000\n"
-             "bias_relu,0,0,40,3000\n");
+             "bias_relu,0,0,40,3000\n"
+             "short_wide,0,0,148,2000\n");
   CHECK(orion_load_kernel_info(0, hp.c_str()) == 2);
-  CHECK(orion_load_kernel_info(1, be.c_str()) == 2);
+  CHECK(orion_load_kernel_info(1, be.c_str()) == 3);
   CHECK(orion_load_kernel_info(2, be.c_str()) == -1);
   CHECK(orion_load_kernel_info(0, (dir + "/missing.csv").c_str()) == -1);
   CHECK(g_orion_state.op_info_vector[0][0].name == "void gemm<float, 128, 64>(Params)");
@@ -251,10 +252,11 @@ static void test_kernel_info_and_decision(const std::string& dir) {
   CHECK(s.peek_sm_requirement(0) == 100);
   CHECK(s.peek_sm_requirement(1) == 60);
   CHECK(s.peek_sm_requirement(1, 1) == 40);
-  CHECK(s.peek_sm_requirement(1, 2) == 60);  // wraps around the table
+  CHECK(s.peek_sm_requirement(1, 3) == 60);  // wraps around the table
 
+  // an opaque BE kernel (re-issued as it is, cannot yield)
   auto be_op = std::make_shared<OperationRecord>();
-  be_op->type = OperationType::CUDNN_CONV_FWD;
+  be_op->type = OperationType::KERNEL_LAUNCH;
   be_op->client_idx = 1;
   auto& hpq = g_capture_state.client_queues[0];
   while (!hpq->empty()) hpq->try_pop();
@@ -266,7 +268,26 @@ static void test_kernel_info_and_decision(const std::string& dir) {
   // next BE kernel needs 40 SMs: 100 + 40 fits
   g_orion_state.seen[1] = 1;
   CHECK(s.orion_should_schedule(be_op, 1));
+  // 100 + 148 does not fit, but the BE kernel is short (2 us <= 50 us)
+  g_orion_state.seen[1] = 2;
+  CHECK(s.peek_duration(1) == 2000.0f);
+  CHECK(s.orion_should_schedule(be_op, 1));
   g_orion_state.seen[1] = 0;
+  // captured dense BE ops yield at tile boundaries: always admitted
+  auto be_dense = std::make_shared<OperationRecord>();
+  be_dense->type = OperationType::CUDNN_CONV_FWD;
+  be_dense->client_idx = 1;
+  CHECK(s.orion_should_schedule(be_dense, 1));
+  // HP queue empty but its flag raised (a request in progress): still held
+  hpq->try_pop();
+  CHECK(s.orion_should_schedule(be_op, 1));
+  int flag[2] = {4, 0};
+  s.hp_flag_host_ = flag;
+  CHECK(!s.orion_should_schedule(be_op, 1));
+  flag[0] = 0;
+  CHECK(s.orion_should_schedule(be_op, 1));
+  s.hp_flag_host_ = nullptr;
+  hpq->push(create_operation(0, OperationType::CUBLAS_SGEMM));
   // memory ops are never held back
   auto mem = std::make_shared<OperationRecord>();
   mem->type = OperationType::MEMCPY_ASYNC;

@@ -250,3 +250,24 @@ def test_oracle_pinned_to_reference_goldens():
             continue
         checked += 1
     assert checked > 0
+
+
+def test_bn_spatial_persistent_mode_is_spatial():
+    """cuDNN's SPATIAL_PERSISTENT mode (2) normalises per channel like
+    SPATIAL (1): the oracle gives identical results and writes only C
+    per-channel statistics."""
+    rng = np.random.default_rng(4)
+    x = (rng.standard_normal((4, 6, 5, 7)) * 2 + 1).astype(np.float32)
+    outs = []
+    for mode in (1, 2):
+        c = 6
+        y = np.zeros_like(x)
+        stats = [np.zeros(c + 8, np.float32) for _ in range(4)]  # 8 guard entries
+        sc, b = np.linspace(0.5, 1.5, c).astype(np.float32), np.zeros(c, np.float32)
+        o.bn_fwd_training(mode, 1.0, 0.0, x, y, sc, b, 0.1, stats[0], stats[1], 1e-5,
+                          stats[2], stats[3])
+        assert all(np.all(s[c:] == 0) for s in stats), mode
+        outs.append((y, [s[:c] for s in stats]))
+    assert np.array_equal(outs[0][0], outs[1][0])
+    for a, b_ in zip(outs[0][1], outs[1][1]):
+        assert np.array_equal(a, b_)
