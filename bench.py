@@ -243,6 +243,20 @@ class Ranks:
             self.pg.destroy_process_group()
 
 
+def pin_cores(local, world):
+    """At N > 1, gives each rank's process (its client threads and the
+    interposer's workers, created later) its own share of the host's cores,
+    so ranks do not preempt each other's threads; only when every rank gets
+    at least 4 cores.  Returns the number of cores this rank may use."""
+    avail = sorted(os.sched_getaffinity(0))
+    if world <= 1 or len(avail) // world < 4:
+        return len(avail)
+    per = len(avail) // world
+    mine = avail[local * per:(local + 1) * per]
+    os.sched_setaffinity(0, mine)
+    return len(mine)
+
+
 def rate(res, units):
     return res.iters * units / (res.elapsed_ms / 1e3) if res.elapsed_ms else 0.0
 
@@ -331,6 +345,7 @@ def run_group(args):
     from kernel_intercept_b200 import configs, harness, kx
 
     rank, world, local = dist_info()
+    pinned = pin_cores(local, world)
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
     ranks = Ranks(world, dev)
@@ -467,7 +482,7 @@ def run_group(args):
                    "l2": "inputs larger than L2 between HP steps (activations of one step "
                          "exceed 126 MB)",
                    "gil_switch_ms": round(sys.getswitchinterval() * 1e3, 3),
-                   "gc_frozen": bool(args.gc_freeze)},
+                   "gc_frozen": bool(args.gc_freeze), "host_cores_per_rank": pinned},
         "hp": hp_block,
         "be": be, "be_total": {k: round(v, 1) for k, v in be_totals.items()},
         "roofline": roof, "roofline_hp_solo": roof_solo, "ops": op_table(kr["cont_recs"]),

@@ -1176,16 +1176,19 @@ __global__ void __launch_bounds__(256, 1)
           tc_fence_after();
 #pragma unroll
           for (int c = 0; c < Cfg::BN / 32; ++c) {
-            uint32_t v[32];
+            // both accumulator halves of the chunk in flight, one wait
+            uint32_t v[32], w[32];
             tmem_ld_32x32b_x32(tmem + a * Cfg::ACC_COLS + c * 32 + lane_off, v);
+            if constexpr (Cfg::ACC_COLS == 2 * Cfg::BN)
+              tmem_ld_32x32b_x32(tmem + a * Cfg::ACC_COLS + Cfg::BN + c * 32 + lane_off, w);
             tmem_ld_wait();
+            tmem_regs_ready(v);
 #pragma unroll
             for (int j = 0; j < 32; ++j) acc[c][j] += __uint_as_float(v[j]);
             if constexpr (Cfg::ACC_COLS == 2 * Cfg::BN) {
-              tmem_ld_32x32b_x32(tmem + a * Cfg::ACC_COLS + Cfg::BN + c * 32 + lane_off, v);
-              tmem_ld_wait();
+              tmem_regs_ready(w);
 #pragma unroll
-              for (int j = 0; j < 32; ++j) acc[c][j] += __uint_as_float(v[j]);
+              for (int j = 0; j < 32; ++j) acc[c][j] += __uint_as_float(w[j]);
             }
           }
           tc_fence_before();
@@ -1216,11 +1219,12 @@ __global__ void __launch_bounds__(256, 1)
         if (!ok) break;
         tc_fence_after();
         const long long t_emit = stats ? clock64() : 0;
-#pragma unroll 1
-        for (int c0 = 0; c0 < Cfg::BN; c0 += 32) {
-          uint32_t v[32];
-          tmem_ld_32x32b_x32(tmem + a * Cfg::ACC_COLS + c0 + lane_off, v);
-          tmem_ld_wait();
+        // Two 32-column register buffers: the TMEM load of the next chunk is
+        // in flight while the current one is converted and stored.
+        const uint32_t tbase = tmem + a * Cfg::ACC_COLS + lane_off;
+        uint32_t va[32], vb[32];
+        auto out = [&](int c0, uint32_t (&v)[32]) {
+          tmem_regs_ready(v);
           float f[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]);
@@ -1228,6 +1232,18 @@ __global__ void __launch_bounds__(256, 1)
             emit_tma(c0, f);
           else
             emit(c0, f);
+        };
+        tmem_ld_32x32b_x32(tbase, va);
+        tmem_ld_wait();
+#pragma unroll 1
+        for (int c0 = 0; c0 < Cfg::BN; c0 += 64) {
+          const bool has_b = c0 + 32 < Cfg::BN;
+          if (has_b) tmem_ld_32x32b_x32(tbase + c0 + 32, vb);
+          out(c0, va);
+          tmem_ld_wait();
+          if (c0 + 64 < Cfg::BN) tmem_ld_32x32b_x32(tbase + c0 + 64, va);
+          if (has_b) out(c0 + 32, vb);
+          tmem_ld_wait();
         }
         if (stats) st_c += static_cast<unsigned long long>(clock64() - t_emit);
         tc_fence_before();

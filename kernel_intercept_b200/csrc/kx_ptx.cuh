@@ -351,6 +351,14 @@ KX_DEV void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
 
 KX_DEV void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// Orders every later use of r after the preceding tcgen05.wait::ld: the
+// registers a tcgen05.ld writes are valid only after the wait, and without a
+// dependence through them the compiler may schedule their uses earlier.
+KX_DEV void tmem_regs_ready(uint32_t (&r)[32]) {
+#pragma unroll
+  for (int j = 0; j < 32; ++j) asm volatile("" : "+r"(r[j]));
+}
+
 // ------------------------------------------------------- UMMA descriptors --
 //
 // Shared-memory matrix descriptor (sm_100 layout):

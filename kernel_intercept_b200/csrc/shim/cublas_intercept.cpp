@@ -20,6 +20,7 @@
 //  * Operand combinations kx does not implement (e.g. fp16 compute, int8)
 //    are outside the captured dense-op contract: the client's queue is drained
 //    first (to keep its order) and the real library runs them.
+#include <chrono>
 #include <cstdlib>
 #include <cstring>
 #include <thread>
@@ -65,11 +66,9 @@ void drain_client(int client) {
   if (client < 0 || client >= g_capture_state.num_clients) return;
   auto& q = g_capture_state.client_queues[client];
   const int64_t limit = wait_timeout_ns() / 1000;
-  int64_t waited_us = 0;
-  while (q && !q->empty() && waited_us < limit) {
-    std::this_thread::sleep_for(std::chrono::microseconds(2));
-    waited_us += 2;
-  }
+  const auto deadline = std::chrono::steady_clock::now() + std::chrono::microseconds(limit);
+  while (q && !q->empty() && std::chrono::steady_clock::now() < deadline)
+    std::this_thread::yield();  // a sleep would oversleep by the timer slack
 }
 
 cudaStream_t real_handle_stream(void* handle) {

@@ -21,6 +21,7 @@
 //    called for captured ops.
 #include <cuda.h>
 
+#include <chrono>
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
@@ -333,11 +334,9 @@ static void drain_own_queue() {
   if (c < 0) return;
   auto& q = g_capture_state.client_queues[c];
   const int64_t limit_us = wait_timeout_ns() / 1000;
-  int64_t waited = 0;
-  while (q && !q->empty() && waited < limit_us) {
-    std::this_thread::sleep_for(std::chrono::microseconds(2));
-    waited += 2;
-  }
+  const auto deadline = std::chrono::steady_clock::now() + std::chrono::microseconds(limit_us);
+  while (q && !q->empty() && std::chrono::steady_clock::now() < deadline)
+    std::this_thread::yield();  // a sleep would oversleep by the timer slack
 }
 
 cudaError_t cudaEventSynchronize(cudaEvent_t event) {

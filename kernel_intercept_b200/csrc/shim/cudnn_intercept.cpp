@@ -21,6 +21,7 @@
 #include <algorithm>
 #include <atomic>
 #include <vector>
+#include <chrono>
 #include <cstdlib>
 #include <cstring>
 #include <memory>
@@ -75,11 +76,9 @@ void drain_client(int client) {
   if (client < 0 || client >= g_capture_state.num_clients) return;
   auto& q = g_capture_state.client_queues[client];
   const int64_t limit = wait_timeout_ns() / 1000;
-  int64_t waited = 0;
-  while (q && !q->empty() && waited < limit) {
-    std::this_thread::sleep_for(std::chrono::microseconds(2));
-    waited += 2;
-  }
+  const auto deadline = std::chrono::steady_clock::now() + std::chrono::microseconds(limit);
+  while (q && !q->empty() && std::chrono::steady_clock::now() < deadline)
+    std::this_thread::yield();  // a sleep would oversleep by the timer slack
 }
 
 struct Tensor4 {

@@ -537,13 +537,17 @@ def scenario_tables(orion):
     tok = torch.randint(0, 32000, (2, 256), device="cuda")
     g = torch.Generator(device="cuda").manual_seed(9)
     A = torch.randn(4096, 4096, device="cuda", generator=g)
+    Bbig = torch.randn(64 << 20, device="cuda", generator=g)
 
     def hp_step():
         with torch.no_grad():
             m(tok)
 
     def be_step():
+        # one captured GEMM (yields to HP at tile boundaries) and one long
+        # re-issued elementwise kernel (cannot yield: the gate holds it back)
         A @ A
+        Bbig.mul_(1.0000001)
 
     assert orion.orion_init_scheduler(2) == 0
     orion.orion_set_capture(0)
