@@ -519,6 +519,7 @@ __global__ void __launch_bounds__(256, 1)
     // ------------------------------------------------------ TMA producer --
     if (lane == 0) {
       uint32_t it = 0;
+      uint32_t prod_s = 0, prod_ph = 0;  // stage and phase of k-block `it`
       uint32_t ia = 0, ib = 0;  // tap reuse: A boxes and B k-blocks issued
       int taken = 0;
       for (uint32_t slot = 0;; ++slot) {
@@ -657,9 +658,13 @@ __global__ void __launch_bounds__(256, 1)
         }
         bool ok = true;
         for (int kb = kb0; kb < kb0 + nkb; ++kb, ++it) {
-          const uint32_t s = it % S;
-          if (!timed_wait(smem_addr(&sb->empty[s]), ((it / S) & 1) ^ 1, wc,
-                          stats ? &st_a : nullptr)) {
+          const uint32_t s = prod_s;
+          const uint32_t ph = prod_ph;
+          if (++prod_s == static_cast<uint32_t>(S)) {
+            prod_s = 0;
+            prod_ph ^= 1u;
+          }
+          if (!timed_wait(smem_addr(&sb->empty[s]), ph ^ 1u, wc, stats ? &st_a : nullptr)) {
             ok = false;
             break;
           }
@@ -788,6 +793,11 @@ __global__ void __launch_bounds__(256, 1)
       // `sc` counts accumulator segments across tiles; segment sc uses TMEM
       // buffer sc & 1 (one segment per tile unless PROMOTE splits K).
       uint32_t it = 0, sc = 0;
+      uint32_t mma_s = 0, mma_ph = 0;  // stage and phase of k-block `it`
+      const uint64_t a_desc0 =
+          sdesc_sw128(smem_addr(stageA(0)), Cfg::A_LBO, Cfg::A_SBO, Cfg::A_LAYOUT);
+      const uint64_t b_desc0 =
+          sdesc_sw128(smem_addr(stageB(0)), Cfg::B_LBO, Cfg::B_SBO, Cfg::B_LAYOUT);
       uint32_t ia = 0, ib = 0;  // tap reuse: A boxes and B k-blocks consumed
       const long long t_loop = stats ? clock64() : 0;
       bool ok = true;
@@ -880,34 +890,42 @@ __global__ void __launch_bounds__(256, 1)
           const int kfirst = kb;
           const long long t_k = stats ? clock64() : 0;
           for (; kb < kend; ++kb, ++it) {
-            const uint32_t s = it % S;
+            // stage and phase of k-block `it`, kept as running counters (the
+            // single issuing thread's instruction count per k-block is on the
+            // critical path)
+            const uint32_t s = mma_s;
+            const uint32_t ph = mma_ph;
+            if (++mma_s == static_cast<uint32_t>(S)) {
+              mma_s = 0;
+              mma_ph ^= 1u;
+            }
             const uint32_t wb = convert ? smem_addr(&sb->conv[s]) : smem_addr(&sb->full[s]);
-            if (!timed_wait(wb, (it / S) & 1, wc, stats ? &st_a : nullptr) ||
-                (PAIR && !mbar_wait_cluster(smem_addr(&sb->pair_full[s]), (it / S) & 1, wc))) {
+            if (!timed_wait(wb, ph, wc, stats ? &st_a : nullptr) ||
+                (PAIR && !mbar_wait_cluster(smem_addr(&sb->pair_full[s]), ph, wc))) {
               ok = false;
               break;
             }
             const long long t_iss = stats ? clock64() : 0;
             tc_fence_after();
-            const uint32_t a_hi = smem_addr(stageA(s));
-            const uint32_t b_hi = smem_addr(stageB(s));
-            const uint32_t a_lo = smem_addr(stageAlo(s));
+            // descriptors of this stage: the stage-0 descriptors plus the
+            // stage offset in the 16-byte address field (no carry: shared
+            // memory addresses stay below 2^18)
+            const uint32_t soff = s * static_cast<uint32_t>(Cfg::STAGE_BYTES >> 4);
 #pragma unroll
             for (int kk = 0; kk < Cfg::BK / Cfg::UMMA_K; ++kk) {
               const uint32_t aoff = Cfg::A_MN ? kk * Cfg::UMMA_K * 128 : kk * 32;
               const uint32_t boff = Cfg::B_MN ? kk * Cfg::UMMA_K * 128 : kk * 32;
-              const uint64_t ad = sdesc_sw128(a_hi + aoff, Cfg::A_LBO, Cfg::A_SBO, Cfg::A_LAYOUT);
-              const uint64_t bd = sdesc_sw128(b_hi + boff, Cfg::B_LBO, Cfg::B_SBO, Cfg::B_LAYOUT);
+              const uint64_t ad = a_desc0 + (soff + (aoff >> 4));
+              const uint64_t bd = b_desc0 + (soff + (boff >> 4));
               const uint32_t acc = (kb > kfirst || kk > 0) ? 1u : 0u;
               if constexpr (PAIR && !Cfg::SPLIT) {
                 // 16-bit operands: one 256 x BN MMA over the pair's A and B rows
                 umma_f16_pair(d_tmem, ad, bd, Cfg::IDESC, acc);
               } else if constexpr (PAIR) {
                 // 256 x BN over the pair: A rows and B rows from both CTAs
-                const uint64_t adl =
-                    sdesc_sw128(a_lo + aoff, Cfg::A_LBO, Cfg::A_SBO, Cfg::A_LAYOUT);
-                const uint64_t bdl = sdesc_sw128(smem_addr(stageBlo(s)) + boff, Cfg::B_LBO,
-                                                 Cfg::B_SBO, Cfg::B_LAYOUT);
+                // (A_lo right after A, B_lo right after B in the stage)
+                const uint64_t adl = ad + (Cfg::A_BYTES >> 4);
+                const uint64_t bdl = bd + (Cfg::B_BYTES >> 4);
                 umma_tf32_pair(d_tmem, ad, bd, Cfg::IDESC, acc);
                 umma_tf32_pair(d_tmem, ad, bdl, Cfg::IDESC, 1u);
                 umma_tf32_pair(d_tmem, adl, bd, Cfg::IDESC, 1u);
@@ -915,8 +933,7 @@ __global__ void __launch_bounds__(256, 1)
                 // hi*hi and hi*lo in one N = 2*BN MMA over [B_hi; B_lo]
                 // (columns [0, BN) and [BN, 2BN)), then lo*hi into [0, BN):
                 // A_hi is read from shared memory once per k-step, not twice
-                const uint64_t adl =
-                    sdesc_sw128(a_lo + aoff, Cfg::A_LBO, Cfg::A_SBO, Cfg::A_LAYOUT);
+                const uint64_t adl = ad + (Cfg::A_BYTES >> 4);  // A_lo follows A
                 umma_tf32(d_tmem, ad, bd, Cfg::IDESC2, acc);
                 umma_tf32(d_tmem, adl, bd, Cfg::IDESC, 1u);
               } else if constexpr (Cfg::AR == Arith::TF32) {

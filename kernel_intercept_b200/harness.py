@@ -12,13 +12,14 @@ CUDA events recorded in the client's stream order (the interposer keeps
 window.
 
 Workloads follow the configurations the reference is benchmarked on:
-* ``make_gpt``   — decoder with per-head q/k/v projections (the reference's
-  CharGPT layout, python/GPT.py:42-149): 6 layers, d_model 512, 8 heads,
-  FFN 2048 with GELU, pre-LayerNorm, learned positions, vocab 32000.
+* ``make_gpt``   — the reference's CharGPT (python/GPT.py:27-149): per-head
+  q/k/v projections, 6 layers, d_model 512, 8 heads, FFN 2048 with GELU,
+  pre-LayerNorm, learned positions, dropout 0.4, vocab 32000.
 * ``make_vgg16`` — torchvision VGG16 (13 conv3x3 + ReLU, 5 max-pools,
   FC 25088-4096-4096-1000), Kaiming-normal init.
-* ``make_llama`` — RMSNorm / RoPE / SwiGLU decoder (python/LLaMA.py layout):
-  12 layers, d_model 2048, 16 heads, FFN 5504, vocab 32000.
+* ``make_llama`` — the reference's CharLLaMA (python/LLaMA.py): RMSNorm,
+  complex rotary embedding, SwiGLU; 12 layers, d_model 2048, 16 heads,
+  FFN 5504, vocab 32000.
 """
 from __future__ import annotations
 
@@ -104,49 +105,74 @@ def preload_env(extra: dict | None = None) -> dict:
 # -------------------------------------------------------------- workloads ---
 
 def make_gpt(vocab=32000, emb=512, head_size=64, layers=6, seq=256, device="cuda",
-             dtype=None):
+             dtype=None, dropout=0.4):
+    """The reference's CharGPT (python/GPT.py:27-149) at the given sizes: per-head
+    q/k/v projections (MaskedAttention) concatenated and projected, GELU FFN,
+    pre-LayerNorm blocks, learned positions, dropout 0.4 on the attention
+    weights, after the projection and after the FFN (active in training
+    only).  Linear and embedding weights N(0, 0.02), biases zero."""
     import torch
     import torch.nn as nn
     import torch.nn.functional as F
 
-    class Head(nn.Module):
+    class Head(nn.Module):  # GPT.py:44-67
         def __init__(self):
             super().__init__()
             self.key = nn.Linear(emb, head_size, bias=False)
             self.query = nn.Linear(emb, head_size, bias=False)
             self.value = nn.Linear(emb, head_size, bias=False)
             self.register_buffer("tril", torch.tril(torch.ones(seq, seq)))
+            self.dropout = nn.Dropout(dropout)
 
         def forward(self, x):
-            T = x.shape[1]
+            B, T, C = x.shape
             q, k, v = self.query(x), self.key(x), self.value(x)
-            s = q @ k.transpose(-2, -1) / math.sqrt(head_size)
-            s = s.masked_fill(self.tril[:T, :T] == 0, float("-inf"))
-            return F.softmax(s, dim=-1) @ v
+            mask = self.tril[:T, :T]
+            # attention(): GPT.py:27-41, scaled by the head width
+            s = q @ k.transpose(-2, -1) / (q.shape[-1] ** 0.5)
+            s = s.masked_fill(mask == 0, float("-inf"))
+            return self.dropout(F.softmax(s, dim=-1)) @ v
 
-    class Block(nn.Module):
+    class MultiHead(nn.Module):  # GPT.py:69-88
         def __init__(self):
             super().__init__()
             self.heads = nn.ModuleList([Head() for _ in range(emb // head_size)])
             self.proj = nn.Linear(emb, emb)
+            self.dropout = nn.Dropout(dropout)
+
+        def forward(self, x):
+            return self.dropout(self.proj(torch.cat([h(x) for h in self.heads], dim=-1)))
+
+    class FeedForward(nn.Module):  # GPT.py:90-102
+        def __init__(self):
+            super().__init__()
             self.l1 = nn.Linear(emb, 4 * emb)
             self.l2 = nn.Linear(4 * emb, emb)
+            self.dropout = nn.Dropout(dropout)
+
+        def forward(self, x):
+            return self.dropout(self.l2(F.gelu(self.l1(x))))
+
+    class Block(nn.Module):  # GPT.py:104-119
+        def __init__(self):
+            super().__init__()
+            self.mha = MultiHead()
+            self.ff = FeedForward()
             self.ln1 = nn.LayerNorm(emb)
             self.ln2 = nn.LayerNorm(emb)
 
         def forward(self, x):
-            h = self.ln1(x)
-            x = x + self.proj(torch.cat([hd(h) for hd in self.heads], dim=-1))
-            return x + self.l2(F.gelu(self.l1(self.ln2(x))))
+            x = x + self.mha(self.ln1(x))
+            return x + self.ff(self.ln2(x))
 
-    class GPT(nn.Module):
+    class GPT(nn.Module):  # CharGPT, GPT.py:121-149
         def __init__(self):
             super().__init__()
-            self.tok = nn.Embedding(vocab, emb)
-            self.pos = nn.Embedding(seq, emb)
+            self.token_embedding = nn.Embedding(vocab, emb)
+            self.position_embedding = nn.Embedding(seq, emb)
             self.blocks = nn.Sequential(*[Block() for _ in range(layers)])
             self.ln = nn.LayerNorm(emb)
-            self.lm = nn.Linear(emb, vocab)
+            self.lm_head = nn.Linear(emb, vocab)
             for m in self.modules():
                 if isinstance(m, nn.Linear):
                     nn.init.normal_(m.weight, 0.0, 0.02)
@@ -156,9 +182,10 @@ def make_gpt(vocab=32000, emb=512, head_size=64, layers=6, seq=256, device="cuda
                     nn.init.normal_(m.weight, 0.0, 0.02)
 
         def forward(self, tokens):
-            T = tokens.shape[1]
-            x = self.tok(tokens) + self.pos(torch.arange(T, device=tokens.device))
-            return self.lm(self.ln(self.blocks(x)))
+            B, T = tokens.shape
+            pos = torch.arange(0, T, dtype=torch.long, device=tokens.device)
+            x = self.token_embedding(tokens) + self.position_embedding(pos)
+            return self.lm_head(self.ln(self.blocks(x)))
 
     m = GPT().to(device)
     if dtype is not None:
@@ -167,84 +194,107 @@ def make_gpt(vocab=32000, emb=512, head_size=64, layers=6, seq=256, device="cuda
 
 
 def make_vgg16(device="cuda"):
+    """torchvision VGG16 (weights=None: Kaiming-normal convolutions), the
+    model the reference's VGG16Model wraps (python/VGG16.py:13-24)."""
     from torchvision.models import vgg16
     return vgg16(weights=None).to(device)
 
 
 def make_llama(vocab=32000, hidden=2048, heads=16, layers=12, inter=5504, eps=1e-6,
                theta=10000.0, seq=1024, device="cuda", dtype=None):
+    """The reference's CharLLaMA (python/LLaMA.py:20-98, LlamaAttention 163-208)
+    at the given sizes, without grouped KV heads (kv heads = heads): RMSNorm
+    x * rsqrt(mean(x^2) + eps) * w in the model's dtype, rotary embedding
+    through complex multiplication with a precomputed freqs_cis buffer,
+    causal masked_fill with a tril buffer, softmax in the model's dtype,
+    SwiGLU MLP.  Linear and embedding weights N(0, 0.02)."""
     import torch
     import torch.nn as nn
     import torch.nn.functional as F
 
     hd = hidden // heads
 
-    class RMSNorm(nn.Module):
+    class RMSNorm(nn.Module):  # LLaMA.py:20-29
         def __init__(self):
             super().__init__()
             self.weight = nn.Parameter(torch.ones(hidden))
 
         def forward(self, x):
-            v = x.float().pow(2).mean(-1, keepdim=True)
-            return (x.float() * torch.rsqrt(v + eps)).to(x.dtype) * self.weight
+            rms = torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps)
+            return x * rms * self.weight
 
-    inv = 1.0 / (theta ** (torch.arange(0, hd, 2).float() / hd))
-    ang = torch.outer(torch.arange(seq).float(), inv)
-    cos, sin = ang.cos(), ang.sin()
+    def freqs_cis_table():  # precompute_freqs_cis, LLaMA.py:33-38
+        freqs = 1.0 / (theta ** (torch.arange(0, hd, 2).float() / hd))
+        t = torch.arange(seq).float()
+        freqs = torch.outer(t, freqs)
+        return torch.polar(torch.ones_like(freqs), freqs)
 
-    def rope(x):
-        T = x.shape[2]
-        c = cos[:T].to(x.device, x.dtype)
-        s = sin[:T].to(x.device, x.dtype)
-        x1, x2 = x[..., 0::2], x[..., 1::2]
-        return torch.stack((x1 * c - x2 * s, x1 * s + x2 * c), dim=-1).flatten(-2)
+    def rotary(xq, xk, freqs_cis):  # apply_rotary_emb, LLaMA.py:41-47
+        xq_c = torch.view_as_complex(xq.float().reshape(*xq.shape[:-1], -1, 2))
+        xk_c = torch.view_as_complex(xk.float().reshape(*xk.shape[:-1], -1, 2))
+        f = freqs_cis.unsqueeze(0).unsqueeze(2)
+        xq_out = torch.view_as_real(xq_c * f).flatten(-2)
+        xk_out = torch.view_as_real(xk_c * f).flatten(-2)
+        return xq_out.type_as(xq), xk_out.type_as(xk)
 
-    class Attn(nn.Module):
+    class Attn(nn.Module):  # LlamaAttention, LLaMA.py:163-208
         def __init__(self):
             super().__init__()
             self.wq = nn.Linear(hidden, hidden, bias=False)
             self.wk = nn.Linear(hidden, hidden, bias=False)
             self.wv = nn.Linear(hidden, hidden, bias=False)
             self.wo = nn.Linear(hidden, hidden, bias=False)
-            self.register_buffer("mask", torch.triu(torch.full((seq, seq), float("-inf")), 1))
+            self.register_buffer("freqs_cis", freqs_cis_table())
+            self.register_buffer("mask", torch.tril(torch.ones(seq, seq)))
 
         def forward(self, x):
             B, T, _ = x.shape
-            q = rope(self.wq(x).view(B, T, heads, hd).transpose(1, 2))
-            k = rope(self.wk(x).view(B, T, heads, hd).transpose(1, 2))
-            v = self.wv(x).view(B, T, heads, hd).transpose(1, 2)
-            s = (q @ k.transpose(-2, -1)) / math.sqrt(hd) + self.mask[:T, :T].to(x.dtype)
-            o = F.softmax(s.float(), dim=-1).to(x.dtype) @ v
-            return self.wo(o.transpose(1, 2).reshape(B, T, hidden))
+            q = self.wq(x).view(B, T, heads, hd)
+            k = self.wk(x).view(B, T, heads, hd)
+            v = self.wv(x).view(B, T, heads, hd)
+            q, k = rotary(q, k, self.freqs_cis[:T])
+            q, k, v = q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2)
+            s = (q @ k.transpose(-2, -1)) / (hd ** 0.5)
+            s = s.masked_fill(self.mask[:T, :T] == 0, float("-inf"))
+            out = F.softmax(s, dim=-1) @ v
+            return self.wo(out.transpose(1, 2).contiguous().view(B, T, -1))
 
-    class Block(nn.Module):
+    class MLP(nn.Module):  # LlamaMLP, LLaMA.py:52-60
         def __init__(self):
             super().__init__()
-            self.attn = Attn()
-            self.gate = nn.Linear(hidden, inter, bias=False)
-            self.up = nn.Linear(hidden, inter, bias=False)
-            self.down = nn.Linear(inter, hidden, bias=False)
-            self.n1 = RMSNorm()
-            self.n2 = RMSNorm()
+            self.gate_proj = nn.Linear(hidden, inter, bias=False)
+            self.up_proj = nn.Linear(hidden, inter, bias=False)
+            self.down_proj = nn.Linear(inter, hidden, bias=False)
 
         def forward(self, x):
-            x = x + self.attn(self.n1(x))
-            h = self.n2(x)
-            return x + self.down(F.silu(self.gate(h)) * self.up(h))
+            return self.down_proj(F.silu(self.gate_proj(x)) * self.up_proj(x))
 
-    class LLaMA(nn.Module):
+    class Block(nn.Module):  # LlamaBlock, LLaMA.py:63-75
         def __init__(self):
             super().__init__()
-            self.emb = nn.Embedding(vocab, hidden)
+            self.attention = Attn()
+            self.feed_forward = MLP()
+            self.attention_norm = RMSNorm()
+            self.ffn_norm = RMSNorm()
+
+        def forward(self, x):
+            x = x + self.attention(self.attention_norm(x))
+            return x + self.feed_forward(self.ffn_norm(x))
+
+    class LLaMA(nn.Module):  # CharLLaMA, LLaMA.py:78-98
+        def __init__(self):
+            super().__init__()
+            self.token_embedding = nn.Embedding(vocab, hidden)
             self.layers = nn.Sequential(*[Block() for _ in range(layers)])
             self.norm = RMSNorm()
-            self.head = nn.Linear(hidden, vocab, bias=False)
+            self.lm_head = nn.Linear(hidden, vocab, bias=False)
             for m in self.modules():
                 if isinstance(m, (nn.Linear, nn.Embedding)):
                     nn.init.normal_(m.weight, 0.0, 0.02)
 
         def forward(self, tokens):
-            return self.head(self.norm(self.layers(self.emb(tokens))))
+            x = self.layers(self.token_embedding(tokens))
+            return self.lm_head(self.norm(x))
 
     m = LLaMA().to(device)
     if dtype is not None:

@@ -490,10 +490,12 @@ def scenario_gpt_train(orion):
     from kernel_intercept_b200 import harness
     torch.backends.cuda.matmul.allow_tf32 = False
     torch.manual_seed(0)
-    m = harness.make_gpt(device="cuda")
+    # dropout off: the three steps compared must see the same masks
+    m = harness.make_gpt(device="cuda", dropout=0.0)
     tok = torch.randint(0, 32000, (16, 256), device="cuda")
     tgt = torch.randint(0, 32000, (16, 256), device="cuda")
-    names = ["lm.weight", "blocks.0.heads.0.query.weight", "blocks.5.l1.weight", "tok.weight"]
+    names = ["lm_head.weight", "blocks.0.mha.heads.0.query.weight", "blocks.5.ff.l1.weight",
+             "token_embedding.weight"]
 
     def step(model):
         model.zero_grad(set_to_none=True)
