@@ -17,7 +17,10 @@ memory (small enough for a multi-pass profiler capture):
   wgrad3_2    the same layer's backward filter (dw from x and dy)
   vgg16_convs the 13 VGG16 convolution layers, batch 32, forward, in order
   gemm_f32    4096^3 fp32 SGEMM (3xTF32 with pre-split operands)
-  gemm_bf16   2048 x 4096 x 2048 bf16 GemmEx (a LLaMA-7B query projection)
+  gemm_bf16   2048 x 4096 x 2048 bf16 GemmEx (the hidden-2048 LLaMA's query
+              projection at 4096 tokens)
+  gemm_scores the same model's attention scores: 64 x (1024 x 1024 x 128) bf16
+              GemmStridedBatchedEx (q k^T, K = head width)
   gemm_fc6    VGG16 fc6 at batch 32: 4096 x 32 x 25088 fp32 SGEMM (TN), weights
               411 MB
   bn_train    batch-norm training forward, spatial, 32 x 256 x 56 x 56
@@ -31,7 +34,7 @@ import os
 import sys
 
 CASES = ("conv3_2", "conv1_2", "dgrad3_2", "wgrad3_2", "vgg16_convs", "gemm_f32", "gemm_bf16",
-         "gemm_fc6", "bn_train", "hp_step")
+         "gemm_scores", "gemm_fc6", "bn_train", "hp_step")
 
 # VGG16 convolution stack: (in channels, out channels, spatial size)
 VGG16_CONVS = [(3, 64, 224), (64, 64, 224), (64, 128, 112), (128, 128, 112),
@@ -95,6 +98,14 @@ def _direct(case, reps):
         calls.append(lambda: kx.gemm_ex(ex, 1, 0, m, n_, k, 1.0, a.data_ptr(), kx.R_16BF, k,
                                         b.data_ptr(), kx.R_16BF, k, 0.0, c_.data_ptr(),
                                         kx.R_16BF, m))
+    elif case == "gemm_scores":
+        batch, t, hd = 64, 1024, 128
+        q = torch.randn(batch, t, hd, device=dev, dtype=torch.bfloat16)
+        k_ = torch.randn(batch, t, hd, device=dev, dtype=torch.bfloat16)
+        s_ = torch.empty(batch, t, t, device=dev, dtype=torch.bfloat16)
+        calls.append(lambda: kx.gemm_strided_batched_ex(
+            ex, 1, 0, t, t, hd, 1.0, k_.data_ptr(), kx.R_16BF, hd, t * hd, q.data_ptr(),
+            kx.R_16BF, hd, t * hd, 0.0, s_.data_ptr(), kx.R_16BF, t, t * t, batch))
     elif case == "bn_train":
         n, c, h, w_ = 32, 256, 56, 56
         x = torch.randn(n, c, h, w_, device=dev)
