@@ -465,6 +465,14 @@ def run_group(args):
     if rank != 0:
         return 0
     be_totals = {}
+    # BE work retained, over all BE clients: captured FLOPs per second (each
+    # client's iterations x its FLOPs per step) with HP against without
+    for key, solo_key in (("retention", "solo_iters_per_s"),
+                          ("paced_retention", "solo_iters_per_s")):
+        run_key = "iters_per_s" if key == "retention" else "paced_iters_per_s"
+        num = sum((b[run_key] or 0.0) * c.flops for b, c in zip(be, bes))
+        den = sum((b[solo_key] or 0.0) * c.flops for b, c in zip(be, bes))
+        be_totals[f"flop_{key}"] = round(num / den, 4) if den else None
     for b, c in zip(be, bes):
         be_totals[f"{c.unit}_per_s"] = be_totals.get(f"{c.unit}_per_s", 0.0) + \
             b[f"{c.unit}_per_s"] * world
@@ -484,7 +492,8 @@ def run_group(args):
                    "gil_switch_ms": round(sys.getswitchinterval() * 1e3, 3),
                    "gc_frozen": bool(args.gc_freeze), "host_cores_per_rank": pinned},
         "hp": hp_block,
-        "be": be, "be_total": {k: round(v, 1) for k, v in be_totals.items()},
+        "be": be, "be_total": {k: (round(v, 4) if "retention" in k else round(v, 1))
+                               for k, v in be_totals.items() if v is not None},
         "roofline": roof, "roofline_hp_solo": roof_solo, "ops": op_table(kr["cont_recs"]),
         "cpu_baseline": cpu, "clocks": kr["clocks"], "gpu_launches": int(kr["launches"]),
         "captured": stats,

@@ -209,7 +209,9 @@ bool Scheduler::init(int num_clients, const SchedulerConfig& config) {
   // HP flag shared with BE kernels (pinned, device-mapped)
   int* h = nullptr;
   int* d = nullptr;
-  if (kx_host_flags_alloc(2, &h, &d) != KX_OK) {
+  // [0] = HP flag; [c] = done flag of BE client c's stoppable op (one per
+  // client: BE workers relaunch their own ops independently)
+  if (kx_host_flags_alloc(1 + MAX_CLIENTS, &h, &d) != KX_OK) {
     LOG_ERROR("cannot allocate the HP flag");
     return false;
   }
@@ -502,11 +504,17 @@ cudaError_t Scheduler::execute_operation(OperationPtr op, cudaStream_t fallback)
   // allowed to finish their op.
   const int keep = be_keep_sms_.load();
   if (!be && !isolated_ && keep > 0 && keep < config_.num_sms) pol.sm_quota = config_.num_sms - keep;
-  const bool can_stop = be && !isolated_ && be_keep_sms_.load() <= 0;
+  // BE ops stop entirely under HP load when BE keeps no SMs; only the
+  // persistent GEMM / convolution kernels report through the done flag
+  // whether they finished or stopped (batch norm runs to completion)
+  const bool persistent = op->type != OperationType::CUDNN_BATCHNORM_FWD &&
+                          op->type != OperationType::CUDNN_BATCHNORM_BWD &&
+                          op->type != OperationType::CUDNN_BATCHNORM_INF;
+  const bool can_stop = be && !isolated_ && be_keep_sms_.load() <= 0 && persistent;
   if (be && !isolated_) pol.yield_flag = hp_flag_devmem_ ? hp_flag_devmem_ : hp_flag_dev_;
   if (can_stop) {
-    hp_flag_host_[1] = -1;
-    pol.done_flag = hp_flag_dev_ + 1;
+    hp_flag_host_[c] = -1;
+    pol.done_flag = hp_flag_dev_ + c;
   }
   cudaEvent_t ev_start = nullptr, ev_end = nullptr;
   const bool profiling = g_profiler.active();
@@ -520,12 +528,12 @@ cudaError_t Scheduler::execute_operation(OperationPtr op, cudaStream_t fallback)
   while (rc == KX_OK && can_stop) {
     // BE op that may have stopped entirely: wait for it, then resume once HP is idle.
     ORION_REAL(cudart, cudaStreamSynchronize)(pol.stream);
-    if (hp_flag_host_[1] == 1) break;
+    if (hp_flag_host_[c] == 1) break;
     st.yields.fetch_add(1);
     const int64_t deadline = mono_ns() + wait_timeout_ns();
     while (hp_flag_host_[0] != 0 && running_.load() && mono_ns() < deadline)
       std::this_thread::sleep_for(std::chrono::microseconds(20));
-    hp_flag_host_[1] = -1;
+    hp_flag_host_[c] = -1;
     rc = dispatch_dense(*op, pol);
   }
   tl_in_scheduler_execution = false;

@@ -267,6 +267,55 @@ def scenario_hpbe(orion):
             "hp_p50_ms": harness.percentile(hp.latencies_ms, 0.5), "be_iters": be.iters}
 
 
+def scenario_hpbe2(orion):
+    """HP (small GEMMs) against two BE clients (a large GEMM; a convolution
+    with batch norm in training) with BE keeping no SMs under HP load
+    (KX_BE_KEEP_SMS=0, set by the parent): BE GEMMs and convolutions stop at
+    tile boundaries while HP works and are relaunched by their own worker
+    (each BE client has its own done flag); results stay exact."""
+    import torch
+    import torch.nn.functional as F
+
+    from kernel_intercept_b200 import harness
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cudnn.allow_tf32 = False
+    g = torch.Generator(device="cuda").manual_seed(4)
+    a = torch.randn(256, 1024, device="cuda", generator=g)
+    b = torch.randn(1024, 1024, device="cuda", generator=g)
+    A = torch.randn(4096, 4096, device="cuda", generator=g)
+    x = torch.randn(16, 64, 56, 56, device="cuda", generator=g)
+    w = torch.randn(128, 64, 3, 3, device="cuda", generator=g) * 0.05
+    gamma = torch.rand(128, device="cuda", generator=g) + 0.5
+    beta_ = torch.randn(128, device="cuda", generator=g)
+
+    def conv_bn():
+        rm, rv = torch.zeros(128, device="cuda"), torch.ones(128, device="cuda")
+        y = F.conv2d(x, w, padding=1)
+        return F.batch_norm(y, rm, rv, gamma, beta_, training=True, momentum=0.1), rm, rv
+
+    assert orion.orion_init_scheduler(3) == 0
+    orion.orion_set_capture(0)
+    ref_hp, ref_be1, ref_be2 = a @ b, A @ A, conv_bn()
+    torch.cuda.synchronize()
+    orion.orion_start_scheduler_thread()
+    orion.orion_set_capture(1)
+    outs = {"hp": [], "be1": [], "be2": []}
+    harness.run_clients(orion, lambda: outs["hp"].append(a @ b),
+                        [lambda: outs["be1"].append(A @ A),
+                         lambda: outs["be2"].append(conv_bn())],
+                        hp_steps=60, hp_warmup=2)
+    orion.orion_set_capture(0)
+    stats = {c: orion.stats(c) for c in (0, 1, 2)}
+    orion.orion_stop_scheduler()
+    torch.cuda.synchronize()
+    errs = {"hp": max(rel(o, ref_hp) for o in outs["hp"]),
+            "be1": max(rel(o, ref_be1) for o in outs["be1"]),
+            "be2_y": max(rel(o[0], ref_be2[0]) for o in outs["be2"]),
+            "be2_rm": max(rel(o[1], ref_be2[1]) for o in outs["be2"]),
+            "be2_rv": max(rel(o[2], ref_be2[2]) for o in outs["be2"])}
+    return {"errors": errs, "stats": stats, "be_iters": [len(outs["be1"]), len(outs["be2"])]}
+
+
 def scenario_trace(orion):
     """Capture trace of an HP + BE run: per-client issue instants, worker
     execution spans, blocking waits and HP-flag markers, as Chrome-trace JSON;

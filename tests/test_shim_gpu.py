@@ -139,6 +139,18 @@ def test_hp_be_clients_contend():
     assert res["be_iters"] >= 1
 
 
+def test_be_clients_stop_and_resume_under_hp():
+    """Two BE clients whose GEMMs and convolutions stop entirely while HP works
+    (KX_BE_KEEP_SMS=0) and are relaunched from their tile queues: every
+    result exact, batch norm (which cannot stop) applied once per call."""
+    res = run_child("hpbe2", extra_env={"KX_BE_KEEP_SMS": "0"})
+    for c in ("0", "1", "2"):
+        assert res["stats"][c]["errors"] == 0, res
+    for name, err in res["errors"].items():
+        assert err <= F32_TOL, (name, err, res)
+    assert min(res["be_iters"]) >= 1, res
+
+
 def test_capture_keeps_op_order_and_counts():
     """The interposer's op log: a GPT training step through the real
     libraries and the same step captured on the kx kernels issue the same
