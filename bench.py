@@ -550,6 +550,7 @@ def run_microbench(args):
     assert orion.orion_init_scheduler(2) == 0
     orion.orion_set_capture(0)
     orion.orion_start_scheduler_thread()
+    keep0 = orion.orion_get_be_keep_sms()
     kxlib = kx.lib()
     launches = 0
     clocks = Clocks(local)
@@ -608,7 +609,7 @@ def run_microbench(args):
                                     (be_solo.iters / be_solo.elapsed_ms), 4),
                 "hp_ops": hp_c.iters})
         orion.orion_set_sm_budgets(0, 0)
-        orion.orion_set_be_keep_sms(8)
+        orion.orion_set_be_keep_sms(keep0)
         orion.orion_set_capture(0)
         out[dtype_name] = {"hp_solo_op_p50_us": rnd(harness.percentile(solo.latencies_ms, 0.5) * 1e3, 1),
                            "hp_solo_op_p99_us": rnd(harness.percentile(solo.latencies_ms, 0.99) * 1e3, 1),

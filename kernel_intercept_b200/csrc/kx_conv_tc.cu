@@ -421,6 +421,8 @@ int launch_conv_tc(const Exec& e, const ConvShape& g, const ConvShape& t, const 
   // 32 channels, 1}, at least 16 bytes wide.
   CUtensorMap md = ma;
   p.tma_store = 0;
+  p.wide16 = 0;
+  p.seg_kb = seg_kb_default();
   if (p.splits == 1 && !tma_store_disabled()) {
     if (pl.im2col) {
       if (pq % 4 == 0 && encode_map_3d(&md, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, y, pq, g.K, g.N,
@@ -620,6 +622,8 @@ int launch_wgrad(const Exec& e, const ConvShape& g, const ConvShape& t, bool fol
   if (static_cast<long long>(p.tiles_per_batch) > 0x7fffffffLL) return KX_ERR_UNSUPPORTED;
   p.num_tiles = p.tiles_per_batch;
   p.tma_store = 0;
+  p.wide16 = 0;
+  p.seg_kb = seg_kb_default();
   auto kern = kx_gemm_tc_kernel<Cfg, true>;
   static bool attr_set[64] = {false};
   const DeviceInfo& di = device_info();

@@ -125,6 +125,11 @@ struct GemmParams {
   // Pipeline diagnostics (nullable): per CTA kPipeStats clock64 counters of
   // the time each role spends waiting (see PipeStat).
   unsigned long long* pipe_stats;
+  // 1: 16-bit D stored 32 rows x 64 columns per TMA store (map tmD's box is
+  // {32, 64}); only with tma_store, for plain GEMMs.
+  int wide16;
+  // 3xTF32: k-blocks per TMEM accumulator segment (0 = Cfg::SEG)
+  int seg_kb;
   // 1: the epilogue writes D through shared memory and TMA stores (map tmD:
   // {m, n, batch} for GEMMs, {Q, P, K, N} for box-tiled convolutions,
   // {P*Q, K, N} for im2col convolutions); 0: one st.global per element
@@ -512,6 +517,10 @@ __global__ void __launch_bounds__(256, 1)
   const long long t_ready = clock64();
 
   WaitCtl wc{&sb->abort_flag, p.err_word, p.timeout_ns};
+  // k-blocks per accumulator segment (3xTF32: the tensor core's fp32
+  // accumulation rounds toward zero, so each TMEM accumulator covers a short
+  // K range and the epilogue folds segments in round-to-nearest registers)
+  const int seg = Cfg::PROMOTE ? (p.seg_kb > 0 ? p.seg_kb : Cfg::SEG) : Cfg::SEG;
   unsigned long long st_a = 0, st_b = 0, st_c = 0, st_d = 0, st_e = 0, st_f = 0;  // per role
   const bool stats = p.pipe_stats != nullptr;
 
@@ -826,7 +835,7 @@ __global__ void __launch_bounds__(256, 1)
             }
             tc_fence_after();
             const uint32_t d_tmem = tmem + a * Cfg::ACC_COLS;
-            const int kend = (nkb - kb > Cfg::SEG) ? kb + Cfg::SEG : nkb;
+            const int kend = (nkb - kb > seg) ? kb + seg : nkb;
             const int kfirst = kb;
             for (; kb < kend; ++kb) {
               if (kb == 0 || tr == 0) {
@@ -886,7 +895,7 @@ __global__ void __launch_bounds__(256, 1)
           }
           tc_fence_after();
           const uint32_t d_tmem = tmem + a * Cfg::ACC_COLS;
-          const int kend = (nkb - kb > Cfg::SEG) ? kb + Cfg::SEG : nkb;
+          const int kend = (nkb - kb > seg) ? kb + seg : nkb;
           const int kfirst = kb;
           const long long t_k = stats ? clock64() : 0;
           for (; kb < kend; ++kb, ++it) {
@@ -1047,7 +1056,7 @@ __global__ void __launch_bounds__(256, 1)
       decode_tile(tile, p, b, ks, mb, nb);
       if constexpr (PAIR) mb = 2 * mb + static_cast<int>(rank);  // this CTA's 128 rows
       tile_k_range(tile, p, kb0, nkb);
-      const int nseg = Cfg::PROMOTE ? (nkb + Cfg::SEG - 1) / Cfg::SEG : 1;
+      const int nseg = Cfg::PROMOTE ? (nkb + seg - 1) / seg : 1;
       int row = mb * Cfg::BM + q * 32 + static_cast<int>(lane);
       bool row_ok = row < p.m;
       size_t d_base = static_cast<size_t>(b) * p.strideD + row;
@@ -1250,17 +1259,55 @@ __global__ void __launch_bounds__(256, 1)
           else
             emit(c0, f);
         };
-        tmem_ld_32x32b_x32(tbase, va);
-        tmem_ld_wait();
+        if (p.wide16 && warp_tma && plain_epi && Cfg::BN % 64 == 0) {
+          // 16-bit D, alpha only: 64 columns (4 KB) per staging buffer and per
+          // TMA store, half the per-store fences, waits and issues
 #pragma unroll 1
-        for (int c0 = 0; c0 < Cfg::BN; c0 += 64) {
-          const bool has_b = c0 + 32 < Cfg::BN;
-          if (has_b) tmem_ld_32x32b_x32(tbase + c0 + 32, vb);
-          out(c0, va);
+          for (int c0 = 0; c0 < Cfg::BN; c0 += 64) {
+            tmem_ld_32x32b_x32(tbase + c0, va);
+            tmem_ld_32x32b_x32(tbase + c0 + 32, vb);
+            tmem_ld_wait();
+            tmem_regs_ready(va);
+            tmem_regs_ready(vb);
+            uint8_t* buf = smem + Cfg::EPI_OFF + (q * 2 + (epi_chunk & 1u)) * 4096;
+            ++epi_chunk;
+            if (lane == 0) bulk_wait_group_read<1>();
+            __syncwarp();
+            if (p.d_type == DT_BF16) {
+              __nv_bfloat16* hb = reinterpret_cast<__nv_bfloat16*>(buf);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                hb[j * 32 + lane] = __float2bfloat16_rn(alpha * __uint_as_float(va[j]));
+                hb[(32 + j) * 32 + lane] = __float2bfloat16_rn(alpha * __uint_as_float(vb[j]));
+              }
+            } else {
+              __half* hh = reinterpret_cast<__half*>(buf);
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                hh[j * 32 + lane] = __float2half_rn(alpha * __uint_as_float(va[j]));
+                hh[(32 + j) * 32 + lane] = __float2half_rn(alpha * __uint_as_float(vb[j]));
+              }
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_3d(&tmD, smem_addr(buf), mb * Cfg::BM + q * 32, nb * Cfg::BN + c0, b);
+              bulk_commit_group();
+            }
+          }
+        } else {
+          tmem_ld_32x32b_x32(tbase, va);
           tmem_ld_wait();
-          if (c0 + 64 < Cfg::BN) tmem_ld_32x32b_x32(tbase + c0 + 64, va);
-          if (has_b) out(c0 + 32, vb);
-          tmem_ld_wait();
+#pragma unroll 1
+          for (int c0 = 0; c0 < Cfg::BN; c0 += 64) {
+            const bool has_b = c0 + 32 < Cfg::BN;
+            if (has_b) tmem_ld_32x32b_x32(tbase + c0 + 32, vb);
+            out(c0, va);
+            tmem_ld_wait();
+            if (c0 + 64 < Cfg::BN) tmem_ld_32x32b_x32(tbase + c0 + 64, va);
+            if (has_b) out(c0 + 32, vb);
+            tmem_ld_wait();
+          }
         }
         if (stats) st_c += static_cast<unsigned long long>(clock64() - t_emit);
         tc_fence_before();

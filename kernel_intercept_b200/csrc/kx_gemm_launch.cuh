@@ -157,6 +157,8 @@ int launch_gemm_tc(const Exec& e, const TcProblem& pr, GemmParams p) {
   // D through TMA stores when D is TMA-addressable (split-K writes partials)
   CUtensorMap md = ma;
   p.tma_store = 0;
+  p.wide16 = 0;
+  p.seg_kb = seg_kb_default();
   if (p.splits == 1 && !tma_store_disabled()) {
     const int des = p.d_type == DT_F32 ? 4 : 2;
     const CUtensorMapDataType ddt = p.d_type == DT_F32    ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
@@ -164,9 +166,14 @@ int launch_gemm_tc(const Exec& e, const TcProblem& pr, GemmParams p) {
                                                           : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     const bool aligned = (p.ldd * des) % 16 == 0 &&
                          (pr.batch <= 1 || p.strideD == 0 || (p.strideD * des) % 16 == 0);
+    // 16-bit D of a 16-bit GEMM: boxes of 32 rows x 64 columns (4 KB, one
+    // staging buffer); the 3xTF32 epilogue stores 32-column chunks
+    const uint32_t box_cols = (des == 2 && BN % 64 == 0 && !Cfg::PROMOTE) ? 64 : 32;
     if (aligned && encode_map_3d(&md, ddt, des, p.D, pr.m, pr.n, pr.batch, p.ldd, p.strideD, 32,
-                                 32, CU_TENSOR_MAP_SWIZZLE_NONE))
+                                 box_cols, CU_TENSOR_MAP_SWIZZLE_NONE)) {
       p.tma_store = 1;
+      p.wide16 = box_cols == 64 ? 1 : 0;
+    }
   }
   int grid = persistent_grid(e, p.num_tiles * (PAIR ? 2 : 1));
   if (PAIR) {

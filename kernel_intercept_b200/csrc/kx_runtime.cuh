@@ -56,6 +56,19 @@ inline bool tma_store_disabled() {
   return off;
 }
 
+// 3xTF32 accumulator segment length in k-blocks (KX_SEG_KB, default 2 =
+// 64 of K for tf32 k-blocks of 32): the tensor core's fp32 accumulation
+// rounds toward zero, and the bias of one accumulator grows with its K
+// length; it is the same sign in every layer of a network, so it compounds.
+inline int seg_kb_default() {
+  static const int v = [] {
+    const char* s = std::getenv("KX_SEG_KB");
+    const int x = s != nullptr ? std::atoi(s) : 2;
+    return x >= 1 && x <= 64 ? x : 2;
+  }();
+  return v;
+}
+
 // KX_SPLITK=0 turns split-K off (every output tile then runs its whole K).
 inline bool split_k_disabled() {
   static const bool off = [] {

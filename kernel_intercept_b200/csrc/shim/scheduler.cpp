@@ -228,9 +228,12 @@ bool Scheduler::init(int num_clients, const SchedulerConfig& config) {
     ORION_REAL(cudart, cudaDeviceGetStreamPriorityRange)(&lo, &hi);
     ORION_REAL(cudart, cudaStreamCreateWithPriority)(&flag_stream_, cudaStreamNonBlocking, hi);
   }
-  // 8 SMs: measured on VGG16-HP / GPT-BE, the largest share BE can keep
-  // while HP p99 stays within 1.1x of solo with HP back to back
-  int keep = 8;
+  // 0: BE GEMMs / convolutions stop at their next tile boundary while HP
+  // works and are relaunched from their tile queues once it idles.  Measured
+  // on the LLaMA-HP / VGG16 + GPT-BE group: paced HP p99 1.07x solo with BE
+  // keeping 0.72 / 0.66 of its rate, against 1.00x and 0.49 / 2.3 with 4 SMs
+  // kept per BE client (an op caught by HP then finishes on those 4 SMs).
+  int keep = 0;
   if (const char* s = std::getenv("KX_BE_KEEP_SMS")) keep = std::atoi(s);
   be_keep_sms_.store(std::max(0, std::min(keep, sms)));
   if (const char* s = std::getenv("KX_HP_HOLD_US")) hp_hold_ns_ = std::max(0LL, std::atoll(s)) * 1000;
