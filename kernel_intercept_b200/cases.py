@@ -24,8 +24,10 @@ memory (small enough for a multi-pass profiler capture):
   gemm_fc6    VGG16 fc6 at batch 32: 4096 x 32 x 25088 fp32 SGEMM (TN), weights
               411 MB
   bn_train    batch-norm training forward, spatial, 32 x 256 x 56 x 56
-  hp_step     one batch-32 VGG16 inference step (the HP client of the
-              benchmark) through the LD_PRELOAD interposer and the scheduler
+  hp_step     one batch-32 VGG16 inference step (the HP client of
+              configuration 1) through the LD_PRELOAD interposer and the scheduler
+  hp_step_llama one batch-4 x 1024 LLaMA-style bf16 inference step (the HP
+              client of configuration 4), the same way
 """
 from __future__ import annotations
 
@@ -34,7 +36,7 @@ import os
 import sys
 
 CASES = ("conv3_2", "conv1_2", "dgrad3_2", "wgrad3_2", "vgg16_convs", "gemm_f32", "gemm_bf16",
-         "gemm_scores", "gemm_fc6", "bn_train", "hp_step")
+         "gemm_scores", "gemm_fc6", "bn_train", "hp_step", "hp_step_llama")
 
 # VGG16 convolution stack: (in channels, out channels, spatial size)
 VGG16_CONVS = [(3, 64, 224), (64, 64, 224), (64, 128, 112), (128, 128, 112),
@@ -126,9 +128,10 @@ def _direct(case, reps):
     return kx.last_kernel_name()
 
 
-def _hp_step(reps):
-    """One untimed and `reps` more batch-32 VGG16 inference steps as the HP
-    client of the scheduler, with every convolution and GEMM captured."""
+def _hp_step(reps, model="vgg16"):
+    """One untimed and `reps` more HP inference steps (batch-32 VGG16, or the
+    batch-4 x 1024 bf16 LLaMA-style decoder) as the HP client of the
+    scheduler, with every convolution and GEMM captured."""
     import torch
 
     from . import harness, kx
@@ -138,12 +141,16 @@ def _hp_step(reps):
     torch.backends.cudnn.benchmark = False
     torch.manual_seed(0)
     orion = harness.Orion()
-    vgg = harness.make_vgg16(dev).eval()
-    img = torch.randn(32, 3, 224, 224, device=dev)
+    if model == "vgg16":
+        net = harness.make_vgg16(dev).eval()
+        inp = torch.randn(32, 3, 224, 224, device=dev)
+    else:
+        net = harness.make_llama(device=dev, dtype=torch.bfloat16).eval()
+        inp = torch.randint(0, 32000, (4, 1024), device=dev)
 
     def step():
         with torch.no_grad():
-            vgg(img)
+            net(inp)
 
     assert orion.orion_init_scheduler(2) == 0, "orion_init_scheduler failed"
     orion.orion_set_capture(0)
@@ -167,14 +174,14 @@ def main(argv=None):
     ap.add_argument("case", choices=CASES)
     ap.add_argument("--reps", type=int, default=1)
     args = ap.parse_args(argv)
-    if args.case == "hp_step":
+    if args.case in ("hp_step", "hp_step_llama"):
         from . import harness
         if not harness.preloaded():
             env = harness.preload_env({"ORION_LOG_LEVEL": os.environ.get("ORION_LOG_LEVEL",
                                                                           "WARN")})
             os.execve(sys.executable, [sys.executable, "-m", "kernel_intercept_b200.cases"]
                       + sys.argv[1:], env)
-        name = _hp_step(args.reps)
+        name = _hp_step(args.reps, "vgg16" if args.case == "hp_step" else "llama")
     else:
         name = _direct(args.case, args.reps)
     print("ok", args.case, name, flush=True)
