@@ -443,6 +443,10 @@ __global__ void __launch_bounds__(256, 1)
   constexpr int R = Cfg::RING;
   // CTA pair (Cfg::PAIR): rank 0 leads (tile ids, MMAs), rank 1 follows
   constexpr bool PAIR = Cfg::PAIR;
+  // 16-bit pairs: the follower's TMA loads complete on the leader's stage
+  // barriers (.cta_group::2 loads); 3xTF32 pairs (convolutions) forward each
+  // landed stage through the follower's MMA thread instead
+  constexpr bool DIRECT = PAIR && !Cfg::SPLIT;
   const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
   const bool leader = rank == 0;
   // in-kernel 3xTF32 split (warps 2-3) unless the low parts come by TMA
@@ -679,9 +683,17 @@ __global__ void __launch_bounds__(256, 1)
           }
           const long long t_iss = stats ? clock64() : 0;
           const uint32_t fb = smem_addr(&sb->full[s]);
-          // 3xTF32 with pre-split operands: the low parts arrive by TMA beside
-          // the high parts.
-          mbar_arrive_expect_tx(fb, Cfg::LOAD_BYTES * (lo_by_tma ? 2 : 1));
+          // 16-bit CTA pair: both CTAs' loads complete on the leader's stage
+          // barrier, which expects the bytes of both (the follower arrives on
+          // nothing and the leader's MMA waits on one barrier)
+          const uint32_t fb_peer = DIRECT ? mapa_shared(fb, 0u) : fb;
+          if constexpr (DIRECT) {
+            if (leader) mbar_arrive_expect_tx(fb, 2 * Cfg::LOAD_BYTES);
+          } else {
+            // 3xTF32 with pre-split operands: the low parts arrive by TMA
+            // beside the high parts.
+            mbar_arrive_expect_tx(fb, Cfg::LOAD_BYTES * (lo_by_tma ? 2 : 1));
+          }
           auto load_a = [&](uint32_t sa, const CUtensorMap* map) {
             if constexpr (CONV) {
               if (p.cv_wgrad) {  // dy rows k = mb*128.., 32 pixels
@@ -695,7 +707,10 @@ __global__ void __launch_bounds__(256, 1)
                             cv_h0 + rr * p.cv_dil_h, cv_img);
               }
             } else if (!Cfg::A_MN) {
-              tma_load_3d(sa, map, fb, kb * Cfg::BK, mb * Cfg::BM, ba);
+              if (DIRECT && !leader)
+                tma_load_3d_pair(sa, map, fb_peer, kb * Cfg::BK, mb * Cfg::BM, ba);
+              else
+                tma_load_3d(sa, map, fb, kb * Cfg::BK, mb * Cfg::BM, ba);
             } else if (p.a_single) {
               tma_load_4d(sa, map, fb, 0, kb * Cfg::BK, mb * (Cfg::BM / Cfg::CHUNK), ba);
             } else {
@@ -716,7 +731,10 @@ __global__ void __launch_bounds__(256, 1)
                                    wg_img, static_cast<uint16_t>(wg_offw),
                                    static_cast<uint16_t>(wg_offh));
             } else if (!Cfg::B_MN) {
-              tma_load_3d(sbb, map, fb, kb * Cfg::BK, n0, bb);
+              if (DIRECT && !leader)
+                tma_load_3d_pair(sbb, map, fb_peer, kb * Cfg::BK, n0, bb);
+              else
+                tma_load_3d(sbb, map, fb, kb * Cfg::BK, n0, bb);
             } else if (p.b_single) {
               tma_load_4d(sbb, map, fb, 0, kb * Cfg::BK, n0 / Cfg::CHUNK, bb);
             } else {
@@ -769,6 +787,13 @@ __global__ void __launch_bounds__(256, 1)
           mbar_wait(smem_addr(&sb->full[j % Cfg::SA]), (j / Cfg::SA) & 1, drain);
         for (uint32_t j = ib > static_cast<uint32_t>(Cfg::SB) ? ib - Cfg::SB : 0; j < ib; ++j)
           mbar_wait(smem_addr(&sb->full[Cfg::SA + j % Cfg::SB]), (j / Cfg::SB) & 1, drain);
+      } else if (DIRECT && !leader) {
+        // the follower's loads complete on the leader's barriers: they have
+        // landed once the leader's MMAs consumed them, i.e. once the commit
+        // that frees each of the last S stages arrived here
+        const uint32_t first = it > static_cast<uint32_t>(S) ? it - S : 0;
+        for (uint32_t j = first; j < it; ++j)
+          mbar_wait(smem_addr(&sb->empty[j % S]), (j / S) & 1, drain);
       } else {
         const uint32_t first = it > static_cast<uint32_t>(S) ? it - S : 0;
         for (uint32_t j = first; j < it; ++j)
@@ -787,6 +812,7 @@ __global__ void __launch_bounds__(256, 1)
         const int tile = sb->ring[r];
         mbar_arrive_cluster(leader_bar(&sb->ring_empty[r]));
         if (tile < 0) break;
+        if constexpr (DIRECT) continue;  // loads signal the leader themselves
         int kb0, nkb;
         tile_k_range(tile, p, kb0, nkb);
         for (int kb = 0; kb < nkb; ++kb, ++it) {
@@ -910,7 +936,7 @@ __global__ void __launch_bounds__(256, 1)
             }
             const uint32_t wb = convert ? smem_addr(&sb->conv[s]) : smem_addr(&sb->full[s]);
             if (!timed_wait(wb, ph, wc, stats ? &st_a : nullptr) ||
-                (PAIR && !mbar_wait_cluster(smem_addr(&sb->pair_full[s]), ph, wc))) {
+                (PAIR && !DIRECT && !mbar_wait_cluster(smem_addr(&sb->pair_full[s]), ph, wc))) {
               ok = false;
               break;
             }

@@ -111,6 +111,19 @@ KX_DEV void tma_load_3d(uint32_t dst, const void* map, uint32_t bar, int c0, int
       : "memory");
 }
 
+// 3-D tile load into this CTA's shared memory whose completion is counted on
+// an mbarrier of the peer CTA of a CTA pair (`bar` is a shared::cluster
+// address from mapa): the follower of a 2-CTA tile signals the leader's
+// stage barrier directly.  No multicast.
+KX_DEV void tma_load_3d_pair(uint32_t dst, const void* map, uint32_t bar, int c0, int c1,
+                             int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      ".cta_group::2 [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(bar)
+      : "memory");
+}
+
 KX_DEV void tma_load_4d(uint32_t dst, const void* map, uint32_t bar, int c0, int c1, int c2,
                         int c3) {
   asm volatile(
