@@ -254,6 +254,10 @@ const char* kx_last_kernel_name(void);
  * For profile tables; 0 before the first such launch. */
 int kx_last_grid(void);
 
+/* cudaError_t (as int) behind the last KX_ERR_DEVICE status this thread got
+ * from the library; 0 before the first.  Diagnostics only. */
+int kx_last_cuda_error(void);
+
 /* Version string of the library. */
 const char* kx_version(void);
 

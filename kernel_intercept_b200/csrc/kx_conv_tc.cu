@@ -410,9 +410,9 @@ int launch_conv_tc(const Exec& e, const ConvShape& g, const ConvShape& t, const 
   static bool attr_set[64] = {false};
   const DeviceInfo& di = device_info();
   if (!attr_set[di.device & 63]) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             Cfg::SMEM_BYTES) != cudaSuccess)
-      return KX_ERR_DEVICE;
+    const cudaError_t ae = cudaFuncSetAttribute(
+        kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
+    if (ae != cudaSuccess) return device_error(ae);
     attr_set[di.device & 63] = true;
   }
   // y through TMA stores (16-byte rows needed).  im2col: {P*Q, K, N} map, a
@@ -449,9 +449,9 @@ int launch_conv_tc(const Exec& e, const ConvShape& g, const ConvShape& t, const 
   p.pipe_stats = pipe_stats_begin();
   note_launch();
   if (PAIR) {
-    if (launch_pair(kern, grid, Cfg::THREADS, Cfg::SMEM_BYTES, e.stream, ma, mb, malo, mblo, md,
-                    p) != cudaSuccess)
-      return KX_ERR_DEVICE;
+    const cudaError_t le = launch_pair(kern, grid, Cfg::THREADS, Cfg::SMEM_BYTES, e.stream, ma,
+                                       mb, malo, mblo, md, p);
+    if (le != cudaSuccess) return device_error(le);
   } else {
     kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, e.stream>>>(ma, mb, malo, mblo, md, p);
   }
@@ -628,9 +628,9 @@ int launch_wgrad(const Exec& e, const ConvShape& g, const ConvShape& t, bool fol
   static bool attr_set[64] = {false};
   const DeviceInfo& di = device_info();
   if (!attr_set[di.device & 63]) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             Cfg::SMEM_BYTES) != cudaSuccess)
-      return KX_ERR_DEVICE;
+    const cudaError_t ae = cudaFuncSetAttribute(
+        kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
+    if (ae != cudaSuccess) return device_error(ae);
     attr_set[di.device & 63] = true;
   }
   CUtensorMap md = ma;  // unused (no TMA stores)

@@ -202,8 +202,11 @@ struct GemmCfg {
       TAPR ? SA * 2 * TAPR_A_BYTES + SB * 2 * B_BYTES : STAGES * STAGE_BYTES;
   static constexpr int RING = 4;  // depth of the tile-id broadcast ring
   // TMEM columns of one accumulator buffer.  3xTF32 on one CTA keeps two
-  // BN-wide halves: [0, BN) = hi*hi + lo*hi and [BN, 2BN) = hi*lo (see the
-  // MMA issuer); a pair issues the three products into one BN-wide buffer.
+  // BN-wide halves: [0, BN) = hi*hi and [BN, 2BN) = hi*lo + lo*hi (see the
+  // MMA issuer).  The tensor core's fp32 accumulate truncates, so each add
+  // into the large half costs up to one ulp of the running sum; the small
+  // half is 2^-11 of it, and its truncations are negligible.  A pair issues
+  // the three products into one BN-wide buffer.
   static constexpr bool MERGED = SPLIT && !PAIR;
   static constexpr int ACC_COLS = MERGED ? 2 * BN : BN;
   static constexpr int TMEM_COLS = (2 * ACC_COLS) <= 32 ? 32 : (2 * ACC_COLS) <= 64 ? 64 : (2 * ACC_COLS) <= 128 ? 128 : (2 * ACC_COLS) <= 256 ? 256 : 512;
@@ -895,8 +898,8 @@ __global__ void __launch_bounds__(256, 1)
                 const uint64_t bd =
                     sdesc_sw128(b_hi + kk * 32, Cfg::B_LBO, Cfg::B_SBO, Cfg::B_LAYOUT);
                 const uint32_t acc = (kb > kfirst || kk > 0) ? 1u : 0u;
-                umma_tf32(d_tmem, ad, bd, Cfg::IDESC2, acc);  // hi x [B_hi; B_lo]
-                umma_tf32(d_tmem, adl, bd, Cfg::IDESC, 1u);   // lo x B_hi
+                umma_tf32(d_tmem, ad, bd, Cfg::IDESC2, acc);           // hi x [B_hi; B_lo]
+                umma_tf32(d_tmem + Cfg::BN, adl, bd, Cfg::IDESC, 1u);  // lo x B_hi
               }
               tc_commit(smem_addr(&sb->empty[Cfg::SA + sbi]));
               ++ib;
@@ -966,11 +969,12 @@ __global__ void __launch_bounds__(256, 1)
                 umma_tf32_pair(d_tmem, adl, bd, Cfg::IDESC, 1u);
               } else if constexpr (Cfg::AR == Arith::F32x3) {
                 // hi*hi and hi*lo in one N = 2*BN MMA over [B_hi; B_lo]
-                // (columns [0, BN) and [BN, 2BN)), then lo*hi into [0, BN):
-                // A_hi is read from shared memory once per k-step, not twice
+                // (columns [0, BN) and [BN, 2BN)), then lo*hi into [BN, 2BN):
+                // A_hi is read from shared memory once per k-step, not twice,
+                // and the large half takes one truncating add per k-step
                 const uint64_t adl = ad + (Cfg::A_BYTES >> 4);  // A_lo follows A
                 umma_tf32(d_tmem, ad, bd, Cfg::IDESC2, acc);
-                umma_tf32(d_tmem, adl, bd, Cfg::IDESC, 1u);
+                umma_tf32(d_tmem + Cfg::BN, adl, bd, Cfg::IDESC, 1u);
               } else if constexpr (Cfg::AR == Arith::TF32) {
                 umma_tf32(d_tmem, ad, bd, Cfg::IDESC, acc);
               } else {
@@ -1235,12 +1239,15 @@ __global__ void __launch_bounds__(256, 1)
               tmem_ld_32x32b_x32(tmem + a * Cfg::ACC_COLS + Cfg::BN + c * 32 + lane_off, w);
             tmem_ld_wait();
             tmem_regs_ready(v);
-#pragma unroll
-            for (int j = 0; j < 32; ++j) acc[c][j] += __uint_as_float(v[j]);
             if constexpr (Cfg::ACC_COLS == 2 * Cfg::BN) {
+              // small half first: one rounding of the segment's sum
               tmem_regs_ready(w);
 #pragma unroll
-              for (int j = 0; j < 32; ++j) acc[c][j] += __uint_as_float(w[j]);
+              for (int j = 0; j < 32; ++j)
+                acc[c][j] += __uint_as_float(v[j]) + __uint_as_float(w[j]);
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) acc[c][j] += __uint_as_float(v[j]);
             }
           }
           tc_fence_before();

@@ -123,9 +123,9 @@ int launch_gemm_tc(const Exec& e, const TcProblem& pr, GemmParams p) {
   static bool attr_set[64] = {false};
   const DeviceInfo& di = device_info();
   if (!attr_set[di.device & 63]) {
-    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             Cfg::SMEM_BYTES) != cudaSuccess)
-      return KX_ERR_DEVICE;
+    const cudaError_t ae = cudaFuncSetAttribute(
+        kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES);
+    if (ae != cudaSuccess) return device_error(ae);
     attr_set[di.device & 63] = true;
   }
   // Split-K when the output tiles cannot fill the CTAs the launch may use and
@@ -183,9 +183,9 @@ int launch_gemm_tc(const Exec& e, const TcProblem& pr, GemmParams p) {
   p.pipe_stats = pipe_stats_begin();
   note_launch();
   if (PAIR) {
-    if (launch_pair(kern, grid, Cfg::THREADS, Cfg::SMEM_BYTES, e.stream, ma, mb, malo, mblo, md,
-                    p) != cudaSuccess)
-      return KX_ERR_DEVICE;
+    const cudaError_t le = launch_pair(kern, grid, Cfg::THREADS, Cfg::SMEM_BYTES, e.stream, ma,
+                                       mb, malo, mblo, md, p);
+    if (le != cudaSuccess) return device_error(le);
   } else {
     kern<<<grid, Cfg::THREADS, Cfg::SMEM_BYTES, e.stream>>>(ma, mb, malo, mblo, md, p);
   }

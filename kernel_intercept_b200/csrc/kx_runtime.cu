@@ -31,6 +31,7 @@ constexpr int kSlotsPerDevice = 4096;
 
 thread_local const char* tl_kernel_name = "none";
 thread_local int tl_last_grid = 0;
+thread_local int tl_last_cuda_error = 0;
 
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                    const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
@@ -375,6 +376,8 @@ static std::atomic<unsigned long long> g_launches{0};
 
 void note_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
 
+void note_cuda_error(cudaError_t e) { tl_last_cuda_error = static_cast<int>(e); }
+
 }  // namespace kx
 
 extern "C" unsigned long long kx_launch_count(void) {
@@ -390,6 +393,8 @@ extern "C" int kx_num_sms(void) { return kx::device_info().num_sms; }
 extern "C" const char* kx_last_kernel_name(void) { return kx::tl_kernel_name; }
 
 extern "C" int kx_last_grid(void) { return kx::tl_last_grid; }
+
+extern "C" int kx_last_cuda_error(void) { return kx::tl_last_cuda_error; }
 
 extern "C" const char* kx_version(void) { return "kx 0.1 sm_100a"; }
 

@@ -56,15 +56,18 @@ inline bool tma_store_disabled() {
   return off;
 }
 
-// 3xTF32 accumulator segment length in k-blocks (KX_SEG_KB, default 2 =
-// 64 of K for tf32 k-blocks of 32): the tensor core's fp32 accumulation
-// rounds toward zero, and the bias of one accumulator grows with its K
-// length; it is the same sign in every layer of a network, so it compounds.
+// 3xTF32 accumulator segment length in k-blocks (KX_SEG_KB, default 4 =
+// 128 of K for tf32 k-blocks of 32): the tensor core's fp32 accumulation
+// truncates, and the bias of one accumulator grows with its K length; it has
+// the same sign in every layer of a network, so it compounds.  Measured on a
+// VGG16 batch-32 forward through the interposer (max normwise error of the
+// logits against a float64 forward): 1.20e-5 at 8, 8.06e-6 at 4, 6.28e-6 at
+// 2; the 13 convolutions take 4.2 % longer at 4 than at 8 and 12 % at 2.
 inline int seg_kb_default() {
   static const int v = [] {
     const char* s = std::getenv("KX_SEG_KB");
-    const int x = s != nullptr ? std::atoi(s) : 2;
-    return x >= 1 && x <= 64 ? x : 2;
+    const int x = s != nullptr ? std::atoi(s) : 4;
+    return x >= 1 && x <= 64 ? x : 4;
   }();
   return v;
 }
@@ -167,10 +170,22 @@ void note_launch();
 // kx_device_alloc_count.  Every cudaMalloc / cudaFree site calls it.
 void note_device_alloc();
 
+// Records the CUDA error behind a KX_ERR_DEVICE status of this thread's last
+// call (read back by kx_last_cuda_error).
+void note_cuda_error(cudaError_t e);
+
 // Status mapping helper.
 inline int launch_status() {
   cudaError_t e = cudaGetLastError();
-  return e == cudaSuccess ? KX_OK : KX_ERR_DEVICE;
+  if (e == cudaSuccess) return KX_OK;
+  note_cuda_error(e);
+  return KX_ERR_DEVICE;
+}
+
+// KX_ERR_DEVICE for a failed runtime call, with its error recorded.
+inline int device_error(cudaError_t e) {
+  note_cuda_error(e);
+  return KX_ERR_DEVICE;
 }
 
 }  // namespace kx

@@ -577,8 +577,17 @@ cudaError_t Scheduler::execute_operation(OperationPtr op, cudaStream_t fallback)
     st.kx_ops.fetch_add(1);
     return cudaSuccess;
   }
-  st.errors.fetch_add(1);
-  LOG_ERROR("client %d: %s failed in kx (status %d)", c, op_type_name(op->type), rc);
+  // the first 16 failures of a client, then every 1024th
+  const uint64_t nerr = st.errors.fetch_add(1);
+  if (nerr < 16 || (nerr & 1023) == 0) {
+    auto err_name = ORION_REAL(cudart, cudaGetErrorName);
+    const char* why = rc == KX_ERR_DEVICE && err_name != nullptr
+                          ? err_name(static_cast<cudaError_t>(kx_last_cuda_error()))
+                          : "";
+    LOG_ERROR("client %d: %s failed in kx (status %d%s%s; %llu failures so far)", c,
+              op_type_name(op->type), rc, rc == KX_ERR_DEVICE ? ", " : "", why,
+              static_cast<unsigned long long>(nerr + 1));
+  }
   return kx_to_cuda(rc);
 }
 

@@ -89,6 +89,7 @@ _SIGNATURES = {
     "kx_num_sms": [],
     "kx_last_kernel_name": [],
     "kx_last_grid": [],
+    "kx_last_cuda_error": [],
     "kx_version": [],
 }
 
