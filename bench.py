@@ -68,6 +68,9 @@ def parse():
                     help="HP steps of the latency phases (solo, paced, e2e)")
     ap.add_argument("--be-keep-sms", type=int, default=-1,
                     help="SMs a BE op keeps while HP runs (default: the scheduler's)")
+    ap.add_argument("--be-host-hold-us", type=int, default=-1,
+                    help="longest wait of a BE client thread before queueing an op while HP "
+                         "is active (default: the scheduler's, KX_BE_HOST_HOLD_US)")
     ap.add_argument("--kernel-info", default="auto",
                     help="per-client kernel tables for the Orion admission gate: 'auto' "
                          "measures them in-process before the timed phases (one step of each "
@@ -381,6 +384,8 @@ def run_group(args):
     # ---- kx arm
     if args.be_keep_sms >= 0:
         orion.orion_set_be_keep_sms(args.be_keep_sms)
+    if args.be_host_hold_us >= 0:
+        orion.orion_set_be_host_hold_us(args.be_host_hold_us)
     orion.orion_start_scheduler_thread()
     orion.orion_set_capture(1)
     tables = None
@@ -490,6 +495,7 @@ def run_group(args):
                    "l2": "inputs larger than L2 between HP steps (activations of one step "
                          "exceed 126 MB)",
                    "gil_switch_ms": round(sys.getswitchinterval() * 1e3, 3),
+                   "be_host_hold_us": orion.orion_get_be_host_hold_us(),
                    "gc_frozen": bool(args.gc_freeze), "host_cores_per_rank": pinned},
         "hp": hp_block,
         "be": be, "be_total": {k: (round(v, 4) if "retention" in k else round(v, 1))
@@ -569,8 +575,18 @@ def run_microbench(args):
             i_hp[0] += 1
             torch.matmul(a, b)
 
+        be_inflight = []
+
         def be_step():
+            # at most two GEMMs in flight, as a training loop that reads its
+            # loss every step keeps it: an unthrottled loop would queue
+            # seconds of work on a 16-SM quota
             torch.matmul(A, B, out=C)
+            ev = torch.cuda.Event()
+            ev.record()
+            be_inflight.append(ev)
+            if len(be_inflight) > 2:
+                be_inflight.pop(0).synchronize()
 
         for step in (hp_step, be_step):  # library warm-up, capture off
             step()

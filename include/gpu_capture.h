@@ -386,6 +386,9 @@ OperationPtr create_operation(int client_idx, OperationType type);
  *  full for wait_timeout_ns(): the record is then completed with
  *  cudaErrorTimeout, never runs, and the client's error latch is set. */
 bool enqueue_operation(OperationPtr op);
+/** BE client threads pass here before queueing an op (see
+ *  Scheduler::be_issue_gate); a no-op for the HP client. */
+void be_issue_gate(int client_idx);
 /** Bounded wait for the worker (see OperationRecord::wait_completion);
  *  returns the op's result, cudaErrorTimeout when the client gave up. */
 cudaError_t wait_operation(OperationPtr op);

@@ -92,6 +92,7 @@ struct ClientStats {
     std::atomic<uint64_t> be_blocked{0};
     std::atomic<uint64_t> yields{0};
     std::atomic<uint64_t> errors{0};
+    std::atomic<uint64_t> host_holds{0};  // ops this BE client's threads waited before queueing
 };
 
 class Scheduler {
@@ -137,6 +138,14 @@ public:
     /** Profiling sessions also time the kernels the interposer re-issues. */
     void set_profile_launches(bool on) { profile_launches_.store(on); }
     int be_keep_sms() const { return be_keep_sms_.load(); }
+    /** A BE client thread about to queue an op while HP is active waits (at
+     *  most KX_BE_HOST_HOLD_US per op; 0, the default, turns it off) until
+     *  HP is idle, unless it holds the Python interpreter lock.  PyTorch
+     *  releases that lock around every operator, so a BE thread held here
+     *  leaves the interpreter to the HP client's thread while HP issues. */
+    void be_issue_gate(int client_idx);
+    void set_be_host_hold_us(int us) { be_host_hold_ns_.store(us < 0 ? 0 : 1000LL * us); }
+    int be_host_hold_us() const { return static_cast<int>(be_host_hold_ns_.load() / 1000); }
     volatile int* hp_flag_host() const { return hp_flag_host_; }
     int* hp_flag_device() const { return hp_flag_dev_; }
 
@@ -189,6 +198,7 @@ private:
     // Longest table duration of a BE kernel that may share SMs with an active
     // HP client (KX_BE_MAX_US, default 50 us); longer ones wait for HP to idle.
     float be_max_ns_{50000.0f};
+    std::atomic<long long> be_host_hold_ns_{0};
     cudaStream_t flag_stream_{nullptr};
     void publish_hp_flag(int value);
     std::atomic<int> be_keep_sms_{0};
@@ -244,6 +254,12 @@ int orion_get_be_keep_sms();
 int orion_set_sm_budgets(int hp_sms, int be_sms);
 /** Counters of one client: ops, kx_ops, passthrough_ops, be_blocked, yields, errors. */
 int orion_get_client_stats(int client_idx, unsigned long long* out6);
+/** Longest time (us) a BE client thread waits before queueing an op while HP
+ *  is active (Scheduler::be_issue_gate); 0 = never waits. */
+void orion_set_be_host_hold_us(int us);
+int orion_get_be_host_hold_us();
+/** Ops of one BE client whose thread waited at the issue gate. */
+unsigned long long orion_get_client_host_holds(int client_idx);
 /** Called by the reference's launch_jobs.py; synchronises the client's stream. */
 void block(int client_idx);
 }

@@ -85,6 +85,17 @@ struct GemmParams {
   // applies alpha / beta / bias / activation.  splits == 1: direct epilogue.
   int splits, kb_per_split;
   float* ws;
+  // Stream-K (16-bit GEMMs without yield; 0 = off): the queue hands out
+  // ranges of sk_units consecutive k-blocks of the sequence (tile, k-block)
+  // of sk_total = output tiles x num_kb k-blocks, one range per CTA; a
+  // range may start and end inside a tile.  The CTA whose range ends inside
+  // a tile (its first k-blocks) finishes it after adding the raw fp32
+  // partial that the next range computed from the rest of the tile, at the
+  // start of that range, into sk_ws[next range] (BM x BN, [column][row]);
+  // sk_flags[range] = sk_epoch says the partial is there.
+  int sk_units, sk_total, sk_epoch;
+  float* sk_ws;
+  int* sk_flags;
   // 3xTF32: 1 = the low parts of A and B were written to global memory
   // before the launch and arrive by TMA (maps tmAlo / tmBlo); 0 = warps 2-3
   // compute them in shared memory from each k-block.
@@ -308,6 +319,34 @@ KX_DEV void tile_k_range(int tile, const GemmParams& p, int& kb0, int& nkb) {
   kb0 = ks * p.kb_per_split;
   const int end = kb0 + p.kb_per_split < p.num_kb ? kb0 + p.kb_per_split : p.num_kb;
   nkb = end - kb0;
+}
+
+// Role of a work item under stream-K: a whole tile; the K tail of a tile
+// whose head an earlier range finishes (the partial goes to this range's
+// slot); the K head of a tile whose tail the next range computed (its
+// partial is added before the epilogue).
+enum : int { SK_FULL = 0, SK_OUT = 1, SK_FINISH = 2 };
+
+// Work item -> output tile, its k-blocks and stream-K role.  Without
+// stream-K an item is a tile id (with its split-K slice); with it, an item
+// is the index of its first k-block in the (tile, k-block) sequence.
+KX_DEV void work_item(int code, const GemmParams& p, int& tile, int& kb0, int& nkb, int& role) {
+  role = SK_FULL;
+  if (p.sk_units == 0) {
+    tile = code;
+    tile_k_range(code, p, kb0, nkb);
+    return;
+  }
+  const int r = code / p.sk_units;
+  const int rend =
+      p.sk_total - r * p.sk_units <= p.sk_units ? p.sk_total : (r + 1) * p.sk_units;
+  tile = code / p.num_kb;
+  kb0 = code - tile * p.num_kb;
+  nkb = p.num_kb - kb0 < rend - code ? p.num_kb - kb0 : rend - code;
+  if (kb0 > 0)
+    role = SK_OUT;
+  else if (nkb < p.num_kb)
+    role = SK_FINISH;
 }
 
 // Sums the split-K partials of every output element and applies the
@@ -538,6 +577,11 @@ __global__ void __launch_bounds__(256, 1)
       uint32_t prod_s = 0, prod_ph = 0;  // stage and phase of k-block `it`
       uint32_t ia = 0, ib = 0;  // tap reuse: A boxes and B k-blocks issued
       int taken = 0;
+      // stream-K: the next work item of this CTA's range and the range's end
+      // (one range per CTA: a CTA that finished its range takes no other, so
+      // a range that waits for the next one never waits for itself)
+      int sk_next = 0, sk_end = 0;
+      bool sk_done = false;
       for (uint32_t slot = 0;; ++slot) {
         int tile;
         const uint32_t r = slot % R;
@@ -545,13 +589,23 @@ __global__ void __launch_bounds__(256, 1)
           // yield flag f: 0 = run; f > 0 = only CTAs below f keep taking tiles
           // (the op still completes on them); f < 0 = every CTA stops.
           const int f = p.yield_flag != nullptr ? *p.yield_flag : 0;
-          if (p.max_tiles > 0 && taken >= p.max_tiles) {
+          if (sk_next < sk_end) {
+            tile = sk_next;
+          } else if (sk_done) {
+            tile = -1;
+          } else if (p.max_tiles > 0 && taken >= p.max_tiles) {
             tile = -2;
           } else if (f < 0 || (f > 0 && static_cast<int>(blockIdx.x) >= f)) {
             tile = -2;
           } else {
             tile = static_cast<int>(atomicAdd(&p.work->next_tile, 1u));
             if (tile >= p.num_tiles) tile = -1;
+            if (p.sk_units != 0 && tile >= 0) {
+              sk_next = tile * p.sk_units;
+              sk_end = p.sk_total - sk_next <= p.sk_units ? p.sk_total : sk_next + p.sk_units;
+              tile = sk_next < sk_end ? sk_next : -1;  // the last ranges may be empty
+              sk_done = true;
+            }
           }
           const uint32_t eb = smem_addr(&sb->ring_empty[r]);
           const uint32_t ep = ((slot / R) & 1) ^ 1;
@@ -572,10 +626,11 @@ __global__ void __launch_bounds__(256, 1)
         }
         if (tile < 0) break;
         ++taken;
-        int b, ks, mb, nb, kb0, nkb;
-        decode_tile(tile, p, b, ks, mb, nb);
+        int b, ks, mb, nb, kb0, nkb, wt, role;
+        work_item(tile, p, wt, kb0, nkb, role);
+        if (p.sk_units != 0) sk_next = tile + nkb;
+        decode_tile(wt, p, b, ks, mb, nb);
         if constexpr (PAIR) mb = 2 * mb + static_cast<int>(rank);  // this CTA's 128 rows
-        tile_k_range(tile, p, kb0, nkb);
         const int ba = p.a_bcast ? 0 : b;
         const int bb = p.b_bcast ? 0 : b;
         // this CTA's rows of B: all BN, or half of them in a pair
@@ -816,8 +871,8 @@ __global__ void __launch_bounds__(256, 1)
         mbar_arrive_cluster(leader_bar(&sb->ring_empty[r]));
         if (tile < 0) break;
         if constexpr (DIRECT) continue;  // loads signal the leader themselves
-        int kb0, nkb;
-        tile_k_range(tile, p, kb0, nkb);
+        int kb0, nkb, wt_, role_;
+        work_item(tile, p, wt_, kb0, nkb, role_);
         for (int kb = 0; kb < nkb; ++kb, ++it) {
           const uint32_t s = it % S;
           if (!timed_wait(smem_addr(&sb->full[s]), (it / S) & 1, wc, stats ? &st_a : nullptr)) {
@@ -847,8 +902,8 @@ __global__ void __launch_bounds__(256, 1)
         const int tile = sb->ring[r];
         mbar_arrive(smem_addr(&sb->ring_empty[r]));
         if (tile < 0) break;
-        int kb0, nkb;
-        tile_k_range(tile, p, kb0, nkb);
+        int kb0, nkb, wt_, role_;
+        work_item(tile, p, wt_, kb0, nkb, role_);
         if constexpr (CONV && Cfg::TAPR) {
           // filter row r reads the A box from row r * dil_h * wbox on (a
           // multiple of 8 rows: whole 1024-byte swizzle atoms)
@@ -1022,8 +1077,8 @@ __global__ void __launch_bounds__(256, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_addr(&sb->ring_empty[r]));
         if (tile < 0) break;
-        int kb0, nkb;
-        tile_k_range(tile, p, kb0, nkb);
+        int kb0, nkb, wt_, role_;
+        work_item(tile, p, wt_, kb0, nkb, role_);
         for (int kb = 0; kb < nkb; ++kb, ++it) {
           const uint32_t s = it % S;
           ok = mbar_wait(smem_addr(&sb->full[s]), (it / S) & 1, wc);
@@ -1062,9 +1117,10 @@ __global__ void __launch_bounds__(256, 1)
     const float beta = p.beta_dev ? *p.beta_dev : p.beta;
     const uint32_t lane_off = (q * 32u) << 16;
     const bool split = p.splits > 1;
-    const bool use_tma_store = p.tma_store != 0 && !split;
     // alpha * acc only (no beta, bias or activation)
     const bool plain_epi = beta == 0.f && p.bias == nullptr && !p.relu && !p.gelu;
+    // a 64-column D box (wide16) serves the plain 16-bit epilogue only
+    const bool use_tma_store = p.tma_store != 0 && !split && (p.wide16 == 0 || plain_epi);
     uint32_t epi_chunk = 0;
     uint32_t sc = 0;
     for (uint32_t slot = 0;; ++slot) {
@@ -1082,10 +1138,10 @@ __global__ void __launch_bounds__(256, 1)
           mbar_arrive_cluster(leader_bar(&sb->ring_empty[r]));
       }
       if (tile < 0) break;
-      int b, ks, mb, nb, kb0, nkb;
-      decode_tile(tile, p, b, ks, mb, nb);
+      int b, ks, mb, nb, kb0, nkb, wt, role;
+      work_item(tile, p, wt, kb0, nkb, role);
+      decode_tile(wt, p, b, ks, mb, nb);
       if constexpr (PAIR) mb = 2 * mb + static_cast<int>(rank);  // this CTA's 128 rows
-      tile_k_range(tile, p, kb0, nkb);
       const int nseg = Cfg::PROMOTE ? (nkb + seg - 1) / seg : 1;
       int row = mb * Cfg::BM + q * 32 + static_cast<int>(lane);
       bool row_ok = row < p.m;
@@ -1282,17 +1338,55 @@ __global__ void __launch_bounds__(256, 1)
         // in flight while the current one is converted and stored.
         const uint32_t tbase = tmem + a * Cfg::ACC_COLS + lane_off;
         uint32_t va[32], vb[32];
+        // Stream-K: a tail item leaves its raw partial (this warp's 32 rows,
+        // [column][row] with 128 rows per column) in its range's slot and
+        // publishes it with the quadrant's flag; a head item adds the next
+        // range's partial, written at that range's start, before the epilogue.
+        const float* sk_in = nullptr;
+        bool sk_emit = true;
+        if (role != SK_FULL) {
+          const int rg = tile / p.sk_units;
+          const size_t slot_elems = static_cast<size_t>(Cfg::BM) * Cfg::BN;
+          const int trow = q * 32 + static_cast<int>(lane);
+          if (role == SK_OUT) {
+            float* dst = p.sk_ws + static_cast<size_t>(rg) * slot_elems + trow;
+#pragma unroll 1
+            for (int c0 = 0; c0 < Cfg::BN; c0 += 32) {
+              tmem_ld_32x32b_x32(tbase + c0, va);
+              tmem_ld_wait();
+              tmem_regs_ready(va);
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                __stcg(dst + static_cast<size_t>(c0 + j) * Cfg::BM, __uint_as_float(va[j]));
+            }
+            __threadfence();
+            __syncwarp();
+            if (lane == 0) flag_release(p.sk_flags + rg * 4 + q, p.sk_epoch);
+            sk_emit = false;
+          } else {
+            ok = flag_wait(p.sk_flags + (rg + 1) * 4 + q, p.sk_epoch, wc);
+            ok = __all_sync(0xffffffffu, ok);
+            if (!ok) break;
+            sk_in = p.sk_ws + static_cast<size_t>(rg + 1) * slot_elems + trow;
+          }
+        }
         auto out = [&](int c0, uint32_t (&v)[32]) {
           tmem_regs_ready(v);
           float f[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]);
+          if (sk_in != nullptr) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) f[j] += __ldcg(sk_in + static_cast<size_t>(c0 + j) * Cfg::BM);
+          }
           if (warp_tma)
             emit_tma(c0, f);
           else
             emit(c0, f);
         };
-        if (p.wide16 && warp_tma && plain_epi && Cfg::BN % 64 == 0) {
+        if (!sk_emit) {
+          // partial only
+        } else if (p.wide16 && warp_tma && plain_epi && Cfg::BN % 64 == 0) {
           // 16-bit D, alpha only: 64 columns (4 KB) per staging buffer and per
           // TMA store, half the per-store fences, waits and issues
 #pragma unroll 1
@@ -1302,6 +1396,15 @@ __global__ void __launch_bounds__(256, 1)
             tmem_ld_wait();
             tmem_regs_ready(va);
             tmem_regs_ready(vb);
+            if (sk_in != nullptr) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                va[j] = __float_as_uint(__uint_as_float(va[j]) +
+                                        __ldcg(sk_in + static_cast<size_t>(c0 + j) * Cfg::BM));
+                vb[j] = __float_as_uint(__uint_as_float(vb[j]) +
+                                        __ldcg(sk_in + static_cast<size_t>(c0 + 32 + j) * Cfg::BM));
+              }
+            }
             uint8_t* buf = smem + Cfg::EPI_OFF + (q * 2 + (epi_chunk & 1u)) * 4096;
             ++epi_chunk;
             if (lane == 0) bulk_wait_group_read<1>();

@@ -89,6 +89,40 @@ KX_DEV bool mbar_wait(uint32_t bar, uint32_t parity, const WaitCtl& w) {
   }
 }
 
+// Waits until a global flag holds `want` (acquire, GPU scope: the data
+// written before the matching release store is visible afterwards).  Returns
+// false if the CTA is aborting or the wait timed out, as mbar_wait.
+KX_DEV bool flag_wait(const int* flag, int want, const WaitCtl& w) {
+  uint64_t t0 = 0;
+  uint32_t spins = 0;
+  while (true) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+    if (v == want) return true;
+    if ((++spins & 63u) == 0) {
+      if (*w.abort_flag) return false;
+      uint64_t now = globaltimer();
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > w.timeout_ns) {
+        *w.abort_flag = 1;
+        if (w.err_word) atomicCAS(w.err_word, 0, 3 /* KX_ERR_TIMEOUT */);
+        return false;
+      }
+    }
+  }
+}
+
+// Release store of a global flag (GPU scope).
+KX_DEV void flag_release(int* flag, int v) {
+  asm volatile("st.release.gpu.global.s32 [%0], %1;" ::"l"(flag), "r"(v) : "memory");
+}
+
+// Barrier over `threads` threads (whole warps) of the CTA on barrier `id`.
+KX_DEV void named_bar_sync(uint32_t id, uint32_t threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
 // ------------------------------------------------------------------ TMA ---
 
 KX_DEV void tma_prefetch_desc(const void* map) {

@@ -23,6 +23,7 @@
 #include "scheduler.h"
 
 #include <cuda.h>
+#include <dlfcn.h>
 
 #include <sys/prctl.h>
 #include <time.h>
@@ -238,6 +239,8 @@ bool Scheduler::init(int num_clients, const SchedulerConfig& config) {
   be_keep_sms_.store(std::max(0, std::min(keep, sms)));
   if (const char* s = std::getenv("KX_HP_HOLD_US")) hp_hold_ns_ = std::max(0LL, std::atoll(s)) * 1000;
   if (const char* s = std::getenv("KX_BE_MAX_US")) be_max_ns_ = std::max(0.0f, std::strtof(s, nullptr)) * 1000.f;
+  if (const char* s = std::getenv("KX_BE_HOST_HOLD_US"))
+    be_host_hold_ns_.store(std::max(0LL, std::atoll(s)) * 1000);
   ORION_REAL(cudart, cudaEventCreateWithFlags)(&hp_last_event_, cudaEventDisableTiming);
   g_orion_state.init(num_clients, sms);
   g_orion_state.sm_threshold = config_.sm_threshold;
@@ -382,6 +385,30 @@ bool Scheduler::orion_should_schedule(OperationPtr op, int client_idx) {
   const float dur = peek_duration(client_idx);
   return dur > 0.f && dur <= be_max_ns_;
 }
+
+namespace {
+// PyGILState_Check of the interpreter hosting the process, if there is one
+int (*gil_check_fn())() {
+  static int (*fn)() = reinterpret_cast<int (*)()>(dlsym(RTLD_DEFAULT, "PyGILState_Check"));
+  return fn;
+}
+}  // namespace
+
+void Scheduler::be_issue_gate(int client_idx) {
+  const long long hold = be_host_hold_ns_.load(std::memory_order_relaxed);
+  if (client_idx <= 0 || hold <= 0 || isolated_ || hp_flag_host_ == nullptr) return;
+  if (hp_flag_host_[0] == 0 || !running_.load()) return;
+  // a thread that holds the interpreter lock (or a process without one)
+  // never waits here: the HP thread would wait for it in turn
+  auto chk = gil_check_fn();
+  if (chk == nullptr || chk() != 0) return;
+  stats(client_idx).host_holds.fetch_add(1);
+  const int64_t deadline = mono_ns() + hold;
+  while (hp_flag_host_[0] != 0 && running_.load() && mono_ns() < deadline)
+    std::this_thread::sleep_for(std::chrono::microseconds(20));
+}
+
+void be_issue_gate(int client_idx) { g_scheduler.be_issue_gate(client_idx); }
 
 void Scheduler::publish_hp_flag(int value) {
   trace_marker(value != 0 ? "hp_flag_raise" : "hp_flag_clear", value);
@@ -881,6 +908,15 @@ int orion_set_sm_budgets(int hp_sms, int be_sms) {
   gc.be_sm_count = static_cast<unsigned>(be_sms);
   gc.enabled = true;
   return orion::g_scheduler.init_green_contexts(gc) ? 0 : -1;
+}
+
+void orion_set_be_host_hold_us(int us) { orion::g_scheduler.set_be_host_hold_us(us); }
+
+int orion_get_be_host_hold_us() { return orion::g_scheduler.be_host_hold_us(); }
+
+unsigned long long orion_get_client_host_holds(int client_idx) {
+  if (client_idx < 0 || client_idx >= orion::MAX_CLIENTS) return 0;
+  return orion::g_scheduler.stats(client_idx).host_holds.load();
 }
 
 int orion_get_client_stats(int client_idx, unsigned long long* out6) {

@@ -58,6 +58,8 @@ class Orion:
             "orion_set_profile_launches": ([I], None),
             "orion_set_sm_budgets": ([I, I], I),
             "orion_get_client_stats": ([I, ctypes.POINTER(ctypes.c_ulonglong)], I),
+            "orion_set_be_host_hold_us": ([I], None), "orion_get_be_host_hold_us": ([], I),
+            "orion_get_client_host_holds": ([I], ctypes.c_ulonglong),
             "orion_load_profile": ([ctypes.c_char_p], I),
             "orion_start_profiling": ([ctypes.c_char_p], None),
             "orion_end_profiling": ([ctypes.c_char_p], None),
@@ -84,7 +86,9 @@ class Orion:
         out = (ctypes.c_ulonglong * 6)()
         self.lib.orion_get_client_stats(client, out)
         keys = ("ops", "kx_ops", "passthrough_ops", "be_blocked", "yields", "errors")
-        return dict(zip(keys, (int(v) for v in out)))
+        d = dict(zip(keys, (int(v) for v in out)))
+        d["host_holds"] = int(self.lib.orion_get_client_host_holds(client))
+        return d
 
 
 def preloaded() -> bool:

@@ -616,7 +616,14 @@ def scenario_tables(orion):
     rows = [profile_tables.read_csv(p) for p in paths]
     loaded = profile_tables.load(orion, paths)
     blocked0 = orion.stats(1)["be_blocked"]
-    harness.run_clients(orion, hp_step, be_step, hp_steps=20, hp_warmup=1)
+
+    def be_gate_step():
+        # the long re-issued kernel alone: a BE GEMM stopped by HP would hold
+        # the BE worker until HP is idle, and the gate would see no BE op
+        # while HP is active
+        Bbig.mul_(1.0000001)
+
+    harness.run_clients(orion, hp_step, be_gate_step, hp_steps=20, hp_warmup=1)
     stats = {c: orion.stats(c) for c in (0, 1)}
     orion.orion_set_capture(0)
     orion.orion_stop_scheduler()

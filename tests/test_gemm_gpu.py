@@ -319,6 +319,73 @@ def test_matmul_epilogues_fp32(cuda, epi):
     assert o.normwise_rel_err(dD.cpu().numpy(), ref) <= TOL_F32
 
 
+def _bf16_matmul_case(m, n, k, epi=1, beta=0.0, batch=1, quota=0, seed=0, ta=1, tb=0):
+    """cublasLtMatmul with bf16 A, B, C, D (fp32 accumulation), an optional
+    bias / activation epilogue and beta, as PyTorch issues it for a bf16
+    nn.Linear; returns the normwise error against the oracle and the kernel
+    name."""
+    kx = _kx()
+    import torch
+    rng = np.random.default_rng(seed)
+    lda = m if ta == 0 else k
+    ldb = k if tb == 0 else n
+    sA, sB, sD = lda * (k if ta == 0 else m), ldb * (n if tb == 0 else k), m * n
+    A = o.f32_to_bf16_bits(rng.standard_normal(sA * batch).astype(np.float32))
+    B = o.f32_to_bf16_bits(rng.standard_normal(sB * batch).astype(np.float32))
+    C = o.f32_to_bf16_bits(rng.standard_normal(sD * batch).astype(np.float32))
+    bias = o.f32_to_bf16_bits(rng.standard_normal(m).astype(np.float32))
+    ref = np.zeros(sD * batch, np.float32)
+    o.gemm_ex(ta, tb, m, n, k, 1.0, A, o.R_16BF, lda, B, o.R_16BF, ldb, beta, C, o.R_16BF, m,
+              D=ref, Dtype=o.R_32F, ldd=m, batch=batch, sA=sA, sB=sB, sC=sD, sD=sD,
+              epilogue=epi, bias=bias, bias_type=o.R_16BF)
+    bf = torch.bfloat16
+    dA = _dev(A.view(np.int16)).view(bf)
+    dB = _dev(B.view(np.int16)).view(bf)
+    dC = _dev(C.view(np.int16)).view(bf)
+    dbias = _dev(bias.view(np.int16)).view(bf)
+    dD = torch.full((sD * batch,), float("nan"), dtype=bf, device="cuda")
+    kx.matmul(kx.current_exec(sm_quota=quota), ta, tb, m, n, k, 1.0, dA.data_ptr(), kx.R_16BF,
+              lda, sA, dB.data_ptr(), kx.R_16BF, ldb, sB, beta, dC.data_ptr(), kx.R_16BF, m, sD,
+              dD.data_ptr(), kx.R_16BF, m, sD, batch, epi, dbias.data_ptr(), kx.R_16BF)
+    torch.cuda.synchronize()
+    got = dD.float().cpu().numpy()
+    return o.normwise_rel_err(got, ref), _kx().last_kernel_name()
+
+
+@pytest.mark.parametrize("epi,beta", [(1, 0.0), (1, 0.5), (4, 0.0), (6, 0.0), (36, 0.0)])
+def test_matmul_epilogues_bf16_wide_tiles(cuda, epi, beta, monkeypatch):
+    """bf16 Lt matmuls on 256-wide tiles: the plain epilogue stores 64-column
+    boxes, every other (beta, bias, ReLU, GELU) 32-column ones."""
+    monkeypatch.setenv("KX_GEMM_BN", "256")
+    err, name = _bf16_matmul_case(384, 640, 200, epi=epi, beta=beta, seed=epi)
+    assert name.startswith("kx_gemm_tc<bn256,bf16"), name
+    assert err <= TOL_BF16, err
+
+
+@pytest.mark.parametrize("m,n,k,quota,epi,batch", [
+    (384, 1024, 1000, 8, 1, 1),     # 12 tiles on 8 CTAs: whole, tail and head items
+    (384, 1024, 1000, 7, 4, 1),     # uneven ranges, bias epilogue
+    (300, 1000, 520, 5, 1, 1),      # ragged M and N edges
+    (256, 512, 4096, 3, 1, 1),      # ranges of many k-blocks
+    (256, 512, 256, 6, 1, 3),       # batched: tiles of several planes
+    (128, 768, 64, 2, 1, 1),        # one k-block per tile
+    (128, 1280, 64, 4, 1, 1),       # more ranges than k-blocks: the last range is empty
+])
+def test_bf16_stream_k(cuda, m, n, k, quota, epi, batch, monkeypatch):
+    """Stream-K (KX_STREAMK=1): each CTA computes an equal range of k-blocks
+    across tile boundaries and the head of a split tile adds the partial the
+    next range left in L2; results match the oracle as whole tiles do."""
+    monkeypatch.setenv("KX_GEMM_BN", "256")
+    monkeypatch.setenv("KX_STREAMK", "1")
+    err, name = _bf16_matmul_case(m, n, k, epi=epi, batch=batch, quota=quota, seed=m + k)
+    assert name.endswith(",streamk>"), name
+    assert err <= TOL_BF16, err
+    monkeypatch.setenv("KX_STREAMK", "0")
+    err0, name0 = _bf16_matmul_case(m, n, k, epi=epi, batch=batch, quota=quota, seed=m + k)
+    assert not name0.endswith(",streamk>"), name0
+    assert err0 <= TOL_BF16, err0
+
+
 def test_yield_and_continuation(cuda):
     """A BE launch that stops at tile boundaries resumes exactly where it left off."""
     kx = _kx()
