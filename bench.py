@@ -271,7 +271,9 @@ def latency_block(harness, solo, cont, paced, hp_units, period):
            "solo_p99_ms": rnd(s99),
            "p50_ms": rnd(harness.percentile(cont.latencies_ms, 0.5)), "p99_ms": rnd(p99),
            "p99_vs_solo": rnd(p99 / s99, 4) if s99 else None,
-           "units_per_s": rnd(rate(cont, hp_units), 1)}
+           "units_per_s": rnd(rate(cont, hp_units), 1),
+           # every contended step, in order (the p99 of a short run is its maximum)
+           "steps_ms": [rnd(x, 2) for x in cont.latencies_ms]}
     if paced is not None:
         pp99 = harness.percentile(paced.latencies_ms, 0.99)
         out["paced"] = {"period_ms": rnd(period), "steps": paced.iters,

@@ -85,17 +85,6 @@ struct GemmParams {
   // applies alpha / beta / bias / activation.  splits == 1: direct epilogue.
   int splits, kb_per_split;
   float* ws;
-  // Stream-K (16-bit GEMMs without yield; 0 = off): the queue hands out
-  // ranges of sk_units consecutive k-blocks of the sequence (tile, k-block)
-  // of sk_total = output tiles x num_kb k-blocks, one range per CTA; a
-  // range may start and end inside a tile.  The CTA whose range ends inside
-  // a tile (its first k-blocks) finishes it after adding the raw fp32
-  // partial that the next range computed from the rest of the tile, at the
-  // start of that range, into sk_ws[next range] (BM x BN, [column][row]);
-  // sk_flags[range] = sk_epoch says the partial is there.
-  int sk_units, sk_total, sk_epoch;
-  float* sk_ws;
-  int* sk_flags;
   // 3xTF32: 1 = the low parts of A and B were written to global memory
   // before the launch and arrive by TMA (maps tmAlo / tmBlo); 0 = warps 2-3
   // compute them in shared memory from each k-block.
@@ -212,14 +201,14 @@ struct GemmCfg {
   static constexpr int STAGE_REGION =
       TAPR ? SA * 2 * TAPR_A_BYTES + SB * 2 * B_BYTES : STAGES * STAGE_BYTES;
   static constexpr int RING = 4;  // depth of the tile-id broadcast ring
-  // TMEM columns of one accumulator buffer.  3xTF32 on one CTA keeps two
-  // BN-wide halves: [0, BN) = hi*hi and [BN, 2BN) = hi*lo + lo*hi (see the
-  // MMA issuer).  The tensor core's fp32 accumulate truncates, so each add
-  // into the large half costs up to one ulp of the running sum; the small
-  // half is 2^-11 of it, and its truncations are negligible.  A pair issues
-  // the three products into one BN-wide buffer.
+  // TMEM columns of one accumulator buffer.  3xTF32 keeps two BN-wide
+  // halves: [0, BN) = hi*hi and [BN, 2BN) = hi*lo + lo*hi (see the MMA
+  // issuer).  The tensor core's fp32 accumulate truncates, so each add into
+  // the large half costs up to one ulp of the running sum; the small half is
+  // 2^-11 of it, and its truncations are negligible.  One CTA issues hi*hi
+  // and hi*lo as one MMA over [B_hi; B_lo] (MERGED); a pair issues three.
   static constexpr bool MERGED = SPLIT && !PAIR;
-  static constexpr int ACC_COLS = MERGED ? 2 * BN : BN;
+  static constexpr int ACC_COLS = SPLIT ? 2 * BN : BN;
   static constexpr int TMEM_COLS = (2 * ACC_COLS) <= 32 ? 32 : (2 * ACC_COLS) <= 64 ? 64 : (2 * ACC_COLS) <= 128 ? 128 : (2 * ACC_COLS) <= 256 ? 256 : 512;
   static constexpr int THREADS = 256;
   static constexpr int NUM_CONS = 1 + 4;  // ring consumers: MMA issuer + epilogue warps
@@ -242,6 +231,7 @@ struct GemmCfg {
   static constexpr uint32_t A_LAYOUT = A_MN32 ? 1 : 2;
   static constexpr uint32_t B_LAYOUT = B_MN32 ? 1 : 2;
   static_assert(!PROMOTE || BN <= 128, "3xTF32 keeps a BN-wide fp32 accumulator per thread");
+  static_assert(!PAIR || (!A_MN && !B_MN), "CTA pairs load K-major tiles only");
   static constexpr uint32_t FMT = (AR == Arith::BF16) ? 1u : (AR == Arith::F16) ? 0u : 2u;
   static constexpr uint32_t IDESC = make_idesc(FMT, A_MN, B_MN, MMA_M, BN);
   // 3xTF32 on one CTA: A_hi x [B_hi; B_lo] as one N = 2*BN product
@@ -265,7 +255,6 @@ struct SmemBars {
   uint64_t full[8], conv[8], empty[8];
   uint64_t tfull[2], tempty[2];
   uint64_t ring_full[4], ring_empty[4];
-  uint64_t pair_full[8];  // leader: the follower's stage has landed
   uint64_t final_mma;
   int ring[4];
   uint32_t tmem_base;
@@ -319,34 +308,6 @@ KX_DEV void tile_k_range(int tile, const GemmParams& p, int& kb0, int& nkb) {
   kb0 = ks * p.kb_per_split;
   const int end = kb0 + p.kb_per_split < p.num_kb ? kb0 + p.kb_per_split : p.num_kb;
   nkb = end - kb0;
-}
-
-// Role of a work item under stream-K: a whole tile; the K tail of a tile
-// whose head an earlier range finishes (the partial goes to this range's
-// slot); the K head of a tile whose tail the next range computed (its
-// partial is added before the epilogue).
-enum : int { SK_FULL = 0, SK_OUT = 1, SK_FINISH = 2 };
-
-// Work item -> output tile, its k-blocks and stream-K role.  Without
-// stream-K an item is a tile id (with its split-K slice); with it, an item
-// is the index of its first k-block in the (tile, k-block) sequence.
-KX_DEV void work_item(int code, const GemmParams& p, int& tile, int& kb0, int& nkb, int& role) {
-  role = SK_FULL;
-  if (p.sk_units == 0) {
-    tile = code;
-    tile_k_range(code, p, kb0, nkb);
-    return;
-  }
-  const int r = code / p.sk_units;
-  const int rend =
-      p.sk_total - r * p.sk_units <= p.sk_units ? p.sk_total : (r + 1) * p.sk_units;
-  tile = code / p.num_kb;
-  kb0 = code - tile * p.num_kb;
-  nkb = p.num_kb - kb0 < rend - code ? p.num_kb - kb0 : rend - code;
-  if (kb0 > 0)
-    role = SK_OUT;
-  else if (nkb < p.num_kb)
-    role = SK_FINISH;
 }
 
 // Sums the split-K partials of every output element and applies the
@@ -485,10 +446,9 @@ __global__ void __launch_bounds__(256, 1)
   constexpr int R = Cfg::RING;
   // CTA pair (Cfg::PAIR): rank 0 leads (tile ids, MMAs), rank 1 follows
   constexpr bool PAIR = Cfg::PAIR;
-  // 16-bit pairs: the follower's TMA loads complete on the leader's stage
-  // barriers (.cta_group::2 loads); 3xTF32 pairs (convolutions) forward each
-  // landed stage through the follower's MMA thread instead
-  constexpr bool DIRECT = PAIR && !Cfg::SPLIT;
+  // pairs: the follower's TMA loads complete on the leader's stage barriers
+  // (.cta_group::2 loads), so the leader's MMA thread waits on one barrier
+  constexpr bool DIRECT = PAIR;
   const uint32_t rank = PAIR ? cluster_ctarank() : 0u;
   const bool leader = rank == 0;
   // in-kernel 3xTF32 split (warps 2-3) unless the low parts come by TMA
@@ -519,7 +479,6 @@ __global__ void __launch_bounds__(256, 1)
       mbar_init(smem_addr(&sb->conv[s]), convert ? 2 : 1);  // one arrival per converter warp
       mbar_init(smem_addr(&sb->empty[s]), 1);
     }
-    for (int s = 0; s < S; ++s) mbar_init(smem_addr(&sb->pair_full[s]), 1);
     // pair: the leader's tempty / ring_empty also count the follower's
     // epilogue warps (4) and its producer and forwarder threads (2)
     for (int a = 0; a < 2; ++a) {
@@ -577,11 +536,6 @@ __global__ void __launch_bounds__(256, 1)
       uint32_t prod_s = 0, prod_ph = 0;  // stage and phase of k-block `it`
       uint32_t ia = 0, ib = 0;  // tap reuse: A boxes and B k-blocks issued
       int taken = 0;
-      // stream-K: the next work item of this CTA's range and the range's end
-      // (one range per CTA: a CTA that finished its range takes no other, so
-      // a range that waits for the next one never waits for itself)
-      int sk_next = 0, sk_end = 0;
-      bool sk_done = false;
       for (uint32_t slot = 0;; ++slot) {
         int tile;
         const uint32_t r = slot % R;
@@ -589,23 +543,13 @@ __global__ void __launch_bounds__(256, 1)
           // yield flag f: 0 = run; f > 0 = only CTAs below f keep taking tiles
           // (the op still completes on them); f < 0 = every CTA stops.
           const int f = p.yield_flag != nullptr ? *p.yield_flag : 0;
-          if (sk_next < sk_end) {
-            tile = sk_next;
-          } else if (sk_done) {
-            tile = -1;
-          } else if (p.max_tiles > 0 && taken >= p.max_tiles) {
+          if (p.max_tiles > 0 && taken >= p.max_tiles) {
             tile = -2;
           } else if (f < 0 || (f > 0 && static_cast<int>(blockIdx.x) >= f)) {
             tile = -2;
           } else {
             tile = static_cast<int>(atomicAdd(&p.work->next_tile, 1u));
             if (tile >= p.num_tiles) tile = -1;
-            if (p.sk_units != 0 && tile >= 0) {
-              sk_next = tile * p.sk_units;
-              sk_end = p.sk_total - sk_next <= p.sk_units ? p.sk_total : sk_next + p.sk_units;
-              tile = sk_next < sk_end ? sk_next : -1;  // the last ranges may be empty
-              sk_done = true;
-            }
           }
           const uint32_t eb = smem_addr(&sb->ring_empty[r]);
           const uint32_t ep = ((slot / R) & 1) ^ 1;
@@ -626,11 +570,10 @@ __global__ void __launch_bounds__(256, 1)
         }
         if (tile < 0) break;
         ++taken;
-        int b, ks, mb, nb, kb0, nkb, wt, role;
-        work_item(tile, p, wt, kb0, nkb, role);
-        if (p.sk_units != 0) sk_next = tile + nkb;
-        decode_tile(wt, p, b, ks, mb, nb);
+        int b, ks, mb, nb, kb0, nkb;
+        decode_tile(tile, p, b, ks, mb, nb);
         if constexpr (PAIR) mb = 2 * mb + static_cast<int>(rank);  // this CTA's 128 rows
+        tile_k_range(tile, p, kb0, nkb);
         const int ba = p.a_bcast ? 0 : b;
         const int bb = p.b_bcast ? 0 : b;
         // this CTA's rows of B: all BN, or half of them in a pair
@@ -741,31 +684,37 @@ __global__ void __launch_bounds__(256, 1)
           }
           const long long t_iss = stats ? clock64() : 0;
           const uint32_t fb = smem_addr(&sb->full[s]);
-          // 16-bit CTA pair: both CTAs' loads complete on the leader's stage
+          // CTA pair: both CTAs' loads complete on the leader's stage
           // barrier, which expects the bytes of both (the follower arrives on
-          // nothing and the leader's MMA waits on one barrier)
+          // nothing and the leader's MMA waits on one barrier).  3xTF32 with
+          // pre-split operands: the low parts arrive by TMA beside the high
+          // parts.
           const uint32_t fb_peer = DIRECT ? mapa_shared(fb, 0u) : fb;
-          if constexpr (DIRECT) {
-            if (leader) mbar_arrive_expect_tx(fb, 2 * Cfg::LOAD_BYTES);
-          } else {
-            // 3xTF32 with pre-split operands: the low parts arrive by TMA
-            // beside the high parts.
-            mbar_arrive_expect_tx(fb, Cfg::LOAD_BYTES * (lo_by_tma ? 2 : 1));
-          }
+          const bool peer_load = DIRECT && !leader;
+          if (!peer_load)
+            mbar_arrive_expect_tx(fb, Cfg::LOAD_BYTES * (lo_by_tma ? 2 : 1) * (PAIR ? 2 : 1));
           auto load_a = [&](uint32_t sa, const CUtensorMap* map) {
             if constexpr (CONV) {
               if (p.cv_wgrad) {  // dy rows k = mb*128.., 32 pixels
                 tma_load_3d(sa, map, fb, wg_f0, mb * Cfg::BM, wg_img);
               } else if (p.cv_im2col) {
-                tma_load_4d_im2col(sa, map, fb, cb * 32, cv_w0, cv_h0, cv_img,
-                                   static_cast<uint16_t>(ss * p.cv_dil_w),
-                                   static_cast<uint16_t>(rr * p.cv_dil_h));
+                if (peer_load)
+                  tma_load_4d_im2col_pair(sa, map, fb_peer, cb * 32, cv_w0, cv_h0, cv_img,
+                                          static_cast<uint16_t>(ss * p.cv_dil_w),
+                                          static_cast<uint16_t>(rr * p.cv_dil_h));
+                else
+                  tma_load_4d_im2col(sa, map, fb, cb * 32, cv_w0, cv_h0, cv_img,
+                                     static_cast<uint16_t>(ss * p.cv_dil_w),
+                                     static_cast<uint16_t>(rr * p.cv_dil_h));
+              } else if (peer_load) {
+                tma_load_4d_pair(sa, map, fb_peer, cb * 32, cv_w0 + ss * p.cv_dil_w,
+                                 cv_h0 + rr * p.cv_dil_h, cv_img);
               } else {
                 tma_load_4d(sa, map, fb, cb * 32, cv_w0 + ss * p.cv_dil_w,
                             cv_h0 + rr * p.cv_dil_h, cv_img);
               }
             } else if (!Cfg::A_MN) {
-              if (DIRECT && !leader)
+              if (peer_load)
                 tma_load_3d_pair(sa, map, fb_peer, kb * Cfg::BK, mb * Cfg::BM, ba);
               else
                 tma_load_3d(sa, map, fb, kb * Cfg::BK, mb * Cfg::BM, ba);
@@ -789,7 +738,7 @@ __global__ void __launch_bounds__(256, 1)
                                    wg_img, static_cast<uint16_t>(wg_offw),
                                    static_cast<uint16_t>(wg_offh));
             } else if (!Cfg::B_MN) {
-              if (DIRECT && !leader)
+              if (peer_load)
                 tma_load_3d_pair(sbb, map, fb_peer, kb * Cfg::BK, n0, bb);
               else
                 tma_load_3d(sbb, map, fb, kb * Cfg::BK, n0, bb);
@@ -861,26 +810,14 @@ __global__ void __launch_bounds__(256, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------- MMA issuer ---
     if (lane == 0 && PAIR && !leader) {
-      // follower: forward each landed stage to the leader's pair_full[s]
-      uint32_t it = 0;
-      bool ok = true;
-      for (uint32_t slot = 0; ok; ++slot) {
+      // follower: the leader issues the pair's MMAs and the follower's loads
+      // signal the leader themselves; this thread only consumes the tile ids
+      for (uint32_t slot = 0;; ++slot) {
         const uint32_t r = slot % R;
         if (!mbar_wait_cluster(smem_addr(&sb->ring_full[r]), (slot / R) & 1, wc)) break;
         const int tile = sb->ring[r];
         mbar_arrive_cluster(leader_bar(&sb->ring_empty[r]));
         if (tile < 0) break;
-        if constexpr (DIRECT) continue;  // loads signal the leader themselves
-        int kb0, nkb, wt_, role_;
-        work_item(tile, p, wt_, kb0, nkb, role_);
-        for (int kb = 0; kb < nkb; ++kb, ++it) {
-          const uint32_t s = it % S;
-          if (!timed_wait(smem_addr(&sb->full[s]), (it / S) & 1, wc, stats ? &st_a : nullptr)) {
-            ok = false;
-            break;
-          }
-          mbar_arrive_cluster(leader_bar(&sb->pair_full[s]));
-        }
       }
     } else if (lane == 0) {
       // `sc` counts accumulator segments across tiles; segment sc uses TMEM
@@ -902,8 +839,8 @@ __global__ void __launch_bounds__(256, 1)
         const int tile = sb->ring[r];
         mbar_arrive(smem_addr(&sb->ring_empty[r]));
         if (tile < 0) break;
-        int kb0, nkb, wt_, role_;
-        work_item(tile, p, wt_, kb0, nkb, role_);
+        int kb0, nkb;
+        tile_k_range(tile, p, kb0, nkb);
         if constexpr (CONV && Cfg::TAPR) {
           // filter row r reads the A box from row r * dil_h * wbox on (a
           // multiple of 8 rows: whole 1024-byte swizzle atoms)
@@ -993,8 +930,7 @@ __global__ void __launch_bounds__(256, 1)
               mma_ph ^= 1u;
             }
             const uint32_t wb = convert ? smem_addr(&sb->conv[s]) : smem_addr(&sb->full[s]);
-            if (!timed_wait(wb, ph, wc, stats ? &st_a : nullptr) ||
-                (PAIR && !DIRECT && !mbar_wait_cluster(smem_addr(&sb->pair_full[s]), ph, wc))) {
+            if (!timed_wait(wb, ph, wc, stats ? &st_a : nullptr)) {
               ok = false;
               break;
             }
@@ -1015,13 +951,14 @@ __global__ void __launch_bounds__(256, 1)
                 // 16-bit operands: one 256 x BN MMA over the pair's A and B rows
                 umma_f16_pair(d_tmem, ad, bd, Cfg::IDESC, acc);
               } else if constexpr (PAIR) {
-                // 256 x BN over the pair: A rows and B rows from both CTAs
-                // (A_lo right after A, B_lo right after B in the stage)
+                // 256 x BN over the pair, A rows and B rows from both CTAs (A_lo
+                // right after A, B_lo right after B in the stage): hi*hi into
+                // [0, BN), hi*lo and lo*hi into [BN, 2BN)
                 const uint64_t adl = ad + (Cfg::A_BYTES >> 4);
                 const uint64_t bdl = bd + (Cfg::B_BYTES >> 4);
                 umma_tf32_pair(d_tmem, ad, bd, Cfg::IDESC, acc);
-                umma_tf32_pair(d_tmem, ad, bdl, Cfg::IDESC, 1u);
-                umma_tf32_pair(d_tmem, adl, bd, Cfg::IDESC, 1u);
+                umma_tf32_pair(d_tmem + Cfg::BN, ad, bdl, Cfg::IDESC, acc);
+                umma_tf32_pair(d_tmem + Cfg::BN, adl, bd, Cfg::IDESC, 1u);
               } else if constexpr (Cfg::AR == Arith::F32x3) {
                 // hi*hi and hi*lo in one N = 2*BN MMA over [B_hi; B_lo]
                 // (columns [0, BN) and [BN, 2BN)), then lo*hi into [BN, 2BN):
@@ -1077,8 +1014,8 @@ __global__ void __launch_bounds__(256, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_addr(&sb->ring_empty[r]));
         if (tile < 0) break;
-        int kb0, nkb, wt_, role_;
-        work_item(tile, p, wt_, kb0, nkb, role_);
+        int kb0, nkb;
+        tile_k_range(tile, p, kb0, nkb);
         for (int kb = 0; kb < nkb; ++kb, ++it) {
           const uint32_t s = it % S;
           ok = mbar_wait(smem_addr(&sb->full[s]), (it / S) & 1, wc);
@@ -1138,10 +1075,10 @@ __global__ void __launch_bounds__(256, 1)
           mbar_arrive_cluster(leader_bar(&sb->ring_empty[r]));
       }
       if (tile < 0) break;
-      int b, ks, mb, nb, kb0, nkb, wt, role;
-      work_item(tile, p, wt, kb0, nkb, role);
-      decode_tile(wt, p, b, ks, mb, nb);
+      int b, ks, mb, nb, kb0, nkb;
+      decode_tile(tile, p, b, ks, mb, nb);
       if constexpr (PAIR) mb = 2 * mb + static_cast<int>(rank);  // this CTA's 128 rows
+      tile_k_range(tile, p, kb0, nkb);
       const int nseg = Cfg::PROMOTE ? (nkb + seg - 1) / seg : 1;
       int row = mb * Cfg::BM + q * 32 + static_cast<int>(lane);
       bool row_ok = row < p.m;
@@ -1338,55 +1275,17 @@ __global__ void __launch_bounds__(256, 1)
         // in flight while the current one is converted and stored.
         const uint32_t tbase = tmem + a * Cfg::ACC_COLS + lane_off;
         uint32_t va[32], vb[32];
-        // Stream-K: a tail item leaves its raw partial (this warp's 32 rows,
-        // [column][row] with 128 rows per column) in its range's slot and
-        // publishes it with the quadrant's flag; a head item adds the next
-        // range's partial, written at that range's start, before the epilogue.
-        const float* sk_in = nullptr;
-        bool sk_emit = true;
-        if (role != SK_FULL) {
-          const int rg = tile / p.sk_units;
-          const size_t slot_elems = static_cast<size_t>(Cfg::BM) * Cfg::BN;
-          const int trow = q * 32 + static_cast<int>(lane);
-          if (role == SK_OUT) {
-            float* dst = p.sk_ws + static_cast<size_t>(rg) * slot_elems + trow;
-#pragma unroll 1
-            for (int c0 = 0; c0 < Cfg::BN; c0 += 32) {
-              tmem_ld_32x32b_x32(tbase + c0, va);
-              tmem_ld_wait();
-              tmem_regs_ready(va);
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                __stcg(dst + static_cast<size_t>(c0 + j) * Cfg::BM, __uint_as_float(va[j]));
-            }
-            __threadfence();
-            __syncwarp();
-            if (lane == 0) flag_release(p.sk_flags + rg * 4 + q, p.sk_epoch);
-            sk_emit = false;
-          } else {
-            ok = flag_wait(p.sk_flags + (rg + 1) * 4 + q, p.sk_epoch, wc);
-            ok = __all_sync(0xffffffffu, ok);
-            if (!ok) break;
-            sk_in = p.sk_ws + static_cast<size_t>(rg + 1) * slot_elems + trow;
-          }
-        }
         auto out = [&](int c0, uint32_t (&v)[32]) {
           tmem_regs_ready(v);
           float f[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) f[j] = __uint_as_float(v[j]);
-          if (sk_in != nullptr) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) f[j] += __ldcg(sk_in + static_cast<size_t>(c0 + j) * Cfg::BM);
-          }
           if (warp_tma)
             emit_tma(c0, f);
           else
             emit(c0, f);
         };
-        if (!sk_emit) {
-          // partial only
-        } else if (p.wide16 && warp_tma && plain_epi && Cfg::BN % 64 == 0) {
+        if (p.wide16 && warp_tma && plain_epi && Cfg::BN % 64 == 0) {
           // 16-bit D, alpha only: 64 columns (4 KB) per staging buffer and per
           // TMA store, half the per-store fences, waits and issues
 #pragma unroll 1
@@ -1396,15 +1295,6 @@ __global__ void __launch_bounds__(256, 1)
             tmem_ld_wait();
             tmem_regs_ready(va);
             tmem_regs_ready(vb);
-            if (sk_in != nullptr) {
-#pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                va[j] = __float_as_uint(__uint_as_float(va[j]) +
-                                        __ldcg(sk_in + static_cast<size_t>(c0 + j) * Cfg::BM));
-                vb[j] = __float_as_uint(__uint_as_float(vb[j]) +
-                                        __ldcg(sk_in + static_cast<size_t>(c0 + 32 + j) * Cfg::BM));
-              }
-            }
             uint8_t* buf = smem + Cfg::EPI_OFF + (q * 2 + (epi_chunk & 1u)) * 4096;
             ++epi_chunk;
             if (lane == 0) bulk_wait_group_read<1>();

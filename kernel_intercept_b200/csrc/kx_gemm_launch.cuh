@@ -2,7 +2,6 @@
 // Each kx_gemm_tc_<arith>.cu includes this and instantiates the launchers
 // for its arithmetic, so the 48 kernel variants compile in parallel.
 #pragma once
-#include <cmath>
 #include <cstdio>
 
 #include "kx_gemm.cuh"
@@ -32,15 +31,6 @@ template <Arith AR>
 constexpr const char* arith_name() {
   return AR == Arith::F32x3 ? "f32x3" : AR == Arith::TF32 ? "tf32" : AR == Arith::BF16 ? "bf16" : "f16";
 }
-
-// KX_STREAMK: unset = stream-K where the last wave's idle share pays for it,
-// "0" = never, "1" = whenever the tiles exceed the grid (tests).
-inline int streamk_mode() {
-  const char* s = std::getenv("KX_STREAMK");
-  return s == nullptr ? -1 : (s[0] == '0' ? 0 : (s[0] == '1' ? 1 : -1));
-}
-inline bool streamk_disabled() { return streamk_mode() == 0; }
-inline bool streamk_forced() { return streamk_mode() == 1; }
 
 // KX_GEMM_PAIR=1: 16-bit GEMMs with K-major operands run on 2-CTA clusters
 // (256-row tiles, cta_group::2 MMAs; each SM loads half of the B tile).  Off
@@ -164,39 +154,6 @@ int launch_gemm_tc(const Exec& e, const TcProblem& pr, GemmParams p) {
       }
     }
   }
-  // Stream-K: a 16-bit GEMM that runs uninterrupted (no yield flag, done
-  // flag or tile budget) and whose tiles fill the CTAs unevenly runs as one
-  // range of equally many k-blocks per CTA instead of whole tiles, when the
-  // idle share of the last wave is worth more than the partial exchange
-  // (about 8 k-blocks of a 256-wide tile: one 128 x 256 fp32 partial written
-  // and read through L2 per range).
-  p.sk_units = 0;
-  p.sk_total = 0;
-  p.sk_epoch = 0;
-  p.sk_ws = nullptr;
-  p.sk_flags = nullptr;
-  if (!Cfg::SPLIT && !PAIR && p.splits == 1 && e.yield_flag == nullptr &&
-      e.done_flag == nullptr && e.max_tiles == 0 && !streamk_disabled()) {
-    const int g = persistent_grid(e, p.num_tiles);
-    const long long total = tiles * p.num_kb;
-    if (g >= 2 && tiles > g && 4LL * g <= kStreamKFlags && total < 0x7fff0000LL) {
-      const double w = static_cast<double>(tiles) / g;
-      const double idle = std::ceil(w) - w;
-      if (streamk_forced() || idle * p.num_kb * (BN / 256.0) >= 8.0) {
-        int epoch = 0;
-        const size_t ws_bytes = sizeof(float) * static_cast<size_t>(g) * Cfg::BM * BN;
-        char* base = static_cast<char*>(streamk_scratch(e.stream, ws_bytes, &epoch));
-        if (base != nullptr) {
-          p.sk_units = static_cast<int>((total + g - 1) / g);
-          p.sk_total = static_cast<int>(total);
-          p.sk_epoch = epoch;
-          p.sk_flags = reinterpret_cast<int*>(base);
-          p.sk_ws = reinterpret_cast<float*>(base + sizeof(int) * kStreamKFlags);
-          p.num_tiles = g;  // queue items: one range per CTA
-        }
-      }
-    }
-  }
   // D through TMA stores when D is TMA-addressable (split-K writes partials)
   CUtensorMap md = ma;
   p.tma_store = 0;
@@ -241,14 +198,11 @@ int launch_gemm_tc(const Exec& e, const TcProblem& pr, GemmParams p) {
     kx_splitk_reduce<<<splitk_reduce_grid(pr.m, pr.n, pr.batch, device_info().num_sms), 256, 0,
                        e.stream>>>(p, pr.batch);
   }
-  static char name[96], name_sk[96];
-  if (name[0] == 0) {
+  static char name[96];
+  if (name[0] == 0)
     snprintf(name, sizeof(name), "kx_gemm_tc<bn%d,%s,A%s,B%s%s>", BN, arith_name<AR>(),
              AMN ? "mn" : "k", BMN ? "mn" : "k", PAIR ? ",pair" : "");
-    snprintf(name_sk, sizeof(name_sk), "kx_gemm_tc<bn%d,%s,A%s,B%s,streamk>", BN,
-             arith_name<AR>(), AMN ? "mn" : "k", BMN ? "mn" : "k");
-  }
-  set_last_kernel_name(p.sk_units != 0 ? name_sk : name);
+  set_last_kernel_name(name);
   return launch_status();
 }
 

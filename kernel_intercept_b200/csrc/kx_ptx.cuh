@@ -89,40 +89,6 @@ KX_DEV bool mbar_wait(uint32_t bar, uint32_t parity, const WaitCtl& w) {
   }
 }
 
-// Waits until a global flag holds `want` (acquire, GPU scope: the data
-// written before the matching release store is visible afterwards).  Returns
-// false if the CTA is aborting or the wait timed out, as mbar_wait.
-KX_DEV bool flag_wait(const int* flag, int want, const WaitCtl& w) {
-  uint64_t t0 = 0;
-  uint32_t spins = 0;
-  while (true) {
-    int v;
-    asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
-    if (v == want) return true;
-    if ((++spins & 63u) == 0) {
-      if (*w.abort_flag) return false;
-      uint64_t now = globaltimer();
-      if (t0 == 0) {
-        t0 = now;
-      } else if (now - t0 > w.timeout_ns) {
-        *w.abort_flag = 1;
-        if (w.err_word) atomicCAS(w.err_word, 0, 3 /* KX_ERR_TIMEOUT */);
-        return false;
-      }
-    }
-  }
-}
-
-// Release store of a global flag (GPU scope).
-KX_DEV void flag_release(int* flag, int v) {
-  asm volatile("st.release.gpu.global.s32 [%0], %1;" ::"l"(flag), "r"(v) : "memory");
-}
-
-// Barrier over `threads` threads (whole warps) of the CTA on barrier `id`.
-KX_DEV void named_bar_sync(uint32_t id, uint32_t threads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
-}
-
 // ------------------------------------------------------------------ TMA ---
 
 KX_DEV void tma_prefetch_desc(const void* map) {
@@ -158,6 +124,17 @@ KX_DEV void tma_load_3d_pair(uint32_t dst, const void* map, uint32_t bar, int c0
       : "memory");
 }
 
+// 4-D tile load of the follower of a CTA pair, counted on the leader's
+// barrier (as tma_load_3d_pair).  No multicast.
+KX_DEV void tma_load_4d_pair(uint32_t dst, const void* map, uint32_t bar, int c0, int c1, int c2,
+                             int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      ".cta_group::2 [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar)
+      : "memory");
+}
+
 KX_DEV void tma_load_4d(uint32_t dst, const void* map, uint32_t bar, int c0, int c1, int c2,
                         int c3) {
   asm volatile(
@@ -176,6 +153,18 @@ KX_DEV void tma_load_4d_im2col(uint32_t dst, const void* map, uint32_t bar, int 
   asm volatile(
       "cp.async.bulk.tensor.4d.shared::cluster.global.im2col.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%2, %3, %4, %5}], [%6], {%7, %8};" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c), "r"(w), "r"(h), "r"(n), "r"(bar),
+      "h"(off_w), "h"(off_h)
+      : "memory");
+}
+
+// im2col-mode 4-D load of the follower of a CTA pair, counted on the
+// leader's barrier (as tma_load_3d_pair).  No multicast.
+KX_DEV void tma_load_4d_im2col_pair(uint32_t dst, const void* map, uint32_t bar, int c, int w,
+                                    int h, int n, uint16_t off_w, uint16_t off_h) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.im2col.mbarrier::complete_tx::bytes"
+      ".cta_group::2 [%0], [%1, {%2, %3, %4, %5}], [%6], {%7, %8};" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c), "r"(w), "r"(h), "r"(n), "r"(bar),
       "h"(off_w), "h"(off_h)
       : "memory");

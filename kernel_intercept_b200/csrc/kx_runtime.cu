@@ -123,7 +123,7 @@ struct Scratch {
   size_t bytes = 0;
   int64_t last_use_ns = 0;
 };
-std::unordered_map<cudaStream_t, Scratch> g_scratch[64][4];
+std::unordered_map<cudaStream_t, Scratch> g_scratch[64][3];
 size_t g_scratch_total[64] = {0};
 
 int64_t now_ns() {
@@ -161,7 +161,7 @@ void evict_idle(int dev, cudaStream_t keep, size_t need, int64_t idle_ns) {
   const size_t budget = scratch_budget(dev);
   while (need == SIZE_MAX || g_scratch_total[dev] + need > budget) {
     Scratch* oldest = nullptr;
-    for (int slot = 0; slot < 4; ++slot)
+    for (int slot = 0; slot < 3; ++slot)
       for (auto& kv : g_scratch[dev][slot]) {
         Scratch& s = kv.second;
         if (kv.first == keep || s.ptr == nullptr || now - s.last_use_ns < idle_ns) continue;
@@ -177,12 +177,11 @@ void evict_idle(int dev, cudaStream_t keep, size_t need, int64_t idle_ns) {
 }
 }  // namespace
 
-void* scratch_for(cudaStream_t stream, size_t bytes, int slot, bool* fresh) {
-  if (fresh != nullptr) *fresh = false;
+void* scratch_for(cudaStream_t stream, size_t bytes, int slot) {
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 64) dev = 0;
-  if (slot < 0 || slot > 3) return nullptr;
+  if (slot < 0 || slot > 2) return nullptr;
   if (bytes == 0) bytes = 256;
   std::lock_guard<std::mutex> lk(g_mu);
   Scratch& s = g_scratch[dev][slot][stream];
@@ -214,36 +213,7 @@ void* scratch_for(cudaStream_t stream, size_t bytes, int slot, bool* fresh) {
   }
   s.bytes = want;
   g_scratch_total[dev] += want;
-  if (fresh != nullptr) *fresh = true;
   return s.ptr;
-}
-
-namespace {
-std::mutex g_sk_mu;
-std::unordered_map<cudaStream_t, int> g_sk_epoch[64];
-}  // namespace
-
-void* streamk_scratch(cudaStream_t stream, size_t bytes, int* epoch) {
-  const size_t fbytes = sizeof(int) * static_cast<size_t>(kStreamKFlags);
-  bool fresh = false;
-  char* base = static_cast<char*>(scratch_for(stream, fbytes + bytes, 3, &fresh));
-  if (base == nullptr) return nullptr;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) dev = 0;
-  std::lock_guard<std::mutex> lk(g_sk_mu);
-  int& ep = g_sk_epoch[dev][stream];
-  if (fresh || ep <= 0 || ep >= 0x7ffffff0) {
-    const cudaError_t e = cudaMemsetAsync(base, 0, fbytes, stream);
-    if (e != cudaSuccess) {
-      note_cuda_error(e);
-      cudaGetLastError();
-      return nullptr;
-    }
-    ep = 0;
-  }
-  *epoch = ++ep;
-  return base;
 }
 
 Exec resolve_exec(const kx_exec* ex) {

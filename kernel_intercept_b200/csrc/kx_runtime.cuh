@@ -41,18 +41,10 @@ WorkSlot* work_slot_for(cudaStream_t stream);
 // failure every other stream's buffer idle for 100 ms is freed and the
 // allocation retried.  Returns nullptr on allocation failure.
 // Slot 0 serves the operator entry points (im2col buffers, batch-norm
-// statistics); slot 1 is the GEMM's own split-K workspace, slot 2 holds the
-// 3xTF32 low parts of its operands and slot 3 its stream-K partials and
-// flags, so a GEMM issued by an operator never overwrites the operator's
-// buffer.  *fresh (if given) tells whether the buffer was just allocated.
-void* scratch_for(cudaStream_t stream, size_t bytes, int slot = 0, bool* fresh = nullptr);
-
-// Stream-K workspace of a stream (slot 3): kStreamKFlags flag ints, then
-// `bytes` of partials.  The flags are zeroed on the stream whenever the
-// buffer is new; *epoch receives the value the next launch on the stream
-// publishes its partials under (1, 2, ... per buffer).  nullptr on failure.
-constexpr int kStreamKFlags = 4096;
-void* streamk_scratch(cudaStream_t stream, size_t bytes, int* epoch);
+// statistics); slot 1 is the GEMM's own split-K workspace and slot 2 holds
+// the 3xTF32 low parts of its operands, so a GEMM issued by an operator never
+// overwrites the operator's buffer.
+void* scratch_for(cudaStream_t stream, size_t bytes, int slot = 0);
 
 // KX_TMA_STORE=0 makes the tcgen05 epilogues store D with one st.global per
 // element instead of staging it through shared memory for TMA stores.

@@ -267,7 +267,7 @@ def test_gemm_ex_bf16_cta_pair(cuda, m, n, k, monkeypatch):
     tile past the end of M."""
     monkeypatch.setenv("KX_GEMM_PAIR", "1")
     test_gemm_ex_bf16(cuda, 1, 0, m, n, k)
-    assert ",pair>" in _kx().last_kernel_name(), _kx().last_kernel_name()
+    assert ",pair" in _kx().last_kernel_name(), _kx().last_kernel_name()
 
 
 @pytest.mark.parametrize("pair", ["0", "1"])
@@ -360,30 +360,6 @@ def test_matmul_epilogues_bf16_wide_tiles(cuda, epi, beta, monkeypatch):
     err, name = _bf16_matmul_case(384, 640, 200, epi=epi, beta=beta, seed=epi)
     assert name.startswith("kx_gemm_tc<bn256,bf16"), name
     assert err <= TOL_BF16, err
-
-
-@pytest.mark.parametrize("m,n,k,quota,epi,batch", [
-    (384, 1024, 1000, 8, 1, 1),     # 12 tiles on 8 CTAs: whole, tail and head items
-    (384, 1024, 1000, 7, 4, 1),     # uneven ranges, bias epilogue
-    (300, 1000, 520, 5, 1, 1),      # ragged M and N edges
-    (256, 512, 4096, 3, 1, 1),      # ranges of many k-blocks
-    (256, 512, 256, 6, 1, 3),       # batched: tiles of several planes
-    (128, 768, 64, 2, 1, 1),        # one k-block per tile
-    (128, 1280, 64, 4, 1, 1),       # more ranges than k-blocks: the last range is empty
-])
-def test_bf16_stream_k(cuda, m, n, k, quota, epi, batch, monkeypatch):
-    """Stream-K (KX_STREAMK=1): each CTA computes an equal range of k-blocks
-    across tile boundaries and the head of a split tile adds the partial the
-    next range left in L2; results match the oracle as whole tiles do."""
-    monkeypatch.setenv("KX_GEMM_BN", "256")
-    monkeypatch.setenv("KX_STREAMK", "1")
-    err, name = _bf16_matmul_case(m, n, k, epi=epi, batch=batch, quota=quota, seed=m + k)
-    assert name.endswith(",streamk>"), name
-    assert err <= TOL_BF16, err
-    monkeypatch.setenv("KX_STREAMK", "0")
-    err0, name0 = _bf16_matmul_case(m, n, k, epi=epi, batch=batch, quota=quota, seed=m + k)
-    assert not name0.endswith(",streamk>"), name0
-    assert err0 <= TOL_BF16, err0
 
 
 def test_yield_and_continuation(cuda):
