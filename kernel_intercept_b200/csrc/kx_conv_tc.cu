@@ -211,12 +211,12 @@ int im2col_mode() {
 }
 
 // KX_CTA_PAIR: "1" = CTA pairs whenever possible; unset or "0" = one CTA per
-// tile.  Pairs stream 4 stages instead of 3 (the MMA waits for operands 6%
-// of its time instead of 27% on VGG16 conv3_2), but each SM still reads its
-// whole B operand half from its own and half from the peer's shared memory,
-// and on B200 the pair kernel measured 16% slower on conv3_2 and 21% slower
-// over the 13 VGG16 layers than the one-CTA kernel
-// with the merged hi*[hi; lo] product, so pairs are opt-in.
+// tile.  Pairs load half of B per SM, but each SM's tensor core still reads
+// all of B (half from the peer's shared memory) and the three 3xTF32
+// products need three instructions instead of the one-CTA kernel's merged
+// hi*[hi; lo]; on B200 the 13 VGG16 forward layers at batch 32 took 7.23 ms
+// with pairs against 6.03 ms without (conv3_2 0.624 against 0.574 ms), so
+// pairs are opt-in.
 int pair_mode() {
   const char* v = std::getenv("KX_CTA_PAIR");
   if (v == nullptr || v[0] == 0) return -1;
