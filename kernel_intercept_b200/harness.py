@@ -396,8 +396,9 @@ def run_clients(orion: Orion | None, hp_step, be_step, hp_steps: int, hp_warmup:
     identity: HP = 0, BE = 1, 2, ... registered on each thread as the
     reference drivers do.  be_step is one step function or a list of them
     (one BE client each); the BE result is returned in the same form.
-    on_start, when given, runs once after every client finished its warm-up
-    and before any issues a measured step."""
+    on_start, when given, runs once right before HP's first timed step (after
+    every client finished its warm-up; HP's last warm-up step runs beside the
+    BE loops), or at the start barrier when there is no HP loop."""
     import torch
 
     be_steps = list(be_step) if isinstance(be_step, (list, tuple)) else [be_step]
@@ -410,7 +411,9 @@ def run_clients(orion: Orion | None, hp_step, be_step, hp_steps: int, hp_warmup:
     dev = torch.cuda.current_device()
     stop = threading.Event()
     parties = (1 if with_hp else 0) + len(be_steps)
-    ready = threading.Barrier(max(1, parties), action=on_start)
+    # on_start runs in the HP thread right before its first timed step (after
+    # its warm-up), or as the start barrier's action when there is no HP loop
+    ready = threading.Barrier(max(1, parties), action=None if with_hp else on_start)
 
     def hp_thread():
         try:
@@ -420,7 +423,11 @@ def run_clients(orion: Orion | None, hp_step, be_step, hp_steps: int, hp_warmup:
                 orion.orion_set_client_idx(0)
                 orion.orion_register_client_stream(0, ctypes.c_void_p(s.cuda_stream))
             with torch.cuda.stream(s):
-                for _ in range(hp_warmup):
+                # the last warm-up step runs after the start barrier, beside the
+                # BE clients' loops, so the first timed step is not the first
+                # one HP issues against them
+                pre = hp_warmup - 1 if hp_warmup > 1 and be_steps else hp_warmup
+                for _ in range(pre):
                     hp_step()
                 # torch creates a CUDA event at its first record, and creating
                 # one can block the thread for milliseconds (the driver grows its
@@ -433,6 +440,11 @@ def run_clients(orion: Orion | None, hp_step, be_step, hp_steps: int, hp_warmup:
                     ev.record(s)
                 s.synchronize()
                 ready.wait()
+                for _ in range(hp_warmup - pre):
+                    hp_step()
+                s.synchronize()
+                if on_start is not None:
+                    on_start()
                 first.record(s)
                 for a, b in evs:
                     t_issue = time.perf_counter()
