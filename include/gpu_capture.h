@@ -389,6 +389,8 @@ bool enqueue_operation(OperationPtr op);
 /** BE client threads pass here before queueing an op (see
  *  Scheduler::be_issue_gate); a no-op for the HP client. */
 void be_issue_gate(int client_idx);
+/** The HP client queued an op (see be_issue_gate). */
+void note_hp_issue();
 /** Bounded wait for the worker (see OperationRecord::wait_completion);
  *  returns the op's result, cudaErrorTimeout when the client gave up. */
 cudaError_t wait_operation(OperationPtr op);

@@ -138,15 +138,17 @@ public:
     /** Profiling sessions also time the kernels the interposer re-issues. */
     void set_profile_launches(bool on) { profile_launches_.store(on); }
     int be_keep_sms() const { return be_keep_sms_.load(); }
-    /** A BE client thread about to queue an op while HP is active waits (at
-     *  most KX_BE_HOST_HOLD_US per op, default 3000; 0 turns it off) until
-     *  HP is idle, unless it holds the Python interpreter lock.  PyTorch
-     *  releases that lock around every operator, so a BE thread held here
-     *  leaves the interpreter to the HP client's thread while HP issues.
-     *  Measured (one B200, HP paced at a third of the time): HP LLaMA vs two
-     *  BE GPT trainings, p99 1.14-1.15x solo without, 1.04x with, BE keeping
-     *  0.64 of its rate (0.67 without). */
+    /** A BE client thread about to queue an op while the HP client is
+     *  issuing (it queued an op within the last KX_BE_HOST_WINDOW_US, default
+     *  500) waits until HP stops issuing, at most KX_BE_HOST_HOLD_US per op
+     *  (default 3000; 0 turns the gate off), unless it holds the Python
+     *  interpreter lock.  PyTorch releases that lock around every operator,
+     *  so a BE thread held here leaves the interpreter to the HP client's
+     *  thread while it issues; once HP waits for its results, BE issues
+     *  again. */
     void be_issue_gate(int client_idx);
+    /** The HP client queued an op (the issue gate's clock). */
+    void note_hp_issue();
     void set_be_host_hold_us(int us) { be_host_hold_ns_.store(us < 0 ? 0 : 1000LL * us); }
     int be_host_hold_us() const { return static_cast<int>(be_host_hold_ns_.load() / 1000); }
     volatile int* hp_flag_host() const { return hp_flag_host_; }
@@ -202,6 +204,8 @@ private:
     // HP client (KX_BE_MAX_US, default 50 us); longer ones wait for HP to idle.
     float be_max_ns_{50000.0f};
     std::atomic<long long> be_host_hold_ns_{3000000};
+    long long be_host_window_ns_{500000};
+    std::atomic<long long> hp_last_issue_ns_{-(1LL << 60)};
     cudaStream_t flag_stream_{nullptr};
     void publish_hp_flag(int value);
     std::atomic<int> be_keep_sms_{0};

@@ -283,7 +283,10 @@ OperationPtr create_operation(int client_idx, OperationType type) {
 
 bool enqueue_operation(OperationPtr op) {
   if (!op) return false;
-  if (op->client_idx > 0) be_issue_gate(op->client_idx);
+  if (op->client_idx > 0)
+    be_issue_gate(op->client_idx);
+  else
+    note_hp_issue();
   if (g_capture_state.client_queues[op->client_idx]->push(op)) return true;
   LOG_ERROR("client %d: queue full for %lld ms; op %lu (%s) dropped", op->client_idx,
             (long long)(wait_timeout_ns() / 1000000), (unsigned long)op->op_id,

@@ -241,6 +241,8 @@ bool Scheduler::init(int num_clients, const SchedulerConfig& config) {
   if (const char* s = std::getenv("KX_BE_MAX_US")) be_max_ns_ = std::max(0.0f, std::strtof(s, nullptr)) * 1000.f;
   if (const char* s = std::getenv("KX_BE_HOST_HOLD_US"))
     be_host_hold_ns_.store(std::max(0LL, std::atoll(s)) * 1000);
+  if (const char* s = std::getenv("KX_BE_HOST_WINDOW_US"))
+    be_host_window_ns_ = std::max(0LL, std::atoll(s)) * 1000;
   ORION_REAL(cudart, cudaEventCreateWithFlags)(&hp_last_event_, cudaEventDisableTiming);
   g_orion_state.init(num_clients, sms);
   g_orion_state.sm_threshold = config_.sm_threshold;
@@ -396,19 +398,30 @@ int (*gil_check_fn())() {
 
 void Scheduler::be_issue_gate(int client_idx) {
   const long long hold = be_host_hold_ns_.load(std::memory_order_relaxed);
-  if (client_idx <= 0 || hold <= 0 || isolated_ || hp_flag_host_ == nullptr) return;
-  if (hp_flag_host_[0] == 0 || !running_.load()) return;
+  if (client_idx <= 0 || hold <= 0 || isolated_) return;
+  // HP is issuing while its client queued an op within the window
+  const long long window = be_host_window_ns_;
+  auto hp_issuing = [&] {
+    return mono_ns() - hp_last_issue_ns_.load(std::memory_order_relaxed) < window;
+  };
+  if (!hp_issuing() || !running_.load()) return;
   // a thread that holds the interpreter lock (or a process without one)
   // never waits here: the HP thread would wait for it in turn
   auto chk = gil_check_fn();
   if (chk == nullptr || chk() != 0) return;
   stats(client_idx).host_holds.fetch_add(1);
   const int64_t deadline = mono_ns() + hold;
-  while (hp_flag_host_[0] != 0 && running_.load() && mono_ns() < deadline)
+  while (hp_issuing() && running_.load() && mono_ns() < deadline)
     std::this_thread::sleep_for(std::chrono::microseconds(20));
 }
 
 void be_issue_gate(int client_idx) { g_scheduler.be_issue_gate(client_idx); }
+
+void Scheduler::note_hp_issue() {
+  hp_last_issue_ns_.store(mono_ns(), std::memory_order_relaxed);
+}
+
+void note_hp_issue() { g_scheduler.note_hp_issue(); }
 
 void Scheduler::publish_hp_flag(int value) {
   trace_marker(value != 0 ? "hp_flag_raise" : "hp_flag_clear", value);

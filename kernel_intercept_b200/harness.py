@@ -396,9 +396,10 @@ def run_clients(orion: Orion | None, hp_step, be_step, hp_steps: int, hp_warmup:
     identity: HP = 0, BE = 1, 2, ... registered on each thread as the
     reference drivers do.  be_step is one step function or a list of them
     (one BE client each); the BE result is returned in the same form.
-    on_start, when given, runs once right before HP's first timed step (after
-    every client finished its warm-up; HP's last warm-up step runs beside the
-    BE loops), or at the start barrier when there is no HP loop."""
+    on_start, when given, runs once in the HP thread after every client
+    finished its warm-up, before HP's last warm-up step, which runs beside
+    the BE loops and flows into the timed steps without a synchronisation
+    (or at the start barrier when there is no HP loop)."""
     import torch
 
     be_steps = list(be_step) if isinstance(be_step, (list, tuple)) else [be_step]
@@ -440,11 +441,14 @@ def run_clients(orion: Orion | None, hp_step, be_step, hp_steps: int, hp_warmup:
                     ev.record(s)
                 s.synchronize()
                 ready.wait()
-                for _ in range(hp_warmup - pre):
-                    hp_step()
-                s.synchronize()
                 if on_start is not None:
                     on_start()
+                # no synchronisation between this warm-up step and the timed
+                # ones: an idle gap would let the scheduler lower the HP flag
+                # and the BE clients' queued work take the GPU just as the
+                # first timed step starts
+                for _ in range(hp_warmup - pre):
+                    hp_step()
                 first.record(s)
                 for a, b in evs:
                     t_issue = time.perf_counter()

@@ -193,13 +193,13 @@ def run_vgg_bwd(batch, check):
     print(json.dumps({k: round(v, 3) for k, v in tot.items()}), flush=True)
 
 
-def run_gemm(check, only=""):
+def run_gemm(check, only="", fp32_mode="3xtf32"):
     import torch
 
     from . import kx
     torch.backends.cuda.matmul.allow_tf32 = False
     torch.manual_seed(0)
-    ex = kx.current_exec()
+    ex = kx.current_exec(fp32_mode=kx.FP32_FFMA if fp32_mode == "ffma" else kx.FP32_3XTF32)
     for name, ta, tb, m, n, k, batch, dt in GEMMS:
         if only and only not in name:
             continue
@@ -261,13 +261,15 @@ def main(argv=None):
     ap.add_argument("--batch", type=int, default=32)
     ap.add_argument("--check", action="store_true")
     ap.add_argument("--only", default="", help="gemm: run the shapes whose name contains this")
+    ap.add_argument("--fp32-mode", default="3xtf32", choices=["3xtf32", "ffma"],
+                    help="gemm: arithmetic of the fp32 shapes on kx")
     args = ap.parse_args(argv)
     if args.what == "vgg":
         run_vgg(args.batch, args.check)
     elif args.what == "vggbwd":
         run_vgg_bwd(args.batch, args.check)
     else:
-        run_gemm(args.check, args.only)
+        run_gemm(args.check, args.only, args.fp32_mode)
     return 0
 
 
