@@ -261,8 +261,8 @@ int orion_get_be_keep_sms();
 int orion_set_sm_budgets(int hp_sms, int be_sms);
 /** Counters of one client: ops, kx_ops, passthrough_ops, be_blocked, yields, errors. */
 int orion_get_client_stats(int client_idx, unsigned long long* out6);
-/** Longest time (us) a BE client thread waits before queueing an op while HP
- *  is active (Scheduler::be_issue_gate); 0 = never waits. */
+/** Longest time (us) a BE client thread waits before queueing an op while the
+ *  HP client is issuing (Scheduler::be_issue_gate); 0 = never waits. */
 void orion_set_be_host_hold_us(int us);
 int orion_get_be_host_hold_us();
 /** Ops of one BE client whose thread waited at the issue gate. */

@@ -130,11 +130,6 @@ struct GemmParams {
   int wide16;
   // 3xTF32: k-blocks per TMEM accumulator segment (0 = Cfg::SEG)
   int seg_kb;
-  // 1: short K (16-bit, a few k-blocks per tile): the launch streams operands
-  // through STAGES - 1 stages and the last stage's shared memory holds
-  // Cfg::EXTRA_BUFS more 4 KB epilogue staging buffers per epilogue warp, so
-  // more TMA stores of D are in flight
-  int short_k;
   // 1: the epilogue writes D through shared memory and TMA stores (map tmD:
   // {m, n, batch} for GEMMs, {Q, P, K, N} for box-tiled convolutions,
   // {P*Q, K, N} for im2col convolutions); 0: one st.global per element
@@ -245,9 +240,6 @@ struct GemmCfg {
   // then the barrier block
   static constexpr int EPI_OFF = STAGE_REGION;
   static constexpr int EPI_BYTES = 4 * 2 * 4096;
-  // staging buffers per epilogue warp that one operand stage can hold
-  static constexpr int EXTRA_BUFS_RAW = STAGE_BYTES / (4 * 4096);
-  static constexpr int EXTRA_BUFS = EXTRA_BUFS_RAW > 6 ? 6 : EXTRA_BUFS_RAW;
   static constexpr int BAR_OFF = EPI_OFF + EPI_BYTES;
   static constexpr int SMEM_BYTES = 1024 /*align slack*/ + BAR_OFF + 1024 /*barriers*/;
   static_assert(STAGES >= 2, "not enough shared memory for two stages");
@@ -450,9 +442,7 @@ __global__ void __launch_bounds__(256, 1)
   static_assert(!CONV || (Cfg::AR == Arith::F32x3 && !Cfg::A_MN),
                 "implicit convolution: 3xTF32 with a K-major A tile");
   const long long t_start = clock64();  // CTA lifetime starts here
-  // operand stages this launch streams through (short K: one fewer; the
-  // last one then holds epilogue staging buffers)
-  const int S = Cfg::STAGES - (p.short_k ? 1 : 0);
+  constexpr int S = Cfg::STAGES;
   constexpr int R = Cfg::RING;
   // CTA pair (Cfg::PAIR): rank 0 leads (tile ids, MMAs), rank 1 follows
   constexpr bool PAIR = Cfg::PAIR;
@@ -1070,20 +1060,6 @@ __global__ void __launch_bounds__(256, 1)
     const bool use_tma_store = p.tma_store != 0 && !split && (p.wide16 == 0 || plain_epi);
     uint32_t epi_chunk = 0;
     uint32_t sc = 0;
-    // this warp's staging buffers: two after the stages, plus EXTRA_BUFS in
-    // the last operand stage for short K; a buffer is rewritten only after
-    // the TMA store issued from it nbuf chunks earlier has read it
-    const uint32_t nbuf = 2u + (p.short_k ? static_cast<uint32_t>(Cfg::EXTRA_BUFS) : 0u);
-    auto next_buf = [&]() -> uint8_t* {
-      const uint32_t k = epi_chunk % nbuf;
-      ++epi_chunk;
-      uint8_t* b = k < 2 ? smem + Cfg::EPI_OFF + (q * 2 + k) * 4096
-                         : smem + (Cfg::STAGES - 1) * Cfg::STAGE_BYTES +
-                               (q * Cfg::EXTRA_BUFS + (k - 2)) * 4096;
-      if (lane == 0) bulk_wait_read_upto(nbuf - 1);
-      __syncwarp();
-      return b;
-    };
     for (uint32_t slot = 0;; ++slot) {
       const uint32_t r = slot % R;
       bool ok = leader ? mbar_wait(smem_addr(&sb->ring_full[r]), (slot / R) & 1, wc)
@@ -1172,7 +1148,10 @@ __global__ void __launch_bounds__(256, 1)
       // two chunks earlier has read it.
       auto emit_tma = [&](int c0, const float* acc) {
         const int col0 = nb * Cfg::BN + c0;
-        uint8_t* buf = next_buf();
+        uint8_t* buf = smem + Cfg::EPI_OFF + (q * 2 + (epi_chunk & 1u)) * 4096;
+        ++epi_chunk;
+        if (lane == 0) bulk_wait_group_read<1>();
+        __syncwarp();
         // element (column j, row lane) at index j*32 + lane of the buffer
         float* fbuf = reinterpret_cast<float*>(buf);
         if (plain_epi && p.d_type == DT_F32) {
@@ -1316,7 +1295,10 @@ __global__ void __launch_bounds__(256, 1)
             tmem_ld_wait();
             tmem_regs_ready(va);
             tmem_regs_ready(vb);
-            uint8_t* buf = next_buf();
+            uint8_t* buf = smem + Cfg::EPI_OFF + (q * 2 + (epi_chunk & 1u)) * 4096;
+            ++epi_chunk;
+            if (lane == 0) bulk_wait_group_read<1>();
+            __syncwarp();
             if (p.d_type == DT_BF16) {
               __nv_bfloat16* hb = reinterpret_cast<__nv_bfloat16*>(buf);
 #pragma unroll

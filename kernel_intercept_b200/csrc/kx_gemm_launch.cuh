@@ -32,11 +32,6 @@ constexpr const char* arith_name() {
   return AR == Arith::F32x3 ? "f32x3" : AR == Arith::TF32 ? "tf32" : AR == Arith::BF16 ? "bf16" : "f16";
 }
 
-inline bool short_k_disabled() {
-  const char* s = std::getenv("KX_SHORT_K");
-  return s != nullptr && s[0] == '0';
-}
-
 // KX_GEMM_PAIR=1: 16-bit GEMMs with K-major operands run on 2-CTA clusters
 // (256-row tiles, cta_group::2 MMAs; each SM loads half of the B tile).  Off
 // by default: on B200 8192^3 bf16 ran at 766 TFLOP/s with pairs against 1328
@@ -183,13 +178,6 @@ int launch_gemm_tc(const Exec& e, const TcProblem& pr, GemmParams p) {
       p.wide16 = box_cols == 64 ? 1 : 0;
     }
   }
-  // Short K: tiles of a few k-blocks are bound by their epilogue's stores;
-  // three operand stages cover the pipeline and the fourth holds staging
-  // buffers (KX_SHORT_K=0 turns it off)
-  p.short_k = (!Cfg::SPLIT && !Cfg::TAPR && p.tma_store && p.splits == 1 && p.num_kb <= 4 &&
-               Cfg::STAGES >= 3 && Cfg::EXTRA_BUFS >= 1 && !short_k_disabled())
-                  ? 1
-                  : 0;
   int grid = persistent_grid(e, p.num_tiles * (PAIR ? 2 : 1));
   if (PAIR) {
     grid = pair_grid(kern, Cfg::THREADS, Cfg::SMEM_BYTES, grid);

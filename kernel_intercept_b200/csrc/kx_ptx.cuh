@@ -202,20 +202,6 @@ KX_DEV void bulk_wait_group_read() {
   asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
 }
 
-// bulk_wait_group_read with a run-time bound (0..7 groups left in flight).
-KX_DEV void bulk_wait_read_upto(uint32_t n) {
-  switch (n) {
-    case 0: bulk_wait_group_read<0>(); break;
-    case 1: bulk_wait_group_read<1>(); break;
-    case 2: bulk_wait_group_read<2>(); break;
-    case 3: bulk_wait_group_read<3>(); break;
-    case 4: bulk_wait_group_read<4>(); break;
-    case 5: bulk_wait_group_read<5>(); break;
-    case 6: bulk_wait_group_read<6>(); break;
-    default: bulk_wait_group_read<7>(); break;
-  }
-}
-
 // Wait until every committed bulk group has completed (writes performed).
 KX_DEV void bulk_wait_group_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
