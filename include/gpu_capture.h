@@ -387,8 +387,9 @@ OperationPtr create_operation(int client_idx, OperationType type);
  *  cudaErrorTimeout, never runs, and the client's error latch is set. */
 bool enqueue_operation(OperationPtr op);
 /** BE client threads pass here before queueing an op (see
- *  Scheduler::be_issue_gate); a no-op for the HP client. */
-void be_issue_gate(int client_idx);
+ *  Scheduler::be_issue_gate); a no-op for the HP client and for ops other
+ *  than kernel launches and captured dense ops. */
+void be_issue_gate(int client_idx, OperationType type);
 /** The HP client queued an op (see be_issue_gate). */
 void note_hp_issue();
 /** Bounded wait for the worker (see OperationRecord::wait_completion);

@@ -138,7 +138,7 @@ public:
     /** Profiling sessions also time the kernels the interposer re-issues. */
     void set_profile_launches(bool on) { profile_launches_.store(on); }
     int be_keep_sms() const { return be_keep_sms_.load(); }
-    /** A BE client thread about to queue an op while the HP client is
+    /** A BE client thread about to queue a kernel while the HP client is
      *  issuing (it queued an op within the last KX_BE_HOST_WINDOW_US, default
      *  500) waits until HP stops issuing, at most KX_BE_HOST_HOLD_US per op
      *  (default 3000; 0 turns the gate off), unless it holds the Python

@@ -284,7 +284,7 @@ OperationPtr create_operation(int client_idx, OperationType type) {
 bool enqueue_operation(OperationPtr op) {
   if (!op) return false;
   if (op->client_idx > 0)
-    be_issue_gate(op->client_idx);
+    be_issue_gate(op->client_idx, op->type);
   else
     note_hp_issue();
   if (g_capture_state.client_queues[op->client_idx]->push(op)) return true;

@@ -415,7 +415,11 @@ void Scheduler::be_issue_gate(int client_idx) {
     std::this_thread::sleep_for(std::chrono::microseconds(20));
 }
 
-void be_issue_gate(int client_idx) { g_scheduler.be_issue_gate(client_idx); }
+void be_issue_gate(int client_idx, OperationType type) {
+  // kernels only: allocations and copies may be issued under a lock (the
+  // caching allocator's) that the HP thread also needs
+  if (is_kernel_op(type)) g_scheduler.be_issue_gate(client_idx);
+}
 
 void Scheduler::note_hp_issue() {
   hp_last_issue_ns_.store(mono_ns(), std::memory_order_relaxed);

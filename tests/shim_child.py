@@ -572,6 +572,64 @@ def scenario_gpt_train(orion):
     return {"errors": errs, "stats": stats, "loss": float(loss_kx)}
 
 
+def scenario_gpt_curve(orion):
+    """End-to-end: 20 AdamW steps of a two-layer GPT decoder (fp32, batch 8 x
+    256, cross-entropy against fixed random targets) from one seed, three
+    times: captured on the kx kernels, on the real libraries (TF32 off), and
+    as a float64 copy.  Returns the three loss curves and the parameters'
+    normwise distance to the float64 run after the last step."""
+    import copy
+
+    import torch
+    import torch.nn.functional as F
+
+    from kernel_intercept_b200 import harness
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.manual_seed(0)
+    base = harness.make_gpt(layers=2, device="cuda", dropout=0.0)
+    tok = torch.randint(0, 32000, (8, 256), device="cuda")
+    tgt = torch.randint(0, 32000, (8, 256), device="cuda")
+    steps = 20
+
+    def train(model):
+        opt = torch.optim.AdamW(model.parameters(), lr=3e-4)
+        losses = []
+        for _ in range(steps):
+            opt.zero_grad(set_to_none=True)
+            logits = model(tok)
+            loss = F.cross_entropy(logits.view(-1, logits.shape[-1]), tgt.view(-1))
+            loss.backward()
+            opt.step()
+            losses.append(loss.detach().double())
+        return torch.stack(losses), model
+
+    m_lib, m_kx, m64 = copy.deepcopy(base), copy.deepcopy(base), copy.deepcopy(base).double()
+    assert orion.orion_init_scheduler(1) == 0
+    orion.orion_set_capture(0)
+    curve_lib, m_lib = train(m_lib)
+    curve64, m64 = train(m64)
+    torch.cuda.synchronize()
+    orion.orion_start_scheduler_thread()
+    orion.orion_set_capture(1)
+    curve_kx, m_kx = run_on_client(orion, 0, lambda: train(m_kx))
+    orion.orion_set_capture(0)
+    stats = orion.stats(0)
+    orion.orion_stop_scheduler()
+    p64 = dict(m64.named_parameters())
+
+    def param_err(m):
+        return max(rel(p.detach(), p64[n].detach()) for n, p in m.named_parameters())
+
+    return {"stats": stats,
+            "curve_kx": curve_kx.tolist(), "curve_lib": curve_lib.tolist(),
+            "curve64": curve64.tolist(),
+            "loss_err_kx": [abs(a - b) / abs(b) for a, b in zip(curve_kx.tolist(),
+                                                               curve64.tolist())],
+            "loss_err_lib": [abs(a - b) / abs(b) for a, b in zip(curve_lib.tolist(),
+                                                                curve64.tolist())],
+            "param_err_kx": param_err(m_kx), "param_err_lib": param_err(m_lib)}
+
+
 def scenario_tables(orion):
     """Per-client kernel tables measured through the interposer's profiler
     (kernel_intercept_b200.profile_tables): one row per kernel op the worker

@@ -131,6 +131,19 @@ def test_gpt_training_step_through_interposer():
         assert e["kx_vs_f64"] <= e["lib_vs_f64"] + F32_TOL, (name, e)
 
 
+def test_gpt_loss_curve_through_interposer():
+    """20 AdamW steps of a two-layer GPT from one seed: at every step the loss
+    on kx is no further from the float64 run than the real libraries' fp32
+    loss is, plus 1e-5, and so are the parameters after the last step."""
+    res = run_child("gpt_curve", timeout=900)
+    st = res["stats"]
+    assert st["errors"] == 0 and st["passthrough_ops"] == 0, st
+    assert res["curve64"][-1] < res["curve64"][0], res["curve64"]  # it trains
+    for i, (ek, el) in enumerate(zip(res["loss_err_kx"], res["loss_err_lib"])):
+        assert ek <= el + F32_TOL, (i, ek, el)
+    assert res["param_err_kx"] <= res["param_err_lib"] + F32_TOL, res
+
+
 def test_hp_be_clients_contend():
     res = run_child("hpbe")
     for c in ("0", "1"):
