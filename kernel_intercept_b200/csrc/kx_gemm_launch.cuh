@@ -32,15 +32,15 @@ constexpr const char* arith_name() {
   return AR == Arith::F32x3 ? "f32x3" : AR == Arith::TF32 ? "tf32" : AR == Arith::BF16 ? "bf16" : "f16";
 }
 
-// KX_GEMM_PAIR=1: 16-bit GEMMs with K-major operands run on 2-CTA clusters
-// (256-row tiles, cta_group::2 MMAs; each SM loads half of the B tile).  Off
-// by default: on B200 8192^3 bf16 ran at 766 TFLOP/s with pairs against 1328
-// without, 2048 x 4096 x 2048 at 594 against 756 (the follower forwards every
-// landed stage to the leader, one more cross-CTA wait per k-block on the MMA
-// issuer's path).
-inline bool gemm_pair_mode() {
+// KX_GEMM_PAIR: "1" = every 16-bit GEMM with K-major operands runs on 2-CTA
+// clusters (256-row tiles, cta_group::2 MMAs, each SM loading half of the B
+// tile); "0" = never; unset = where pairs measured faster on B200: K of at
+// least 4096 over at least four waves of 128 x 256 tiles (8192^3: 1434-1438
+// TFLOP/s against 1287-1340 with one CTA per tile; the K = 2048 GEMMs of the
+// LLaMA step lose 3-9% on pairs).
+inline int gemm_pair_mode() {
   const char* s = std::getenv("KX_GEMM_PAIR");
-  return s != nullptr && s[0] == '1';
+  return s == nullptr ? -1 : (s[0] == '1' ? 1 : (s[0] == '0' ? 0 : -1));
 }
 
 template <int BN, Arith AR, bool AMN, bool BMN, bool PAIR = false>
@@ -218,7 +218,14 @@ int dispatch_gemm_tc(int bn, bool amn, bool bmn, const Exec& e, const TcProblem&
     return launch_gemm_tc<BNV, AR, true, true>(e, pr, p);                       \
   }
   if constexpr (AR == Arith::BF16 || AR == Arith::F16) {
-    if (!amn && !bmn && gemm_pair_mode()) {
+    bool pair = false;
+    if (!amn && !bmn) {
+      const int pm = gemm_pair_mode();
+      const long long tiles = static_cast<long long>((pr.m + 127) / 128) * ((pr.n + 255) / 256) *
+                              (pr.batch > 0 ? pr.batch : 1);
+      pair = pm == 1 || (pm < 0 && pr.k >= 4096 && tiles >= 4LL * device_info().num_sms);
+    }
+    if (pair) {
       const int rc = bn == 256   ? launch_gemm_tc<256, AR, false, false, true>(e, pr, p)
                      : bn == 128 ? launch_gemm_tc<128, AR, false, false, true>(e, pr, p)
                                  : launch_gemm_tc<64, AR, false, false, true>(e, pr, p);

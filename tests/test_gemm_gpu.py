@@ -362,8 +362,11 @@ def test_matmul_epilogues_bf16_wide_tiles(cuda, epi, beta, monkeypatch):
     assert err <= TOL_BF16, err
 
 
-def test_yield_and_continuation(cuda):
-    """A BE launch that stops at tile boundaries resumes exactly where it left off."""
+@pytest.mark.parametrize("arith", ["f32", "bf16_pair"])
+def test_yield_and_continuation(cuda, arith, monkeypatch):
+    """A BE launch that stops at tile boundaries resumes exactly where it left
+    off: 3xTF32 on single CTAs, and bf16 on 2-CTA clusters (the leader takes
+    the tiles and the follower follows its stops)."""
     kx = _kx()
     import torch
     rng = np.random.default_rng(31)
@@ -371,21 +374,41 @@ def test_yield_and_continuation(cuda):
     A = rng.standard_normal(k * m).astype(np.float32)
     B = rng.standard_normal(k * n).astype(np.float32)
     ref = np.zeros(m * n, np.float32)
-    o.sgemm(1, 0, m, n, k, 1.0, A, k, B, k, 0.0, ref, m)
-    dA, dB = _dev(A), _dev(B)
-    dC = torch.zeros(m * n, device="cuda")
+    if arith == "f32":
+        o.sgemm(1, 0, m, n, k, 1.0, A, k, B, k, 0.0, ref, m)
+        dA, dB = _dev(A), _dev(B)
+        dC = torch.zeros(m * n, device="cuda")
+        tol = TOL_F32
+
+        def op(ex):
+            kx.sgemm(ex, 1, 0, m, n, k, 1.0, dA.data_ptr(), k, dB.data_ptr(), k, 0.0,
+                     dC.data_ptr(), m)
+    else:
+        monkeypatch.setenv("KX_GEMM_PAIR", "1")
+        A16, B16 = o.f32_to_bf16_bits(A), o.f32_to_bf16_bits(B)
+        o.gemm_ex(1, 0, m, n, k, 1.0, A16, o.R_16BF, k, B16, o.R_16BF, k, 0.0, None, o.R_32F,
+                  m, D=ref, Dtype=o.R_32F, ldd=m)
+        dA = _dev(A16.view(np.int16)).view(torch.bfloat16)
+        dB = _dev(B16.view(np.int16)).view(torch.bfloat16)
+        dC = torch.zeros(m * n, device="cuda")
+        tol = TOL_BF16
+
+        def op(ex):
+            kx.gemm_ex(ex, 1, 0, m, n, k, 1.0, dA.data_ptr(), kx.R_16BF, k, dB.data_ptr(),
+                       kx.R_16BF, k, 0.0, dC.data_ptr(), kx.R_32F, m)
     flags = kx.HostFlags(2)  # [0] = yield flag, [1] = done flag
     stream = torch.cuda.Stream()
     try:
         # 1) flag < 0 before launch: no CTA takes a tile, op reports "not done"
         flags[0] = -1
         flags[1] = -1
-        ex = kx.make_exec(stream=stream, sm_quota=4, yield_flag=flags.dev(0),
-                          done_flag=flags.dev(1))
-        kx.sgemm(ex, 1, 0, m, n, k, 1.0, dA.data_ptr(), k, dB.data_ptr(), k, 0.0, dC.data_ptr(), m)
+        op(kx.make_exec(stream=stream, sm_quota=4, yield_flag=flags.dev(0),
+                        done_flag=flags.dev(1)))
         stream.synchronize()
         assert flags[1] == 0
         assert float(dC.abs().max()) == 0.0
+        if arith != "f32":
+            assert ",pair>" in kx.last_kernel_name(), kx.last_kernel_name()
         # 2) flag lowered; per-launch budget of one tile per CTA forces many relaunches
         flags[0] = 0
         ex = kx.make_exec(stream=stream, sm_quota=4, yield_flag=flags.dev(0),
@@ -393,34 +416,31 @@ def test_yield_and_continuation(cuda):
         launches = 0
         while True:
             flags[1] = -1
-            kx.sgemm(ex, 1, 0, m, n, k, 1.0, dA.data_ptr(), k, dB.data_ptr(), k, 0.0,
-                     dC.data_ptr(), m)
+            op(ex)
             stream.synchronize()
             launches += 1
             if flags[1] == 1:
                 break
             assert flags[1] == 0 and launches < 1000
         assert launches > 2
-        assert o.normwise_rel_err(dC.cpu().numpy(), ref) <= TOL_F32
+        assert o.normwise_rel_err(dC.cpu().numpy(), ref) <= tol
         # 3) flag > 0: CTAs at or above the budget retire, the rest finish the op
         dC.zero_()
         flags[0] = 2
         flags[1] = -1
-        ex = kx.make_exec(stream=stream, sm_quota=16, yield_flag=flags.dev(0),
-                          done_flag=flags.dev(1))
-        kx.sgemm(ex, 1, 0, m, n, k, 1.0, dA.data_ptr(), k, dB.data_ptr(), k, 0.0, dC.data_ptr(), m)
+        op(kx.make_exec(stream=stream, sm_quota=16, yield_flag=flags.dev(0),
+                        done_flag=flags.dev(1)))
         stream.synchronize()
         assert flags[1] == 1
-        assert o.normwise_rel_err(dC.cpu().numpy(), ref) <= TOL_F32
+        assert o.normwise_rel_err(dC.cpu().numpy(), ref) <= tol
         flags[0] = 0
         # 4) the slot was reset: a plain follow-up op on the same stream is complete
         dC.zero_()
-        ex = kx.make_exec(stream=stream, done_flag=flags.dev(1))
         flags[1] = -1
-        kx.sgemm(ex, 1, 0, m, n, k, 1.0, dA.data_ptr(), k, dB.data_ptr(), k, 0.0, dC.data_ptr(), m)
+        op(kx.make_exec(stream=stream, done_flag=flags.dev(1)))
         stream.synchronize()
         assert flags[1] == 1
-        assert o.normwise_rel_err(dC.cpu().numpy(), ref) <= TOL_F32
+        assert o.normwise_rel_err(dC.cpu().numpy(), ref) <= tol
     finally:
         flags.close()
 
