@@ -166,41 +166,7 @@ struct ConvPlan {
   int splits;  // K slices (partials reduced by kx_splitk_reduce)
   int wbox, hbox;
   bool pair;   // 2-CTA clusters: 256-row tiles, cta_group::2 MMAs
-  bool tapr;   // box tiles whose A box serves every filter row (tap reuse)
 };
-
-// KX_CONV_TAPR: unset or "0" = off; "1" = tap reuse where whole boxes tile
-// the output exactly; "2" = wherever the geometry allows it.  Off by
-// default: on B200 it cut the L2 -> SM bytes of VGG16 conv1_2 by 1.6x yet
-// ran 10% slower (1.18 vs 1.07 ms; conv2_x 3-4% slower), the MMA issuer and
-// not operand delivery being what limits these layers.
-int tapr_mode() {
-  const char* v = std::getenv("KX_CONV_TAPR");
-  if (v == nullptr || v[0] == 0) return 0;
-  return v[0] - '0';
-}
-
-// Box tile for tap reuse: wbox x hbox = 128 output pixels, wbox a multiple
-// of 8 (a filter row's A rows then start on a 1024-byte swizzle atom) and the
-// haloed box (hbox + (R-1) * dil_h rows) within the A stage.  Fewest tiles,
-// then the narrowest halo.  Returns false when no box fits.
-bool choose_box_tapr(int P, int Q, int R, int dh, int& wbox, int& hbox, bool& exact) {
-  long long best = -1;
-  for (int wb : {16, 32, 8}) {
-    const int hb = 128 / wb;
-    const int rows = wb * (hb + (R - 1) * dh);
-    if (rows > 192 || hb + (R - 1) * dh > 256) continue;
-    const long long tiles = static_cast<long long>((Q + wb - 1) / wb) * ((P + hb - 1) / hb);
-    if (best < 0 || tiles < best) {
-      best = tiles;
-      wbox = wb;
-      hbox = hb;
-    }
-  }
-  if (best < 0) return false;
-  exact = Q % wbox == 0 && P % hbox == 0;
-  return true;
-}
 
 // KX_CONV_IM2COL: "0" = box tiles; unset or "1" = im2col tiles whenever the
 // map can express the geometry (see plan_conv).
@@ -232,21 +198,8 @@ void im2col_corners(const ConvShape& t, int lower[2], int upper[2]) {
 }
 
 ConvPlan plan_conv(const ConvShape& g, const ConvShape& t, int cp, int sms) {
-  ConvPlan pl{64, false, 1, 0, 0, false, false};
+  ConvPlan pl{64, false, 1, 0, 0, false};
   choose_box(g.P, g.Q, t.sw, t.sh, pl.wbox, pl.hbox);
-  // Tap reuse: a box loaded once per (filter column, channel block) feeds
-  // all R filter rows, so each input row crosses L2 -> SM about 128 / rows
-  // of the box times R times less often than with per-tap tiles.
-  const int tmode = tapr_mode();
-  if (tmode != 0 && t.sw == 1 && t.sh == 1 && t.R >= 2) {
-    int wb = 0, hb = 0;
-    bool exact = false;
-    if (choose_box_tapr(g.P, g.Q, t.R, t.dh, wb, hb, exact) && (exact || tmode == 2)) {
-      pl.tapr = true;
-      pl.wbox = wb;
-      pl.hbox = hb;
-    }
-  }
   const long long m = static_cast<long long>(g.N) * g.P * g.Q;
   int lo[2], up[2];
   im2col_corners(t, lo, up);
@@ -261,14 +214,14 @@ ConvPlan plan_conv(const ConvShape& g, const ConvShape& t, int cp, int sms) {
   // 32: im2col 5.70 ms over the 13 layers, boxes 5.94 ms (no layer more than
   // 0.7% slower with im2col).
   const int mode = im2col_mode();
-  pl.im2col = im2col_ok && mode != 0 && !pl.tapr;
+  pl.im2col = im2col_ok && mode != 0;
   const long long mt = pl.im2col ? (m + 127) / 128 : box_mt;
   // 128-wide channel tiles when they fill the GPU and waste nothing
   if (g.K % 128 == 0 && mt * (g.K / 128) >= sms) pl.bn = 128;
   // CTA pairs: each CTA loads half of B, so 4 stages fit instead of 3
   const long long pair_tiles = (mt + 1) / 2 * ((g.K + pl.bn - 1) / pl.bn);
   const int pmode = pair_mode();
-  pl.pair = sms >= 2 && pmode == 1 && pair_tiles >= 1 && !pl.tapr;
+  pl.pair = sms >= 2 && pmode == 1 && pair_tiles >= 1;
   if (pl.pair) return pl;  // no split-K with pairs
   if (split_k_disabled()) return pl;
   // Split K when the tiles leave the last wave mostly empty: per slice count
@@ -295,15 +248,12 @@ ConvPlan plan_conv(const ConvShape& g, const ConvShape& t, int cp, int sms) {
   return pl;
 }
 
-template <int BN, bool PAIR, bool TAPR = false>
+template <int BN, bool PAIR>
 int launch_conv_tc(const Exec& e, const ConvShape& g, const ConvShape& t, const float* xh,
                    const float* xl, int cp, const float* wp, const float* wp_lo, float* y,
                    float alpha, float beta, const ConvPlan& pl) {
   // t: the geometry the kernel sees (g itself, or the folded 1x1 problem)
-  using Cfg = GemmCfg<BN, Arith::F32x3, false, false, PAIR, TAPR>;
-  if (TAPR && (t.sw != 1 || t.sh != 1 || pl.wbox % 8 != 0 || pl.wbox * pl.hbox != Cfg::BM ||
-               pl.wbox * (pl.hbox + (t.R - 1) * t.dh) > Cfg::TAPR_AROWS))
-    return KX_ERR_UNSUPPORTED;
+  using Cfg = GemmCfg<BN, Arith::F32x3, false, false, PAIR>;
   const long long kd = static_cast<long long>(t.R) * t.S * cp;
   const long long pq = static_cast<long long>(g.P) * g.Q;
   const int wbox = pl.wbox, hbox = pl.hbox;
@@ -322,10 +272,8 @@ int launch_conv_tc(const Exec& e, const ConvShape& g, const ConvShape& t, const 
         !encode_im2col_map(&malo, xl, dims, strides, lo, up, 32, Cfg::BM, es))
       return KX_ERR_UNSUPPORTED;
   } else {
-    // tap reuse: the box also covers the rows of the lower filter rows
     const uint32_t box[4] = {32u, static_cast<uint32_t>(wbox * t.sw),
-                             static_cast<uint32_t>(TAPR ? hbox + (t.R - 1) * t.dh : hbox * t.sh),
-                             1u};
+                             static_cast<uint32_t>(hbox * t.sh), 1u};
     if (!encode_map(&ma, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, xh, dims, strides, box,
                     CU_TENSOR_MAP_SWIZZLE_128B, es) ||
         !encode_map(&malo, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, xl, dims, strides, box,
@@ -375,8 +323,6 @@ int launch_conv_tc(const Exec& e, const ConvShape& g, const ConvShape& t, const 
   p.cv_dil_w = t.dw;
   p.cv_im2col = pl.im2col ? 1 : 0;
   p.cv_pq = static_cast<int>(pq);
-  p.cv_r = t.R;
-  p.cv_arows = TAPR ? wbox * (hbox + (t.R - 1) * t.dh) : 0;
   p.num_mb = pl.im2col ? (p.m + Cfg::BM - 1) / Cfg::BM
                        : p.cv_tiles_w * ((g.P + hbox - 1) / hbox);
   // a pair tile covers two consecutive 128-row blocks (the second may lie
@@ -465,7 +411,7 @@ int launch_conv_tc(const Exec& e, const ConvShape& g, const ConvShape& t, const 
   char* name = names[pl.im2col ? 1 : 0];
   if (name[0] == 0)
     snprintf(name, 64, "kx_conv_fwd_tc<bn%d,f32x3,%s%s>", BN,
-             pl.im2col ? "im2col" : (TAPR ? "box,tapr" : "box"), PAIR ? ",pair" : "");
+             pl.im2col ? "im2col" : "box", PAIR ? ",pair" : "");
   set_last_kernel_name(name);
   return launch_status();
 }
@@ -706,13 +652,6 @@ int conv_fwd_implicit(const Exec& e, const ConvShape& g, const float* x, const f
     const int rc =
         pl.bn == 128 ? launch_conv_tc<128, true>(e, g, t, xh, xl, cp, wp, wp_lo, y, alpha, beta, pl)
                      : launch_conv_tc<64, true>(e, g, t, xh, xl, cp, wp, wp_lo, y, alpha, beta, pl);
-    if (rc != KX_ERR_UNSUPPORTED) return rc;
-  }
-  if (pl.tapr) {
-    const int rc =
-        pl.bn == 128
-            ? launch_conv_tc<128, false, true>(e, g, t, xh, xl, cp, wp, wp_lo, y, alpha, beta, pl)
-            : launch_conv_tc<64, false, true>(e, g, t, xh, xl, cp, wp, wp_lo, y, alpha, beta, pl);
     if (rc != KX_ERR_UNSUPPORTED) return rc;
   }
   if (pl.bn == 128)

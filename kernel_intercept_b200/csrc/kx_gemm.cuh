@@ -102,13 +102,6 @@ struct GemmParams {
   // output pixels whatever row or image they fall in, and output row f is
   // pixel f % cv_pq of image f / cv_pq (D offset image * strideD + pixel).
   int cv_im2col, cv_pq;
-  // Tap reuse (kernel instantiated with Cfg::TAPR; box tiles, stride 1): the
-  // A box covers cv_hbox + (cv_r - 1) * cv_dil_h input rows (cv_arows rows of
-  // 128 bytes in shared memory) and serves the cv_r filter rows of one
-  // (filter column, channel block): filter row r reads it from row
-  // r * cv_dil_h * cv_wbox on.  K runs over (filter column, channel block,
-  // filter row), r innermost.
-  int cv_r, cv_arows;
   // cv_wgrad = 1: backward filter (kernel instantiated with CONV = true and an
   // MN-major B).  M = output channels, N = (filter tap, input channel) as
   // cv_nb_per_tap channel blocks of BN per tap, K = output pixels of every
@@ -165,7 +158,7 @@ KX_DEV bool timed_wait(uint32_t bar, uint32_t parity, const WaitCtl& wc,
   return ok;
 }
 
-template <int BN_, Arith AR_, bool A_MN_, bool B_MN_, bool PAIR_ = false, bool TAPR_ = false>
+template <int BN_, Arith AR_, bool A_MN_, bool B_MN_, bool PAIR_ = false>
 struct GemmCfg {
   static constexpr int BM = 128;  // accumulator rows per CTA
   static constexpr int BN = BN_;
@@ -187,19 +180,9 @@ struct GemmCfg {
   static constexpr int B_BYTES = B_ROWS * 128;
   static constexpr int LOAD_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGE_BYTES = LOAD_BYTES * (SPLIT ? 2 : 1);
-  // Tap reuse (implicit convolution, box tiles): an A ring of SA stages, each
-  // one box of up to TAPR_AROWS rows (hi and lo), and a B ring of SB stages
-  // (B_hi, B_lo); barriers [0, SA) belong to A, [SA, SA + SB) to B.
-  static constexpr bool TAPR = TAPR_;
-  static constexpr int TAPR_AROWS = 192;
-  static constexpr int TAPR_A_BYTES = TAPR_AROWS * 128;
-  static constexpr int SA = TAPR ? 2 : 0;
-  static constexpr int SB_RAW = TAPR ? (192 * 1024 - SA * 2 * TAPR_A_BYTES) / (2 * B_BYTES) : 0;
-  static constexpr int SB = SB_RAW > 8 - SA ? 8 - SA : SB_RAW;
   static constexpr int STAGES_RAW = (192 * 1024) / STAGE_BYTES;
-  static constexpr int STAGES = TAPR ? SA + SB : (STAGES_RAW > 8 ? 8 : STAGES_RAW);
-  static constexpr int STAGE_REGION =
-      TAPR ? SA * 2 * TAPR_A_BYTES + SB * 2 * B_BYTES : STAGES * STAGE_BYTES;
+  static constexpr int STAGES = STAGES_RAW > 8 ? 8 : STAGES_RAW;
+  static constexpr int STAGE_REGION = STAGES * STAGE_BYTES;
   static constexpr int RING = 4;  // depth of the tile-id broadcast ring
   // TMEM columns of one accumulator buffer.  3xTF32 keeps two BN-wide
   // halves: [0, BN) = hi*hi and [BN, 2BN) = hi*lo + lo*hi (see the MMA
@@ -247,8 +230,6 @@ struct GemmCfg {
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
   static_assert(!PAIR || (BN >= 64 && (SPLIT || (!A_MN && !B_MN && ESIZE == 2))),
                 "CTA pairs: 3xTF32, or 16-bit operands with K-major A and B; BN >= 64");
-  static_assert(!TAPR || (SPLIT && !PAIR && !A_MN && !B_MN && SB >= 2),
-                "tap reuse: 3xTF32 K-major operands on one CTA");
 };
 
 struct SmemBars {
@@ -534,7 +515,6 @@ __global__ void __launch_bounds__(256, 1)
     if (lane == 0) {
       uint32_t it = 0;
       uint32_t prod_s = 0, prod_ph = 0;  // stage and phase of k-block `it`
-      uint32_t ia = 0, ib = 0;  // tap reuse: A boxes and B k-blocks issued
       int taken = 0;
       for (uint32_t slot = 0;; ++slot) {
         int tile;
@@ -617,58 +597,6 @@ __global__ void __launch_bounds__(256, 1)
             rr = tap / p.cv_s;
             ss = tap - rr * p.cv_s;
           }
-        }
-        if constexpr (CONV && Cfg::TAPR) {
-          // K order (filter column ss, channel block cb, filter row r), r
-          // innermost: one A box per (ss, cb) serves the R filter rows.
-          const int ab0 = kb0 / p.cv_r;
-          int tr = kb0 - ab0 * p.cv_r;
-          int tss = ab0 / p.cv_cb;
-          int tcb = ab0 - tss * p.cv_cb;
-          const uint32_t a_bytes = static_cast<uint32_t>(p.cv_arows) * 128u;
-          bool ok = true;
-          for (int kb = kb0; kb < kb0 + nkb; ++kb) {
-            const long long t_iss = stats ? clock64() : 0;
-            if (kb == kb0 || tr == 0) {
-              const uint32_t sa = ia % Cfg::SA;
-              if (!timed_wait(smem_addr(&sb->empty[sa]), ((ia / Cfg::SA) & 1) ^ 1, wc,
-                              stats ? &st_a : nullptr)) {
-                ok = false;
-                break;
-              }
-              const uint32_t fa = smem_addr(&sb->full[sa]);
-              mbar_arrive_expect_tx(fa, 2u * a_bytes);
-              const uint32_t abase = smem_addr(smem + sa * 2 * Cfg::TAPR_A_BYTES);
-              const int wx = cv_w0 + tss * p.cv_dil_w;
-              tma_load_4d(abase, &tmA, fa, tcb * 32, wx, cv_h0, cv_img);
-              tma_load_4d(abase + Cfg::TAPR_A_BYTES, &tmAlo, fa, tcb * 32, wx, cv_h0, cv_img);
-              ++ia;
-            }
-            const uint32_t sbi = ib % Cfg::SB;
-            if (!timed_wait(smem_addr(&sb->empty[Cfg::SA + sbi]), ((ib / Cfg::SB) & 1) ^ 1, wc,
-                            stats ? &st_a : nullptr)) {
-              ok = false;
-              break;
-            }
-            const uint32_t fbb = smem_addr(&sb->full[Cfg::SA + sbi]);
-            mbar_arrive_expect_tx(fbb, 2u * Cfg::B_BYTES);
-            const uint32_t bbase =
-                smem_addr(smem + Cfg::SA * 2 * Cfg::TAPR_A_BYTES + sbi * 2 * Cfg::B_BYTES);
-            const int kbb = (tr * p.cv_s + tss) * p.cv_cb + tcb;  // packed filter k-block
-            tma_load_3d(bbase, &tmB, fbb, kbb * Cfg::BK, n0, bb);
-            tma_load_3d(bbase + Cfg::B_BYTES, &tmBlo, fbb, kbb * Cfg::BK, n0, bb);
-            ++ib;
-            if (++tr == p.cv_r) {
-              tr = 0;
-              if (++tcb == p.cv_cb) {
-                tcb = 0;
-                ++tss;
-              }
-            }
-            if (stats) st_c += static_cast<unsigned long long>(clock64() - t_iss);
-          }
-          if (!ok) break;
-          continue;
         }
         bool ok = true;
         for (int kb = kb0; kb < kb0 + nkb; ++kb, ++it) {
@@ -789,12 +717,7 @@ __global__ void __launch_bounds__(256, 1)
       WaitCtl drain{&sb->abort_flag, nullptr, p.timeout_ns};
       int dummy_abort = 0;
       drain.abort_flag = &dummy_abort;
-      if constexpr (Cfg::TAPR) {
-        for (uint32_t j = ia > static_cast<uint32_t>(Cfg::SA) ? ia - Cfg::SA : 0; j < ia; ++j)
-          mbar_wait(smem_addr(&sb->full[j % Cfg::SA]), (j / Cfg::SA) & 1, drain);
-        for (uint32_t j = ib > static_cast<uint32_t>(Cfg::SB) ? ib - Cfg::SB : 0; j < ib; ++j)
-          mbar_wait(smem_addr(&sb->full[Cfg::SA + j % Cfg::SB]), (j / Cfg::SB) & 1, drain);
-      } else if (DIRECT && !leader) {
+      if (DIRECT && !leader) {
         // the follower's loads complete on the leader's barriers: they have
         // landed once the leader's MMAs consumed them, i.e. once the commit
         // that frees each of the last S stages arrived here
@@ -828,7 +751,6 @@ __global__ void __launch_bounds__(256, 1)
           sdesc_sw128(smem_addr(stageA(0)), Cfg::A_LBO, Cfg::A_SBO, Cfg::A_LAYOUT);
       const uint64_t b_desc0 =
           sdesc_sw128(smem_addr(stageB(0)), Cfg::B_LBO, Cfg::B_SBO, Cfg::B_LAYOUT);
-      uint32_t ia = 0, ib = 0;  // tap reuse: A boxes and B k-blocks consumed
       const long long t_loop = stats ? clock64() : 0;
       bool ok = true;
       for (uint32_t slot = 0; ok; ++slot) {
@@ -841,69 +763,6 @@ __global__ void __launch_bounds__(256, 1)
         if (tile < 0) break;
         int kb0, nkb;
         tile_k_range(tile, p, kb0, nkb);
-        if constexpr (CONV && Cfg::TAPR) {
-          // filter row r reads the A box from row r * dil_h * wbox on (a
-          // multiple of 8 rows: whole 1024-byte swizzle atoms)
-          int tr = kb0 - (kb0 / p.cv_r) * p.cv_r;
-          uint32_t a_cur = 0;
-          const uint32_t rstep = static_cast<uint32_t>(p.cv_dil_h * p.cv_wbox) * 128u;
-          for (int kb = 0; kb < nkb && ok; ++sc) {
-            const uint32_t a = sc & 1;
-            if (!timed_wait(smem_addr(&sb->tempty[a]), ((sc >> 1) & 1) ^ 1, wc,
-                            stats ? &st_b : nullptr)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            const uint32_t d_tmem = tmem + a * Cfg::ACC_COLS;
-            const int kend = (nkb - kb > seg) ? kb + seg : nkb;
-            const int kfirst = kb;
-            for (; kb < kend; ++kb) {
-              if (kb == 0 || tr == 0) {
-                a_cur = ia % Cfg::SA;
-                if (!timed_wait(smem_addr(&sb->full[a_cur]), (ia / Cfg::SA) & 1, wc,
-                                stats ? &st_a : nullptr)) {
-                  ok = false;
-                  break;
-                }
-                ++ia;
-              }
-              const uint32_t sbi = ib % Cfg::SB;
-              if (!timed_wait(smem_addr(&sb->full[Cfg::SA + sbi]), (ib / Cfg::SB) & 1, wc,
-                              stats ? &st_a : nullptr)) {
-                ok = false;
-                break;
-              }
-              const long long t_iss = stats ? clock64() : 0;
-              tc_fence_after();
-              const uint32_t a_hi =
-                  smem_addr(smem + a_cur * 2 * Cfg::TAPR_A_BYTES) + static_cast<uint32_t>(tr) * rstep;
-              const uint32_t a_lo = a_hi + Cfg::TAPR_A_BYTES;
-              const uint32_t b_hi =
-                  smem_addr(smem + Cfg::SA * 2 * Cfg::TAPR_A_BYTES + sbi * 2 * Cfg::B_BYTES);
-#pragma unroll
-              for (int kk = 0; kk < Cfg::BK / Cfg::UMMA_K; ++kk) {
-                const uint64_t ad =
-                    sdesc_sw128(a_hi + kk * 32, Cfg::A_LBO, Cfg::A_SBO, Cfg::A_LAYOUT);
-                const uint64_t adl =
-                    sdesc_sw128(a_lo + kk * 32, Cfg::A_LBO, Cfg::A_SBO, Cfg::A_LAYOUT);
-                const uint64_t bd =
-                    sdesc_sw128(b_hi + kk * 32, Cfg::B_LBO, Cfg::B_SBO, Cfg::B_LAYOUT);
-                const uint32_t acc = (kb > kfirst || kk > 0) ? 1u : 0u;
-                umma_tf32(d_tmem, ad, bd, Cfg::IDESC2, acc);           // hi x [B_hi; B_lo]
-                umma_tf32(d_tmem + Cfg::BN, adl, bd, Cfg::IDESC, 1u);  // lo x B_hi
-              }
-              tc_commit(smem_addr(&sb->empty[Cfg::SA + sbi]));
-              ++ib;
-              if (tr == p.cv_r - 1 || kb == nkb - 1) tc_commit(smem_addr(&sb->empty[a_cur]));
-              if (++tr == p.cv_r) tr = 0;
-              if (stats) st_d += static_cast<unsigned long long>(clock64() - t_iss);
-            }
-            if (!ok) break;
-            tc_commit(smem_addr(&sb->tfull[a]));
-          }
-          continue;
-        }
         for (int kb = 0; kb < nkb && ok; ++sc) {
           const uint32_t a = sc & 1;
           const bool tfree =

@@ -92,10 +92,7 @@ def test_conv_fwd_implicit_gemm(cuda, case):
     name = kx.last_kernel_name()
     assert name.startswith("kx_conv_fwd_tc<")
     mode = os.environ.get("KX_CONV_IM2COL")
-    tapr = os.environ.get("KX_CONV_TAPR")
-    if tapr is not None:
-        assert ("tapr" in name) == (tapr == "2" and _tapr_eligible(case)), name
-    if mode is not None and "tapr" not in name:
+    if mode is not None:
         assert ("box" if mode == "0" else "im2col") in name
     pair = os.environ.get("KX_CTA_PAIR")
     if pair is not None:
@@ -111,72 +108,10 @@ def test_conv_fwd_tile_modes(cuda, case, mode, pair, monkeypatch):
     output rows (KX_CONV_IM2COL=0) or im2col-mode loads of 128 consecutive
     output pixels (KX_CONV_IM2COL=1), on one CTA per 128-row tile
     (KX_CTA_PAIR=0) or on 2-CTA clusters with cta_group::2 MMAs over
-    256-row tiles (KX_CTA_PAIR=1); tap reuse off."""
+    256-row tiles (KX_CTA_PAIR=1)."""
     monkeypatch.setenv("KX_CONV_IM2COL", mode)
     monkeypatch.setenv("KX_CTA_PAIR", pair)
-    monkeypatch.setenv("KX_CONV_TAPR", "0")
     test_conv_fwd_implicit_gemm(cuda, case)
-
-
-def _tapr_eligible(case, dgrad=False):
-    """Tap reuse applies to stride-1 filters with at least 2 rows whose taps
-    the kernel does not fold into channels (it folds when that at least
-    halves K: ceil32(C*R*S) * 2 <= ceil32(C) * R * S, C the kernel's input
-    channels, K of the forward problem for backward data)."""
-    n, c, h, w, k, r, s, pad, stride, dil, xc = case
-    ch = k if dgrad else c
-    kf = (ch * r * s + 31) // 32 * 32
-    folded = kf * 2 <= (ch + 31) // 32 * 32 * r * s
-    return stride == (1, 1) and r >= 2 and not folded
-
-
-# tap reuse forced (KX_CONV_TAPR=2): ragged boxes, partial channel blocks,
-# dilation, R = 5, R != S, split K, tiles smaller than an image row
-TAPR_CASES = [
-    (2, 64, 32, 32, 64, 3, 3, (1, 1), (1, 1), (1, 1), True),    # boxes tile exactly
-    (8, 32, 56, 56, 128, 3, 3, (1, 1), (1, 1), (1, 1), True),   # 128-wide channel tiles
-    (2, 40, 17, 19, 72, 3, 3, (1, 1), (1, 1), (1, 1), True),    # ragged everything
-    (2, 16, 30, 30, 32, 5, 5, (2, 2), (1, 1), (1, 1), False),   # 5x5, flipped
-    (2, 32, 20, 22, 64, 3, 3, (2, 2), (1, 1), (2, 2), True),    # dilated rows
-    (2, 48, 21, 26, 96, 3, 5, (1, 2), (1, 1), (1, 1), True),    # R != S
-    (4, 32, 7, 7, 64, 3, 3, (1, 1), (1, 1), (1, 1), True),      # per-element stores
-    (8, 256, 14, 14, 256, 3, 3, (1, 1), (1, 1), (1, 1), True),  # split K
-]
-
-
-@pytest.mark.parametrize("case", TAPR_CASES)
-def test_conv_fwd_tap_reuse(cuda, case, monkeypatch):
-    """Forward convolution with tap reuse: one A box per (filter column,
-    channel block) feeds every filter row through shifted descriptors."""
-    monkeypatch.setenv("KX_CONV_TAPR", "2")
-    test_conv_fwd_implicit_gemm(cuda, case)
-
-
-def test_conv_tap_reuse_modes(cuda, monkeypatch):
-    """Tap reuse is off by default; KX_CONV_TAPR=1 runs it where whole boxes
-    tile the output exactly (VGG16's 224- and 112-wide layers) and not on
-    ragged maps."""
-    monkeypatch.delenv("KX_CONV_IM2COL", raising=False)
-    kx = _kx()
-    monkeypatch.delenv("KX_CONV_TAPR", raising=False)
-    test_conv_fwd_implicit_gemm(cuda, TAPR_CASES[0])
-    assert "tapr" not in kx.last_kernel_name()
-    monkeypatch.setenv("KX_CONV_TAPR", "1")
-    for case, expect in ((TAPR_CASES[0], True), (TAPR_CASES[1], False)):
-        kd, od = _desc(case)
-        rng = np.random.default_rng(5)
-        x = rng.standard_normal((od.n, od.c, od.h, od.w)).astype(np.float32)
-        w = rng.standard_normal((od.k, od.c, od.r, od.s)).astype(np.float32)
-        ref = o.conv_fwd(od, 1.0, x, w)
-        p, q = o.conv_out_dims(od)
-        dx, dw = _dev(x), _dev(w)
-        dy = _dev(np.zeros((od.n, od.k, p, q), np.float32))
-        kx.conv_fwd(kx.current_exec(), kd, 1.0, dx.data_ptr(), dw.data_ptr(), 0.0,
-                    dy.data_ptr())
-        import torch
-        torch.cuda.synchronize()
-        assert ("tapr" in kx.last_kernel_name()) == expect
-        assert o.normwise_rel_err(dy.cpu().numpy(), ref) <= TOL_F32
 
 
 @pytest.mark.parametrize("case", CONV_CASES)
@@ -215,16 +150,6 @@ def test_conv_bwd_data_implicit(cuda, case):
     kx = _kx()
     test_conv_bwd_data(cuda, case)
     assert kx.last_kernel_name().startswith("kx_conv_fwd_tc<")
-
-
-@pytest.mark.parametrize("case", DGRAD_IMPLICIT_CASES)
-def test_conv_bwd_data_tap_reuse(cuda, case, monkeypatch):
-    """Backward data through the forward kernel with tap reuse forced."""
-    monkeypatch.setenv("KX_CONV_TAPR", "2")
-    kx = _kx()
-    test_conv_bwd_data(cuda, case)
-    if _tapr_eligible(case, dgrad=True):
-        assert "tapr" in kx.last_kernel_name()
 
 
 @pytest.mark.parametrize("case", CONV_CASES)
