@@ -82,6 +82,12 @@ def parse():
     ap.add_argument("--gc-freeze", type=int, default=0,
                     help="1: freeze the warm-up's objects and pause Python's cyclic garbage "
                          "collector while the clients run (collections stop every thread)")
+    ap.add_argument("--no-profile", action="store_true",
+                    help="no profiling session in the kx arm's timed phases (no roofline)")
+    ap.add_argument("--profile-every", type=int, default=4,
+                    help="the timed phases' profiling sessions time every n-th captured "
+                         "dense op of each client (each timed op costs two event records "
+                         "on the dispatching thread)")
     ap.add_argument("--trace", default="",
                     help="write a Chrome trace of the interposer's activity in the paced phase "
                          "to this path; a .gz path is compressed")
@@ -409,6 +415,8 @@ def run_group(args):
         gc.freeze()
         gc.disable()
     kxlib = kx.lib()
+    # the kernel tables above timed every op; the timed phases sample
+    orion.orion_set_profile_every(max(1, args.profile_every))
 
     def profiled(tag, run):
         """Runs run(on_start); the profiling session opens in on_start (after
@@ -435,7 +443,8 @@ def run_group(args):
     for c in range(n_clients):
         orion.waits(c, reset=True)
     kr = run_phases(harness, orion, hp, bes, args, lat_steps, args.steps, e2e=not args.no_e2e,
-                    profiled=profiled, clocks=Clocks(local), kxlib=kxlib, ranks=ranks)
+                    profiled=None if args.no_profile else profiled, clocks=Clocks(local),
+                    kxlib=kxlib, ranks=ranks)
     waits = {c: orion.waits(c) for c in range(n_clients)}
     stats = {c: orion.stats(c) for c in range(n_clients)}
     orion.orion_set_capture(0)
@@ -504,6 +513,8 @@ def run_group(args):
                                for k, v in be_totals.items() if v is not None},
         "roofline": roof, "roofline_hp_solo": roof_solo, "ops": op_table(kr["cont_recs"]),
         "cpu_baseline": cpu, "clocks": kr["clocks"], "gpu_launches": int(kr["launches"]),
+        # roofline and ops: every n-th captured dense op of each client is timed
+        "profile_sampled_every": max(1, args.profile_every),
         "captured": stats,
         "client_waits": {str(c): {k: rnd(v) if isinstance(v, float) else v for k, v in w.items()}
                          for c, w in waits.items()},
@@ -714,7 +725,7 @@ def roofline(recs, peaks, peak_src, tf32, sustained, cfg):
            "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
            "traffic": NCU_TRAFFIC_PER_LAUNCH.get((cfg, f"{client}:{op}")),
            "peak_source": f"{key} of {peak_src}",
-           "op": f"{client}:{op}", "kernel": top, "launches": agg["n"],
+           "op": f"{client}:{op}", "kernel": top, "launches_timed": agg["n"],
            "avg_ms": round(avg_ms, 4), "share_of_captured_ms":
            round(agg["ms"] / sum(v["ms"] for v in by_op.values()), 4)}
     if "bf16" not in top and "f16" not in top:

@@ -150,6 +150,8 @@ public:
     /** The HP client queued an op (the issue gate's clock). */
     void note_hp_issue();
     void set_be_host_hold_us(int us) { be_host_hold_ns_.store(us < 0 ? 0 : 1000LL * us); }
+    /** Profiling sessions time every n-th dense op of each client (n >= 1). */
+    void set_profile_every(int n) { profile_every_.store(n < 1 ? 1 : n); }
     int be_host_hold_us() const { return static_cast<int>(be_host_hold_ns_.load() / 1000); }
     volatile int* hp_flag_host() const { return hp_flag_host_; }
     int* hp_flag_device() const { return hp_flag_dev_; }
@@ -205,6 +207,8 @@ private:
     float be_max_ns_{50000.0f};
     std::atomic<long long> be_host_hold_ns_{3000000};
     long long be_host_window_ns_{500000};
+    std::atomic<int> profile_every_{1};            // see execute_operation
+    std::atomic<uint64_t> prof_seq_[MAX_CLIENTS];  // dense ops per client
     std::atomic<long long> hp_last_issue_ns_{-(1LL << 60)};
     cudaStream_t flag_stream_{nullptr};
     void publish_hp_flag(int value);
@@ -267,6 +271,9 @@ void orion_set_be_host_hold_us(int us);
 int orion_get_be_host_hold_us();
 /** Ops of one BE client whose thread waited at the issue gate. */
 unsigned long long orion_get_client_host_holds(int client_idx);
+/** Addition: profiling sessions time every n-th captured dense op of each
+ *  client (default 1: every op; ORION_PROFILE_EVERY sets the initial value). */
+void orion_set_profile_every(int n);
 /** Called by the reference's launch_jobs.py; synchronises the client's stream. */
 void block(int client_idx);
 }

@@ -6,6 +6,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <cstring>
+#include <unordered_map>
 #include <vector>
 
 namespace kx {
@@ -239,11 +240,51 @@ int persistent_grid(const Exec& e, int tiles) {
   return tl_last_grid;
 }
 
+namespace {
+// Tensor maps by their complete description.  An encoded map is a pure
+// function of these arguments, and a model step's activations and weights
+// come back at the same addresses step after step, so most encodes repeat
+// (a GEMM launch encodes up to five maps, a microsecond or more each on the
+// dispatching thread).  Per thread, so no lock; cleared when it grows large.
+struct MapKey {
+  uint64_t w[24];
+  int n;
+  bool operator==(const MapKey& o) const {
+    return n == o.n && std::memcmp(w, o.w, sizeof(uint64_t) * n) == 0;
+  }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& k) const {
+    uint64_t h = 1469598103934665603ull;
+    for (int i = 0; i < k.n; ++i) h = (h ^ k.w[i]) * 1099511628211ull;
+    return static_cast<size_t>(h);
+  }
+};
+thread_local std::unordered_map<MapKey, CUtensorMap, MapKeyHash> tl_map_cache;
+constexpr size_t kMapCacheMax = 8192;
+}  // namespace
+
 bool encode_map(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* base,
                 const uint64_t* dims, const uint64_t* strides_bytes, const uint32_t* box,
                 CUtensorMapSwizzle swz, const uint32_t* elem_strides) {
   EncodeTiledFn fn = encode_fn();
   if (fn == nullptr) return false;
+  if (rank < 1 || rank > 5) return false;
+  MapKey key;
+  key.n = 0;
+  key.w[key.n++] = reinterpret_cast<uintptr_t>(base);
+  key.w[key.n++] = (static_cast<uint64_t>(dt) << 32) | (static_cast<uint64_t>(swz) << 8) |
+                   static_cast<uint64_t>(rank);
+  for (int i = 0; i < rank; ++i) key.w[key.n++] = dims[i];
+  for (int i = 0; i + 1 < rank; ++i) key.w[key.n++] = strides_bytes[i];
+  for (int i = 0; i < rank; ++i)
+    key.w[key.n++] = (static_cast<uint64_t>(box[i]) << 32) |
+                     (elem_strides != nullptr ? elem_strides[i] : 1u);
+  auto hit = tl_map_cache.find(key);
+  if (hit != tl_map_cache.end()) {
+    std::memcpy(map, &hit->second, sizeof(CUtensorMap));
+    return true;
+  }
   if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0) return false;
   cuuint64_t d[5];
   cuuint64_t s[4];
@@ -267,7 +308,10 @@ bool encode_map(CUtensorMap* map, CUtensorMapDataType dt, int rank, const void* 
   CUresult r = fn(map, dt, static_cast<cuuint32_t>(rank), const_cast<void*>(base), d, s, b, es,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS;
+  if (r != CUDA_SUCCESS) return false;
+  if (tl_map_cache.size() >= kMapCacheMax) tl_map_cache.clear();
+  tl_map_cache.emplace(key, *map);
+  return true;
 }
 
 bool encode_im2col_map(CUtensorMap* map, const void* base, const uint64_t* dims,

@@ -243,6 +243,7 @@ bool Scheduler::init(int num_clients, const SchedulerConfig& config) {
     be_host_hold_ns_.store(std::max(0LL, std::atoll(s)) * 1000);
   if (const char* s = std::getenv("KX_BE_HOST_WINDOW_US"))
     be_host_window_ns_ = std::max(0LL, std::atoll(s)) * 1000;
+  if (const char* s = std::getenv("ORION_PROFILE_EVERY")) set_profile_every(std::atoi(s));
   ORION_REAL(cudart, cudaEventCreateWithFlags)(&hp_last_event_, cudaEventDisableTiming);
   g_orion_state.init(num_clients, sms);
   g_orion_state.sm_threshold = config_.sm_threshold;
@@ -564,7 +565,12 @@ cudaError_t Scheduler::execute_operation(OperationPtr op, cudaStream_t fallback)
     pol.done_flag = hp_flag_dev_ + c;
   }
   cudaEvent_t ev_start = nullptr, ev_end = nullptr;
-  const bool profiling = g_profiler.active();
+  // a profiling session times every n-th dense op of each client (two
+  // events around it), so a session over a timed region costs that region
+  // 1/n of the event records (orion_set_profile_every, ORION_PROFILE_EVERY)
+  const int every = profile_every_.load(std::memory_order_relaxed);
+  const bool profiling =
+      g_profiler.active() && (every <= 1 || prof_seq_[c].fetch_add(1) % every == 0);
   if (profiling) {
     ev_start = take_profile_event();
     ev_end = take_profile_event();
@@ -930,6 +936,8 @@ int orion_set_sm_budgets(int hp_sms, int be_sms) {
 void orion_set_be_host_hold_us(int us) { orion::g_scheduler.set_be_host_hold_us(us); }
 
 int orion_get_be_host_hold_us() { return orion::g_scheduler.be_host_hold_us(); }
+
+void orion_set_profile_every(int n) { orion::g_scheduler.set_profile_every(n); }
 
 unsigned long long orion_get_client_host_holds(int client_idx) {
   if (client_idx < 0 || client_idx >= orion::MAX_CLIENTS) return 0;

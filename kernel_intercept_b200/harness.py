@@ -60,6 +60,7 @@ class Orion:
             "orion_get_client_stats": ([I, ctypes.POINTER(ctypes.c_ulonglong)], I),
             "orion_set_be_host_hold_us": ([I], None), "orion_get_be_host_hold_us": ([], I),
             "orion_get_client_host_holds": ([I], ctypes.c_ulonglong),
+            "orion_set_profile_every": ([I], None),
             "orion_load_profile": ([ctypes.c_char_p], I),
             "orion_start_profiling": ([ctypes.c_char_p], None),
             "orion_end_profiling": ([ctypes.c_char_p], None),

@@ -49,6 +49,7 @@ cudaEventSynchronize cudaEventQuery cudaStreamQuery orion_set_be_keep_sms orion_
 orion_set_sm_budgets orion_get_client_stats orion_op_log_start orion_op_log_end
 orion_get_client_waits orion_trace_start orion_trace_end orion_set_profile_launches
 orion_set_be_host_hold_us orion_get_be_host_hold_us orion_get_client_host_holds
+orion_set_profile_every
 """.split()
 
 
@@ -135,6 +136,7 @@ L.orion_set_async_mode(0); assert L.orion_get_async_mode() == 0
 L.orion_set_be_keep_sms(24); assert L.orion_get_be_keep_sms() == 24
 L.orion_set_be_host_hold_us(300); assert L.orion_get_be_host_hold_us() == 300
 L.orion_set_be_host_hold_us(0); assert L.orion_get_be_host_hold_us() == 0
+L.orion_set_profile_every(4); L.orion_set_profile_every(1)
 L.orion_get_client_host_holds.restype = ctypes.c_ulonglong
 assert L.orion_get_client_host_holds(1) == 0 and L.orion_get_client_host_holds(99) == 0
 out = (ctypes.c_ulonglong * 6)()
