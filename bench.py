@@ -81,13 +81,13 @@ def parse():
                          "0: Python's default of 5 ms)")
     ap.add_argument("--gc-freeze", type=int, default=0,
                     help="1: freeze the warm-up's objects and pause Python's cyclic garbage "
-                         "collector while the clients run (collections stop every thread)")
+                         "collector while the clients run, in both arms (collections stop every thread)")
     ap.add_argument("--no-profile", action="store_true",
                     help="no profiling session in the kx arm's timed phases (no roofline)")
     ap.add_argument("--profile-every", type=int, default=4,
-                    help="the timed phases' profiling sessions time every n-th captured "
-                         "dense op of each client (each timed op costs two event records "
-                         "on the dispatching thread)")
+                    help="the timed phases' profiling sessions time one in n captured dense "
+                         "ops of each client, picked by a hash of the op's sequence number "
+                         "(each timed op costs two event records on the dispatching thread)")
     ap.add_argument("--trace", default="",
                     help="write a Chrome trace of the interposer's activity in the paced phase "
                          "to this path; a .gz path is compressed")
@@ -345,6 +345,18 @@ def run_phases(harness, orion, hp, bes, args, lat_steps, hp_steps, e2e, profiled
     return res
 
 
+def gc_pause(on):
+    """With --gc-freeze 1, before each arm's timed phases: collect, freeze the
+    survivors and keep Python's cyclic collector off.  A collection runs on
+    whichever client thread triggers it and stops every other Python thread
+    until it ends, so the HP thread's issue stalls behind the BE thread's."""
+    if on:
+        import gc
+        gc.collect()
+        gc.freeze()
+        gc.disable()
+
+
 def run_group(args):
     import torch
 
@@ -378,6 +390,7 @@ def run_group(args):
     lat_steps = max(args.steps, args.lat_steps)
 
     # ---- library arm: capture off, PyTorch calls cuBLAS / cuDNN itself
+    gc_pause(args.gc_freeze)
     lib = None
     if not args.no_library:
         lr = run_phases(harness, None, hp, bes, args, max(50, lat_steps // 2), args.steps,
@@ -409,11 +422,7 @@ def run_group(args):
         rows = profile_tables.load(orion, paths)
         tables = {"source": args.kernel_info, "rows": rows,
                   "hp_kernels_ms": rnd(sum(r[4] for r in profile_tables.read_csv(paths[0])) / 1e6)}
-    if args.gc_freeze:
-        import gc
-        gc.collect()
-        gc.freeze()
-        gc.disable()
+    gc_pause(args.gc_freeze)
     kxlib = kx.lib()
     # the kernel tables above timed every op; the timed phases sample
     orion.orion_set_profile_every(max(1, args.profile_every))
@@ -513,7 +522,7 @@ def run_group(args):
                                for k, v in be_totals.items() if v is not None},
         "roofline": roof, "roofline_hp_solo": roof_solo, "ops": op_table(kr["cont_recs"]),
         "cpu_baseline": cpu, "clocks": kr["clocks"], "gpu_launches": int(kr["launches"]),
-        # roofline and ops: every n-th captured dense op of each client is timed
+        # roofline and ops: one in n captured dense ops of each client is timed
         "profile_sampled_every": max(1, args.profile_every),
         "captured": stats,
         "client_waits": {str(c): {k: rnd(v) if isinstance(v, float) else v for k, v in w.items()}
@@ -726,8 +735,11 @@ def roofline(recs, peaks, peak_src, tf32, sustained, cfg):
            "traffic": NCU_TRAFFIC_PER_LAUNCH.get((cfg, f"{client}:{op}")),
            "peak_source": f"{key} of {peak_src}",
            "op": f"{client}:{op}", "kernel": top, "launches_timed": agg["n"],
-           "avg_ms": round(avg_ms, 4), "share_of_captured_ms":
-           round(agg["ms"] / sum(v["ms"] for v in by_op.values()), 4)}
+           "avg_ms": round(avg_ms, 4),
+           # of the HP client's timed captured ops (a BE op's events also
+           # span the time it spends stopped while HP runs)
+           "share_of_hp_captured_ms":
+           round(agg["ms"] / sum(v["ms"] for k, v in by_op.items() if k[0] == client), 4)}
     if "bf16" not in top and "f16" not in top:
         # fp32 runs as 3xTF32 (three TF32 products per MAC): its ceiling is the TF32 rate / 3
         ceiling = tf32 / 3.0

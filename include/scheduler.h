@@ -150,7 +150,7 @@ public:
     /** The HP client queued an op (the issue gate's clock). */
     void note_hp_issue();
     void set_be_host_hold_us(int us) { be_host_hold_ns_.store(us < 0 ? 0 : 1000LL * us); }
-    /** Profiling sessions time every n-th dense op of each client (n >= 1). */
+    /** Profiling sessions time one in n dense ops of each client (n >= 1). */
     void set_profile_every(int n) { profile_every_.store(n < 1 ? 1 : n); }
     int be_host_hold_us() const { return static_cast<int>(be_host_hold_ns_.load() / 1000); }
     volatile int* hp_flag_host() const { return hp_flag_host_; }
@@ -271,8 +271,9 @@ void orion_set_be_host_hold_us(int us);
 int orion_get_be_host_hold_us();
 /** Ops of one BE client whose thread waited at the issue gate. */
 unsigned long long orion_get_client_host_holds(int client_idx);
-/** Addition: profiling sessions time every n-th captured dense op of each
- *  client (default 1: every op; ORION_PROFILE_EVERY sets the initial value). */
+/** Addition: profiling sessions time one in n captured dense ops of each
+ *  client, picked by a hash of the op's sequence number (default 1: every op;
+ *  ORION_PROFILE_EVERY sets the initial value). */
 void orion_set_profile_every(int n);
 /** Called by the reference's launch_jobs.py; synchronises the client's stream. */
 void block(int client_idx);

@@ -390,6 +390,16 @@ bool Scheduler::orion_should_schedule(OperationPtr op, int client_idx) {
 }
 
 namespace {
+// splitmix64's finaliser (Steele, Lea, Flood 2014) over a sequence number,
+// reduced to a 1-in-n pick that has no period of its own
+bool sampled(uint64_t seq, int n) {
+  uint64_t z = seq + 0x9e3779b97f4a7c15ull;
+  z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+  z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+  z ^= z >> 31;
+  return z % static_cast<uint64_t>(n) == 0;
+}
+
 // PyGILState_Check of the interpreter hosting the process, if there is one
 int (*gil_check_fn())() {
   static int (*fn)() = reinterpret_cast<int (*)()>(dlsym(RTLD_DEFAULT, "PyGILState_Check"));
@@ -565,12 +575,15 @@ cudaError_t Scheduler::execute_operation(OperationPtr op, cudaStream_t fallback)
     pol.done_flag = hp_flag_dev_ + c;
   }
   cudaEvent_t ev_start = nullptr, ev_end = nullptr;
-  // a profiling session times every n-th dense op of each client (two
-  // events around it), so a session over a timed region costs that region
-  // 1/n of the event records (orion_set_profile_every, ORION_PROFILE_EVERY)
+  // a profiling session times one in n dense ops of each client (two events
+  // around it), so a session over a timed region costs that region 1/n of
+  // the event records (orion_set_profile_every, ORION_PROFILE_EVERY).  The
+  // choice hashes the op's sequence number: a plain "every n-th op" aliases
+  // with a step whose dense-op count is a multiple of n and then times the
+  // same few layers of every step
   const int every = profile_every_.load(std::memory_order_relaxed);
   const bool profiling =
-      g_profiler.active() && (every <= 1 || prof_seq_[c].fetch_add(1) % every == 0);
+      g_profiler.active() && (every <= 1 || sampled(prof_seq_[c].fetch_add(1), every));
   if (profiling) {
     ev_start = take_profile_event();
     ev_end = take_profile_event();

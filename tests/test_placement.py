@@ -93,3 +93,22 @@ def test_bench_reference_arm_other_ranks_exit_quietly(capsys):
     finally:
         os.environ.pop("RANK")
     assert capsys.readouterr().out == ""
+
+
+def test_bench_roofline_is_the_hp_clients_dominant_op():
+    """The roofline's op class, rate and share come from the HP client's
+    timed ops alone: a BE op's events also span the time it spends stopped."""
+    import bench
+    recs = [{"client": 0, "op_type": "CUBLAS_GEMM_EX", "duration_ms": 0.5, "work": 1e12,
+             "kernel_id": "kx_gemm_tc<bn256,bf16,Ak,Bk>"} for _ in range(4)]
+    recs += [{"client": 0, "op_type": "CUBLAS_SGEMM", "duration_ms": 1.0, "work": 1e10,
+              "kernel_id": "kx_gemm_tc<bn64,f32x3,Ak,Bk>"}]
+    recs += [{"client": 1, "op_type": "CUDNN_CONV_FWD", "duration_ms": 500.0, "work": 1e12,
+              "kernel_id": "kx_conv_fwd_tc<bn128,f32x3,im2col>"}]
+    r = bench.roofline(recs, {"bf16_tflops": 1600.0, "bf16_tflops_sustained": 1400.0},
+                       "test", 700.0, True, 4)
+    assert r["op"] == "HP:CUBLAS_GEMM_EX" and r["launches_timed"] == 4
+    assert r["achieved"] == pytest.approx(2000.0)  # 1e12 FLOP in 0.5 ms
+    assert r["peak"] == 1400.0 and r["frac"] == pytest.approx(2000.0 / 1400.0, rel=1e-3)
+    assert r["share_of_hp_captured_ms"] == pytest.approx(2.0 / 3.0, rel=1e-3)
+    assert "fp32_3xtf32_ceiling" not in r
